@@ -1,0 +1,361 @@
+#!/usr/bin/env python3
+"""Benchmark: teacher-forced window scoring of the Mamba-2 8B FP4-G16 / SQ3.25 model.
+
+Workload: full 56-layer model (vocab 256000, released per-layer
+layouts), random-init FP4 G16 weights and statics of the recorded shapes, a random-init
+Resurface adapter (soft gate), 16 reset windows x (2048 targets + 1 overlap token) per
+GPU, token ids Zipf(s=1.1) over the vocabulary.  One step = scoring all local windows
+(forward over 16 x 2048 tokens, fused lm_head + cross entropy) plus the one NLL-sum
+all-reduce across ranks.  `value` = scored tokens/s over all ranks with the windows
+already resident on the device; `e2e` = the same through the public scoring API from
+pinned host buffers (H2D of the windows, D2H of the per-window NLLs, every step).
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+  torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU, NCCL)
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import platform
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / 'mamb2_8b_fp4_recall_sq3.25_b200'))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = 'scored tokens/s (8B, per-token SQ3.25 requant)'
+UNIT = 'tokens/s'
+WINDOWS_PER_GPU, SEQLEN, VOCAB, N_LAYER = 16, 2048, 256000, 56
+FLOP_PER_TOKEN = 2 * (56 * (18560 * 4096 + 4096 * 8192) + 256000 * 4096)   # 14,369,685,504
+DECODE_BYTES_B1 = 4_111_674_420
+
+
+def peaks():
+    p = ROOT / 'MEASURED_PEAKS.json'
+    if p.exists():
+        d = json.loads(p.read_text())
+        return dict(hbm=d['hbm_gbs'], tf=d['bf16_tflops'], tf_sus=d['bf16_tflops_sustained'], src='measured')
+    return dict(hbm=6650.0, tf=1590.0, tf_sus=1400.0, src='fallback')
+
+
+def zipf_tokens(n, rng, s=1.1, vocab=VOCAB):
+    k = np.arange(1, vocab + 1, dtype=np.float64)
+    p = k ** -s
+    p /= p.sum()
+    return rng.choice(vocab, size=n, p=p).astype(np.int64)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', '-i', str(self.index), '--query-gpu=' + self.FIELDS,
+                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(',')])
+
+    def stop(self):
+        if self.proc is None:
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=['nvidia-smi unavailable'])
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = [r for r in self.rows if len(r) >= 9]
+        if not rows:
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=['no samples'])
+        sm = [float(r[1]) for r in rows if r[1].replace('.', '').isdigit()]
+        load = [x for x in sm if x > 0.5 * max(sm)] or sm
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower().startswith('active')})
+        return dict(sm_mhz=statistics.median(load), sm_max_mhz=float(rows[0][2]), reasons=reasons,
+                    samples=len(rows), power_w_max=max(float(r[3]) for r in rows if r[3].replace('.', '').isdigit()))
+
+
+def dist_init(n):
+    rank, world, local = int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1)), \
+        int(os.environ.get('LOCAL_RANK', 0))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device('cuda', local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+# ------------------------------------------------------------------ CPU reference arm
+
+def cpu_sample(tokens=16, layers=2, vocab_slice=32768, seed=0):
+    """The CPU oracle port (oracle/) on a bounded slice of the workload: one window of
+    `tokens` tokens through `layers` full-geometry layers plus the lm_head + CE over a
+    `vocab_slice`-row slice of the vocabulary, all host threads.  Returns seconds per
+    scored token extrapolated to 56 layers and the full 256000-row head."""
+    sys.path.insert(0, str(ROOT / 'tests'))
+    from _models import build_pair
+    torch.set_num_threads(os.cpu_count())
+    _, ora, _ = build_pair(n_layer=layers, vocab=vocab_slice, seed=seed, adapter=True, device='cpu')
+    rng = np.random.default_rng(seed)
+    ids = zipf_tokens(tokens + 1, rng, vocab=vocab_slice)[None]
+    ora.reset(1)
+    t0 = time.perf_counter()
+    hid = ora.backbone(ids[:, :-1])
+    t1 = time.perf_counter()
+    ora.nll(hid, ids[:, 1:])
+    t2 = time.perf_counter()
+    per_token = ((t1 - t0) * N_LAYER / layers + (t2 - t1) * VOCAB / vocab_slice) / tokens
+    return per_token, dict(tokens=tokens, layers=layers, vocab_slice=vocab_slice, seconds=t2 - t0)
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    vals = []
+    for _ in range(args.warmup_ref):
+        cpu_sample(tokens=args.ref_tokens)
+    info = None
+    for _ in range(max(1, args.steps_ref)):
+        per_tok, info = cpu_sample(tokens=args.ref_tokens)
+        vals.append(1.0 / per_tok)
+    v = statistics.median(vals)
+    line = dict(metric=METRIC, value=v, unit=UNIT, n_gpus=args.gpus, steps=len(vals), warmup=args.warmup_ref,
+                ms_per_step=None, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='f32',
+                data='synthetic', impl='reference',
+                config=dict(workload='config4: 56-layer 8B scoring, 16 x 2049-token Zipf windows per GPU',
+                            windows_per_gpu=WINDOWS_PER_GPU, seq_len=SEQLEN, vocab=VOCAB),
+                cpu_baseline=dict(value=v, unit=UNIT, cores=os.cpu_count(), kind='port',
+                                  sample=f"oracle port, 1 window x {info['tokens']} tokens through {info['layers']} "
+                                         f"layers + lm_head/CE over a {info['vocab_slice']}-row vocab slice, "
+                                         f"extrapolated to 56 layers and 256000 rows ({platform.processor() or 'cpu'})"),
+                e2e=dict(value=v, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm
+
+def build_workload(rank, device):
+    from sq325 import model as M, resurface as R
+    from sq325.state import PredictorState
+    t0 = time.time()
+    model = M.synthetic_model(seed=4, n_layer=N_LAYER, vocab=VOCAB, device=device)
+    model.adapter = R.random_bank(N_LAYER, seed=5, device=device)
+    statics = M.synthetic_statics(M.RELEASED_LAYOUTS, seed=4, device=device)
+    ex = PredictorState(model, *statics).install()
+    rng = np.random.default_rng(1000 + rank)
+    wins = zipf_tokens(WINDOWS_PER_GPU * (SEQLEN + 1), rng).reshape(WINDOWS_PER_GPU, SEQLEN + 1)
+    torch.cuda.synchronize()
+    return model, ex, wins, time.time() - t0
+
+
+def launches_per_step(M_rows, n_layer=N_LAYER, vocab=VOCAB):
+    lin = 1 if M_rows <= 64 else 2
+    per_layer = 1 + lin + 1 + 1 + 1 + lin          # add_rmsnorm, in_proj, conv, scan, resurface+norm, out_proj
+    score = 2 * ((vocab + 32767) // 32768) + 1     # per 32768-row chunk: decode + gemm; finalize
+    return 1 + n_layer * per_layer + 1 + score     # embed, layers, norm_f, head
+
+
+def time_gemm_kernel(model, rows, device, reps=5):
+    """Dominant kernel: the tcgen05 in_proj GEMM at the workload's shape, CUDA events on
+    the launching stream (the operand decode is excluded by decoding once up front)."""
+    from sq325 import _lib
+    w = model.layers[0].in_proj
+    lib = _lib.load()
+    stage = torch.empty((w.rows, w.cols), device=device, dtype=torch.float16)
+    _lib.call('sq_fp4_decode', _lib.ptr(w.codes), _lib.ptr(w.block_scale_bytes), _lib.ptr(w.global_scale),
+              w.rows, w.cols, _lib.ptr(stage), w.cols, _lib.stream_ptr())
+    x = torch.randn(rows, w.cols, device=device).half()
+    y = torch.empty(rows, w.rows, device=device, dtype=torch.float16)
+    s = torch.cuda.current_stream()
+    for _ in range(2):
+        _lib.call('sq_gemm_f16', _lib.ptr(x), w.cols, _lib.ptr(stage), w.cols, _lib.ptr(y), w.rows, rows, w.rows,
+                  w.cols, _lib.stream_ptr())
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ts = []
+    for _ in range(reps):
+        ev[0].record(s)
+        _lib.call('sq_gemm_f16', _lib.ptr(x), w.cols, _lib.ptr(stage), w.cols, _lib.ptr(y), w.rows, rows, w.rows,
+                  w.cols, _lib.stream_ptr())
+        ev[1].record(s)
+        torch.cuda.synchronize()
+        ts.append(ev[0].elapsed_time(ev[1]) / 1e3)
+    del lib
+    return statistics.median(ts), 2.0 * rows * w.rows * w.cols
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=4)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', default='native', choices=['native', 'reference'])
+    ap.add_argument('--ref-tokens', type=int, default=16)
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--decode-steps', type=int, default=32)
+    args = ap.parse_args()
+    args.steps_ref = min(args.steps, 3)
+    args.warmup_ref = 1 if args.warmup > 0 else 0
+    if args.impl == 'reference':
+        rank = int(os.environ.get('RANK', 0))
+        run_reference(args, rank, int(os.environ.get('WORLD_SIZE', 1)))
+        return
+    rank, world, local = dist_init(args.gpus)
+    device = torch.device('cuda', local)
+    import torch.distributed as dist
+    from sq325 import scoring
+
+    model, ex, wins, setup_s = build_workload(rank, device)
+    B, T = WINDOWS_PER_GPU, SEQLEN
+    ex.reserve(B * T)
+    ids_dev = torch.from_numpy(wins).to(device)
+    inp, tgt = ids_dev[:, :-1].contiguous(), ids_dev[:, 1:].contiguous()
+    hid = torch.empty((B, T, 4096), device=device, dtype=torch.float16)
+    nll = torch.empty(B * T, device=device, dtype=torch.float32)
+    red = torch.zeros(2, device=device, dtype=torch.float64)
+
+    def step():
+        ex.backbone(inp, reset=True, out=hid)
+        ex.score(hid, tgt, out=nll)
+        red[0] = nll.double().sum()
+        red[1] = float(B * T)
+        if world > 1:
+            dist.all_reduce(red)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ex.check()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0.record(s)
+    for _ in range(args.steps):
+        step()
+    e1.record(s)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    elapsed = e0.elapsed_time(e1) / 1e3
+    clk = clocks.stop()
+    ex.check()
+    t = torch.tensor([elapsed], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed = float(t)
+    tokens_all = world * B * T * args.steps
+    value = tokens_all / elapsed
+
+    # e2e through the public scoring API from pinned host windows
+    host_wins = [(i * (SEQLEN + 1), torch.from_numpy(wins[i]).pin_memory()) for i in range(B)]
+    h2d = B * (SEQLEN + 1) * 8
+    d2h = B * 8
+    scoring.evaluate_ppl(ex, host_wins, batch_windows=B, rank=0, world=1)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    e2e_steps = max(1, min(args.steps, 2))
+    for _ in range(e2e_steps):
+        res = scoring.evaluate_ppl(ex, host_wins, batch_windows=B, rank=0, world=1)
+        if world > 1:
+            buf = torch.tensor([res['nll'], float(res['target_tokens'])], dtype=torch.float64, device=device)
+            dist.all_reduce(buf)
+    torch.cuda.synchronize()
+    e2e_el = time.perf_counter() - t0
+    te = torch.tensor([e2e_el], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * B * T * e2e_steps / float(te)
+
+    # dominant kernel roofline (in_proj GEMM at the workload's M)
+    pk = peaks()
+    gemm_s, gemm_flop = time_gemm_kernel(model, B * T, device)
+    achieved = gemm_flop / gemm_s / 1e12
+
+    # batch-1 decode (greedy generation token step) on this GPU
+    decode = None
+    if rank == 0 and args.decode_steps > 0:
+        prompt = torch.from_numpy(wins[0, :64][None]).to(device)
+        h = ex.backbone(prompt, reset=True)[:, -1]
+        tok = ex.greedy(h)
+        for _ in range(4):
+            h = ex.backbone(tok[:, None])[:, 0]
+            tok = ex.greedy(h)
+        torch.cuda.synchronize()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record(s)
+        for _ in range(args.decode_steps):
+            h = ex.backbone(tok[:, None])[:, 0]
+            tok = ex.greedy(h)
+        d1.record(s)
+        torch.cuda.synchronize()
+        dt = d0.elapsed_time(d1) / 1e3 / args.decode_steps
+        roof = pk['hbm'] * 1e9 / DECODE_BYTES_B1
+        decode = dict(tokens_per_s=1.0 / dt, ms_per_token=dt * 1e3, roofline_tokens_per_s=roof,
+                      frac=(1.0 / dt) / roof, bytes_per_token=DECODE_BYTES_B1, note='no CUDA graph; batch 1')
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        per_tok, info = cpu_sample(tokens=args.ref_tokens)
+        cpu = dict(value=1.0 / per_tok, unit=UNIT, cores=os.cpu_count(), kind='port',
+                   sample=f"oracle port, 1 window x {info['tokens']} tokens through {info['layers']} layers + "
+                          f"lm_head/CE over a {info['vocab_slice']}-row vocab slice, extrapolated to 56 layers and "
+                          f"256000 rows; {info['seconds']:.1f} s of CPU work")
+    if rank == 0:
+        line = dict(
+            metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
+            ms_per_step=elapsed / args.steps * 1e3, higher_is_better=True, scaling='weak', vs_baseline=None,
+            dtype='fp16 (fp32 accumulate)', data='synthetic',
+            config=dict(workload='config4: 56-layer 8B scoring, FP4-G16 weights, SQ3.25 state, Resurface soft',
+                        windows_per_gpu=B, seq_len=T, global_batch=world * B, vocab=VOCAB,
+                        parallelism=f'dp{world} (window-sharded, one NLL all-reduce)', l2='inputs larger than L2'),
+            e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h),
+            roofline=dict(bound='tensor', kernel='tcgen05 in_proj GEMM (M=%d,N=18560,K=4096)' % (B * T),
+                          achieved=achieved, peak=pk['tf'], unit='TFLOP/s', frac=achieved / pk['tf'], traffic=None,
+                          peak_source=pk['src'] + ' bf16_tflops (burst)'),
+            step_roofline=dict(flop_per_token=FLOP_PER_TOKEN,
+                               achieved_tflops=FLOP_PER_TOKEN * B * T * world / elapsed * args.steps / 1e12 / world,
+                               frac=FLOP_PER_TOKEN * value / world / 1e12 / pk['tf_sus']),
+            decode_b1=decode, cpu_baseline=cpu, clocks=clk,
+            gpu_launches=launches_per_step(B * T) * args.steps + (1 if world > 1 else 0) * 0,
+            setup_seconds=setup_s)
+        print(json.dumps(line), flush=True)
+    ex.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

@@ -1,0 +1,414 @@
+// C-ABI entry points (include/sq325.h) and the native model runtime that sequences the
+// per-layer kernels.  Host code only; all device work is in scan.cu / codec.cu / fp4.cu /
+// gemm.cu / layer.cu.
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/sq325.h"
+#include "common.cuh"
+#include "fp4.cuh"
+#include "layer.cuh"
+#include "scan.cuh"
+
+namespace sq {
+int launch_decode_rows(int layout, int batch, int heads, int dim, int groups, const uint8_t* lo,
+                       const uint8_t* hi, const uint8_t* q4, const uint8_t* latent, const uint16_t* s8,
+                       const uint16_t* s4, const uint16_t* latent_scale, float* tiers, float* z, cudaStream_t st);
+int launch_encode_rows(int layout, int batch, int heads, int dim, int groups, int mode, const float* tiers,
+                       const float* z, const uint16_t* latent_scale, uint8_t* lo, uint8_t* hi, uint8_t* q4,
+                       uint8_t* latent, uint16_t* s8, uint16_t* s4, cudaStream_t st);
+}  // namespace sq
+
+using namespace sq;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+int cuda_fail(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  return fail(SQ_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+int check(int st, const char* what) {
+  if (st == kOk) return SQ_OK;
+  if (st == kECuda) return cuda_fail(what);
+  return fail(st, std::string(what) + ": invalid arguments");
+}
+#define SQ_TRY(expr, what)                 \
+  do {                                     \
+    int _s = check((expr), (what));        \
+    if (_s != SQ_OK) return _s;            \
+  } while (0)
+
+bool aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+constexpr int kDModel = 4096, kDInner = 8192, kXbc = 10240, kZx = 18560, kHeads = 128, kHeadDim = 64,
+              kGroups = 8;
+constexpr int kLmChunk = 32768;    // lm_head rows decoded per staging pass
+
+}  // namespace
+
+struct sq_model {
+  sq_model_config cfg;
+  std::vector<sq_layer_desc> layers;
+  std::vector<AdapterPtrs> adapters;
+  struct St { int batch = 0; uint8_t *lo = 0, *hi = 0, *q4 = 0, *latent = 0; uint16_t *s8 = 0, *s4 = 0, *ring = 0; };
+  std::vector<St> states;
+  sq_fp4_matrix embed{}, head{};
+  const uint16_t* norm_f = nullptr;
+  int max_tokens = 0;
+  // workspaces
+  uint16_t *h = 0, *res = 0, *hn = 0, *zx = 0, *xbc = 0, *y = 0, *yn = 0, *stage = 0, *logits = 0;
+  float2* partials = 0;
+  float* tlogit = 0;
+  int* d_err = 0;
+  size_t stage_elems = 0;
+  std::atomic<int> busy{0};
+};
+
+namespace {
+
+Fp4Weight fw(const sq_fp4_matrix& m) { return Fp4Weight{m.codes, m.block_scales, m.global_scale, m.rows, m.cols}; }
+
+void free_ws(sq_model* m) {
+  void* ptrs[] = {m->h, m->res, m->hn, m->zx, m->xbc, m->y, m->yn, m->stage, m->logits, m->partials, m->tlogit};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+  m->h = m->res = m->hn = m->zx = m->xbc = m->y = m->yn = m->stage = m->logits = nullptr;
+  m->partials = nullptr; m->tlogit = nullptr;
+  m->max_tokens = 0;
+}
+
+int linear(sq_model* m, const sq_fp4_matrix& W, const uint16_t* X, long long ldx, int M, uint16_t* Y,
+           long long ldy, cudaStream_t st) {
+  const Fp4Weight w = fw(W);
+  if (M <= 64) return check(launch_fp4_gemv(w, X, ldx, M, Y, ldy, st), "fp4 gemv");
+  if ((size_t)W.rows * W.cols > m->stage_elems) return fail(SQ_EINVAL, "staging buffer too small");
+  SQ_TRY(launch_fp4_decode(w, m->stage, W.cols, st), "fp4 decode");
+  return check(launch_gemm_f16(X, ldx, m->stage, W.cols, Y, ldy, M, W.rows, W.cols, 0, nullptr, m->d_err, st),
+               "tcgen05 gemm");
+}
+
+}  // namespace
+
+extern "C" {
+
+int sq_abi_version(void) { return SQ325_ABI_VERSION; }
+const char* sq_last_error(void) { return g_err.c_str(); }
+
+int sq_layout_index(const char* name) {
+  if (!name) return -1;
+  for (int i = 0; i < 7; ++i)
+    if (std::strcmp(name, kLayouts[i].name) == 0) return i;
+  return -1;
+}
+
+int sq_layout_counts(int layout, int* n8, int* n4, int* nzero) {
+  if (layout < 0 || layout > 6) return fail(SQ_EINVAL, "unknown layout index");
+  if (n8) *n8 = kLayouts[layout].n8;
+  if (n4) *n4 = kLayouts[layout].n4;
+  if (nzero) *nzero = kLayouts[layout].nz;
+  return SQ_OK;
+}
+
+int64_t sq_state_bytes(int batch, int heads, int dim) { return (int64_t)batch * heads * dim * 52; }
+
+int sq_scan(const sq_scan_args* a, void* stream) {
+  if (!a) return fail(SQ_EINVAL, "null scan args");
+  const void* req[] = {a->x, a->dt, a->A, a->B, a->C, a->D, a->dt_bias, a->permutation, a->basis,
+                       a->latent_scale, a->predictor, a->lo, a->hi, a->q4, a->latent, a->s8, a->s4, a->y};
+  for (const void* p : req)
+    if (!p) return fail(SQ_EINVAL, "scan: null pointer argument");
+  const void* st4[] = {a->lo, a->hi, a->q4, a->latent, a->s8, a->s4};
+  for (const void* p : st4)
+    if (!aligned(p, 4)) return fail(SQ_EINVAL, "scan: packed state buffers must be 4-byte aligned");
+  ScanParams P{};
+  P.batch = a->batch; P.length = a->length; P.heads = a->heads; P.dim = a->dim; P.groups = a->groups;
+  P.layout = a->layout;
+  P.x = a->x; P.x_sb = a->x_batch_stride; P.x_st = a->x_token_stride;
+  P.dt = a->dt; P.dt_sb = a->dt_batch_stride; P.dt_st = a->dt_token_stride;
+  P.A = a->A;
+  P.B = a->B; P.b_sb = a->b_batch_stride; P.b_st = a->b_token_stride;
+  P.C = a->C; P.c_sb = a->c_batch_stride; P.c_st = a->c_token_stride;
+  P.D = a->D; P.d_is_f32 = a->d_is_f32; P.dt_bias = a->dt_bias; P.dt_bias_is_f32 = a->dt_bias_is_f32;
+  P.perm = a->permutation; P.basis = a->basis; P.latent_scale = a->latent_scale; P.predictor = a->predictor;
+  P.lo = a->lo; P.hi = a->hi; P.q4 = a->q4; P.latent = a->latent; P.s8 = a->s8; P.s4 = a->s4;
+  P.y = a->y; P.y_sb = a->y_batch_stride; P.y_st = a->y_token_stride;
+  return check(launch_scan(P, (cudaStream_t)stream), "sq_scan");
+}
+
+int sq_state_decode(int layout, int batch, int heads, int dim, int groups, const uint8_t* lo, const uint8_t* hi,
+                    const uint8_t* q4, const uint8_t* latent, const uint16_t* s8, const uint16_t* s4,
+                    const uint16_t* latent_scale, float* tiers, float* z, void* stream) {
+  if (!lo || !hi || !q4 || !latent || !s8 || !s4 || !latent_scale || !tiers || !z)
+    return fail(SQ_EINVAL, "state_decode: null pointer");
+  return check(launch_decode_rows(layout, batch, heads, dim, groups, lo, hi, q4, latent, s8, s4, latent_scale,
+                                  tiers, z, (cudaStream_t)stream), "sq_state_decode");
+}
+
+int sq_state_encode(int layout, int batch, int heads, int dim, int groups, int mode, const float* tiers,
+                    const float* z, const uint16_t* latent_scale, uint8_t* lo, uint8_t* hi, uint8_t* q4,
+                    uint8_t* latent, uint16_t* s8, uint16_t* s4, void* stream) {
+  if (!lo || !hi || !q4 || !latent || !s8 || !s4 || !tiers || (mode == 0 && (!z || !latent_scale)))
+    return fail(SQ_EINVAL, "state_encode: null pointer");
+  return check(launch_encode_rows(layout, batch, heads, dim, groups, mode, tiers, z, latent_scale, lo, hi, q4,
+                                  latent, s8, s4, (cudaStream_t)stream), "sq_state_encode");
+}
+
+int sq_fp4_decode(const uint8_t* codes, const uint8_t* block_scales, const float* global_scale, int rows, int cols,
+                  uint16_t* out, int64_t ldo, void* stream) {
+  if (!codes || !block_scales || !global_scale || !out) return fail(SQ_EINVAL, "fp4_decode: null pointer");
+  if (!aligned(codes, 4) || !aligned(out, 16)) return fail(SQ_EINVAL, "fp4_decode: misaligned buffers");
+  Fp4Weight w{codes, block_scales, global_scale, rows, cols};
+  return check(launch_fp4_decode(w, out, ldo, (cudaStream_t)stream), "sq_fp4_decode");
+}
+
+int64_t sq_fp4_linear_workspace(int m, int n, int k) { return m <= 64 ? 0 : (int64_t)n * k * 2; }
+
+int sq_fp4_linear(const uint8_t* codes, const uint8_t* block_scales, const float* global_scale, int n, int k,
+                  const uint16_t* x, int64_t ldx, int m, uint16_t* y, int64_t ldy, void* workspace,
+                  int64_t workspace_bytes, void* stream) {
+  if (!codes || !block_scales || !global_scale || !x || !y) return fail(SQ_EINVAL, "fp4_linear: null pointer");
+  if (m <= 0 || n <= 0 || k <= 0 || k % 128) return fail(SQ_EINVAL, "fp4_linear: k must be a positive multiple of 128");
+  if (!aligned(codes, 16) || !aligned(x, 16)) return fail(SQ_EINVAL, "fp4_linear: misaligned buffers");
+  Fp4Weight w{codes, block_scales, global_scale, n, k};
+  cudaStream_t st = (cudaStream_t)stream;
+  if (m <= 64) return check(launch_fp4_gemv(w, x, ldx, m, y, ldy, st), "fp4 gemv");
+  if (!workspace || workspace_bytes < sq_fp4_linear_workspace(m, n, k) || !aligned(workspace, 16))
+    return fail(SQ_EINVAL, "fp4_linear: workspace too small");
+  static int* d_err = nullptr;
+  if (!d_err) {
+    if (cudaMalloc(&d_err, sizeof(int)) != cudaSuccess) return cuda_fail("cudaMalloc");
+    cudaMemset(d_err, 0, sizeof(int));
+  }
+  uint16_t* stg = (uint16_t*)workspace;
+  SQ_TRY(launch_fp4_decode(w, stg, k, st), "fp4 decode");
+  return check(launch_gemm_f16(x, ldx, stg, k, y, ldy, m, n, k, 0, nullptr, d_err, st), "tcgen05 gemm");
+}
+
+int sq_gemm_f16(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, uint16_t* c, int64_t ldc, int m,
+                int n, int k, void* stream) {
+  if (!a || !b || !c) return fail(SQ_EINVAL, "gemm: null pointer");
+  static int* d_err = nullptr;
+  if (!d_err) {
+    if (cudaMalloc(&d_err, sizeof(int)) != cudaSuccess) return cuda_fail("cudaMalloc");
+    cudaMemset(d_err, 0, sizeof(int));
+  }
+  SQ_TRY(launch_gemm_f16(a, lda, b, ldb, c, ldc, m, n, k, 0, nullptr, d_err, (cudaStream_t)stream), "tcgen05 gemm");
+  cudaStreamSynchronize((cudaStream_t)stream);
+  int h = 0;
+  cudaMemcpy(&h, d_err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (h) { cudaMemset(d_err, 0, sizeof(int)); return fail(SQ_ETIMEOUT, "tcgen05 gemm: device wait expired"); }
+  return SQ_OK;
+}
+
+// ---------------------------------------------------------------- model runtime
+
+int sq_model_create(const sq_model_config* cfg, sq_model** out) {
+  if (!cfg || !out) return fail(SQ_EINVAL, "model_create: null pointer");
+  if (cfg->n_layer <= 0 || cfg->vocab < 16 || cfg->vocab % 16 || !(cfg->eps > 0.f))
+    return fail(SQ_EINVAL, "model_create: invalid config");
+  sq_model* m = new sq_model();
+  m->cfg = *cfg;
+  m->layers.resize(cfg->n_layer);
+  std::memset(m->layers.data(), 0, sizeof(sq_layer_desc) * cfg->n_layer);
+  m->adapters.assign(cfg->n_layer, AdapterPtrs{});
+  m->states.resize(cfg->n_layer);
+  if (cudaMalloc(&m->d_err, sizeof(int)) != cudaSuccess) { delete m; return cuda_fail("cudaMalloc"); }
+  cudaMemset(m->d_err, 0, sizeof(int));
+  *out = m;
+  return SQ_OK;
+}
+
+int sq_model_destroy(sq_model* m) {
+  if (!m) return SQ_OK;
+  free_ws(m);
+  if (m->d_err) cudaFree(m->d_err);
+  delete m;
+  return SQ_OK;
+}
+
+static bool fp4_ok(const sq_fp4_matrix& w, int rows, int cols) {
+  return w.codes && w.block_scales && w.global_scale && w.rows == rows && w.cols == cols && aligned(w.codes, 16);
+}
+
+int sq_model_set_layer(sq_model* m, int layer, const sq_layer_desc* d) {
+  if (!m || !d || layer < 0 || layer >= m->cfg.n_layer) return fail(SQ_EINVAL, "set_layer: bad layer");
+  if (!fp4_ok(d->in_proj, kZx, kDModel) || !fp4_ok(d->out_proj, kDModel, kDInner))
+    return fail(SQ_EINVAL, "set_layer: projection geometry differs ([18560,4096] / [4096,8192])");
+  if (d->layout < 0 || d->layout > 6) return fail(SQ_EINVAL, "set_layer: unknown layout");
+  const void* req[] = {d->norm_weight, d->conv_weight, d->conv_bias, d->A, d->D, d->dt_bias, d->gated_norm_weight,
+                       d->permutation, d->basis, d->latent_scale, d->predictor};
+  for (const void* p : req)
+    if (!p) return fail(SQ_EINVAL, "set_layer: null pointer");
+  m->layers[layer] = *d;
+  return SQ_OK;
+}
+
+int sq_model_set_globals(sq_model* m, const sq_fp4_matrix* e, const sq_fp4_matrix* h, const uint16_t* nf) {
+  if (!m || !e || !h || !nf) return fail(SQ_EINVAL, "set_globals: null pointer");
+  if (!fp4_ok(*e, m->cfg.vocab, kDModel) || !fp4_ok(*h, m->cfg.vocab, kDModel))
+    return fail(SQ_EINVAL, "set_globals: embedding / lm_head must be [vocab,4096]");
+  m->embed = *e; m->head = *h; m->norm_f = nf;
+  return SQ_OK;
+}
+
+int sq_model_set_adapter(sq_model* m, int layer, const uint16_t* V, const uint16_t* g, const uint16_t* w,
+                         const uint16_t* b, int hard) {
+  if (!m || layer < 0 || layer >= m->cfg.n_layer) return fail(SQ_EINVAL, "set_adapter: bad layer");
+  if (V && (!g || !w || !b)) return fail(SQ_EINVAL, "set_adapter: null pointer");
+  m->adapters[layer] = AdapterPtrs{V, g, w, b, hard};
+  return SQ_OK;
+}
+
+int sq_model_bind_state(sq_model* m, int layer, int batch, uint8_t* lo, uint8_t* hi, uint8_t* q4, uint8_t* latent,
+                        uint16_t* s8, uint16_t* s4, uint16_t* ring) {
+  if (!m || layer < 0 || layer >= m->cfg.n_layer || batch <= 0) return fail(SQ_EINVAL, "bind_state: bad layer/batch");
+  const void* p[] = {lo, hi, q4, latent, s8, s4, ring};
+  for (const void* q : p)
+    if (!q || !aligned(q, 4)) return fail(SQ_EINVAL, "bind_state: null or misaligned buffer");
+  sq_model::St& s = m->states[layer];
+  s.batch = batch; s.lo = lo; s.hi = hi; s.q4 = q4; s.latent = latent; s.s8 = s8; s.s4 = s4; s.ring = ring;
+  return SQ_OK;
+}
+
+int sq_model_reserve(sq_model* m, int max_tokens) {
+  if (!m || max_tokens <= 0) return fail(SQ_EINVAL, "reserve: bad size");
+  if (max_tokens <= m->max_tokens) return SQ_OK;
+  free_ws(m);
+  const size_t T = (size_t)max_tokens;
+  const int nt = gemm_num_ntiles(m->cfg.vocab);
+  size_t stage = (size_t)kZx * kDModel;
+  stage = std::max(stage, (size_t)kDModel * kDInner);
+  stage = std::max(stage, (size_t)std::min(m->cfg.vocab, kLmChunk) * kDModel);
+  struct A { void** p; size_t bytes; } allocs[] = {
+      {(void**)&m->h, T * kDModel * 2}, {(void**)&m->res, T * kDModel * 2}, {(void**)&m->hn, T * kDModel * 2},
+      {(void**)&m->zx, T * kZx * 2}, {(void**)&m->xbc, T * kXbc * 2}, {(void**)&m->y, T * kDInner * 2},
+      {(void**)&m->yn, T * kDInner * 2}, {(void**)&m->stage, stage * 2},
+      {(void**)&m->logits, (size_t)64 * m->cfg.vocab * 2}, {(void**)&m->partials, T * nt * sizeof(float2)},
+      {(void**)&m->tlogit, T * sizeof(float)}};
+  for (auto& a : allocs) {
+    if (cudaMalloc(a.p, a.bytes) != cudaSuccess) {
+      cudaGetLastError();
+      free_ws(m);
+      return fail(SQ_ENOMEM, "reserve: cudaMalloc failed");
+    }
+  }
+  m->stage_elems = stage;
+  m->max_tokens = max_tokens;
+  return SQ_OK;
+}
+
+namespace {
+struct Busy {
+  sq_model* m; bool ok;
+  explicit Busy(sq_model* mm) : m(mm) { int z = 0; ok = m->busy.compare_exchange_strong(z, 1); }
+  ~Busy() { if (ok) m->busy.store(0); }
+};
+}  // namespace
+
+int sq_model_forward(sq_model* m, const int64_t* ids, int batch, int tokens, int pos0, uint16_t* hidden_out,
+                     void* stream) {
+  if (!m || !ids || !hidden_out || batch <= 0 || tokens <= 0 || pos0 < 0) return fail(SQ_EINVAL, "forward: bad args");
+  Busy busy(m);
+  if (!busy.ok) return fail(SQ_ESTATE, "forward: concurrent/reentrant use of one model context");
+  const int M = batch * tokens;
+  if (M > m->max_tokens) return fail(SQ_EINVAL, "forward: batch*tokens exceeds reserved workspace");
+  if (!m->embed.codes || !m->norm_f) return fail(SQ_ESTATE, "forward: globals not set");
+  cudaStream_t st = (cudaStream_t)stream;
+  SQ_TRY(launch_fp4_embed(fw(m->embed), (const long long*)ids, M, m->h, m->d_err, st), "embedding");
+  const bool step = pos0 > 0 && tokens == 1;
+  for (int l = 0; l < m->cfg.n_layer; ++l) {
+    const sq_layer_desc& L = m->layers[l];
+    const sq_model::St& S = m->states[l];
+    if (!L.in_proj.codes) return fail(SQ_ESTATE, "forward: layer weights not set");
+    if (S.batch != batch) return fail(SQ_ESTATE, "forward: state batch differs from the call (reset required)");
+    SQ_TRY(launch_add_rmsnorm(m->h, m->res, l > 0, L.norm_weight, m->cfg.eps, m->hn, M, kDModel, st), "add_rmsnorm");
+    int s = linear(m, L.in_proj, m->hn, kDModel, M, m->zx, kZx, st);
+    if (s != SQ_OK) return s;
+    ScanParams P{};
+    P.batch = batch; P.length = tokens; P.heads = kHeads; P.dim = kHeadDim; P.groups = kGroups; P.layout = L.layout;
+    P.dt = m->zx + 2 * kDInner + 2 * 1024; P.dt_sb = (long long)tokens * kZx; P.dt_st = kZx;
+    P.A = L.A; P.D = L.D; P.d_is_f32 = 0; P.dt_bias = L.dt_bias; P.dt_bias_is_f32 = 0;
+    P.perm = L.permutation; P.basis = L.basis; P.latent_scale = L.latent_scale; P.predictor = L.predictor;
+    P.lo = S.lo; P.hi = S.hi; P.q4 = S.q4; P.latent = S.latent; P.s8 = S.s8; P.s4 = S.s4;
+    P.y = m->y; P.y_sb = (long long)tokens * kDInner; P.y_st = kDInner;
+    if (step) {
+      const uint16_t* raw = m->zx + kDInner;
+      P.x = raw; P.B = raw + kDInner; P.C = raw + kDInner + 1024;
+      P.x_sb = P.b_sb = P.c_sb = kZx; P.x_st = P.b_st = P.c_st = kZx;
+      P.conv_w = L.conv_weight; P.conv_b = L.conv_bias; P.conv_cache = S.ring; P.conv_pos = pos0;
+      P.conv_cache_sb = 4LL * kXbc;
+    } else {
+      SQ_TRY(launch_conv_prefill(m->zx + kDInner, (long long)tokens * kZx, kZx, batch, tokens, kXbc, L.conv_weight,
+                                 L.conv_bias, S.ring, 4LL * kXbc, pos0, m->xbc, (long long)tokens * kXbc, kXbc, st),
+             "conv prefill");
+      P.x = m->xbc; P.B = m->xbc + kDInner; P.C = m->xbc + kDInner + 1024;
+      P.x_sb = P.b_sb = P.c_sb = (long long)tokens * kXbc; P.x_st = P.b_st = P.c_st = kXbc;
+    }
+    SQ_TRY(launch_scan(P, st), "ssu scan");
+    const AdapterPtrs& ad = m->adapters[l];
+    SQ_TRY(launch_resurface_gatednorm(m->y, m->zx, kZx, m->hn, kDModel, ad.V ? &ad : nullptr, L.gated_norm_weight,
+                                      m->cfg.eps, m->yn, M, st), "resurface + gated norm");
+    s = linear(m, L.out_proj, m->yn, kDInner, M, m->h, kDModel, st);
+    if (s != SQ_OK) return s;
+  }
+  SQ_TRY(launch_add_rmsnorm(m->h, m->res, 1, m->norm_f, m->cfg.eps, hidden_out, M, kDModel, st), "norm_f");
+  return SQ_OK;
+}
+
+int sq_model_score(sq_model* m, const uint16_t* hidden, int rows, const int64_t* targets, float* nll, void* stream) {
+  if (!m || !hidden || !targets || !nll || rows <= 0) return fail(SQ_EINVAL, "score: bad args");
+  Busy busy(m);
+  if (!busy.ok) return fail(SQ_ESTATE, "score: concurrent/reentrant use of one model context");
+  if (rows > m->max_tokens) return fail(SQ_EINVAL, "score: rows exceed reserved workspace");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int V = m->cfg.vocab;
+  const int nt = gemm_num_ntiles(V);
+  for (int n0 = 0; n0 < V; n0 += kLmChunk) {
+    const int nc = std::min(kLmChunk, V - n0);
+    Fp4Weight w = fw(m->head);
+    w.codes += (size_t)n0 * (kDModel / 2);
+    w.scales += (size_t)n0 * (kDModel / 16);
+    w.rows = nc;
+    SQ_TRY(launch_fp4_decode(w, m->stage, kDModel, st), "lm_head decode");
+    GemmCE ce{(const long long*)targets, m->partials, m->tlogit, n0, nt};
+    SQ_TRY(launch_gemm_f16(hidden, kDModel, m->stage, kDModel, nullptr, 0, rows, nc, kDModel, 1, &ce, m->d_err, st),
+           "lm_head gemm + ce");
+  }
+  return check(launch_ce_finalize(m->partials, nt, m->tlogit, rows, nll, st), "ce finalize");
+}
+
+int sq_model_greedy(sq_model* m, const uint16_t* hidden, int rows, uint16_t* logits_out, int64_t* tokens_out,
+                    void* stream) {
+  if (!m || !hidden || !tokens_out || rows <= 0 || rows > 64) return fail(SQ_EINVAL, "greedy: rows must be 1..64");
+  Busy busy(m);
+  if (!busy.ok) return fail(SQ_ESTATE, "greedy: concurrent/reentrant use of one model context");
+  if (!m->logits) return fail(SQ_ESTATE, "greedy: reserve() first");
+  cudaStream_t st = (cudaStream_t)stream;
+  uint16_t* lg = logits_out ? logits_out : m->logits;
+  SQ_TRY(launch_fp4_gemv(fw(m->head), hidden, kDModel, rows, lg, m->cfg.vocab, st), "lm_head gemv");
+  return check(launch_argmax(lg, rows, m->cfg.vocab, m->cfg.vocab, (long long*)tokens_out, st), "argmax");
+}
+
+int sq_model_check(sq_model* m, void* stream) {
+  if (!m) return fail(SQ_EINVAL, "check: null model");
+  if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return cuda_fail("stream synchronize");
+  int h = 0;
+  if (cudaMemcpy(&h, m->d_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return cuda_fail("read error word");
+  if (h) {
+    cudaMemset(m->d_err, 0, sizeof(int));
+    if (h & (int)kDevBadArgs) return fail(SQ_EINVAL, "device: token id outside the vocabulary");
+    return fail(SQ_ETIMEOUT, "device: a bounded wait expired (code " + std::to_string(h) + ")");
+  }
+  return SQ_OK;
+}
+
+}  // extern "C"

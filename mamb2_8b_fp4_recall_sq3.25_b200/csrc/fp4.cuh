@@ -1,0 +1,39 @@
+// Packed FP4-E2M1 G16 weight descriptor and kernel launchers.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sq {
+
+// One packed matrix exactly as the reference checkpoint stores it
+// (mamba2_recall/fp4_checkpoint.py:100-114): codes u8[rows, cols/2] (low nibble =
+// even column), block_scale_bytes u8[rows, cols/16] (E4M3FN), global_scale f32.
+struct Fp4Weight {
+  const uint8_t* codes;
+  const uint8_t* scales;
+  const float* global_scale;   // device pointer to one fp32
+  int rows, cols;
+};
+
+int launch_fp4_decode(const Fp4Weight& W, uint16_t* out, long long ldo, cudaStream_t st);
+int launch_fp4_embed(const Fp4Weight& E, const long long* ids, int ntok, uint16_t* out, int* err, cudaStream_t st);
+int launch_fp4_gemv(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,
+                    cudaStream_t st);
+
+// tcgen05 GEMM: C[M,N] = A[M,K] . B[N,K]^T, fp16 in, fp32 accumulate in TMEM.
+// mode 0: store fp16 C.  mode 1: cross-entropy partials of fp16-rounded logits
+// (per row and 256-column tile: running max and sum of exp), plus the target
+// logit, never writing C.
+struct GemmCE {
+  const long long* targets;    // [M] target column per row (row < M), in the full vocabulary
+  float2* partials;            // [M, ntiles_total]
+  float* target_logit;         // [M]
+  int n_offset;                // first vocabulary column of this launch (multiple of 256)
+  int ntiles_total;            // row stride of `partials` (tiles over the full vocabulary)
+};
+int launch_gemm_f16(const uint16_t* A, long long lda, const uint16_t* B, long long ldb,
+                    uint16_t* C, long long ldc, int M, int N, int K, int mode, const GemmCE* ce,
+                    int* dev_err, cudaStream_t st);
+int gemm_num_ntiles(int N);
+
+}  // namespace sq

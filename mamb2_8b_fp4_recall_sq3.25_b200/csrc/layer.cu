@@ -1,0 +1,327 @@
+// Block / mixer elementwise kernels around the codec and the FP4 projections.
+//
+//  add_rmsnorm          mamba_ssm Block (unfused add, fp16 residual) + RMSNorm(eps)
+//  conv_prefill         StateQuant._convolution prefill branch (mamba2_recall/state_quant.py:303-317)
+//  resurface_gatednorm  resurface_native._Adapter.forward (:105-118) applied in the
+//                       norm pre-hook (:201-222), then RMSNormGated(norm_before_gate=False,
+//                       group_size=1024) as called at fp4_zero_predictor_codec_v1.py:356-359
+//  ce_finalize / window_sum / argmax   the scoring and greedy heads
+//                       (scripts/run_fp4_ridge_resurface_v3.py:105-109,
+//                        scripts/infer_fp4_ridge_resurface_v1.py:103-105)
+#include "common.cuh"
+#include "layer.cuh"
+
+namespace sq {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// one CTA (256 threads) per row; D % 8 == 0, D <= 8192
+__global__ void add_rmsnorm_kernel(const uint16_t* __restrict__ h, uint16_t* __restrict__ res, int has_res,
+                                   const uint16_t* __restrict__ w, float eps, uint16_t* __restrict__ out, int D) {
+  __shared__ float red[8];
+  const long long row = blockIdx.x;
+  const uint16_t* hr = h + row * D;
+  uint16_t* rr = res + row * D;
+  float vals[32];
+  float ss = 0.f;
+  int n = 0;
+  for (int c = threadIdx.x * 8; c < D; c += blockDim.x * 8, ++n) {
+    uint4 hv = *reinterpret_cast<const uint4*>(hr + c);
+    const uint16_t* hp = reinterpret_cast<const uint16_t*>(&hv);
+    uint4 ov;
+    uint16_t* op = reinterpret_cast<uint16_t*>(&ov);
+    if (has_res) {
+      uint4 rv = *reinterpret_cast<const uint4*>(rr + c);
+      const uint16_t* rp = reinterpret_cast<const uint16_t*>(&rv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) op[i] = f2h(h2f(hp[i]) + h2f(rp[i]));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) op[i] = hp[i];
+    }
+    *reinterpret_cast<uint4*>(rr + c) = ov;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float x = h2f(op[i]);
+      vals[n * 8 + i] = x;
+      ss += x * x;
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+  const float rstd = 1.0f / sqrtf(tot / (float)D + eps);
+  n = 0;
+  for (int c = threadIdx.x * 8; c < D; c += blockDim.x * 8, ++n) {
+    uint4 wv = *reinterpret_cast<const uint4*>(w + c);
+    const uint16_t* wp = reinterpret_cast<const uint16_t*>(&wv);
+    uint4 ov;
+    uint16_t* op = reinterpret_cast<uint16_t*>(&ov);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) op[i] = f2h((vals[n * 8 + i] * rstd) * h2f(wp[i]));
+    *reinterpret_cast<uint4*>(out + row * D + c) = ov;
+  }
+}
+
+constexpr int kConvChunk = 64;
+
+__device__ __forceinline__ float silu_f16(float v16) { return h2f(f2h(v16 / (1.0f + expf(-v16)))); }
+
+// thread = (b, channel, chunk of kConvChunk positions)
+__global__ void conv_prefill_kernel(const uint16_t* __restrict__ raw, long long raw_sb, long long raw_st,
+                                    int B, int L, int C, const uint16_t* __restrict__ w,
+                                    const uint16_t* __restrict__ bias, uint16_t* __restrict__ cache,
+                                    long long cache_sb, int pos0, uint16_t* __restrict__ out,
+                                    long long out_sb, long long out_st) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int chunk = blockIdx.y;
+  const int b = blockIdx.z;
+  if (c >= C) return;
+  const int t0 = chunk * kConvChunk;
+  if (t0 >= L) return;
+  const int t1 = min(L, t0 + kConvChunk);
+  const uint16_t* rb = raw + (long long)b * raw_sb + c;
+  uint16_t* ring = cache + (long long)b * cache_sb + c;
+  const float w0 = h2f(w[c * 4 + 0]), w1 = h2f(w[c * 4 + 1]), w2 = h2f(w[c * 4 + 2]), w3 = h2f(w[c * 4 + 3]);
+  const float bb = h2f(bias[c]);
+  // history: raw values at local positions t0-3 .. t0-1 (negative -> ring or zeros)
+  float x0, x1, x2;
+  auto hist = [&](int lt) -> float {
+    if (lt >= 0) return h2f(rb[(long long)lt * raw_st]);
+    const int ap = pos0 + lt;                  // absolute position
+    if (ap < 0) return 0.f;
+    return h2f(ring[(long long)(ap & 3) * C]);
+  };
+  x0 = hist(t0 - 3); x1 = hist(t0 - 2); x2 = hist(t0 - 1);
+  for (int t = t0; t < t1; ++t) {
+    const float x3 = h2f(rb[(long long)t * raw_st]);
+    float acc = w0 * x0 + w1 * x1 + w2 * x2 + w3 * x3 + bb;
+    float v = h2f(f2h(acc));
+    out[(long long)b * out_sb + (long long)t * out_st + c] = f2h(silu_f16(v));
+    x0 = x1; x1 = x2; x2 = x3;
+  }
+  if (chunk == 0) {
+    // the only thread of this (b, c) that touches the ring: write the last raw columns
+    for (int lt = max(0, L - 4); lt < L; ++lt) ring[(long long)((pos0 + lt) & 3) * C] = rb[(long long)lt * raw_st];
+  }
+}
+
+// one CTA (256 threads = 8 warps = the 8 norm groups) processes tokens t = blockIdx.x, += gridDim.x
+__global__ void __launch_bounds__(256)
+resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __restrict__ z, long long z_st,
+                           const uint16_t* __restrict__ u, long long u_st, AdapterPtrs ad, int has_ad,
+                           const uint16_t* __restrict__ nw, float eps, uint16_t* __restrict__ out, int T) {
+  extern __shared__ float sm[];
+  float* ys = sm;                   // [8192]
+  float* Vs = sm + 8192;            // [128*128] (adapter only)
+  __shared__ float sgate;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (has_ad)
+    for (int i = threadIdx.x; i < 128 * 128; i += blockDim.x) Vs[i] = h2f(ad.V[i]);
+  for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    __syncthreads();
+    const uint16_t* yr = y + (long long)t * 8192;
+    for (int i = threadIdx.x * 8; i < 8192; i += blockDim.x * 8) {
+      uint4 v = *reinterpret_cast<const uint4*>(yr + i);
+      const uint16_t* vp = reinterpret_cast<const uint16_t*>(&v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ys[i + k] = h2f(vp[k]);
+    }
+    if (has_ad && warp == 0) {
+      // logit = fp16(fp16(u . w) + b)
+      float s = 0.f;
+      const uint16_t* ur = u + (long long)t * u_st;
+      for (int i = lane; i < 4096; i += 32) s += h2f(ur[i]) * h2f(ad.w[i]);
+      s = warp_sum(s);
+      if (lane == 0) {
+        float lg = h2f(f2h(h2f(f2h(s)) + h2f(ad.b[0])));
+        float gate = ad.hard ? (lg > 0.f ? 1.f : 0.f) : 1.0f / (1.0f + expf(-lg));
+        sgate = h2f(f2h(gate));
+      }
+    }
+    __syncthreads();
+    float newy[16][2];
+    if (has_ad) {
+      float acc[16][2];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = 0.f;
+      for (int j = 0; j < 128; ++j) {
+        const float y0 = ys[j * 64 + lane], y1 = ys[j * 64 + lane + 32];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float v = Vs[(warp * 16 + i) * 128 + j];
+          acc[i][0] = fmaf(v, y0, acc[i][0]);
+          acc[i][1] = fmaf(v, y1, acc[i][1]);
+        }
+      }
+      const float g16 = sgate;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int hh = warp * 16 + i;
+        const float gg = h2f(f2h(g16 * h2f(ad.g[hh])));
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const float mix = h2f(f2h(acc[i][k]));
+          const float corr = h2f(f2h(gg * mix));
+          newy[i][k] = h2f(f2h(ys[hh * 64 + lane + 32 * k] + corr));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        newy[i][0] = ys[(warp * 16 + i) * 64 + lane];
+        newy[i][1] = ys[(warp * 16 + i) * 64 + lane + 32];
+      }
+    }
+    // gated RMSNorm over this warp's group (heads warp*16 .. +15 = 1024 channels)
+    const uint16_t* zr = z + (long long)t * z_st;
+    float xv[16][2];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int ch = (warp * 16 + i) * 64 + lane + 32 * k;
+        const float zz = h2f(zr[ch]);
+        const float gz = zz * (1.0f / (1.0f + expf(-zz)));
+        const float x = newy[i][k] * gz;
+        xv[i][k] = x;
+        ss += x * x;
+      }
+    ss = warp_sum(ss);
+    const float rstd = 1.0f / sqrtf(ss / 1024.0f + eps);
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int ch = (warp * 16 + i) * 64 + lane + 32 * k;
+        out[(long long)t * 8192 + ch] = f2h((xv[i][k] * rstd) * h2f(nw[ch]));
+      }
+  }
+}
+
+__global__ void ce_finalize_kernel(const float2* __restrict__ part, int nt, const float* __restrict__ tl,
+                                   int rows, float* __restrict__ nll) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float2* p = part + (long long)row * nt;
+  float mx = -INFINITY;
+  for (int i = lane; i < nt; i += 32) mx = fmaxf(mx, p[i].x);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float s = 0.f;
+  for (int i = lane; i < nt; i += 32) { float2 v = p[i]; if (v.y > 0.f) s += v.y * expf(v.x - mx); }
+  s = warp_sum(s);
+  if (lane == 0) nll[row] = (mx + logf(s)) - tl[row];
+}
+
+__global__ void window_sum_kernel(const float* __restrict__ nll, int per, const int* __restrict__ counts,
+                                  double* __restrict__ out) {
+  __shared__ double red[256];
+  const int w = blockIdx.x;
+  const int n = counts[w];
+  double s = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += (double)nll[(long long)w * per + i];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o; o >>= 1) {
+    if ((int)threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[w] = red[0];
+}
+
+__global__ void argmax_kernel(const uint16_t* __restrict__ logits, int V, long long ld, long long* __restrict__ out) {
+  __shared__ float bv[256];
+  __shared__ int bi[256];
+  const uint16_t* r = logits + (long long)blockIdx.x * ld;
+  float best = -INFINITY; int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    float v = h2f(r[i]);
+    if (v > best) { best = v; idx = i; }
+  }
+  bv[threadIdx.x] = best; bi[threadIdx.x] = idx;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o; o >>= 1) {
+    if ((int)threadIdx.x < o) {
+      float v2 = bv[threadIdx.x + o]; int i2 = bi[threadIdx.x + o];
+      if (v2 > bv[threadIdx.x] || (v2 == bv[threadIdx.x] && i2 < bi[threadIdx.x])) { bv[threadIdx.x] = v2; bi[threadIdx.x] = i2; }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[blockIdx.x] = bi[0] == 0x7fffffff ? 0 : bi[0];
+}
+
+int g_sms = 0;
+int num_sms() {
+  if (!g_sms) { int d = 0; cudaGetDevice(&d); cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, d); }
+  return g_sms > 0 ? g_sms : 148;
+}
+
+}  // namespace
+
+int launch_add_rmsnorm(const uint16_t* h, uint16_t* res, int has_res, const uint16_t* w, float eps,
+                       uint16_t* out, int rows, int D, cudaStream_t st) {
+  if (rows <= 0 || D % 8 || D > 8192) return kEInval;
+  add_rmsnorm_kernel<<<rows, 256, 0, st>>>(h, res, has_res, w, eps, out, D);
+  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+}
+
+int launch_conv_prefill(const uint16_t* raw, long long raw_sb, long long raw_st, int B, int L, int C,
+                        const uint16_t* w, const uint16_t* bias, uint16_t* cache, long long cache_sb,
+                        int pos0, uint16_t* out, long long out_sb, long long out_st, cudaStream_t st) {
+  if (B <= 0 || L <= 0 || C <= 0 || pos0 < 0) return kEInval;
+  dim3 grid((C + 255) / 256, (L + kConvChunk - 1) / kConvChunk, B);
+  conv_prefill_kernel<<<grid, 256, 0, st>>>(raw, raw_sb, raw_st, B, L, C, w, bias, cache, cache_sb, pos0, out,
+                                            out_sb, out_st);
+  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+}
+
+int launch_resurface_gatednorm(const uint16_t* y, const uint16_t* z, long long z_st, const uint16_t* u,
+                               long long u_st, const AdapterPtrs* ad, const uint16_t* norm_w, float eps,
+                               uint16_t* out, int T, cudaStream_t st) {
+  if (T <= 0) return kEInval;
+  const int has_ad = ad && ad->V;
+  AdapterPtrs a{};
+  if (has_ad) a = *ad;
+  const size_t smem = (8192 + (has_ad ? 128 * 128 : 0)) * sizeof(float);
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(resurface_gatednorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (8192 + 128 * 128) * (int)sizeof(float)) != cudaSuccess)
+      return kECuda;
+    attr = true;
+  }
+  const int grid = T < 2 * num_sms() ? T : 2 * num_sms();
+  resurface_gatednorm_kernel<<<grid, 256, smem, st>>>(y, z, z_st, u, u_st, a, has_ad, norm_w, eps, out, T);
+  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+}
+
+int launch_ce_finalize(const float2* partials, int ntiles, const float* tlogit, int rows, float* nll,
+                       cudaStream_t st) {
+  if (rows <= 0 || ntiles <= 0) return kEInval;
+  ce_finalize_kernel<<<(rows + 7) / 8, 256, 0, st>>>(partials, ntiles, tlogit, rows, nll);
+  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+}
+
+int launch_window_sum(const float* nll, int windows, int per, const int* counts, double* out, cudaStream_t st) {
+  if (windows <= 0 || per <= 0) return kEInval;
+  window_sum_kernel<<<windows, 256, 0, st>>>(nll, per, counts, out);
+  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+}
+
+int launch_argmax(const uint16_t* logits, int rows, int V, long long ld, long long* out, cudaStream_t st) {
+  if (rows <= 0 || V <= 0) return kEInval;
+  argmax_kernel<<<rows, 256, 0, st>>>(logits, V, ld, out);
+  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+}
+
+}  // namespace sq

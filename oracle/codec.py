@@ -1,0 +1,371 @@
+"""numpy restatement of the production SQ3.25 latent codec (CPU, test only).
+
+Every function mirrors one piece of the reference, op for op, in IEEE fp32
+without fused multiply-add, so that it reproduces the reference kernel run
+under the Triton CPU interpreter bit for bit (tests/golden/make_golden.py
+records those runs):
+
+  layout_counts / layout_descriptor
+      scripts/w4_state_repair_codec_v2.py:22-45 (tier counts) and
+      scripts/fp4_zero_predictor_codec_v1.py:28-36 (latent shift: 4 INT4
+      coordinates move to the zero tier, two FP8 latents take their bytes).
+  stored_quantize
+      scripts/state_ppl_codec_v6.py:52-61 (div_rn, round half away, clip).
+  predictor_correction
+      scripts/fp4_zero_predictor_codec_v1.py:221-225 (host einsum).
+  latent_scan
+      scripts/fp4_zero_predictor_codec_v1.py:76-181 (decode, per-token
+      recurrence, readout, FP8 latent requant, INT8/INT4 requant, pack).
+  encode_diagnostic
+      mamba2_recall/state_codec.py:299-331 (encode_state_: fp32
+      denominators, floor(|z|+0.5)).
+
+Reductions use np.sum over the reference kernel's padded tile widths
+(next power of two, zero padded) because the interpreter reduces with
+np.sum over exactly those shapes; the padding changes numpy's pairwise
+summation tree and therefore the fp32 rounding.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+# Base (pre-latent) tier counts of the seven released layouts
+# (scripts/w4_state_repair_codec_v2.py:22-28, scripts/state_ppl_codec_v10.py:24-26).
+BASE_COUNTS = {
+    '32_32_64': (32, 32, 64), '16_64_48': (16, 64, 48), '8_80_40': (8, 80, 40),
+    '24_48_56': (24, 48, 56), '36_24_68': (36, 24, 68), '40_16_72': (40, 16, 72),
+    '44_8_76': (44, 8, 76),
+}
+LAYOUTS = tuple(BASE_COUNTS)
+ROW_BYTES = 52
+TILE = 16
+F32 = np.float32
+
+
+def layout_counts(layout):
+    """(n8, n4, nzero) after the latent shift (fp4_zero_predictor_codec_v1.py:29-33)."""
+    if layout not in BASE_COUNTS:
+        raise ValueError('Unknown fixed W4 state repair tier layout')
+    n8, n4, nz = BASE_COUNTS[layout]
+    n4, nz = n4 - 4, nz + 4
+    if n4 < 4 or n8 + n4 + nz != 128 or n8 + n4 // 2 + 2 + 4 != 52:
+        raise ValueError('Latent tier layout violates same-byte geometry')
+    return n8, n4, nz
+
+
+def layout_descriptor(layout):
+    n8, n4, nz = layout_counts(layout)
+    return dict(layout=layout, n8=n8, n4=n4, nzero=nz, payload_bytes=48, scale_bytes=4,
+                row_bytes=52, latent_coefficients=2, latent_dtype='torch.float8_e4m3fn',
+                tensor_widths=dict(lo=n8 // 2, hi=n8 // 2, q4=n4 // 2, latent=2))
+
+
+def next_pow2(n):
+    return 1 << (int(n) - 1).bit_length()
+
+
+def allocate_state(batch, heads, dim, layout):
+    """Six zeroed arrays with the reference's names and widths (:39-49)."""
+    w = layout_descriptor(layout)['tensor_widths']
+    base = (batch, heads, dim)
+    st = {k: np.zeros(base + (w[k],), np.uint8) for k in ('lo', 'hi', 'q4', 'latent')}
+    st['s8'] = np.zeros(base, np.float16)
+    st['s4'] = np.zeros(base, np.float16)
+    return st
+
+
+# ---------------------------------------------------------------- FP8 E4M3FN bytes
+
+def _e4m3_table():
+    b = np.arange(256)
+    s = np.where(b >> 7, -1.0, 1.0)
+    e = (b >> 3) & 15
+    m = b & 7
+    v = np.where(e == 0, m * 2.0 ** -9, (1 + m / 8.0) * 2.0 ** (e - 7.0))
+    v = s * v
+    v[(b & 0x7F) == 0x7F] = np.nan
+    return v.astype(np.float32)
+
+
+E4M3_VALUES = _e4m3_table()
+
+
+def e4m3_to_f32(byte):
+    return E4M3_VALUES[np.asarray(byte, np.uint8)]
+
+
+def f32_to_e4m3(value):
+    """fp32 -> E4M3FN byte, round to nearest even, saturate finite (|v| > 448 -> 448).
+
+    Matches cvt.rn.satfinite.e4m3x2.f32 and torch's float8_e4m3fn cast on
+    finite inputs inside +-448. Exact: uses float64 scaling by powers of two.
+    """
+    v = np.asarray(value, np.float32).astype(np.float64)
+    sign = np.signbit(v)
+    a = np.abs(v)
+    a = np.minimum(a, 448.0)
+    # exponent of the binade, clamped to the normal range [-6, 8]
+    with np.errstate(divide='ignore'):
+        e = np.floor(np.log2(np.where(a > 0, a, 1.0)))
+    e = np.clip(e, -6, 8)
+    ulp = 2.0 ** (e - 3)
+    q = np.rint(a / ulp) * ulp            # RNE on the 3-bit mantissa grid (or subnormal grid)
+    q = np.minimum(q, 448.0)
+    # encode q (exact member of the E4M3 value set)
+    eq = np.floor(np.log2(np.where(q > 0, q, 1.0)))
+    sub = q < 2.0 ** -6
+    mant_sub = np.rint(q / 2.0 ** -9).astype(np.int64)
+    expo = np.clip(eq, -6, 8).astype(np.int64)
+    mant_n = np.rint((q / 2.0 ** expo - 1.0) * 8).astype(np.int64)
+    byte = np.where(sub, mant_sub, ((expo + 7) << 3) | mant_n)
+    byte = np.where(q == 0, 0, byte)
+    byte = byte | (sign.astype(np.int64) << 7)
+    return byte.astype(np.uint8)
+
+
+# ---------------------------------------------------------------- rounding / requant
+
+def round_half_away(q):
+    """libdevice.round semantics: nearest, ties away from zero (C round())."""
+    q = np.asarray(q, np.float32)
+    a = np.abs(q)
+    r = np.floor(a)
+    r = np.where(a - r >= F32(0.5), r + F32(1.0), r).astype(np.float32)
+    return np.where(q < 0, -r, r).astype(np.float32)
+
+
+def stored_quantize(value, scale, limit):
+    """scripts/state_ppl_codec_v6.py:52-61 -> int32 codes."""
+    value = np.asarray(value, np.float32)
+    scale = np.asarray(scale, np.float32)
+    safe = np.where(scale > 0, scale, F32(1.0)).astype(np.float32)
+    with np.errstate(invalid='ignore', divide='ignore'):
+        quotient = (value / safe).astype(np.float32)
+    rounded = round_half_away(quotient)
+    clipped = np.minimum(np.maximum(rounded, F32(-limit)), F32(limit))
+    return np.where(scale > 0, clipped, F32(0.0)).astype(np.int32)
+
+
+def tier_scale(maxabs, limit):
+    """den = max(div_rn(max|s|, limit), 1e-8) -> fp16 -> fp32 (:157-160)."""
+    den = np.maximum((np.asarray(maxabs, np.float32) / F32(limit)).astype(np.float32), F32(1e-8))
+    return den.astype(np.float16).astype(np.float32)
+
+
+# ---------------------------------------------------------------- nibble planes
+
+def unpack_nibbles(packed):
+    p = np.asarray(packed, np.uint8).astype(np.int32)
+    return np.stack((p & 15, (p >> 4) & 15), -1).reshape(*p.shape[:-1], p.shape[-1] * 2)
+
+
+def pack_nibbles(codes):
+    c = np.asarray(codes).astype(np.int32) & 15
+    return (c[..., 0::2] | (c[..., 1::2] << 4)).astype(np.uint8)
+
+
+def decode_codes(state, layout):
+    """Packed rows -> signed int codes (q8 [.., n8], q4 [.., n4]) (:81-97)."""
+    lo, hi = unpack_nibbles(state['lo']), unpack_nibbles(state['hi'])
+    ub = (hi << 4) | lo
+    q8 = ub - 256 * (ub > 127)
+    nib = unpack_nibbles(state['q4'])
+    q4 = nib - 16 * (nib > 7)
+    return q8.astype(np.int32), q4.astype(np.int32)
+
+
+def decode_state(state, layout, latent_scale, heads_per_group):
+    """Packed rows -> fp32 tier values (permuted order, [.., n8+n4]) and latent z [.., 2].
+
+    z_k = f32(e4m3 latent_k) * f32(latent_scale[g, k]) as in the kernel prologue (:98-114).
+    """
+    q8, q4 = decode_codes(state, layout)
+    s8 = state['s8'].astype(np.float32)[..., None]
+    s4 = state['s4'].astype(np.float32)[..., None]
+    tiers = np.concatenate((q8.astype(np.float32) * s8, q4.astype(np.float32) * s4), -1)
+    ls = np.asarray(latent_scale, np.float16).astype(np.float32)          # [G,2]
+    g = np.arange(state['s8'].shape[1]) // heads_per_group
+    z = e4m3_to_f32(state['latent']) * ls[g][None, :, None, :]
+    return tiers.astype(np.float32), z.astype(np.float32)
+
+
+def encode_state(tiers, z, layout, latent_scale, heads_per_group):
+    """fp32 tier values + latent z -> packed rows, with the kernel's requant rule.
+
+    INT tiers: s = f32(f16(max(div_rn(max|v|, L), 1e-8))), q = stored_quantize(v, s, L)
+    (:155-162); latent: e4m3(clamp(z / ls, +-448)) (:151-154, :176-179).
+    """
+    n8, n4, nz = layout_counts(layout)
+    tiers = np.asarray(tiers, np.float32)
+    v8, v4 = tiers[..., :n8], tiers[..., n8:n8 + n4]
+    s8 = tier_scale(np.max(np.abs(v8), -1), 127)
+    s4 = tier_scale(np.max(np.abs(v4), -1), 7)
+    q8 = stored_quantize(v8, s8[..., None], 127)
+    q4 = stored_quantize(v4, s4[..., None], 7)
+    ls = np.asarray(latent_scale, np.float16).astype(np.float32)
+    g = np.arange(tiers.shape[1]) // heads_per_group
+    lsr = ls[g][None, :, None, :]
+    zq = np.minimum(np.maximum((np.asarray(z, np.float32) / lsr).astype(np.float32), F32(-448)), F32(448))
+    return dict(lo=pack_nibbles(q8 & 15), hi=pack_nibbles((q8 >> 4) & 15), q4=pack_nibbles(q4 & 15),
+                latent=f32_to_e4m3(zq), s8=s8.astype(np.float16), s4=s4.astype(np.float16))
+
+
+def encode_diagnostic(tiers, layout):
+    """mamba2_recall/state_codec.py:299-331 rule on the latent layout's INT tiers.
+
+    fp32 denominators max(|v|max/L, 1e-8) (NOT fp16-rounded before dividing),
+    q = sign(z)*floor(|z|+0.5) clamped; scales stored as fp16. Latent bytes 0.
+    """
+    n8, n4, _ = layout_counts(layout)
+    v = np.asarray(tiers, np.float32)
+    v8, v4 = v[..., :n8], v[..., n8:n8 + n4]
+    s8 = np.maximum((np.max(np.abs(v8), -1) / F32(127)).astype(np.float32), F32(1e-8))
+    s4 = np.maximum((np.max(np.abs(v4), -1) / F32(7)).astype(np.float32), F32(1e-8))
+
+    def quant(x, s, lim):
+        zq = (x / s[..., None]).astype(np.float32)
+        r = (np.sign(zq) * np.floor(np.abs(zq) + F32(0.5))).astype(np.float32)
+        return np.clip(r, -lim, lim).astype(np.int32)
+    q8, q4 = quant(v8, s8, 127), quant(v4, s4, 7)
+    base = v.shape[:-1]
+    return dict(lo=pack_nibbles(q8 & 15), hi=pack_nibbles((q8 >> 4) & 15), q4=pack_nibbles(q4 & 15),
+                latent=np.zeros(base + (2,), np.uint8),
+                s8=s8.astype(np.float16), s4=s4.astype(np.float16))
+
+
+# ---------------------------------------------------------------- predictor correction
+
+def predictor_correction(C, permutation, predictor, layout):
+    """corr[b,l,g,f] = sum_d C[b,l,g,perm[g,n8+n4+d]] * Pred[g,f,d] in fp32 (:221-225).
+
+    Restates the reference's host code with the same torch CPU einsum call.
+    """
+    import torch
+    n8, n4, _ = layout_counts(layout)
+    C = torch.as_tensor(np.asarray(C, np.float16))
+    perm = torch.as_tensor(np.asarray(permutation, np.uint8))
+    pred = torch.as_tensor(np.asarray(predictor, np.float16))
+    batch, length = C.shape[:2]
+    dead_ix = perm[:, n8 + n4:].long()
+    dead_c = C.float().gather(3, dead_ix[None, None, :, :].expand(batch, length, -1, -1))
+    corr = torch.einsum('blgd,gfd->blgf', dead_c, pred.float()).contiguous()
+    return corr.numpy()
+
+
+# ---------------------------------------------------------------- the scan
+
+def latent_scan(x, dt, A, B, C, D, dt_bias, state, permutation, basis, latent_scale,
+                predictor, layout, corr=None):
+    """One call of the production codec over L tokens; mutates ``state``; returns y fp16.
+
+    x fp16 [Bt,L,H,P]; dt fp16 [Bt,L,H]; A fp32 [H]; B, C fp16 [Bt,L,G,128];
+    D, dt_bias fp16/fp32 [H]; permutation u8 [G,128]; basis f16 [G,nz,2];
+    latent_scale f16 [G,2]; predictor f16 [G,n8+n4+2,nz].
+    """
+    n8, n4, nz = layout_counts(layout)
+    R8, R4, RZ = next_pow2(n8), next_pow2(n4), next_pow2(nz)
+    x = np.asarray(x, np.float16)
+    Bt, L, H, P = x.shape
+    G = np.asarray(B).shape[2]
+    hg = H // G
+    gidx = np.arange(H) // hg
+    if corr is None:
+        corr = predictor_correction(C, permutation, predictor, layout)
+    corr = np.asarray(corr, np.float32)
+    perm = np.asarray(permutation, np.uint8).astype(np.int64)
+    Bf = np.asarray(B, np.float16).astype(np.float32)
+    Cf = np.asarray(C, np.float16).astype(np.float32)
+
+    def padded(width, count):
+        return np.arange(width) < count
+
+    m8, m4, mz = padded(R8, n8), padded(R4, n4), padded(RZ, nz)
+    pos8 = np.zeros((G, R8), np.int64); pos8[:, :n8] = perm[:, :n8]
+    pos4 = np.zeros((G, R4), np.int64); pos4[:, :n4] = perm[:, n8:n8 + n4]
+    posd = np.zeros((G, RZ), np.int64); posd[:, :nz] = perm[:, n8 + n4:]
+    bas = np.asarray(basis, np.float16).astype(np.float32)
+    basis0 = np.zeros((G, RZ), np.float32); basis0[:, :nz] = bas[:, :, 0]
+    basis1 = np.zeros((G, RZ), np.float32); basis1[:, :nz] = bas[:, :, 1]
+    ls = np.asarray(latent_scale, np.float16).astype(np.float32)
+    ls0 = ls[gidx, 0][None, :, None]
+    ls1 = ls[gidx, 1][None, :, None]
+    av = np.asarray(A, np.float32)[None, :, None]
+    dv = np.asarray(D).astype(np.float32)[None, :, None]
+    bias = np.asarray(dt_bias).astype(np.float32)[None, :]
+
+    # decode (:81-114), padded tier widths
+    q8c, q4c = decode_codes(state, layout)
+    q8 = np.zeros((Bt, H, P, R8), np.int32); q8[..., :n8] = q8c
+    q4 = np.zeros((Bt, H, P, R4), np.int32); q4[..., :n4] = q4c
+    s8 = state['s8'].astype(np.float32)
+    s4 = state['s4'].astype(np.float32)
+    state8 = (q8.astype(np.float32) * s8[..., None]).astype(np.float32)
+    state4 = (q4.astype(np.float32) * s4[..., None]).astype(np.float32)
+    lat = e4m3_to_f32(state['latent'])
+    z0 = (lat[..., 0] * ls0).astype(np.float32)
+    z1 = (lat[..., 1] * ls1).astype(np.float32)
+    F = n8 + n4 + 2
+    y = np.zeros((Bt, L, H, P), np.float16)
+    for t in range(L):
+        cp = corr[:, t]                                  # [Bt,G,F]
+        pc8 = np.zeros((Bt, G, R8), np.float32); pc8[..., :n8] = cp[..., :n8]
+        pc4 = np.zeros((Bt, G, R4), np.float32); pc4[..., :n4] = cp[..., n8:n8 + n4]
+        pcz0 = cp[..., n8 + n4]; pcz1 = cp[..., n8 + n4 + 1]
+        assert F == cp.shape[-1]
+        xv = x[:, t].astype(np.float32)                  # [Bt,H,P]
+        dtv = np.asarray(dt, np.float16)[:, t].astype(np.float32) + bias
+        with np.errstate(over='ignore'):
+            dtv = np.where(dtv <= F32(20.0), np.log(np.exp(dtv) + F32(1.0)), dtv).astype(np.float32)
+        decay = np.exp(av[..., 0] * dtv).astype(np.float32)       # [Bt,H]
+        bt, ct = Bf[:, t], Cf[:, t]                      # [Bt,G,128]
+        gi = np.arange(G)[None, :, None]
+        bi = np.arange(Bt)[:, None, None]
+        bv8 = np.where(m8, bt[bi, gi, pos8[None]], F32(0)); cv8 = np.where(m8, ct[bi, gi, pos8[None]], F32(0))
+        bv4 = np.where(m4, bt[bi, gi, pos4[None]], F32(0)); cv4 = np.where(m4, ct[bi, gi, pos4[None]], F32(0))
+        bvd = np.where(mz, bt[bi, gi, posd[None]], F32(0)); cvd = np.where(mz, ct[bi, gi, posd[None]], F32(0))
+        # per-head views [Bt,H,1,R]
+        hsel = (slice(None), gidx)
+        dec = decay[:, :, None]
+        dtr = dtv[:, :, None]
+        prior8, prior4 = state8, state4
+        state8 = prior8 * dec[..., None] + (bv8[hsel][:, :, None, :] * dtr[..., None]) * xv[..., None]
+        state4 = prior4 * dec[..., None] + (bv4[hsel][:, :, None, :] * dtr[..., None]) * xv[..., None]
+        state8 = np.where(m8, state8, F32(0)).astype(np.float32)
+        state4 = np.where(m4, state4, F32(0)).astype(np.float32)
+        dot_bc = np.sum(bvd * cvd, -1)                   # [Bt,G]
+        dot_c0 = np.sum(basis0[None] * cvd, -1)
+        dot_c1 = np.sum(basis1[None] * cvd, -1)
+        dot_b0 = np.sum(basis0[None] * bvd, -1)
+        dot_b1 = np.sum(basis1[None] * bvd, -1)
+        h_bc, h_c0, h_c1 = dot_bc[hsel][..., None], dot_c0[hsel][..., None], dot_c1[hsel][..., None]
+        h_b0, h_b1 = dot_b0[hsel][..., None], dot_b1[hsel][..., None]
+        out = (np.sum(state8 * cv8[hsel][:, :, None, :], -1) +
+               np.sum(state4 * cv4[hsel][:, :, None, :], -1))
+        out = out + (dec * (z0 * h_c0 + z1 * h_c1) + (xv * dtr) * h_bc + xv * dv)
+        out = out + dec * (np.sum(prior8 * pc8[hsel][:, :, None, :], -1) +
+                           np.sum(prior4 * pc4[hsel][:, :, None, :], -1) +
+                           z0 * pcz0[hsel][..., None] + z1 * pcz1[hsel][..., None])
+        y[:, t] = out.astype(np.float32).astype(np.float16)
+        z0 = (z0 * dec + (xv * dtr) * h_b0).astype(np.float32)
+        z1 = (z1 * dec + (xv * dtr) * h_b1).astype(np.float32)
+        qz0 = f32_to_e4m3(np.minimum(np.maximum((z0 / ls0).astype(np.float32), F32(-448)), F32(448)))
+        qz1 = f32_to_e4m3(np.minimum(np.maximum((z1 / ls1).astype(np.float32), F32(-448)), F32(448)))
+        z0 = (e4m3_to_f32(qz0) * ls0).astype(np.float32)
+        z1 = (e4m3_to_f32(qz1) * ls1).astype(np.float32)
+        s8 = tier_scale(np.max(np.abs(state8), -1), 127)
+        s4 = tier_scale(np.max(np.abs(state4), -1), 7)
+        q8 = stored_quantize(state8, s8[..., None], 127)
+        q4 = stored_quantize(state4, s4[..., None], 7)
+        state8 = (q8.astype(np.float32) * s8[..., None]).astype(np.float32)
+        state4 = (q4.astype(np.float32) * s4[..., None]).astype(np.float32)
+    # pack + store once (:163-181)
+    state['lo'][...] = pack_nibbles(q8[..., :n8] & 15)
+    state['hi'][...] = pack_nibbles((q8[..., :n8] >> 4) & 15)
+    state['q4'][...] = pack_nibbles(q4[..., :n4] & 15)
+    qz0 = f32_to_e4m3(np.minimum(np.maximum((z0 / ls0).astype(np.float32), F32(-448)), F32(448)))
+    qz1 = f32_to_e4m3(np.minimum(np.maximum((z1 / ls1).astype(np.float32), F32(-448)), F32(448)))
+    state['latent'][..., 0] = qz0
+    state['latent'][..., 1] = qz1
+    state['s8'][...] = s8.astype(np.float16)
+    state['s4'][...] = s4.astype(np.float16)
+    return y

@@ -1,0 +1,195 @@
+#!/usr/bin/env python3
+"""Regenerate the golden vectors in this directory from the reference's own code.
+
+Runs ONLY in the build container, where the reference tree is mounted (path
+given by --reference, default /root/reference). The GPU box never runs it;
+tests read the committed .npz files.
+
+What is recorded
+  codec_<layout>.npz   the production latent codec kernel `_latent_scan`
+                       (scripts/fp4_zero_predictor_codec_v1.py:76-181) executed
+                       by the Triton CPU interpreter, with the host correction of
+                       :221-225, on seeded inputs: one multi-token call from
+                       random packed bytes, and one known-answer call (A=0,
+                       x=0 => decay 1, no update: decode -> requant -> pack).
+  fp4_g16.npz          mamba2_recall/fp4.py quantize_chunk + decode_packet on a
+                       seeded matrix (codes, E4M3 block bytes, global, FP16).
+  adapter.npz          mamba2_recall/resurface_native._Adapter.forward (soft
+                       gate, FP16 parameters) on CPU.
+
+Interpreter shims (the interpreter cannot run two device intrinsics as the
+GPU does):
+  * libdevice.round -> C round() semantics (nearest, ties away from zero).
+  * fp32 <-> float8e4nv casts -> torch's float8_e4m3fn cast (round to nearest
+    even), matching the GPU's cvt.rn.satfinite on the kernel's +-448 clamp.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+from pathlib import Path
+
+os.environ['TRITON_INTERPRET'] = '1'
+HERE = Path(__file__).resolve().parent
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import triton  # noqa: E402
+import triton.language as tl  # noqa: E402
+
+
+@triton.jit
+def _round_half_away(x):
+    a = tl.abs(x)
+    r = tl.floor(a)
+    r = tl.where(a - r >= 0.5, r + 1.0, r)
+    return tl.where(x < 0, -r, r)
+
+
+def install_shims(reference):
+    sys.path.insert(0, str(reference / 'scripts'))
+    sys.path.insert(0, str(reference))
+    from triton.runtime import interpreter as interp
+    import state_ppl_codec_v6 as v6
+
+    class _Libdevice:
+        round = _round_half_away
+
+    v6.libdevice = _Libdevice
+    original = interp._convert_float
+
+    def convert(data, src, dst, rounding_mode):
+        names = (str(src), str(dst))
+        if names == ('fp32', 'fp8e4nv'):
+            t = torch.from_numpy(np.ascontiguousarray(data).view(np.float32).copy())
+            return t.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+        if names == ('fp8e4nv', 'fp32'):
+            t = torch.from_numpy(np.ascontiguousarray(data).view(np.uint8).copy())
+            return t.view(torch.float8_e4m3fn).float().numpy().view(np.uint32)
+        return original(data, src, dst, rounding_mode)
+
+    interp._convert_float = convert
+    import fp4_zero_predictor_codec_v1 as ref
+    return ref
+
+
+def random_state(gen, batch, heads, dim, spec):
+    w = spec['tensor_widths']
+    t = {}
+    for k in ('lo', 'hi', 'q4'):
+        t[k] = torch.randint(0, 256, (batch, heads, dim, w[k]), generator=gen, dtype=torch.uint8)
+    lat = torch.randint(0, 256, (batch, heads, dim, 2), generator=gen, dtype=torch.uint8)
+    lat = torch.where((lat & 0x7F) == 0x7F, lat ^ 0x01, lat)          # no NaN bytes
+    t['latent'] = lat.view(torch.float8_e4m3fn)
+    for k, lim in (('s8', 1e-2), ('s4', 1e-1)):
+        t[k] = (torch.rand(batch, heads, dim, generator=gen) * lim + 1e-5).half()
+    return t
+
+
+def codec_case(ref, layout, seed, batch=2, length=4, heads=4, dim=32, groups=2, known_answer=False):
+    spec = ref.layout_descriptor(layout)
+    n8, n4, nz = spec['n8'], spec['n4'], spec['nzero']
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(batch, length, heads, dim, generator=gen).half()
+    dt = (torch.randn(batch, length, heads, generator=gen) * 0.7).half()
+    A = -(torch.rand(heads, generator=gen) * 3 + 0.05).float()
+    Bm = torch.randn(batch, length, groups, 128, generator=gen).half()
+    Cm = torch.randn(batch, length, groups, 128, generator=gen).half()
+    D = torch.randn(heads, generator=gen).half()
+    dt_bias = (torch.rand(heads, generator=gen) * 3 - 4).half()
+    perm = torch.stack([torch.randperm(128, generator=gen) for _ in range(groups)]).to(torch.uint8)
+    basis = torch.randn(groups, nz, 2, generator=gen).half()
+    ls = (torch.rand(groups, 2, generator=gen) + 0.1).half()
+    pred = (torch.randn(groups, n8 + n4 + 2, nz, generator=gen) / np.sqrt(n8 + n4 + 2)).half()
+    if known_answer:
+        length = 1
+        x = torch.zeros(batch, 1, heads, dim).half()
+        dt, Bm, Cm = dt[:, :1].contiguous(), Bm[:, :1].contiguous(), Cm[:, :1].contiguous()
+        A = torch.zeros(heads).float()
+    state = random_state(gen, batch, heads, dim, spec)
+    initial = {k: v.clone() for k, v in state.items()}
+    dead = perm[:, n8 + n4:].long()
+    dead_c = Cm.float().gather(3, dead[None, None].expand(batch, length, -1, -1))
+    corr = torch.einsum('blgd,gfd->blgf', dead_c, pred.float()).contiguous()
+    out = torch.empty_like(x)
+    ref._latent_scan[(batch, heads, triton.cdiv(dim, 16))](
+        x, dt, A, Bm, Cm, corr, D, dt_bias, perm,
+        *(state[k] for k in ('lo', 'hi', 'q4', 'latent', 's8', 's4')),
+        basis, ls, out, length, heads, dim, groups, n8, n4, nz,
+        triton.next_power_of_2(n8), triton.next_power_of_2(n4), triton.next_power_of_2(nz), 16,
+        num_warps=4)
+
+    def np_(t):
+        if t.dtype == torch.float8_e4m3fn:
+            return t.view(torch.uint8).numpy()
+        return t.numpy()
+    rec = dict(x=x, dt=dt, A=A, B=Bm, C=Cm, D=D, dt_bias=dt_bias, permutation=perm, basis=basis,
+               latent_scale=ls, predictor=pred, corr=corr, y=out)
+    rec = {k: np_(v) for k, v in rec.items()}
+    rec.update({'in_' + k: np_(v) for k, v in initial.items()})
+    rec.update({'out_' + k: np_(v) for k, v in state.items()})
+    return rec
+
+
+def fp4_case(reference, seed=7):
+    sys.path.insert(0, str(reference))
+    from mamba2_recall import fp4
+    gen = torch.Generator().manual_seed(seed)
+    rows, cols = 48, 256
+    w = torch.randn(rows, cols, generator=gen) * torch.exp(torch.randn(rows, cols // 16, 1, generator=gen)).repeat(1, 1, 16).reshape(rows, cols) * 0.02
+    w[3, 16:32] = 0                        # an all-zero group
+    w[5, :] *= 1e-4                        # tiny row (fp16 subnormal decode)
+    w[7, 0] = 0.7                          # a large outlier sets the global scale
+    w = w.half()
+    g = fp4.tensor_global_scale(w)
+    packet = fp4.quantize_chunk(w, 'fp4_g16_e4m3', g)
+    decoded = fp4.decode_packet(packet)
+    ties = torch.tensor([.25, .75, 1.25, 1.75, 2.5, 3.5, 5.0, -.25, -.75, -5.0, 0.0, -0.0, 7.0, -7.0])
+    return dict(source=w.numpy(), codes=packet['packed'].numpy(),
+                block_scale_bytes=packet['scales'].view(torch.uint8).numpy(),
+                global_scale=np.asarray(packet['global_scale'].item(), np.float32),
+                decoded=decoded.numpy(), tie_values=ties.numpy(),
+                tie_codes=fp4.encode_e2m1(ties.float()).numpy())
+
+
+def adapter_case(reference, seed=11):
+    sys.path.insert(0, str(reference))
+    from mamba2_recall import resurface_native as native
+    gen = torch.Generator().manual_seed(seed)
+    width, heads, hd, tokens = 256, 16, 8, 5
+    ad = native._Adapter(width, heads, device='cpu', trainable=False)
+    with torch.no_grad():
+        ad.V_read.copy_((torch.randn(heads, heads, generator=gen) * 0.1).half())
+        ad.g_read.copy_((torch.rand(heads, generator=gen) + 0.5).half())
+        ad.router_w.copy_((torch.randn(width, generator=gen) * 0.05).half())
+        ad.router_b.copy_(torch.tensor(-0.5).half())
+    y = torch.randn(2, tokens, heads * hd, generator=gen).half()
+    u = torch.randn(2, tokens, width, generator=gen).half()
+    with torch.no_grad():
+        out, logits = ad(y, u, heads, hd, 'soft', False)
+    return dict(V=ad.V_read.numpy(), g=ad.g_read.numpy(), w=ad.router_w.numpy(),
+                b=ad.router_b.numpy(), y=y.numpy(), u=u.numpy(), out=out.numpy(),
+                logits=logits.numpy())
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--reference', type=Path, default=Path('/root/reference'))
+    args = ap.parse_args()
+    ref = install_shims(args.reference)
+    layouts = ('32_32_64', '16_64_48', '8_80_40', '24_48_56', '36_24_68', '40_16_72', '44_8_76')
+    for i, layout in enumerate(layouts):
+        scan = codec_case(ref, layout, seed=100 + i)
+        ka = codec_case(ref, layout, seed=200 + i, known_answer=True)
+        rec = {'scan_' + k: v for k, v in scan.items()}
+        rec.update({'ka_' + k: v for k, v in ka.items()})
+        np.savez_compressed(HERE / f'codec_{layout}.npz', **rec)
+        print('wrote', layout)
+    np.savez_compressed(HERE / 'fp4_g16.npz', **fp4_case(args.reference))
+    np.savez_compressed(HERE / 'adapter.npz', **adapter_case(args.reference))
+    print('done')
+
+
+if __name__ == '__main__':
+    main()

@@ -1,0 +1,139 @@
+"""GPU parity of the SQ3.25 codec entry points (sq_scan, sq_state_encode/decode) against
+the reference kernel's golden vectors and the CPU oracle."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import codec as oc
+
+pytestmark = pytest.mark.gpu
+
+# y tolerance: the GPU evaluates exp/log with CUDA's libm and contracts a*b+c into FMA,
+# so fp32 values differ from the reference (numpy) by a few ulps; an fp32 difference that
+# straddles an fp16 rounding boundary shows up as one fp16 ulp of y, and a requant code
+# that straddles a half-integer moves one stored coordinate by one code step.
+Y_RTOL, Y_ATOL = 2e-2, 2e-2
+
+
+def _state_from(d, pre, device):
+    t = {}
+    for k in ('lo', 'hi', 'q4', 's8', 's4'):
+        t[k] = torch.from_numpy(d[pre + k].copy()).to(device)
+    t['latent'] = torch.from_numpy(d[pre + 'latent'].copy()).to(device).view(torch.float8_e4m3fn)
+    return t
+
+
+def _run_scan(d, pre, layout, device='cuda'):
+    from sq325 import codec
+    g = lambda k: torch.from_numpy(np.ascontiguousarray(d[pre + k])).to(device)
+    st = codec.PackedState('latent_fp8_' + layout, _state_from(d, pre + 'in_', device),
+                           tuple(d[pre + 'x'].shape[:1]) + (d[pre + 'x'].shape[2], d[pre + 'x'].shape[3], 128))
+    y, _ = codec.scan(g('x'), g('dt'), g('A'), g('B'), g('C'), g('D'), g('dt_bias'), st, g('permutation'),
+                      g('basis'), g('latent_scale'), g('predictor'), layout=layout)
+    torch.cuda.synchronize()
+    return y.cpu().numpy(), {k: (v.view(torch.uint8) if v.dtype == torch.float8_e4m3fn else v).cpu().numpy()
+                             for k, v in st.tensors.items()}
+
+
+@pytest.mark.parametrize('layout', oc.LAYOUTS)
+def test_scan_known_answer_bytes_exact(golden, layout):
+    """A=0, x=0: one token is decode -> requant -> pack; the packed bytes must equal the
+    reference kernel's exactly (a zero latent may keep or drop its sign)."""
+    d = golden(f'codec_{layout}.npz')
+    y, st = _run_scan(d, 'ka_', layout)
+    for k in ('lo', 'hi', 'q4', 's8', 's4'):
+        assert np.array_equal(st[k].view(np.uint8), d['ka_out_' + k].view(np.uint8)), k
+    a, b = st['latent'], d['ka_out_latent'].view(np.uint8)
+    assert np.array_equal(np.where(a == 0x80, 0, a), np.where(b == 0x80, 0, b))
+    ref = d['ka_y'].astype(np.float32)
+    assert np.allclose(y.astype(np.float32), ref, rtol=Y_RTOL, atol=Y_ATOL)
+
+
+@pytest.mark.parametrize('layout', oc.LAYOUTS)
+def test_scan_multi_token_matches_reference(golden, layout):
+    d = golden(f'codec_{layout}.npz')
+    y, st = _run_scan(d, 'scan_', layout)
+    ref = d['scan_y'].astype(np.float32)
+    yf = y.astype(np.float32)
+    assert np.allclose(yf, ref, rtol=Y_RTOL, atol=Y_ATOL), float(np.abs(yf - ref).max())
+    # >= 99% of readouts bit-identical to the reference fp16
+    assert (y.view(np.uint16) == d['scan_y'].view(np.uint16)).mean() >= 0.99
+    # requantised codes: >= 99% identical, all within one code step
+    q8, q4 = oc.decode_codes(st, layout)
+    r8, r4 = oc.decode_codes({k: d['scan_out_' + k] for k in ('lo', 'hi', 'q4')}, layout)
+    assert (q8 == r8).mean() >= 0.99 and (q4 == r4).mean() >= 0.99
+    assert np.abs(q8 - r8).max() <= 1 and np.abs(q4 - r4).max() <= 1
+
+
+@pytest.mark.parametrize('layout', oc.LAYOUTS)
+def test_encode_decode_bit_exact(layout):
+    from sq325 import codec
+    rng = np.random.default_rng(7)
+    B, H, P, G = 2, 16, 64, 8
+    n8, n4, nz = oc.layout_counts(layout)
+    sig = np.exp(rng.uniform(np.log(1e-3), 0, (1, H, 1, 1))).astype(np.float32)
+    tiers = (rng.standard_normal((B, H, P, n8 + n4)) * sig).astype(np.float32)
+    tiers[0, 0, 0] = 0.0                                 # all-zero row -> zero scales
+    tiers[0, 0, 1] = 1e-9                                # underflowing fp16 scale
+    z = (rng.standard_normal((B, H, P, 2)) * 30).astype(np.float32)
+    ls = rng.uniform(0.1, 1.1, (G, 2)).astype(np.float16)
+    st = codec.allocate_state(B, H, P, 128, 'cuda', layout=layout)
+    codec.encode_state_(st, torch.from_numpy(tiers), torch.from_numpy(z), torch.from_numpy(ls), layout=layout)
+    torch.cuda.synchronize()
+    got = {k: (v.view(torch.uint8) if v.dtype == torch.float8_e4m3fn else v).cpu().numpy()
+           for k, v in st.tensors.items()}
+    ref = oc.encode_state(tiers, z, layout, ls, H // G)
+    for k in ref:
+        assert np.array_equal(got[k].view(np.uint8), ref[k].view(np.uint8)), k
+    t2, z2 = codec.decode_state(st, torch.from_numpy(ls), layout=layout)
+    rt, rz = oc.decode_state(ref, layout, ls, H // G)
+    assert np.array_equal(t2.cpu().numpy().view(np.uint32), rt.view(np.uint32))
+    assert np.array_equal(z2.cpu().numpy().view(np.uint32), rz.view(np.uint32))
+
+
+def test_encode_diagnostic_matches_reference_rule():
+    from sq325 import codec
+    layout = '32_32_64'
+    rng = np.random.default_rng(3)
+    tiers = (rng.standard_normal((1, 8, 64, 60)) * 0.1).astype(np.float32)
+    st = codec.allocate_state(1, 8, 64, 128, 'cuda', layout=layout)
+    codec.encode_state_(st, torch.from_numpy(tiers), layout=layout, mode='diagnostic')
+    torch.cuda.synchronize()
+    ref = oc.encode_diagnostic(tiers, layout)
+    for k in ('lo', 'hi', 'q4', 's8', 's4'):
+        assert np.array_equal(st.tensors[k].cpu().numpy().view(np.uint8), ref[k].view(np.uint8)), k
+
+
+def test_codec_round_trip_many_steps():
+    """Config-1 style: decay + rank-1 update with encode/decode every step, 256 steps of
+    L=1 calls; the GPU carry tracks the oracle carry (same per-step arithmetic)."""
+    from sq325 import codec
+    layout = '24_48_56'
+    n8, n4, nz = oc.layout_counts(layout)
+    rng = np.random.default_rng(0)
+    B, L, H, P, G = 1, 1, 16, 64, 8
+    perm = np.stack([rng.permutation(128) for _ in range(G)]).astype(np.uint8)
+    basis = rng.standard_normal((G, nz, 2)).astype(np.float16)
+    ls = rng.uniform(0.1, 1.1, (G, 2)).astype(np.float16)
+    pred = (rng.standard_normal((G, n8 + n4 + 2, nz)) / np.sqrt(n8 + n4 + 2)).astype(np.float16)
+    A = -(rng.uniform(0.01, 0.5, H)).astype(np.float32)
+    D = rng.standard_normal(H).astype(np.float16)
+    dtb = np.zeros(H, np.float16)
+    st_g = codec.allocate_state(B, H, P, 128, 'cuda', layout=layout)
+    st_o = oc.allocate_state(B, H, P, layout)
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    ys, yo = [], []
+    for step in range(256):
+        x = rng.standard_normal((B, L, H, P)).astype(np.float16)
+        dt = np.full((B, L, H), 0.5413, np.float16)          # softplus(0.5413) ~= 1
+        Bm = rng.standard_normal((B, L, G, 128)).astype(np.float16)
+        Cm = rng.standard_normal((B, L, G, 128)).astype(np.float16)
+        y, _ = codec.scan(T(x), T(dt), T(A), T(Bm), T(Cm), T(D), T(dtb), st_g, T(perm), T(basis), T(ls), T(pred),
+                          layout=layout)
+        ys.append(y.cpu().numpy())
+        yo.append(oc.latent_scan(x, dt, A, Bm, Cm, D, dtb, st_o, perm, basis, ls, pred, layout))
+    ys, yo = np.stack(ys).astype(np.float32), np.stack(yo).astype(np.float32)
+    err = np.abs(ys - yo)
+    scale = np.abs(yo).max()
+    assert err.max() <= 0.05 * scale, (err.max(), scale)
+    assert np.sqrt((err ** 2).mean()) <= 5e-3 * scale

@@ -1,0 +1,121 @@
+"""GPU parity of the full native model path (embedding -> layers -> norm_f -> heads)
+against the CPU oracle on matched tiny models (real layer geometry, 2 layers)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from _models import build_pair, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+NLL_RTOL = 1e-3      # north-star tolerance on per-window NLL
+
+
+@pytest.fixture(scope='module')
+def pair():
+    return build_pair(n_layer=2, vocab=512, seed=1, adapter=True)
+
+
+def _ids(rng, B, T, vocab):
+    return rng.integers(0, vocab, (B, T)).astype(np.int64)
+
+
+@pytest.mark.parametrize('B,T', [(2, 16), (2, 48)])
+def test_prefill_hidden_and_nll(pair, B, T):
+    from sq325 import PredictorState
+    gm, ora, statics = pair
+    rng = np.random.default_rng(B * 100 + T)
+    ids = _ids(rng, B, T + 1, gm.vocab)
+    with PredictorState(gm, *statics) as ex:
+        hid = ex.backbone(torch.from_numpy(ids[:, :-1]).cuda(), reset=True)
+        nll = ex.score(hid, torch.from_numpy(ids[:, 1:]).cuda())
+        torch.cuda.synchronize()
+        ex.check()
+    ora.reset(B)
+    href = ora.backbone(ids[:, :-1])
+    nref = ora.nll(href, ids[:, 1:])
+    assert rel_l2(hid.float(), href.float()) < 2e-2
+    got = nll.double().cpu().view(B, T).sum(1)
+    exp = nref.view(B, T).sum(1)
+    assert torch.allclose(got, exp, rtol=NLL_RTOL, atol=0), (got, exp)
+
+
+def test_decode_steps_and_greedy(pair):
+    from sq325 import PredictorState
+    gm, ora, statics = pair
+    rng = np.random.default_rng(5)
+    B, T = 2, 12
+    ids = _ids(rng, B, T, gm.vocab)
+    with PredictorState(gm, *statics) as ex:
+        h = ex.backbone(torch.from_numpy(ids).cuda(), reset=True)
+        ora.reset(B)
+        hr = ora.backbone(ids)
+        assert rel_l2(h.float(), hr.float()) < 2e-2
+        for step in range(4):
+            nxt = rng.integers(0, gm.vocab, (B, 1)).astype(np.int64)
+            h = ex.backbone(torch.from_numpy(nxt).cuda())
+            hr = ora.backbone(nxt)
+            assert rel_l2(h.float(), hr.float()) < 3e-2, step
+            # conv ring in the reference's chronological order
+            for layer in range(gm.n_layer):
+                got = ex.conv_chronological(layer).cpu()
+                assert torch.equal(got, ora.caches[layer]['conv']), (step, layer)
+        logits = torch.empty(B, gm.vocab, device='cuda', dtype=torch.float16)
+        tok = ex.greedy(h[:, -1], logits=logits)
+        torch.cuda.synchronize()
+        lref = ora.logits(h[:, -1].cpu())
+        assert rel_l2(logits.float(), lref.float()) < 1e-2
+        # argmax of the GPU's own fp16 logits, first index on ties
+        assert torch.equal(tok.cpu(), logits.float().cpu().argmax(-1))
+
+
+def test_repeated_reset_is_bit_identical(pair):
+    """scripts/run_fp4_ridge_resurface_v3.py:90-98: the same probe twice after reset gives
+    identical hidden states and identical cache bytes."""
+    from sq325 import PredictorState
+    gm, _, statics = pair
+    ids = torch.from_numpy(np.random.default_rng(9).integers(0, gm.vocab, (1, 128))).cuda()
+    with PredictorState(gm, *statics) as ex:
+        a = ex.backbone(ids, reset=True).clone()
+        ca = [{k: v.clone() for k, v in e.state.tensors.items()} for e in ex._cache]
+        b = ex.backbone(ids, reset=True)
+        torch.cuda.synchronize()
+        assert torch.equal(a, b)
+        for x, e in zip(ca, ex._cache):
+            for k in x:
+                assert torch.equal(x[k].view(torch.uint8), e.state.tensors[k].view(torch.uint8))
+        ex.assert_finite_cache()
+        desc = ex.storage_descriptor()
+        assert desc['row_bytes'] == 52 and len(desc['layers']) == gm.n_layer
+
+
+def test_bad_token_id_is_reported(pair):
+    from sq325 import PredictorState
+    gm, _, statics = pair
+    with PredictorState(gm, *statics) as ex:
+        ids = torch.tensor([[1, 2, gm.vocab + 5]], device='cuda')
+        ex.backbone(ids, reset=True)
+        with pytest.raises(ValueError):
+            ex.check()
+
+
+def test_scoring_driver_pooled_ppl(pair):
+    from sq325 import PredictorState, ppl_windows, evaluate_ppl
+    gm, ora, statics = pair
+    rng = np.random.default_rng(11)
+    ids = rng.integers(0, gm.vocab, 3 * 32 + 10).astype(np.int64)
+    windows = [(s, torch.from_numpy(w)) for s, w in ppl_windows(ids, 32)]
+    assert [len(w) for _, w in windows] == [33, 33, 33, 11]
+    with PredictorState(gm, *statics) as ex:
+        res = evaluate_ppl(ex, windows, batch_windows=2)
+    total = 0.0
+    for (s, w), rec in zip(windows, res['windows']):
+        ora.reset(1)
+        hr = ora.backbone(w[None, :-1].numpy())
+        ref = float(ora.nll(hr, w[None, 1:].numpy()).sum())
+        assert math.isclose(rec['nll'], ref, rel_tol=NLL_RTOL), (rec['nll'], ref)
+        total += ref
+    assert math.isclose(res['nll'], total, rel_tol=NLL_RTOL)
+    assert res['target_tokens'] == sum(len(w) - 1 for _, w in windows)
