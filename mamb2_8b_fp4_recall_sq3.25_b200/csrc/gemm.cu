@@ -115,6 +115,7 @@ struct GemmArgs {
   int mode;
   const long long* targets; float2* partials; float* tlogit;
   int n_offset, ntiles_total;
+  int vec;                      // C rows are 16-byte aligned: vector stores allowed
   int* err;
 };
 
@@ -227,7 +228,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
           tmem_ld32(tbase + c0, r);
           if (row < args.M) {
             uint16_t* dst = args.C + (long long)row * args.ldc + n0 + c0;
-            if (n0 + c0 + 32 <= args.N) {
+            if (args.vec && n0 + c0 + 32 <= args.N) {
 #pragma unroll
               for (int v = 0; v < 4; ++v) {
                 uint4 o;
@@ -326,7 +327,7 @@ int launch_gemm_f16(const uint16_t* A, long long lda, const uint16_t* B, long lo
                     int* dev_err, cudaStream_t st) {
   if (M <= 0 || N <= 0 || K <= 0 || K % BK) return kEInval;
   if ((lda * 2) % 16 || (ldb * 2) % 16 || ((uintptr_t)A % 16) || ((uintptr_t)B % 16)) return kEInval;
-  if (mode == 0 && (!C || ldc < N || ldc % 8 || ((uintptr_t)C % 16))) return kEInval;
+  if (mode == 0 && (!C || ldc < N)) return kEInval;
   if (mode == 1 && (!ce || !ce->targets || !ce->partials || !ce->target_logit)) return kEInval;
   if (!dev_err) return kEInval;
   CUtensorMap ma, mb;
@@ -348,6 +349,7 @@ int launch_gemm_f16(const uint16_t* A, long long lda, const uint16_t* B, long lo
   a.targets = ce ? ce->targets : nullptr; a.partials = ce ? ce->partials : nullptr;
   a.tlogit = ce ? ce->target_logit : nullptr; a.err = dev_err;
   a.n_offset = ce ? ce->n_offset : 0; a.ntiles_total = ce ? ce->ntiles_total : 0;
+  a.vec = (mode == 0 && ldc % 8 == 0 && ((uintptr_t)C % 16) == 0) ? 1 : 0;
   if (mode == 1 && (a.n_offset % BN || a.ntiles_total < a.n_offset / BN + (N + BN - 1) / BN)) return kEInval;
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < g_num_sms ? tiles : g_num_sms;

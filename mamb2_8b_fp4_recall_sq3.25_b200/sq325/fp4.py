@@ -120,11 +120,13 @@ def synthetic_arrays(rows, cols, rng, mu=-4.0, sigma=0.5):
 
 
 @torch.no_grad()
-def synthetic(rows, cols, generator, device='cuda', mu=-4.0, sigma=0.5):
-    """Config-2 weights generated on the device from a seeded torch.Generator."""
+def synthetic(rows, cols, generator, device='cuda', mu=-4.0, sigma=0.5, row_mu=None):
+    """Config-2 weights generated on the device from a seeded torch.Generator; `row_mu`
+    (optional tensor [rows]) overrides the log-normal mean per output row."""
     codes = torch.randint(0, 256, (rows, cols // 2), generator=generator, device=device, dtype=torch.uint8)
-    eff = torch.empty((rows, cols // 16), device=device, dtype=torch.float32).log_normal_(mu, sigma,
-                                                                                       generator=generator)
+    n = torch.empty((rows, cols // 16), device=device, dtype=torch.float32).normal_(0.0, 1.0, generator=generator)
+    mus = mu if row_mu is None else row_mu.to(device=device, dtype=torch.float32)[:, None]
+    eff = torch.exp(mus + sigma * n)
     g = (eff.max() / 448.0).reshape(1).float()
     blocks = (eff / g).to(torch.float8_e4m3fn).view(torch.uint8).contiguous()
     return Fp4Tensor(codes, blocks, g, (rows, cols))

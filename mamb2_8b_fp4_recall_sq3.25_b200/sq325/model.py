@@ -25,6 +25,8 @@ MODEL_CONFIG = {
 }
 D_MODEL, D_INNER, D_XBC, D_ZX, HEADS, HEAD_DIM, GROUPS, D_CONV = 4096, 8192, 10240, 18560, 128, 64, 8, 4
 EPS = 1e-5
+# log-normal mean of the effective block scale per in_proj output row (z | xBC | dt)
+IN_PROJ_ROW_MU = torch.cat([torch.full((D_ZX - HEADS,), -4.0), torch.full((HEADS,), -7.0)])
 
 
 @dataclass
@@ -88,15 +90,20 @@ def _fp16(gen, shape, device, kind, **kw):
 @torch.no_grad()
 def synthetic_model(seed=4, n_layer=56, vocab=256000, device='cuda'):
     """Random-init weights of the 8B architecture (config 3/4/5 distributions):
-    FP4 codes uniform, effective block scales logNormal(-4, 0.5); A_log so that
-    A in [-16, -1]; D ~ N(0,1); dt_bias ~ U[-4,-1]; conv weight ~ N(0, 0.5), conv bias
-    ~ N(0, 0.1); norm weights 1."""
+    FP4 codes uniform, effective block scales logNormal(-4, 0.5) — except the 128 dt
+    rows of in_proj, which use logNormal(-7, 0.5) so that softplus(dt + dt_bias) stays
+    in the small-step range of a trained Mamba-2 (with -4 the raw dt reaches +-15, the
+    carry explodes and the fp16 readout overflows); A_log so that A in [-16, -1];
+    D ~ N(0,1); dt_bias ~ U[-4,-1]; conv weight ~ N(0, 0.5), conv bias ~ N(0, 0.1);
+    norm weights 1."""
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
     layers = []
+    row_mu = IN_PROJ_ROW_MU.to(device)
     for _ in range(n_layer):
         layers.append(MixerWeights(
-            in_proj=F.synthetic(D_ZX, D_MODEL, gen, device), out_proj=F.synthetic(D_MODEL, D_INNER, gen, device),
+            in_proj=F.synthetic(D_ZX, D_MODEL, gen, device, row_mu=row_mu),
+            out_proj=F.synthetic(D_MODEL, D_INNER, gen, device),
             norm_weight=_fp16(gen, (D_MODEL,), device, 'ones'),
             conv_weight=_fp16(gen, (D_XBC, D_CONV), device, 'normal', std=0.5),
             conv_bias=_fp16(gen, (D_XBC,), device, 'normal', std=0.1),

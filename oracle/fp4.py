@@ -58,10 +58,12 @@ def decode(codes_packed, block_scale_bytes, global_scale, cols=None):
     return vals.reshape(rows, cols).astype(np.float16)
 
 
-def synthetic_matrix(rows, cols, rng, mu=-4.0, sigma=0.5):
-    """(codes u8[rows,cols/2], block bytes u8[rows,cols/16], global f32) for config 2."""
+def synthetic_matrix(rows, cols, rng, mu=-4.0, sigma=0.5, row_mu=None):
+    """(codes u8[rows,cols/2], block bytes u8[rows,cols/16], global f32) for config 2.
+    `row_mu` (optional, [rows]) overrides mu per output row."""
     codes = rng.integers(0, 256, size=(rows, cols // 2), dtype=np.uint8)
-    eff = np.exp(rng.normal(mu, sigma, size=(rows, cols // 16))).astype(np.float32)
+    mus = mu if row_mu is None else np.asarray(row_mu, np.float64)[:, None]
+    eff = np.exp(mus + sigma * rng.standard_normal(size=(rows, cols // 16))).astype(np.float32)
     g = np.float32(eff.max() / 448.0)
     blocks = f32_to_e4m3((eff / g).astype(np.float32))
     return codes, blocks, g

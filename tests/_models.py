@@ -27,7 +27,7 @@ def build_pair(n_layer=2, vocab=512, layouts=None, seed=0, adapter=True, hard=Fa
     bases, scales, preds = [], [], []
     for i, layout in enumerate(layouts):
         n8, n4, nz = oc.layout_counts(layout)
-        win = packed(rng, 18560, 4096)
+        win = of.synthetic_matrix(18560, 4096, rng, row_mu=np.r_[np.full(18432, -4.0), np.full(128, -7.0)])
         wout = packed(rng, 4096, 8192)
         f16 = lambda a: np.asarray(a, np.float32).astype(np.float16)
         norm_w = f16(1.0 + 0.1 * rng.standard_normal(4096))
