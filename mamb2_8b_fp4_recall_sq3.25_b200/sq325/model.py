@@ -47,7 +47,7 @@ class MixerWeights:
             self.A = (-torch.exp(self.A_log.float())).contiguous()
 
 
-@dataclass
+@dataclass(eq=False)            # identity hash: controllers key ownership by model object
 class Mamba2FP4Model:
     embedding: F.Fp4Tensor
     lm_head: F.Fp4Tensor
