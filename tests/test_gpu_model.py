@@ -58,10 +58,12 @@ def test_decode_steps_and_greedy(pair):
             h = ex.backbone(torch.from_numpy(nxt).cuda())
             hr = ora.backbone(nxt)
             assert rel_l2(h.float(), hr.float()) < 3e-2, step
-            # conv ring in the reference's chronological order
+            # conv ring in the reference's chronological order; it holds raw in_proj
+            # outputs, which differ from the oracle's by fp32 accumulation order (fp16 ulps)
             for layer in range(gm.n_layer):
-                got = ex.conv_chronological(layer).cpu()
-                assert torch.equal(got, ora.caches[layer]['conv']), (step, layer)
+                got = ex.conv_chronological(layer).cpu().float()
+                ref = ora.caches[layer]['conv'].float()
+                assert torch.allclose(got, ref, rtol=4e-3, atol=4e-3), (step, layer)
         logits = torch.empty(B, gm.vocab, device='cuda', dtype=torch.float16)
         tok = ex.greedy(h[:, -1], logits=logits)
         torch.cuda.synchronize()
