@@ -107,7 +107,7 @@ def test_scoring_driver_pooled_ppl(pair):
     from sq325 import PredictorState, ppl_windows, evaluate_ppl
     gm, ora, statics = pair
     rng = np.random.default_rng(11)
-    ids = rng.integers(0, gm.vocab, 3 * 32 + 10).astype(np.int64)
+    ids = rng.integers(0, gm.vocab, 3 * 32 + 11).astype(np.int64)
     windows = [(s, torch.from_numpy(w)) for s, w in ppl_windows(ids, 32)]
     assert [len(w) for _, w in windows] == [33, 33, 33, 11]
     with PredictorState(gm, *statics) as ex:
