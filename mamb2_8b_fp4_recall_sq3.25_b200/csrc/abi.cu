@@ -340,10 +340,13 @@ int sq_model_forward(sq_model* m, const int64_t* ids, int batch, int tokens, int
     P.perm = L.permutation; P.basis = L.basis; P.latent_scale = L.latent_scale; P.predictor = L.predictor;
     P.lo = S.lo; P.hi = S.hi; P.q4 = S.q4; P.latent = S.latent; P.s8 = S.s8; P.s4 = S.s4;
     P.y = m->y; P.y_sb = (long long)tokens * kDInner; P.y_st = kDInner;
-    if (step) {
+    if (step || pos0 == 0) {
+      // conv fused into the scan: step numerics for a one-token step, conv1d numerics
+      // for a prefill from a reset state
       const uint16_t* raw = m->zx + kDInner;
       P.x = raw; P.B = raw + kDInner; P.C = raw + kDInner + 1024;
-      P.x_sb = P.b_sb = P.c_sb = kZx; P.x_st = P.b_st = P.c_st = kZx;
+      P.x_sb = P.b_sb = P.c_sb = (long long)tokens * kZx; P.x_st = P.b_st = P.c_st = kZx;
+      P.conv_mode = step ? 2 : 1;
       P.conv_w = L.conv_weight; P.conv_b = L.conv_bias; P.conv_cache = S.ring; P.conv_pos = pos0;
       P.conv_cache_sb = 4LL * kXbc;
     } else {

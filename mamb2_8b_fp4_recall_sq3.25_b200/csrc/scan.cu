@@ -1,18 +1,21 @@
 // Fused SQ3.25 selective-state update (the production latent codec), sm_100a.
 //
-// Semantics: scripts/fp4_zero_predictor_codec_v1.py:76-181 (kernel) plus the
-// host predictor correction of :221-225, which is folded in here (one group
-// dot-product pass per token in shared memory instead of a separate einsum
-// and an HBM round trip of the [B,L,G,F] correction tensor).
+// Semantics: scripts/fp4_zero_predictor_codec_v1.py:76-181 (kernel) plus the host
+// predictor correction of :221-225, which is folded in here (group dot products in
+// shared memory instead of a separate einsum and an HBM round trip of the [B,L,G,F]
+// correction tensor).  Optionally the causal depthwise conv of
+// mamba2_recall/state_quant.py:283-317 is fused in front (prefill from a reset state,
+// or the one-token step), so the kernel reads the raw in_proj columns directly.
 //
-// Mapping: one thread owns one recurrent row (b,h,p) of 128 coordinates and
-// keeps its n8+n4 stored coordinates in registers for the whole call (the
-// zero tier carries no state).  A CTA holds `hpc` heads of the same B/C group.
-// Per token the CTA stages the group's B/C values in tier order together with
-// the predictor readout vector cvec (= the reference's `correction`) and the
-// five zero-tier group dots, then every thread updates, reads out, and
-// requantizes its row in registers.  Packed rows are read once at the start
-// and written once at the end of the call, as in the reference.
+// Mapping: one thread owns one recurrent row (b,h,p) of 128 coordinates and keeps its
+// n8+n4 stored coordinates in registers for the whole call (the zero tier carries no
+// state).  A CTA holds `hpc` heads of one B/C group (hpc*dim <= 128 threads).  Tokens are
+// processed in chunks of TC: per chunk the CTA publishes the group's B/C values in tier
+// order, dt/decay per (token, head), the predictor readout vector cvec (= the reference's
+// `correction`) and the five zero-tier dots for all TC tokens, then every thread runs
+// the TC recurrence steps on its row with packed fp32x2 arithmetic.  The next chunk's
+// raw inputs are prefetched into registers while the current one is computed.  Packed
+// rows are read once at the start and written once at the end of the call.
 #include "common.cuh"
 #include "scan.cuh"
 
@@ -20,61 +23,64 @@ namespace sq {
 
 namespace {
 
-constexpr int kMaxF = 88;      // n8+n4+2 <= 86
-constexpr int kMaxNz = 80;
+constexpr int kTC = 16;        // tokens per chunk
+constexpr int kMaxHpc = 8;     // heads per CTA (dim >= 16)
 
-struct __align__(16) Coord { float b, c, cvec, pad; };
-
-// Exactly-rounded fp32 quotient a/s given inv = RN(1/s) (Markstein's
-// correction step: one FMA remainder + one FMA update gives RN(a/s)).
+// Exactly rounded fp32 quotient a/s given inv = RN(1/s): one FMA remainder and one FMA
+// update (Markstein's correction) give RN(a/s) for normal operands.
 __device__ __forceinline__ float div_exact(float a, float s, float inv) {
   float q0 = a * inv;
   float r = fmaf(-q0, s, a);
   return fmaf(r, inv, q0);
 }
-
+__device__ __forceinline__ float2 div_exact2(float2 a, float2 ns, float2 inv) {
+  float2 q0 = __fmul2_rn(a, inv);
+  float2 r = __ffma2_rn(q0, ns, a);           // a - q0*s, exact
+  return __ffma2_rn(r, inv, q0);
+}
 __device__ __forceinline__ float softplus_ref(float v) {
-  // dt = dt <= 20 ? log(exp(dt) + 1) : dt   (:124)
-  return v <= 20.0f ? logf(expf(v) + 1.0f) : v;
+  return v <= 20.0f ? logf(expf(v) + 1.0f) : v;   // :124
 }
-
 __device__ __forceinline__ float silu16(float v16) {
-  // torch SiLU on an fp16 tensor: computed in fp32, rounded to fp16.
-  float r = v16 / (1.0f + expf(-v16));
-  return h2f(f2h(r));
+  return h2f(f2h(v16 / (1.0f + expf(-v16))));      // torch SiLU on fp16: fp32 math, fp16 out
 }
-
-// Causal conv step of StateQuant._convolution (mamba2_recall/state_quant.py:291-297):
-// value = fp16(sum_k fp16(cache_k * w_k)) + bias (fp16), then SiLU -> fp16.
-__device__ __forceinline__ float conv_step_value(const ScanParams& P, int b, int ch, uint16_t raw) {
-  const uint16_t* ring = P.conv_cache + (long long)b * P.conv_cache_sb;
-  float acc = 0.0f;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    uint16_t v = (k == 3) ? raw : ring[((P.conv_pos - 3 + k) & 3) * 10240 + ch];
-    float prod = h2f(f2h(h2f(v) * h2f(P.conv_w[ch * 4 + k])));
-    acc += prod;
-  }
+// conv1d prefill numerics (state_quant.py:311-312): fp32 accumulate incl. bias -> fp16, SiLU -> fp16
+__device__ __forceinline__ float conv_prefill_value(const float (&w)[5], float x0, float x1, float x2, float x3) {
+  float acc = w[0] * x0 + w[1] * x1 + w[2] * x2 + w[3] * x3 + w[4];
+  return silu16(h2f(f2h(acc)));
+}
+// conv step numerics (state_quant.py:291-297): fp16 products summed, fp16, + bias (fp16), SiLU
+__device__ __forceinline__ float conv_step_value(const float (&w)[5], float x0, float x1, float x2, float x3) {
+  float acc = h2f(f2h(x0 * w[0])) + h2f(f2h(x1 * w[1])) + h2f(f2h(x2 * w[2])) + h2f(f2h(x3 * w[3]));
   float s = h2f(f2h(acc));
-  s = h2f(f2h(s + h2f(P.conv_b[ch])));
+  s = h2f(f2h(s + w[4]));
   return silu16(s);
 }
+__device__ __forceinline__ float requant(float q, float lim) {
+  return fminf(fmaxf(round_half_away(q), -lim), lim);
+}
 
-template <int N8, int N4>
-__global__ void __launch_bounds__(256)
+template <int N8, int N4, int KJ>
+__global__ void __launch_bounds__(128)
 ssu_sq325_kernel(const ScanParams P) {
   constexpr int NZ = 128 - N8 - N4;
   constexpr int F = N8 + N4 + 2;
   constexpr int W8 = N8 / 2, W4 = N4 / 2;
-  static_assert(F <= kMaxF && NZ <= kMaxNz, "layout out of range");
+  constexpr int NP = (N8 + N4) / 2;            // stored coordinate pairs
+  constexpr int TC = kTC;
+  static_assert(N8 % 2 == 0 && N4 % 2 == 0, "tiers are nibble pairs");
 
   extern __shared__ __align__(16) unsigned char smem[];
-  Coord* sCoord = reinterpret_cast<Coord*>(smem);                          // [128]
-  float* sDots = reinterpret_cast<float*>(sCoord + 128);                   // [8]
-  float* sPred = sDots + 8;                                                // [F][NZ+1]
-  float* sBasis = sPred + F * (NZ + 1);                                    // [2][NZ]
-  int* sPerm = reinterpret_cast<int*>(sBasis + 2 * NZ);                    // [128]
-  unsigned char* sPack = reinterpret_cast<unsigned char*>(sPerm + 128);   // rows*52
+  float4* sP4 = reinterpret_cast<float4*>(smem);                     // [TC][64] {b_j,b_j+1,c_j,c_j+1}
+  float2* sV2 = reinterpret_cast<float2*>(sP4 + TC * 64);            // [TC][64] {cvec_j,cvec_j+1}
+  float* sDots = reinterpret_cast<float*>(sV2 + TC * 64);            // [TC][8]
+  float* sDD = sDots + TC * 8;                                       // [TC][kMaxHpc][2] (dt, decay)
+  float* sX = sDD + TC * kMaxHpc * 2;                                // [TC][blockDim] own x value
+  float* sPred = sX + TC * 128;                                      // [F][NZ+1]
+  float* sBasis = sPred + F * (NZ + 1);                              // [2][NZ]
+  int* sPerm = reinterpret_cast<int*>(sBasis + 2 * NZ);              // [128]
+  unsigned char* sPack = reinterpret_cast<unsigned char*>(sPerm + 128);
+  float* sPf = reinterpret_cast<float*>(sP4);
 
   const int tid = threadIdx.x;
   const int bd = blockDim.x;
@@ -85,9 +91,13 @@ ssu_sq325_kernel(const ScanParams P) {
   const int hl = tid / dim;
   const int p = tid - hl * dim;
   const int h = h0 + hl;
-  const int g = h0 / (P.heads / P.groups);
-  const long long row0 = ((long long)b * P.heads + h0) * dim;   // first row of this CTA
+  const int hpg = P.heads / P.groups;
+  const int g = h0 / hpg;
+  const bool group_leader = (h0 % hpg) == 0;       // writes the group's B/C conv ring entries
+  const long long row0 = ((long long)b * P.heads + h0) * dim;
   const int rows = bd;
+  const int mode = P.conv_mode;
+  const int kj = KJ;                                // coordinates per thread: 128 / blockDim
 
   // ---- static tables for this group ----
   for (int i = tid; i < 128; i += bd) sPerm[i] = P.perm[g * 128 + i];
@@ -99,239 +109,339 @@ ssu_sq325_kernel(const ScanParams P) {
     sBasis[i] = h2f(P.basis[(g * NZ + i) * 2 + 0]);
     sBasis[NZ + i] = h2f(P.basis[(g * NZ + i) * 2 + 1]);
   }
-  // ---- stage packed rows (coalesced 32-bit copies; regions are 4-byte multiples) ----
+  // ---- stage packed rows (coalesced 32-bit copies; every region is a 4-byte multiple) ----
   unsigned char* pLo = sPack;
   unsigned char* pHi = pLo + rows * W8;
   unsigned char* pQ4 = pHi + rows * W8;
   unsigned char* pLat = pQ4 + rows * W4;
   uint16_t* pS8 = reinterpret_cast<uint16_t*>(pLat + rows * 2);
   uint16_t* pS4 = pS8 + rows;
-  {
-    auto copy_in = [&](unsigned char* dst, const unsigned char* src, int bytes) {
-      const uint32_t* s = reinterpret_cast<const uint32_t*>(src);
-      uint32_t* d = reinterpret_cast<uint32_t*>(dst);
-      for (int i = tid; i < bytes / 4; i += bd) d[i] = s[i];
-    };
-    copy_in(pLo, P.lo + row0 * W8, rows * W8);
-    copy_in(pHi, P.hi + row0 * W8, rows * W8);
-    copy_in(pQ4, P.q4 + row0 * W4, rows * W4);
-    copy_in(pLat, P.latent + row0 * 2, rows * 2);
-    copy_in(reinterpret_cast<unsigned char*>(pS8), reinterpret_cast<const unsigned char*>(P.s8 + row0), rows * 2);
-    copy_in(reinterpret_cast<unsigned char*>(pS4), reinterpret_cast<const unsigned char*>(P.s4 + row0), rows * 2);
-  }
+  auto copy_words = [&](unsigned char* dst, const unsigned char* src, int bytes) {
+    const uint32_t* s = reinterpret_cast<const uint32_t*>(src);
+    uint32_t* d = reinterpret_cast<uint32_t*>(dst);
+    for (int i = tid; i < bytes / 4; i += bd) d[i] = s[i];
+  };
+  copy_words(pLo, P.lo + row0 * W8, rows * W8);
+  copy_words(pHi, P.hi + row0 * W8, rows * W8);
+  copy_words(pQ4, P.q4 + row0 * W4, rows * W4);
+  copy_words(pLat, P.latent + row0 * 2, rows * 2);
+  copy_words(reinterpret_cast<unsigned char*>(pS8), reinterpret_cast<const unsigned char*>(P.s8 + row0), rows * 2);
+  copy_words(reinterpret_cast<unsigned char*>(pS4), reinterpret_cast<const unsigned char*>(P.s4 + row0), rows * 2);
   __syncthreads();
 
   // ---- decode own row (:81-114) ----
-  float S8[N8 > 0 ? N8 : 1], S4[N4 > 0 ? N4 : 1];
+  float S[N8 + N4];
   {
-    float s8 = h2f(pS8[tid]), s4 = h2f(pS4[tid]);
+    const float s8 = h2f(pS8[tid]), s4 = h2f(pS4[tid]);
 #pragma unroll
     for (int j = 0; j < N8; ++j) {
       int lo = (pLo[tid * W8 + j / 2] >> (4 * (j & 1))) & 15;
       int hi = (pHi[tid * W8 + j / 2] >> (4 * (j & 1))) & 15;
       int ub = (hi << 4) | lo;
-      int q = ub - 256 * (ub > 127);
-      S8[j] = (float)q * s8;
+      S[j] = (float)(ub - 256 * (ub > 127)) * s8;
     }
 #pragma unroll
     for (int j = 0; j < N4; ++j) {
       int nib = (pQ4[tid * W4 + j / 2] >> (4 * (j & 1))) & 15;
-      int q = nib - 16 * (nib > 7);
-      S4[j] = (float)q * s4;
+      S[N8 + j] = (float)(nib - 16 * (nib > 7)) * s4;
     }
   }
-  const float ls0 = h2f(P.latent_scale[g * 2 + 0]);
-  const float ls1 = h2f(P.latent_scale[g * 2 + 1]);
+  const float ls0 = h2f(P.latent_scale[g * 2 + 0]), ls1 = h2f(P.latent_scale[g * 2 + 1]);
+  const float ils0 = __frcp_rn(ls0), ils1 = __frcp_rn(ls1);
   float z0 = e4m3_to_f32(pLat[tid * 2 + 0]) * ls0;
   float z1 = e4m3_to_f32(pLat[tid * 2 + 1]) * ls1;
-  const float av = P.A[h];
   const float dv = P.d_is_f32 ? reinterpret_cast<const float*>(P.D)[h] : h2f(reinterpret_cast<const uint16_t*>(P.D)[h]);
-  const float bias = P.dt_bias_is_f32 ? reinterpret_cast<const float*>(P.dt_bias)[h]
-                                      : h2f(reinterpret_cast<const uint16_t*>(P.dt_bias)[h]);
-  const bool fuse_conv = P.conv_w != nullptr;
 
-  // ---- token loop with one-token register prefetch ----
-  constexpr int kMaxJ = 4;                  // 128 / min blockDim (32)
-  uint16_t pre_b[kMaxJ], pre_c[kMaxJ], pre_x = 0, pre_dt = 0;
-  auto prefetch = [&](int t) {
-    const long long xo = (long long)b * P.x_sb + (long long)t * P.x_st + (long long)h * dim + p;
-    pre_x = P.x[xo];
-    pre_dt = P.dt[(long long)b * P.dt_sb + (long long)t * P.dt_st + h];
-    const uint16_t* Bt = P.B + (long long)b * P.b_sb + (long long)t * P.b_st + g * 128;
-    const uint16_t* Ct = P.C + (long long)b * P.c_sb + (long long)t * P.c_st + g * 128;
+  // ---- conv weights / history for the channels this thread converts ----
+  const int chx = h * dim + p;                                      // own x channel
+  float wx[5] = {0, 0, 0, 0, 0}, hx[4] = {0, 0, 0, 0};             // hx: raw x at t-3..t (hx[3] newest)
+  float wb[KJ][5], wc[KJ][5], hb[KJ][4], hc[KJ][4];
+  int chb[KJ], chc[KJ];
 #pragma unroll
-    for (int i = 0; i < kMaxJ; ++i) {
-      int j = tid + i * bd;
-      if (j < 128) { int n = sPerm[j]; pre_b[i] = Bt[n]; pre_c[i] = Ct[n]; }
+  for (int k = 0; k < KJ; ++k) {
+    const int j = tid + k * bd;
+    chb[k] = chc[k] = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) hb[k][i] = hc[k][i] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 5; ++i) wb[k][i] = wc[k][i] = 0.f;
+    if (mode != 0 && k < kj && j < 128) {
+      chb[k] = 8192 + g * 128 + sPerm[j];
+      chc[k] = 9216 + g * 128 + sPerm[j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) { wb[k][i] = h2f(P.conv_w[chb[k] * 4 + i]); wc[k][i] = h2f(P.conv_w[chc[k] * 4 + i]); }
+      wb[k][4] = h2f(P.conv_b[chb[k]]); wc[k][4] = h2f(P.conv_b[chc[k]]);
+    }
+  }
+  if (mode != 0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) wx[i] = h2f(P.conv_w[chx * 4 + i]);
+    wx[4] = h2f(P.conv_b[chx]);
+  }
+  if (mode == 2) {
+    // one-token step: history = the ring's previous three positions
+    const uint16_t* ring = P.conv_cache + (long long)b * P.conv_cache_sb;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      const int slot = (P.conv_pos - 3 + i) & 3;
+      hx[i + 1] = h2f(ring[slot * 10240 + chx]);
+#pragma unroll
+      for (int k = 0; k < KJ; ++k)
+        if (k < kj && tid + k * bd < 128) {
+          hb[k][i + 1] = h2f(ring[slot * 10240 + chb[k]]);
+          hc[k][i + 1] = h2f(ring[slot * 10240 + chc[k]]);
+        }
+    }
+  }
+
+  // ---- raw-input prefetch (registers) ----
+  // packed raw prefetch: x of token pairs, and (B | C << 16) per owned coordinate
+  uint32_t pre_x[TC / 2], pre_bc[TC][KJ];
+  uint16_t pre_dt = 0;
+  auto prefetch = [&](int c0) {
+    const int nt = min(TC, P.length - c0);
+#pragma unroll
+    for (int t = 0; t < TC; ++t) {
+      if (t < nt) {
+        const long long tt = c0 + t;
+        const uint32_t xr = P.x[(long long)b * P.x_sb + tt * P.x_st + (long long)h * dim + p];
+        pre_x[t / 2] = (t & 1) ? ((pre_x[t / 2] & 0xFFFFu) | (xr << 16)) : xr;
+        const uint16_t* Bt = P.B + (long long)b * P.b_sb + tt * P.b_st + g * 128;
+        const uint16_t* Ct = P.C + (long long)b * P.c_sb + tt * P.c_st + g * 128;
+#pragma unroll
+        for (int k = 0; k < KJ; ++k) {
+          const int j = tid + k * bd;
+          if (k < kj && j < 128) { const int n = sPerm[j]; pre_bc[t][k] = (uint32_t)Bt[n] | ((uint32_t)Ct[n] << 16); }
+        }
+      }
+    }
+    if (tid < nt * hpc) {
+      const int t = tid / hpc, hh = h0 + tid % hpc;
+      pre_dt = P.dt[(long long)b * P.dt_sb + (long long)(c0 + t) * P.dt_st + hh];
     }
   };
   prefetch(0);
-  float S8n_max = 0.f, S4n_max = 0.f;   // last scales (kept for the final pack)
+
+  const float bias_own = P.dt_bias_is_f32 ? reinterpret_cast<const float*>(P.dt_bias)[h0 + (tid % max(hpc, 1))]
+                                          : h2f(reinterpret_cast<const uint16_t*>(P.dt_bias)[h0 + (tid % max(hpc, 1))]);
+  const float A_own = P.A[h0 + (tid % max(hpc, 1))];
+  const float inv127 = 1.0f / 127.0f, inv7 = 1.0f / 7.0f;
   float s8 = 0.f, s4 = 0.f;
-  for (int t = 0; t < P.length; ++t) {
-    __syncthreads();                                   // previous token done with sCoord
-    float xv, dtraw;
+
+  for (int c0 = 0; c0 < P.length; c0 += TC) {
+    const int nt = min(TC, P.length - c0);
+    __syncthreads();                                   // previous chunk finished reading shared tables
+    // -- publish B/C (tier order), dt/decay, and own x values for this chunk --
 #pragma unroll
-    for (int i = 0; i < kMaxJ; ++i) {
-      int j = tid + i * bd;
-      if (j < 128) {
-        float bv, cv;
-        if (fuse_conv) {
-          int n = sPerm[j];
-          bv = conv_step_value(P, b, 8192 + g * 128 + n, pre_b[i]);
-          cv = conv_step_value(P, b, 9216 + g * 128 + n, pre_c[i]);
-        } else {
-          bv = h2f(pre_b[i]); cv = h2f(pre_c[i]);
+    for (int t = 0; t < TC; ++t) {
+      if (t < nt) {
+#pragma unroll
+        for (int k = 0; k < KJ; ++k) {
+          const int j = tid + k * bd;
+          if (k < kj && j < 128) {
+            float bv = h2f((uint16_t)(pre_bc[t][k] & 0xFFFFu)), cv = h2f((uint16_t)(pre_bc[t][k] >> 16));
+            if (mode != 0) {
+              hb[k][0] = hb[k][1]; hb[k][1] = hb[k][2]; hb[k][2] = hb[k][3]; hb[k][3] = bv;
+              hc[k][0] = hc[k][1]; hc[k][1] = hc[k][2]; hc[k][2] = hc[k][3]; hc[k][3] = cv;
+              if (mode == 1) {
+                bv = conv_prefill_value(wb[k], hb[k][0], hb[k][1], hb[k][2], hb[k][3]);
+                cv = conv_prefill_value(wc[k], hc[k][0], hc[k][1], hc[k][2], hc[k][3]);
+              } else {
+                bv = conv_step_value(wb[k], hb[k][0], hb[k][1], hb[k][2], hb[k][3]);
+                cv = conv_step_value(wc[k], hc[k][0], hc[k][1], hc[k][2], hc[k][3]);
+              }
+            }
+            sPf[t * 256 + (j >> 1) * 4 + (j & 1)] = bv;
+            sPf[t * 256 + (j >> 1) * 4 + 2 + (j & 1)] = cv;
+          }
         }
-        sCoord[j].b = bv; sCoord[j].c = cv;
+        float x = h2f((uint16_t)((t & 1) ? (pre_x[t / 2] >> 16) : (pre_x[t / 2] & 0xFFFFu)));
+        if (mode != 0) {
+          hx[0] = hx[1]; hx[1] = hx[2]; hx[2] = hx[3]; hx[3] = x;
+          x = (mode == 1) ? conv_prefill_value(wx, hx[0], hx[1], hx[2], hx[3])
+                          : conv_step_value(wx, hx[0], hx[1], hx[2], hx[3]);
+        }
+        sX[t * 128 + tid] = x;
       }
     }
-    if (fuse_conv) xv = conv_step_value(P, b, h * dim + p, pre_x);
-    else xv = h2f(pre_x);
-    dtraw = h2f(pre_dt);
-    if (fuse_conv) {
-      // ring write of this token's raw values (slot pos%4 is not read this step)
-      uint16_t* ring = P.conv_cache + (long long)b * P.conv_cache_sb + (P.conv_pos & 3) * 10240;
-      ring[h * dim + p] = pre_x;
-      if ((h0 % (P.heads / P.groups)) == 0) {
-#pragma unroll
-        for (int i = 0; i < kMaxJ; ++i) {
-          int j = tid + i * bd;
-          if (j < 128) { int n = sPerm[j]; ring[8192 + g * 128 + n] = pre_b[i]; ring[9216 + g * 128 + n] = pre_c[i]; }
-        }
-      }
+    if (tid < nt * hpc) {
+      const float dtv = softplus_ref(h2f(pre_dt) + bias_own);
+      sDD[((tid / hpc) * kMaxHpc + tid % hpc) * 2 + 0] = dtv;
+      sDD[((tid / hpc) * kMaxHpc + tid % hpc) * 2 + 1] = expf(A_own * dtv);
     }
-    if (t + 1 < P.length) prefetch(t + 1);
-    __syncthreads();                                   // B/C of token t visible
-    // group-level dots: cvec (the reference's host correction) and zero-tier dots
-    for (int f = tid; f < F + 5; f += bd) {
-      float acc = 0.f;
+    if (c0 + TC < P.length) prefetch(c0 + TC);
+    __syncthreads();                                   // B/C of the chunk visible
+    // -- group-level dots for every token of the chunk --
+    for (int task = tid; task < nt * (F + 5); task += bd) {
+      const int t = task / (F + 5), f = task - t * (F + 5);
+      const float* tb = sPf + t * 256;
+      float acc0 = 0.f, acc1 = 0.f;
       if (f < F) {
         const float* pr = sPred + f * (NZ + 1);
-#pragma unroll 8
-        for (int d = 0; d < NZ; ++d) acc = fmaf(sCoord[N8 + N4 + d].c, pr[d], acc);
-        if (f < N8 + N4) sCoord[f].cvec = acc; else sDots[5 + f - (N8 + N4)] = acc;
-      } else {
-        int k = f - F;
-#pragma unroll 8
-        for (int d = 0; d < NZ; ++d) {
-          const Coord cz = sCoord[N8 + N4 + d];
-          float u = (k == 0) ? cz.b : (k <= 2 ? sBasis[(k - 1) * NZ + d] : sBasis[(k - 3) * NZ + d]);
-          float v = (k == 0) ? cz.c : (k <= 2 ? cz.c : cz.b);
-          acc = fmaf(u, v, acc);
+#pragma unroll 4
+        for (int d = 0; d < NZ; d += 2) {
+          const int j0 = N8 + N4 + d;                  // even: pairs never straddle
+          acc0 = fmaf(tb[(j0 >> 1) * 4 + 2], pr[d], acc0);
+          acc1 = fmaf(tb[(j0 >> 1) * 4 + 3], pr[d + 1], acc1);
         }
-        sDots[k] = acc;
+        const float acc = acc0 + acc1;
+        if (f < N8 + N4) reinterpret_cast<float*>(sV2)[t * 128 + f] = acc;
+        else sDots[t * 8 + 5 + f - (N8 + N4)] = acc;
+      } else {
+        const int k = f - F;   // 0: B.C, 1: basis0.C, 2: basis1.C, 3: basis0.B, 4: basis1.B
+        const float* us = (k == 0) ? nullptr : sBasis + ((k - 1) & 1) * NZ;
+        const int voff = (k >= 3 || k == 0) ? 0 : 2;   // 0 -> B, 2 -> C (within the float4)
+#pragma unroll 4
+        for (int d = 0; d < NZ; d += 2) {
+          const int j0 = N8 + N4 + d;
+          const float* q = tb + (j0 >> 1) * 4;
+          const float u0 = (k == 0) ? q[0] : us[d], u1 = (k == 0) ? q[1] : us[d + 1];
+          const float v0 = (k == 0) ? q[2] : q[voff], v1 = (k == 0) ? q[3] : q[voff + 1];
+          acc0 = fmaf(u0, v0, acc0);
+          acc1 = fmaf(u1, v1, acc1);
+        }
+        sDots[t * 8 + k] = acc0 + acc1;
       }
     }
     __syncthreads();                                   // cvec and dots visible
 
-    // ---- per-row recurrence, readout and requant (:115-162) ----
-    float dtv = softplus_ref(dtraw + bias);
-    float dec = expf(av * dtv);
-    float ysum = 0.f, ycorr = 0.f, m8 = 0.f, m4 = 0.f;
+    // -- per-row recurrence, readout and requant (:115-162) for the chunk's tokens --
+#pragma unroll 1
+    for (int t = 0; t < nt; ++t) {
+      const float dtv = sDD[(t * kMaxHpc + hl) * 2 + 0];
+      const float dec = sDD[(t * kMaxHpc + hl) * 2 + 1];
+      const float x = sX[t * 128 + tid];
+      const float2 dd = make_float2(dec, dec), dt2 = make_float2(dtv, dtv), xx = make_float2(x, x);
+      const float4* cp = sP4 + t * 64;
+      const float2* vp = sV2 + t * 64;
+      float2 ya = make_float2(0.f, 0.f), yb = ya, ca = ya, cb = ya;
+      float m8a = 0.f, m8b = 0.f, m4a = 0.f, m4b = 0.f;
 #pragma unroll
-    for (int j = 0; j < N8; ++j) {
-      const Coord c = sCoord[j];
-      float pr = S8[j];
-      float sn = fmaf(pr, dec, (c.b * dtv) * xv);
-      S8[j] = sn;
-      ysum = fmaf(sn, c.c, ysum);
-      ycorr = fmaf(pr, c.cvec, ycorr);
-      m8 = fmaxf(m8, fabsf(sn));
-    }
+      for (int jp = 0; jp < NP; ++jp) {
+        const float4 bc = cp[jp];
+        const float2 cv = vp[jp];
+        const float2 pr = make_float2(S[2 * jp], S[2 * jp + 1]);
+        const float2 upd = __fmul2_rn(__fmul2_rn(make_float2(bc.x, bc.y), dt2), xx);   // (B*dt)*x
+        const float2 sn = __ffma2_rn(pr, dd, upd);                                      // prior*decay + upd
+        S[2 * jp] = sn.x; S[2 * jp + 1] = sn.y;
+        if (jp & 1) { yb = __ffma2_rn(sn, make_float2(bc.z, bc.w), yb); cb = __ffma2_rn(pr, cv, cb); }
+        else        { ya = __ffma2_rn(sn, make_float2(bc.z, bc.w), ya); ca = __ffma2_rn(pr, cv, ca); }
+        if (2 * jp < N8) { m8a = fmaxf(m8a, fabsf(sn.x)); m8b = fmaxf(m8b, fabsf(sn.y)); }
+        else             { m4a = fmaxf(m4a, fabsf(sn.x)); m4b = fmaxf(m4b, fabsf(sn.y)); }
+      }
+      const float* dots = sDots + t * 8;
+      const float dbc = dots[0], dc0 = dots[1], dc1 = dots[2], db0 = dots[3], db1 = dots[4];
+      const float pcz0 = dots[5], pcz1 = dots[6];
+      const float ysum = (ya.x + ya.y) + (yb.x + yb.y);
+      const float ycorr = (ca.x + ca.y) + (cb.x + cb.y);
+      const float xdt = x * dtv;
+      float out = ysum + (dec * (z0 * dc0 + z1 * dc1) + xdt * dbc + x * dv);
+      out = out + dec * (ycorr + z0 * pcz0 + z1 * pcz1);
+      P.y[(long long)b * P.y_sb + (long long)(c0 + t) * P.y_st + (long long)h * dim + p] = f2h(out);
+      // latent FP8 requant (:149-154)
+      z0 = z0 * dec + xdt * db0;
+      z1 = z1 * dec + xdt * db1;
+      z0 = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(div_exact(z0, ls0, ils0), -448.f), 448.f))) * ls0;
+      z1 = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(div_exact(z1, ls1, ils1), -448.f), 448.f))) * ls1;
+      // INT8 / INT4 requant (:155-162, scripts/state_ppl_codec_v6.py:52-61)
+      const float m8 = fmaxf(m8a, m8b), m4 = fmaxf(m4a, m4b);
+      s8 = h2f(f2h(fmaxf(div_exact(m8, 127.f, inv127), 1e-8f)));
+      s4 = h2f(f2h(fmaxf(div_exact(m4, 7.f, inv7), 1e-8f)));
+      const float i8 = s8 > 0.f ? __frcp_rn(s8) : 0.f;
+      const float i4 = s4 > 0.f ? __frcp_rn(s4) : 0.f;
+      const float2 s82 = make_float2(s8, s8), ns82 = make_float2(-s8, -s8), i82 = make_float2(i8, i8);
+      const float2 s42 = make_float2(s4, s4), ns42 = make_float2(-s4, -s4), i42 = make_float2(i4, i4);
 #pragma unroll
-    for (int j = 0; j < N4; ++j) {
-      const Coord c = sCoord[N8 + j];
-      float pr = S4[j];
-      float sn = fmaf(pr, dec, (c.b * dtv) * xv);
-      S4[j] = sn;
-      ysum = fmaf(sn, c.c, ysum);
-      ycorr = fmaf(pr, c.cvec, ycorr);
-      m4 = fmaxf(m4, fabsf(sn));
-    }
-    const float dbc = sDots[0], dc0 = sDots[1], dc1 = sDots[2], db0 = sDots[3], db1 = sDots[4];
-    const float pcz0 = sDots[5], pcz1 = sDots[6];
-    const float xdt = xv * dtv;
-    float out = ysum + (dec * (z0 * dc0 + z1 * dc1) + xdt * dbc + xv * dv);
-    out = out + dec * (ycorr + z0 * pcz0 + z1 * pcz1);
-    P.y[(long long)b * P.y_sb + (long long)t * P.y_st + (long long)h * dim + p] = f2h(out);
-    // latent FP8 requant (:149-154)
-    z0 = z0 * dec + xdt * db0;
-    z1 = z1 * dec + xdt * db1;
-    z0 = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(__fdiv_rn(z0, ls0), -448.f), 448.f))) * ls0;
-    z1 = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(__fdiv_rn(z1, ls1), -448.f), 448.f))) * ls1;
-    // INT8 / INT4 requant (:155-162, state_ppl_codec_v6.py:52-61)
-    s8 = h2f(f2h(fmaxf(__fdiv_rn(m8, 127.f), 1e-8f)));
-    s4 = h2f(f2h(fmaxf(__fdiv_rn(m4, 7.f), 1e-8f)));
-    const float i8 = s8 > 0.f ? __frcp_rn(s8) : 0.f;
-    const float i4 = s4 > 0.f ? __frcp_rn(s4) : 0.f;
-#pragma unroll
-    for (int j = 0; j < N8; ++j) {
-      float q = round_half_away(div_exact(S8[j], s8, i8));
-      q = fminf(fmaxf(q, -127.f), 127.f);
-      S8[j] = q * s8;
-    }
-#pragma unroll
-    for (int j = 0; j < N4; ++j) {
-      float q = round_half_away(div_exact(S4[j], s4, i4));
-      q = fminf(fmaxf(q, -7.f), 7.f);
-      S4[j] = q * s4;
+      for (int jp = 0; jp < NP; ++jp) {
+        const bool t8 = 2 * jp < N8;
+        float2 q = div_exact2(make_float2(S[2 * jp], S[2 * jp + 1]), t8 ? ns82 : ns42, t8 ? i82 : i42);
+        const float lim = t8 ? 127.f : 7.f;
+        q.x = requant(q.x, lim);
+        q.y = requant(q.y, lim);
+        const float2 v = __fmul2_rn(q, t8 ? s82 : s42);
+        S[2 * jp] = v.x; S[2 * jp + 1] = v.y;
+      }
     }
   }
-  (void)S8n_max; (void)S4n_max;
+
+  // ---- conv ring update (raw columns of the last positions) ----
+  if (mode != 0) {
+    uint16_t* ring = P.conv_cache + (long long)b * P.conv_cache_sb;
+    const int last = P.conv_pos + P.length - 1;       // absolute position of the newest token
+    const int nwrite = mode == 2 ? 1 : min(4, P.length);
+    for (int i = 0; i < nwrite; ++i) {
+      const int pos = last - i;
+      const int slot = pos & 3;
+      ring[slot * 10240 + chx] = f2h(hx[3 - i]);
+      if (group_leader) {
+#pragma unroll
+        for (int k = 0; k < KJ; ++k)
+          if (k < kj && tid + k * bd < 128) {
+            ring[slot * 10240 + chb[k]] = f2h(hb[k][3 - i]);
+            ring[slot * 10240 + chc[k]] = f2h(hc[k][3 - i]);
+          }
+      }
+    }
+  }
 
   // ---- pack once (:163-181) and store coalesced ----
+  __syncthreads();
   {
     const float i8 = s8 > 0.f ? __frcp_rn(s8) : 0.f;
     const float i4 = s4 > 0.f ? __frcp_rn(s4) : 0.f;
 #pragma unroll
     for (int j = 0; j < N8; j += 2) {
-      int qa = __float2int_rn(div_exact(S8[j], s8, i8));
-      int qb = __float2int_rn(div_exact(S8[j + 1], s8, i8));
+      const int qa = __float2int_rn(div_exact(S[j], s8, i8));
+      const int qb = __float2int_rn(div_exact(S[j + 1], s8, i8));
       pLo[tid * W8 + j / 2] = (unsigned char)((qa & 15) | ((qb & 15) << 4));
       pHi[tid * W8 + j / 2] = (unsigned char)(((qa >> 4) & 15) | (((qb >> 4) & 15) << 4));
     }
 #pragma unroll
     for (int j = 0; j < N4; j += 2) {
-      int qa = __float2int_rn(div_exact(S4[j], s4, i4));
-      int qb = __float2int_rn(div_exact(S4[j + 1], s4, i4));
+      const int qa = __float2int_rn(div_exact(S[N8 + j], s4, i4));
+      const int qb = __float2int_rn(div_exact(S[N8 + j + 1], s4, i4));
       pQ4[tid * W4 + j / 2] = (unsigned char)((qa & 15) | ((qb & 15) << 4));
     }
-    pLat[tid * 2 + 0] = f32_to_e4m3(fminf(fmaxf(__fdiv_rn(z0, ls0), -448.f), 448.f));
-    pLat[tid * 2 + 1] = f32_to_e4m3(fminf(fmaxf(__fdiv_rn(z1, ls1), -448.f), 448.f));
+    pLat[tid * 2 + 0] = f32_to_e4m3(fminf(fmaxf(div_exact(z0, ls0, ils0), -448.f), 448.f));
+    pLat[tid * 2 + 1] = f32_to_e4m3(fminf(fmaxf(div_exact(z1, ls1, ils1), -448.f), 448.f));
     pS8[tid] = f2h(s8);
     pS4[tid] = f2h(s4);
   }
   __syncthreads();
-  {
-    auto copy_out = [&](unsigned char* dst, const unsigned char* src, int bytes) {
-      const uint32_t* s = reinterpret_cast<const uint32_t*>(src);
-      uint32_t* d = reinterpret_cast<uint32_t*>(dst);
-      for (int i = tid; i < bytes / 4; i += bd) d[i] = s[i];
-    };
-    copy_out(P.lo + row0 * W8, pLo, rows * W8);
-    copy_out(P.hi + row0 * W8, pHi, rows * W8);
-    copy_out(P.q4 + row0 * W4, pQ4, rows * W4);
-    copy_out(P.latent + row0 * 2, pLat, rows * 2);
-    copy_out(reinterpret_cast<unsigned char*>(P.s8 + row0), reinterpret_cast<unsigned char*>(pS8), rows * 2);
-    copy_out(reinterpret_cast<unsigned char*>(P.s4 + row0), reinterpret_cast<unsigned char*>(pS4), rows * 2);
-  }
+  copy_words(P.lo + row0 * W8, pLo, rows * W8);
+  copy_words(P.hi + row0 * W8, pHi, rows * W8);
+  copy_words(P.q4 + row0 * W4, pQ4, rows * W4);
+  copy_words(P.latent + row0 * 2, pLat, rows * 2);
+  copy_words(reinterpret_cast<unsigned char*>(P.s8 + row0), reinterpret_cast<unsigned char*>(pS8), rows * 2);
+  copy_words(reinterpret_cast<unsigned char*>(P.s4 + row0), reinterpret_cast<unsigned char*>(pS4), rows * 2);
 }
 
-template <int N8, int N4>
-int launch_t(const ScanParams& P, int hpc, cudaStream_t stream) {
+template <int N8, int N4, int KJ>
+int launch_kj(const ScanParams& P, int hpc, cudaStream_t stream) {
   constexpr int NZ = 128 - N8 - N4;
   constexpr int F = N8 + N4 + 2;
   const int bd = hpc * P.dim;
-  size_t smem = 128 * sizeof(Coord) + 8 * 4 + (size_t)F * (NZ + 1) * 4 + 2 * NZ * 4 + 128 * 4 + (size_t)bd * 52;
-  auto kern = ssu_sq325_kernel<N8, N4>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return kECuda;
+  const size_t smem = (size_t)kTC * 64 * 16 + (size_t)kTC * 64 * 8 + (size_t)kTC * 8 * 4 +
+                      (size_t)kTC * kMaxHpc * 2 * 4 + (size_t)kTC * 128 * 4 + (size_t)F * (NZ + 1) * 4 +
+                      2 * NZ * 4 + 128 * 4 + (size_t)bd * 52;
+  auto kern = ssu_sq325_kernel<N8, N4, KJ>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) != cudaSuccess)
+      return kECuda;
+    attr = true;
   }
   dim3 grid(P.heads / hpc, P.batch);
   kern<<<grid, bd, smem, stream>>>(P);
   return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+}
+
+template <int N8, int N4>
+int launch_t(const ScanParams& P, int hpc, cudaStream_t stream) {
+  const int bd = hpc * P.dim;
+  if (bd >= 128) return launch_kj<N8, N4, 1>(P, hpc, stream);
+  if (bd >= 64) return launch_kj<N8, N4, 2>(P, hpc, stream);
+  return launch_kj<N8, N4, 4>(P, hpc, stream);
 }
 
 }  // namespace
@@ -339,13 +449,17 @@ int launch_t(const ScanParams& P, int hpc, cudaStream_t stream) {
 int launch_scan(const ScanParams& P, cudaStream_t stream) {
   if (P.layout < 0 || P.layout > 6) return kEInval;
   if (P.batch <= 0 || P.length <= 0 || P.heads <= 0 || P.groups <= 0 || P.heads % P.groups) return kEInval;
-  if (P.dim <= 0 || P.dim % 16 || P.dim > 256) return kEInval;
-  if (P.conv_w && P.length != 1) return kEInval;
+  if (P.dim <= 0 || P.dim % 16 || P.dim > 128) return kEInval;
+  if (P.conv_mode < 0 || P.conv_mode > 2) return kEInval;
+  if (P.conv_mode != 0 && (!P.conv_w || !P.conv_b || !P.conv_cache || P.heads * P.dim + 2 * P.groups * 128 != 10240))
+    return kEInval;
+  if (P.conv_mode == 1 && P.conv_pos != 0) return kEInval;     // fused prefill only from a reset state
+  if (P.conv_mode == 2 && (P.length != 1 || P.conv_pos <= 0)) return kEInval;
   const int hpg = P.heads / P.groups;
   int hpc = 1;
-  for (int c = 1; c <= hpg; ++c)
+  for (int c = 1; c <= hpg && c <= kMaxHpc; ++c)
     if (hpg % c == 0 && c * P.dim <= 128) hpc = c;
-  if (hpc * P.dim < 32 && hpg > hpc) return kEInval;
+  if (hpc * P.dim < 32) return kEInval;
   switch (P.layout) {
     case 0: return launch_t<32, 28>(P, hpc, stream);
     case 1: return launch_t<16, 60>(P, hpc, stream);

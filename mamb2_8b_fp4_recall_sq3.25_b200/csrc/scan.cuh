@@ -30,14 +30,16 @@ struct ScanParams {
   const uint16_t* predictor;                           // [G,n8+n4+2,nz] fp16
   uint8_t* lo; uint8_t* hi; uint8_t* q4; uint8_t* latent; uint16_t* s8; uint16_t* s4;
   uint16_t* y; long long y_sb, y_st;                   // (b,t,h,p) at y + b*y_sb + t*y_st + h*dim + p
-  // Optional fused causal-conv step (length == 1 only): when conv_w != nullptr,
-  // x/B/C above point at the RAW in_proj columns and the kernel applies the
-  // width-4 depthwise conv + bias + SiLU of StateQuant._convolution's step path
-  // itself, reading/writing the ring-ordered cache below.
-  const uint16_t* conv_w;   // [10240,4] fp16 (channel-major, tap k = time t-3+k)
+  // Optional fused causal conv (mamba2_recall/state_quant.py:283-317).  conv_mode 0: x/B/C
+  // are conv outputs.  1: prefill from a reset state (conv_pos == 0) with the conv1d
+  // numerics; 2: one-token step (length 1, conv_pos > 0) with the step numerics.  In
+  // modes 1/2 x/B/C point at the RAW in_proj xBC columns and the ring below is read
+  // (mode 2) and updated with the newest raw columns.
+  int conv_mode;
+  const uint16_t* conv_w;   // [10240,4] fp16 (tap k multiplies position t-3+k)
   const uint16_t* conv_b;   // [10240]
   uint16_t* conv_cache;     // [B,4,10240] fp16 ring, slot = position % 4
-  int conv_pos;             // absolute position of this token
+  int conv_pos;             // absolute position of the first token of this call
   long long conv_cache_sb;  // batch stride of the ring (elements)
 };
 
