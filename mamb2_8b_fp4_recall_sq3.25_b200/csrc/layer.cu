@@ -113,97 +113,140 @@ __global__ void conv_prefill_kernel(const uint16_t* __restrict__ raw, long long 
   }
 }
 
-// one CTA (256 threads = 8 warps = the 8 norm groups) processes tokens t = blockIdx.x, += gridDim.x
+// One CTA (256 threads = 8 warps; warp w owns heads 16w..16w+15 = gated-norm group w)
+// processes tokens t = blockIdx.x, += gridDim.x.  The 128x128 head mix
+// mix[i,p] = sum_j V[i,j] y[j,p] runs on the tensor cores (mma.sync m16n8k16, fp16 in,
+// fp32 accumulate; V and the token's y staged in shared memory, B fragments through
+// ldmatrix.trans), then each warp applies the gate correction and the gated RMSNorm of its
+// group entirely in registers.
+constexpr int kVPitch = 136;   // fp16 elements per staged V row (128 + 8 pad, 272 B)
+constexpr int kYPitch = 72;    // fp16 elements per staged y row (64 + 8 pad, 144 B)
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+               "{%0,%1,%2,%3};\n"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 __global__ void __launch_bounds__(256)
 resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __restrict__ z, long long z_st,
                            const uint16_t* __restrict__ u, long long u_st, AdapterPtrs ad, int has_ad,
                            const uint16_t* __restrict__ nw, float eps, uint16_t* __restrict__ out, int T) {
-  extern __shared__ float sm[];
-  float* ys = sm;                   // [8192]
-  float* Vs = sm + 8192;            // [128*128] (adapter only)
-  __shared__ float sgate;
+  extern __shared__ __align__(16) unsigned char smraw[];
+  uint16_t* Vs = reinterpret_cast<uint16_t*>(smraw);                 // [128][kVPitch]
+  uint16_t* Ys = Vs + 128 * kVPitch;                                  // [128][kYPitch]
+  __shared__ float spart[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gq = lane >> 2, tq = lane & 3;
   if (has_ad)
-    for (int i = threadIdx.x; i < 128 * 128; i += blockDim.x) Vs[i] = h2f(ad.V[i]);
+    for (int i = threadIdx.x; i < 128 * 16; i += blockDim.x) {      // 16-byte chunks of V
+      const int r = i >> 4, c = (i & 15) * 8;
+      *reinterpret_cast<uint4*>(Vs + r * kVPitch + c) = *reinterpret_cast<const uint4*>(ad.V + r * 128 + c);
+    }
   for (int t = blockIdx.x; t < T; t += gridDim.x) {
-    __syncthreads();
+    __syncthreads();                                   // previous token done with Ys / spart
     const uint16_t* yr = y + (long long)t * 8192;
-    for (int i = threadIdx.x * 8; i < 8192; i += blockDim.x * 8) {
-      uint4 v = *reinterpret_cast<const uint4*>(yr + i);
-      const uint16_t* vp = reinterpret_cast<const uint16_t*>(&v);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) ys[i + k] = h2f(vp[k]);
+    for (int i = threadIdx.x; i < 128 * 8; i += blockDim.x) {        // stage y[j][p] (16 B chunks)
+      const int r = i >> 3, c = (i & 7) * 8;
+      *reinterpret_cast<uint4*>(Ys + r * kYPitch + c) = *reinterpret_cast<const uint4*>(yr + r * 64 + c);
     }
-    if (has_ad && warp == 0) {
-      // logit = fp16(fp16(u . w) + b)
+    if (has_ad) {
+      // gate logit partials: fp16(u . w) + b (fp16), deterministic 8-way split
       float s = 0.f;
-      const uint16_t* ur = u + (long long)t * u_st;
-      for (int i = lane; i < 4096; i += 32) s += h2f(ur[i]) * h2f(ad.w[i]);
-      s = warp_sum(s);
-      if (lane == 0) {
-        float lg = h2f(f2h(h2f(f2h(s)) + h2f(ad.b[0])));
-        float gate = ad.hard ? (lg > 0.f ? 1.f : 0.f) : 1.0f / (1.0f + expf(-lg));
-        sgate = h2f(f2h(gate));
+      const uint16_t* ur = u + (long long)t * u_st + warp * 512;
+      const uint16_t* wr = ad.w + warp * 512;
+      for (int i = lane * 8; i < 512; i += 256) {
+        const uint4 uv = *reinterpret_cast<const uint4*>(ur + i);
+        const uint4 wv = *reinterpret_cast<const uint4*>(wr + i);
+        const uint16_t* up = reinterpret_cast<const uint16_t*>(&uv);
+        const uint16_t* wp = reinterpret_cast<const uint16_t*>(&wv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s = fmaf(h2f(up[k]), h2f(wp[k]), s);
       }
+      s = warp_sum(s);
+      if (lane == 0) spart[warp] = s;
     }
     __syncthreads();
-    float newy[16][2];
+    float acc[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+    float gate = 0.f;
     if (has_ad) {
-      float acc[16][2];
+      float tot = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = 0.f;
-      for (int j = 0; j < 128; ++j) {
-        const float y0 = ys[j * 64 + lane], y1 = ys[j * 64 + lane + 32];
+      for (int w = 0; w < 8; ++w) tot += spart[w];
+      const float lg = h2f(f2h(h2f(f2h(tot)) + h2f(ad.b[0])));
+      gate = h2f(f2h(ad.hard ? (lg > 0.f ? 1.f : 0.f) : 1.0f / (1.0f + expf(-lg))));
+      const int i0 = warp * 16;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float v = Vs[(warp * 16 + i) * 128 + j];
-          acc[i][0] = fmaf(v, y0, acc[i][0]);
-          acc[i][1] = fmaf(v, y1, acc[i][1]);
+      for (int k0 = 0; k0 < 128; k0 += 16) {
+        uint32_t a[4];
+        // matrices: (rows i0..+7, k0), (i0+8.., k0), (i0.., k0+8), (i0+8.., k0+8)
+        const int mi = lane >> 3, rr = lane & 7;
+        ldsm_x4(a, Vs + (i0 + rr + (mi & 1) * 8) * kVPitch + k0 + (mi >> 1) * 8);
+#pragma unroll
+        for (int n2 = 0; n2 < 4; ++n2) {
+          uint32_t bfr[4];
+          // matrices: (j k0..+7, p n), (j k0+8.., p n), (j k0.., p n+8), (j k0+8.., p n+8)
+          const int pn = n2 * 16 + (mi >> 1) * 8;
+          ldsm_x4_t(bfr, Ys + (k0 + rr + (mi & 1) * 8) * kYPitch + pn);
+          mma_f16(acc[2 * n2], a, bfr[0], bfr[1]);
+          mma_f16(acc[2 * n2 + 1], a, bfr[2], bfr[3]);
         }
-      }
-      const float g16 = sgate;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int hh = warp * 16 + i;
-        const float gg = h2f(f2h(g16 * h2f(ad.g[hh])));
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const float mix = h2f(f2h(acc[i][k]));
-          const float corr = h2f(f2h(gg * mix));
-          newy[i][k] = h2f(f2h(ys[hh * 64 + lane + 32 * k] + corr));
-        }
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        newy[i][0] = ys[(warp * 16 + i) * 64 + lane];
-        newy[i][1] = ys[(warp * 16 + i) * 64 + lane + 32];
       }
     }
-    // gated RMSNorm over this warp's group (heads warp*16 .. +15 = 1024 channels)
+    // epilogue: correction, gated RMSNorm over this warp's group (1024 channels)
     const uint16_t* zr = z + (long long)t * z_st;
-    float xv[16][2];
+    float xv[8][4];
     float ss = 0.f;
+    const int ia = warp * 16 + gq, ib = ia + 8;
+    const float ga = has_ad ? h2f(f2h(gate * h2f(ad.g[ia]))) : 0.f;
+    const float gb = has_ad ? h2f(f2h(gate * h2f(ad.g[ib]))) : 0.f;
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
+    for (int n = 0; n < 8; ++n) {
+      const int p0 = n * 8 + 2 * tq;
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int ch = (warp * 16 + i) * 64 + lane + 32 * k;
-        const float zz = h2f(zr[ch]);
-        const float gz = zz * (1.0f / (1.0f + expf(-zz)));
-        const float x = newy[i][k] * gz;
-        xv[i][k] = x;
+      for (int e = 0; e < 4; ++e) {
+        const int i = (e < 2) ? ia : ib;
+        const int pp = p0 + (e & 1);
+        float yv = h2f(Ys[i * kYPitch + pp]);
+        if (has_ad) {
+          const float mix = h2f(f2h(acc[n][e]));
+          const float corr = h2f(f2h(((e < 2) ? ga : gb) * mix));
+          yv = h2f(f2h(yv + corr));
+        }
+        const float zz = h2f(zr[i * 64 + pp]);
+        const float x = yv * (zz * (1.0f / (1.0f + expf(-zz))));
+        xv[n][e] = x;
         ss += x * x;
       }
+    }
     ss = warp_sum(ss);
     const float rstd = 1.0f / sqrtf(ss / 1024.0f + eps);
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
+    for (int n = 0; n < 8; ++n) {
+      const int p0 = n * 8 + 2 * tq;
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int ch = (warp * 16 + i) * 64 + lane + 32 * k;
-        out[(long long)t * 8192 + ch] = f2h((xv[i][k] * rstd) * h2f(nw[ch]));
+      for (int half = 0; half < 2; ++half) {
+        const int i = half ? ib : ia;
+        const int ch = i * 64 + p0;
+        const float o0 = (xv[n][2 * half] * rstd) * h2f(nw[ch]);
+        const float o1 = (xv[n][2 * half + 1] * rstd) * h2f(nw[ch + 1]);
+        __half2 hv = __floats2half2_rn(o0, o1);
+        *reinterpret_cast<__half2*>(out + (long long)t * 8192 + ch) = hv;
       }
+    }
   }
 }
 
@@ -292,15 +335,15 @@ int launch_resurface_gatednorm(const uint16_t* y, const uint16_t* z, long long z
   const int has_ad = ad && ad->V;
   AdapterPtrs a{};
   if (has_ad) a = *ad;
-  const size_t smem = (8192 + (has_ad ? 128 * 128 : 0)) * sizeof(float);
+  const size_t smem = (size_t)(128 * kVPitch + 128 * kYPitch) * 2;
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(resurface_gatednorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (8192 + 128 * 128) * (int)sizeof(float)) != cudaSuccess)
+    if (cudaFuncSetAttribute(resurface_gatednorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
       return kECuda;
     attr = true;
   }
-  const int grid = T < 2 * num_sms() ? T : 2 * num_sms();
+  const int grid = T < 3 * num_sms() ? T : 3 * num_sms();
   resurface_gatednorm_kernel<<<grid, 256, smem, st>>>(y, z, z_st, u, u_st, a, has_ad, norm_w, eps, out, T);
   return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
 }
