@@ -292,7 +292,8 @@ int sq_model_reserve(sq_model* m, int max_tokens) {
       {(void**)&m->h, T * kDModel * 2}, {(void**)&m->res, T * kDModel * 2}, {(void**)&m->hn, T * kDModel * 2},
       {(void**)&m->zx, T * kZx * 2}, {(void**)&m->xbc, T * kXbc * 2}, {(void**)&m->y, T * kDInner * 2},
       {(void**)&m->yn, T * kDInner * 2}, {(void**)&m->stage, stage * 2},
-      {(void**)&m->logits, (size_t)64 * m->cfg.vocab * 2}, {(void**)&m->partials, T * nt * sizeof(float2)},
+      {(void**)&m->logits, (size_t)64 * m->cfg.vocab * 2},
+      {(void**)&m->partials, std::max(T * nt * sizeof(float2), (size_t)argmax_workspace_bytes(64, m->cfg.vocab))},
       {(void**)&m->tlogit, T * sizeof(float)}};
   for (auto& a : allocs) {
     if (cudaMalloc(a.p, a.bytes) != cudaSuccess) {
@@ -398,7 +399,8 @@ int sq_model_greedy(sq_model* m, const uint16_t* hidden, int rows, uint16_t* log
   cudaStream_t st = (cudaStream_t)stream;
   uint16_t* lg = logits_out ? logits_out : m->logits;
   SQ_TRY(launch_fp4_gemv(fw(m->head), hidden, kDModel, rows, lg, m->cfg.vocab, st), "lm_head gemv");
-  return check(launch_argmax(lg, rows, m->cfg.vocab, m->cfg.vocab, (long long*)tokens_out, st), "argmax");
+  return check(launch_argmax(lg, rows, m->cfg.vocab, m->cfg.vocab, (long long*)tokens_out, m->partials, st),
+               "argmax");
 }
 
 int sq_model_check(sq_model* m, void* stream) {

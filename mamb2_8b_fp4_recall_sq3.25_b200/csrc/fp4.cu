@@ -12,20 +12,30 @@
 namespace sq {
 namespace {
 
-// E2M1 code (4 bits) -> fp32 bit pattern, sign included.
-__device__ __forceinline__ float e2m1_to_f32(uint32_t c) {
-  const uint32_t e = (c >> 1) & 3u, m = c & 1u;
-  uint32_t bits = e ? (((126u + e) << 23) | (m << 22)) : (m ? (126u << 23) : 0u);
-  bits |= (c & 8u) << 28;
-  return __uint_as_float(bits);
+// Hardware conversions (sm_100a): four code bytes -> four f16x2 magnitudes*sign
+// (element 2i in the low half), and one E4M3 byte -> {v, v} as f16x2.  Both are exact:
+// every E2M1 and E4M3 value is representable in fp16.
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
+  asm("{\n.reg .b8 q0, q1, q2, q3;\nmov.b32 {q0, q1, q2, q3}, %4;\n"
+      "cvt.rn.f16x2.e2m1x2 %0, q0;\ncvt.rn.f16x2.e2m1x2 %1, q1;\n"
+      "cvt.rn.f16x2.e2m1x2 %2, q2;\ncvt.rn.f16x2.e2m1x2 %3, q3;\n}\n"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3]) : "r"(w));
+}
+__device__ __forceinline__ uint32_t e4m3_splat_f16x2(uint32_t byte) {
+  uint32_t r;
+  const uint16_t two = (uint16_t)(byte | (byte << 8));
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;\n" : "=r"(r) : "h"(two));
+  return r;
 }
 
-// Two codes (one byte) -> exactly decoded fp16x2 (low nibble in the low half).
-__device__ __forceinline__ uint32_t decode_pair(uint32_t byte, float bscale, float gscale) {
-  float lo = (e2m1_to_f32(byte & 15u) * bscale) * gscale;
-  float hi = (e2m1_to_f32((byte >> 4) & 15u) * bscale) * gscale;
-  __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&h);
+// Exact decode of one code pair: FP16(FP32(FP32(m*b)*g)).  m*b is exact in fp16 (<= 6
+// significant bits, |m*b| <= 2688, >= 2^-10), so HMUL2 gives it exactly; the product with
+// the fp32 global scale is then rounded once to fp32 and once to fp16, as the reference.
+__device__ __forceinline__ uint32_t scale_pair(uint32_t m16x2, uint32_t b16x2, float2 g2) {
+  __half2 p = __hmul2(*reinterpret_cast<__half2*>(&m16x2), *reinterpret_cast<__half2*>(&b16x2));
+  const float2 f = __fmul2_rn(__half22float2(p), g2);
+  __half2 r = __float22half2_rn(f);
+  return *reinterpret_cast<uint32_t*>(&r);
 }
 
 __global__ void fp4_decode_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales,
@@ -38,13 +48,16 @@ __global__ void fp4_decode_kernel(const uint8_t* __restrict__ codes, const uint8
   const long long r = idx / per_row;
   const int c8 = (int)(idx - r * per_row);
   const float g = *gptr;
+  const float2 g2 = make_float2(g, g);
   const uint32_t w = *reinterpret_cast<const uint32_t*>(codes + r * (cols / 2) + c8 * 4);
-  const float bs = e4m3_to_f32(scales[r * (cols / 16) + (c8 >> 1)]);
+  const uint32_t bs = e4m3_splat_f16x2(scales[r * (cols / 16) + (c8 >> 1)]);
+  uint32_t m[4];
+  e2m1x8_to_f16x2(w, m);
   uint4 o;
-  o.x = decode_pair(w & 0xFF, bs, g);
-  o.y = decode_pair((w >> 8) & 0xFF, bs, g);
-  o.z = decode_pair((w >> 16) & 0xFF, bs, g);
-  o.w = decode_pair(w >> 24, bs, g);
+  o.x = scale_pair(m[0], bs, g2);
+  o.y = scale_pair(m[1], bs, g2);
+  o.z = scale_pair(m[2], bs, g2);
+  o.w = scale_pair(m[3], bs, g2);
   *reinterpret_cast<uint4*>(out + r * ldo + c8 * 8) = o;
 }
 
@@ -57,14 +70,17 @@ __global__ void fp4_embed_kernel(const uint8_t* __restrict__ codes, const uint8_
   long long id = ids[t];
   if (id < 0 || id >= vocab) { if (threadIdx.x == 0) atomicOr(err, (int)kDevBadArgs); id = 0; }
   const float g = *gptr;
+  const float2 g2 = make_float2(g, g);
   for (int c8 = threadIdx.x; c8 < cols / 8; c8 += blockDim.x) {
     const uint32_t w = *reinterpret_cast<const uint32_t*>(codes + id * (cols / 2) + c8 * 4);
-    const float bs = e4m3_to_f32(scales[id * (cols / 16) + (c8 >> 1)]);
+    const uint32_t bs = e4m3_splat_f16x2(scales[id * (cols / 16) + (c8 >> 1)]);
+    uint32_t m[4];
+    e2m1x8_to_f16x2(w, m);
     uint4 o;
-    o.x = decode_pair(w & 0xFF, bs, g);
-    o.y = decode_pair((w >> 8) & 0xFF, bs, g);
-    o.z = decode_pair((w >> 16) & 0xFF, bs, g);
-    o.w = decode_pair(w >> 24, bs, g);
+    o.x = scale_pair(m[0], bs, g2);
+    o.y = scale_pair(m[1], bs, g2);
+    o.z = scale_pair(m[2], bs, g2);
+    o.w = scale_pair(m[3], bs, g2);
     *reinterpret_cast<uint4*>(out + (long long)t * cols + c8 * 8) = o;
   }
 }
@@ -91,6 +107,7 @@ fp4_gemv_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ s
   const int gq = lane >> 2, tq = lane & 3;
   const int n0 = blockIdx.x * 16;
   const float gsc = *gptr;
+  const float2 g2 = make_float2(gsc, gsc);
   const int nchunks = K / 128;
   const int per = (nchunks + KS - 1) / KS;
   const int c_begin = warp * per, c_end = min(nchunks, c_begin + per);
@@ -120,19 +137,23 @@ fp4_gemv_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ s
     }
     const uint32_t wa[4] = {cca.x, cca.y, cca.z, cca.w};
     const uint32_t wb[4] = {ccb.x, ccb.y, ccb.z, ccb.w};
-    const float bsa0 = e4m3_to_f32(ssa & 0xFF), bsa1 = e4m3_to_f32(ssa >> 8);
-    const float bsb0 = e4m3_to_f32(ssb & 0xFF), bsb1 = e4m3_to_f32(ssb >> 8);
+    const uint32_t bsa0 = e4m3_splat_f16x2(ssa & 0xFF), bsa1 = e4m3_splat_f16x2(ssa >> 8);
+    const uint32_t bsb0 = e4m3_splat_f16x2(ssb & 0xFF), bsb1 = e4m3_splat_f16x2(ssb >> 8);
     const int kbase = c * 128 + tq * 32;       // physical k of this lane's 32 elements
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t wordA = wa[j >> 1], wordB = wb[j >> 1];
-      const int sh = (j & 1) * 16;
-      const float bsA = (j < 4) ? bsa0 : bsa1, bsB = (j < 4) ? bsb0 : bsb1;
+    for (int w4 = 0; w4 < 4; ++w4) {           // one 32-bit code word = 2 mma k-steps per row
+      uint32_t ma[4], mb[4];
+      e2m1x8_to_f16x2(wa[w4], ma);
+      e2m1x8_to_f16x2(wb[w4], mb);
+      const uint32_t bsA = (w4 < 2) ? bsa0 : bsa1, bsB = (w4 < 2) ? bsb0 : bsb1;
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+      const int j = w4 * 2 + jj;
       uint32_t a[4];
-      a[0] = decode_pair((wordA >> sh) & 0xFF, bsA, gsc);
-      a[1] = decode_pair((wordB >> sh) & 0xFF, bsB, gsc);
-      a[2] = decode_pair((wordA >> (sh + 8)) & 0xFF, bsA, gsc);
-      a[3] = decode_pair((wordB >> (sh + 8)) & 0xFF, bsB, gsc);
+      a[0] = scale_pair(ma[2 * jj], bsA, g2);
+      a[1] = scale_pair(mb[2 * jj], bsB, g2);
+      a[2] = scale_pair(ma[2 * jj + 1], bsA, g2);
+      a[3] = scale_pair(mb[2 * jj + 1], bsB, g2);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
         const int m = mt * 8 + gq;
@@ -142,6 +163,7 @@ fp4_gemv_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ s
           b0 = xv.x; b1 = xv.y;
         }
         mma16816(acc[mt], a, b0, b1);
+      }
       }
     }
   }

@@ -113,8 +113,9 @@ __global__ void conv_prefill_kernel(const uint16_t* __restrict__ raw, long long 
   }
 }
 
-// One CTA (256 threads = 8 warps; warp w owns heads 16w..16w+15 = gated-norm group w)
-// processes tokens t = blockIdx.x, += gridDim.x.  The 128x128 head mix
+// A CTA of `gpb` warps (8 for long sequences, 1 for decode batches) covers gated-norm
+// groups blockIdx.x*gpb .. +gpb-1 (warp w owns heads 16g..16g+15 of its group g) and
+// processes tokens t = blockIdx.y, += gridDim.y.  The 128x128 head mix
 // mix[i,p] = sum_j V[i,j] y[j,p] runs on the tensor cores (mma.sync m16n8k16, fp16 in,
 // fp32 accumulate; V and the token's y staged in shared memory, B fragments through
 // ldmatrix.trans), then each warp applies the gate correction and the gated RMSNorm of its
@@ -144,17 +145,21 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
                            const uint16_t* __restrict__ u, long long u_st, AdapterPtrs ad, int has_ad,
                            const uint16_t* __restrict__ nw, float eps, uint16_t* __restrict__ out, int T) {
   extern __shared__ __align__(16) unsigned char smraw[];
-  uint16_t* Vs = reinterpret_cast<uint16_t*>(smraw);                 // [128][kVPitch]
-  uint16_t* Ys = Vs + 128 * kVPitch;                                  // [128][kYPitch]
+  const int gpb = blockDim.x >> 5;
+  uint16_t* Ys = reinterpret_cast<uint16_t*>(smraw);                  // [128][kYPitch]
+  uint16_t* Vs = Ys + 128 * kYPitch;                                  // [gpb*16][kVPitch]
   __shared__ float spart[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gq = lane >> 2, tq = lane & 3;
+  const int grp = blockIdx.x * gpb + warp;                            // norm group of this warp
+  const int vrow0 = blockIdx.x * gpb * 16;                            // first V row staged here
   if (has_ad)
-    for (int i = threadIdx.x; i < 128 * 16; i += blockDim.x) {      // 16-byte chunks of V
+    for (int i = threadIdx.x; i < gpb * 16 * 16; i += blockDim.x) {  // 16-byte chunks of V rows
       const int r = i >> 4, c = (i & 15) * 8;
-      *reinterpret_cast<uint4*>(Vs + r * kVPitch + c) = *reinterpret_cast<const uint4*>(ad.V + r * 128 + c);
+      *reinterpret_cast<uint4*>(Vs + r * kVPitch + c) =
+          *reinterpret_cast<const uint4*>(ad.V + (vrow0 + r) * 128 + c);
     }
-  for (int t = blockIdx.x; t < T; t += gridDim.x) {
+  for (int t = blockIdx.y; t < T; t += gridDim.y) {
     __syncthreads();                                   // previous token done with Ys / spart
     const uint16_t* yr = y + (long long)t * 8192;
     for (int i = threadIdx.x; i < 128 * 8; i += blockDim.x) {        // stage y[j][p] (16 B chunks)
@@ -162,11 +167,12 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
       *reinterpret_cast<uint4*>(Ys + r * kYPitch + c) = *reinterpret_cast<const uint4*>(yr + r * 64 + c);
     }
     if (has_ad) {
-      // gate logit partials: fp16(u . w) + b (fp16), deterministic 8-way split
+      // gate logit partials: fp16(u . w) + b (fp16), deterministic gpb-way split
       float s = 0.f;
-      const uint16_t* ur = u + (long long)t * u_st + warp * 512;
-      const uint16_t* wr = ad.w + warp * 512;
-      for (int i = lane * 8; i < 512; i += 256) {
+      const int span = 4096 / gpb;
+      const uint16_t* ur = u + (long long)t * u_st + warp * span;
+      const uint16_t* wr = ad.w + warp * span;
+      for (int i = lane * 8; i < span; i += 256) {
         const uint4 uv = *reinterpret_cast<const uint4*>(ur + i);
         const uint4 wv = *reinterpret_cast<const uint4*>(wr + i);
         const uint16_t* up = reinterpret_cast<const uint16_t*>(&uv);
@@ -185,10 +191,10 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
     if (has_ad) {
       float tot = 0.f;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) tot += spart[w];
+      for (int w = 0; w < gpb; ++w) tot += spart[w];
       const float lg = h2f(f2h(h2f(f2h(tot)) + h2f(ad.b[0])));
       gate = h2f(f2h(ad.hard ? (lg > 0.f ? 1.f : 0.f) : 1.0f / (1.0f + expf(-lg))));
-      const int i0 = warp * 16;
+      const int i0 = warp * 16;                        // local V row of this warp's heads
 #pragma unroll
       for (int k0 = 0; k0 < 128; k0 += 16) {
         uint32_t a[4];
@@ -210,7 +216,7 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
     const uint16_t* zr = z + (long long)t * z_st;
     float xv[8][4];
     float ss = 0.f;
-    const int ia = warp * 16 + gq, ib = ia + 8;
+    const int ia = grp * 16 + gq, ib = ia + 8;
     const float ga = has_ad ? h2f(f2h(gate * h2f(ad.g[ia]))) : 0.f;
     const float gb = has_ad ? h2f(f2h(gate * h2f(ad.g[ib]))) : 0.f;
 #pragma unroll
@@ -282,25 +288,43 @@ __global__ void window_sum_kernel(const float* __restrict__ nll, int per, const 
   if (threadIdx.x == 0) out[w] = red[0];
 }
 
-__global__ void argmax_kernel(const uint16_t* __restrict__ logits, int V, long long ld, long long* __restrict__ out) {
-  __shared__ float bv[256];
-  __shared__ int bi[256];
-  const uint16_t* r = logits + (long long)blockIdx.x * ld;
+// first-occurrence argmax in two stages: per (row, slice) partials, then per row
+constexpr int kArgSlice = 4096;
+__device__ __forceinline__ void argmax_merge(float& bv, int& bi, float v2, int i2) {
+  if (v2 > bv || (v2 == bv && i2 < bi)) { bv = v2; bi = i2; }
+}
+__global__ void argmax_partial_kernel(const uint16_t* __restrict__ logits, int V, long long ld,
+                                      float* __restrict__ pv, int* __restrict__ pi, int nslice) {
+  __shared__ float sv[256];
+  __shared__ int si[256];
+  const int row = blockIdx.y, sl = blockIdx.x;
+  const uint16_t* r = logits + (long long)row * ld;
   float best = -INFINITY; int idx = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    float v = h2f(r[i]);
+  const int end = min(V, (sl + 1) * kArgSlice);
+  for (int i = sl * kArgSlice + threadIdx.x; i < end; i += blockDim.x) {
+    const float v = h2f(r[i]);
     if (v > best) { best = v; idx = i; }
   }
-  bv[threadIdx.x] = best; bi[threadIdx.x] = idx;
+  sv[threadIdx.x] = best; si[threadIdx.x] = idx;
   __syncthreads();
   for (int o = blockDim.x / 2; o; o >>= 1) {
-    if ((int)threadIdx.x < o) {
-      float v2 = bv[threadIdx.x + o]; int i2 = bi[threadIdx.x + o];
-      if (v2 > bv[threadIdx.x] || (v2 == bv[threadIdx.x] && i2 < bi[threadIdx.x])) { bv[threadIdx.x] = v2; bi[threadIdx.x] = i2; }
-    }
+    if ((int)threadIdx.x < o) argmax_merge(sv[threadIdx.x], si[threadIdx.x], sv[threadIdx.x + o], si[threadIdx.x + o]);
     __syncthreads();
   }
-  if (threadIdx.x == 0) out[blockIdx.x] = bi[0] == 0x7fffffff ? 0 : bi[0];
+  if (threadIdx.x == 0) { pv[row * nslice + sl] = sv[0]; pi[row * nslice + sl] = si[0]; }
+}
+__global__ void argmax_final_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int nslice,
+                                    long long* __restrict__ out) {
+  const int row = blockIdx.x, lane = threadIdx.x;
+  float best = -INFINITY; int idx = 0x7fffffff;
+  for (int i = lane; i < nslice; i += 32) argmax_merge(best, idx, pv[row * nslice + i], pi[row * nslice + i]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+    argmax_merge(best, idx, v2, i2);
+  }
+  if (lane == 0) out[row] = idx == 0x7fffffff ? 0 : idx;
 }
 
 int g_sms = 0;
@@ -335,16 +359,20 @@ int launch_resurface_gatednorm(const uint16_t* y, const uint16_t* z, long long z
   const int has_ad = ad && ad->V;
   AdapterPtrs a{};
   if (has_ad) a = *ad;
-  const size_t smem = (size_t)(128 * kVPitch + 128 * kYPitch) * 2;
+  // few tokens: one warp (one norm group) per CTA spreads a token over 8 SMs;
+  // many tokens: 8 warps per CTA share one staged copy of each token's y
+  const int gpb = T < 64 ? 1 : 8;
+  const size_t smem = (size_t)(128 * kYPitch + gpb * 16 * kVPitch) * 2;
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(resurface_gatednorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(resurface_gatednorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (128 * kYPitch + 128 * kVPitch) * 2) != cudaSuccess)
       return kECuda;
     attr = true;
   }
-  const int grid = T < 3 * num_sms() ? T : 3 * num_sms();
-  resurface_gatednorm_kernel<<<grid, 256, smem, st>>>(y, z, z_st, u, u_st, a, has_ad, norm_w, eps, out, T);
+  const int ty = gpb == 8 ? (T < 3 * num_sms() ? T : 3 * num_sms()) : T;
+  dim3 grid(8 / gpb, ty);
+  resurface_gatednorm_kernel<<<grid, 32 * gpb, smem, st>>>(y, z, z_st, u, u_st, a, has_ad, norm_w, eps, out, T);
   return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
 }
 
@@ -361,9 +389,18 @@ int launch_window_sum(const float* nll, int windows, int per, const int* counts,
   return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
 }
 
-int launch_argmax(const uint16_t* logits, int rows, int V, long long ld, long long* out, cudaStream_t st) {
-  if (rows <= 0 || V <= 0) return kEInval;
-  argmax_kernel<<<rows, 256, 0, st>>>(logits, V, ld, out);
+int argmax_workspace_bytes(int rows, int V) {
+  const int ns = (V + kArgSlice - 1) / kArgSlice;
+  return rows * ns * 8;
+}
+
+int launch_argmax(const uint16_t* logits, int rows, int V, long long ld, long long* out, void* ws, cudaStream_t st) {
+  if (rows <= 0 || V <= 0 || !ws) return kEInval;
+  const int ns = (V + kArgSlice - 1) / kArgSlice;
+  float* pv = reinterpret_cast<float*>(ws);
+  int* pi = reinterpret_cast<int*>(pv + rows * ns);
+  argmax_partial_kernel<<<dim3(ns, rows), 256, 0, st>>>(logits, V, ld, pv, pi, ns);
+  argmax_final_kernel<<<rows, 32, 0, st>>>(pv, pi, ns, out);
   return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
 }
 

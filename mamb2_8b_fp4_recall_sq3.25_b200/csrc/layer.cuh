@@ -34,7 +34,8 @@ int launch_ce_finalize(const float2* partials, int ntiles, const float* tlogit, 
                        cudaStream_t st);
 // Per-window fp64 sums of nll over `per` consecutive rows.
 int launch_window_sum(const float* nll, int windows, int per, const int* counts, double* out, cudaStream_t st);
-// First-occurrence argmax over fp16 rows.
-int launch_argmax(const uint16_t* logits, int rows, int V, long long ld, long long* out, cudaStream_t st);
+// First-occurrence argmax over fp16 rows (two stages; `ws` >= argmax_workspace_bytes).
+int argmax_workspace_bytes(int rows, int V);
+int launch_argmax(const uint16_t* logits, int rows, int V, long long ld, long long* out, void* ws, cudaStream_t st);
 
 }  // namespace sq
