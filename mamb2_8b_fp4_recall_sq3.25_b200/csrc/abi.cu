@@ -126,9 +126,9 @@ int sq_scan(const sq_scan_args* a, void* stream) {
                        a->latent_scale, a->predictor, a->lo, a->hi, a->q4, a->latent, a->s8, a->s4, a->y};
   for (const void* p : req)
     if (!p) return fail(SQ_EINVAL, "scan: null pointer argument");
-  const void* st4[] = {a->lo, a->hi, a->q4, a->latent, a->s8, a->s4};
-  for (const void* p : st4)
-    if (!aligned(p, 4)) return fail(SQ_EINVAL, "scan: packed state buffers must be 4-byte aligned");
+  const void* st16[] = {a->lo, a->hi, a->q4, a->latent, a->s8, a->s4, a->permutation, a->basis, a->predictor};
+  for (const void* p : st16)
+    if (!aligned(p, 16)) return fail(SQ_EINVAL, "scan: state buffers and static tables must be 16-byte aligned");
   ScanParams P{};
   P.batch = a->batch; P.length = a->length; P.heads = a->heads; P.dim = a->dim; P.groups = a->groups;
   P.layout = a->layout;
@@ -248,6 +248,8 @@ int sq_model_set_layer(sq_model* m, int layer, const sq_layer_desc* d) {
                        d->permutation, d->basis, d->latent_scale, d->predictor};
   for (const void* p : req)
     if (!p) return fail(SQ_EINVAL, "set_layer: null pointer");
+  if (!aligned(d->permutation, 16) || !aligned(d->basis, 16) || !aligned(d->predictor, 16))
+    return fail(SQ_EINVAL, "set_layer: permutation / basis / predictor must be 16-byte aligned");
   m->layers[layer] = *d;
   return SQ_OK;
 }
@@ -273,7 +275,7 @@ int sq_model_bind_state(sq_model* m, int layer, int batch, uint8_t* lo, uint8_t*
   if (!m || layer < 0 || layer >= m->cfg.n_layer || batch <= 0) return fail(SQ_EINVAL, "bind_state: bad layer/batch");
   const void* p[] = {lo, hi, q4, latent, s8, s4, ring};
   for (const void* q : p)
-    if (!q || !aligned(q, 4)) return fail(SQ_EINVAL, "bind_state: null or misaligned buffer");
+    if (!q || !aligned(q, 16)) return fail(SQ_EINVAL, "bind_state: null or misaligned (16 B) buffer");
   sq_model::St& s = m->states[layer];
   s.batch = batch; s.lo = lo; s.hi = hi; s.q4 = q4; s.latent = latent; s.s8 = s8; s.s4 = s4; s.ring = ring;
   return SQ_OK;

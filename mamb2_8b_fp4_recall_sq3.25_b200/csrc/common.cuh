@@ -41,6 +41,21 @@ __device__ __forceinline__ float round_half_away(float q) {
   return copysignf(r, q);
 }
 
+// Asynchronous 16-byte global -> shared copies (LDGSTS); both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" :: "r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_all;\n" ::: "memory");
+}
+// Block-cooperative copy of `bytes` (multiple of 16) from global to shared memory.
+__device__ __forceinline__ void stage16(void* smem_dst, const void* gsrc, int bytes, int tid, int nthreads) {
+  const int n = bytes >> 4;
+  for (int i = tid; i < n; i += nthreads)
+    cp_async16(reinterpret_cast<char*>(smem_dst) + 16 * i, reinterpret_cast<const char*>(gsrc) + 16 * i);
+}
+
 // Bounded mbarrier / flag waits: every spin has an iteration limit.
 constexpr uint32_t kSpinLimit = 1u << 26;
 

@@ -156,15 +156,14 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
   if (has_ad)
     for (int i = threadIdx.x; i < gpb * 16 * 16; i += blockDim.x) {  // 16-byte chunks of V rows
       const int r = i >> 4, c = (i & 15) * 8;
-      *reinterpret_cast<uint4*>(Vs + r * kVPitch + c) =
-          *reinterpret_cast<const uint4*>(ad.V + (vrow0 + r) * 128 + c);
+      cp_async16(Vs + r * kVPitch + c, ad.V + (vrow0 + r) * 128 + c);
     }
   for (int t = blockIdx.y; t < T; t += gridDim.y) {
     __syncthreads();                                   // previous token done with Ys / spart
     const uint16_t* yr = y + (long long)t * 8192;
     for (int i = threadIdx.x; i < 128 * 8; i += blockDim.x) {        // stage y[j][p] (16 B chunks)
       const int r = i >> 3, c = (i & 7) * 8;
-      *reinterpret_cast<uint4*>(Ys + r * kYPitch + c) = *reinterpret_cast<const uint4*>(yr + r * 64 + c);
+      cp_async16(Ys + r * kYPitch + c, yr + r * 64 + c);
     }
     if (has_ad) {
       // gate logit partials: fp16(u . w) + b (fp16), deterministic gpb-way split
@@ -183,6 +182,7 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
       s = warp_sum(s);
       if (lane == 0) spart[warp] = s;
     }
+    cp_async_wait_all();
     __syncthreads();
     float acc[8][4];
 #pragma unroll

@@ -60,7 +60,7 @@ __device__ __forceinline__ float requant(float q, float lim) {
   return fminf(fmaxf(round_half_away(q), -lim), lim);
 }
 
-template <int N8, int N4, int KJ>
+template <int N8, int N4, int KJ, int MODE>
 __global__ void __launch_bounds__(128)
 ssu_sq325_kernel(const ScanParams P) {
   constexpr int NZ = 128 - N8 - N4;
@@ -76,11 +76,15 @@ ssu_sq325_kernel(const ScanParams P) {
   float* sDots = reinterpret_cast<float*>(sV2 + TC * 64);            // [TC][8]
   float* sDD = sDots + TC * 8;                                       // [TC][kMaxHpc][2] (dt, decay)
   float* sX = sDD + TC * kMaxHpc * 2;                                // [TC][blockDim] own x value
-  float* sPred = sX + TC * 128;                                      // [F][NZ+1]
+  unsigned char* sPack = reinterpret_cast<unsigned char*>(sX + TC * 128);   // rows*52 (16-B aligned)
+  float* sPred = reinterpret_cast<float*>(sPack + 128 * 52);         // [F][NZ+1]
   float* sBasis = sPred + F * (NZ + 1);                              // [2][NZ]
   int* sPerm = reinterpret_cast<int*>(sBasis + 2 * NZ);              // [128]
-  unsigned char* sPack = reinterpret_cast<unsigned char*>(sPerm + 128);
   float* sPf = reinterpret_cast<float*>(sP4);
+  // raw fp16 staging of the static tables lives in the (not yet used) token tables
+  uint16_t* rawPred = reinterpret_cast<uint16_t*>(sP4);              // F*NZ fp16  (<= 8.6 KB)
+  uint16_t* rawBasis = rawPred + F * NZ + 8;                         // NZ*2 fp16
+  uint8_t* rawPerm = reinterpret_cast<uint8_t*>(sV2);                // 128 B
 
   const int tid = threadIdx.x;
   const int bd = blockDim.x;
@@ -96,37 +100,37 @@ ssu_sq325_kernel(const ScanParams P) {
   const bool group_leader = (h0 % hpg) == 0;       // writes the group's B/C conv ring entries
   const long long row0 = ((long long)b * P.heads + h0) * dim;
   const int rows = bd;
-  const int mode = P.conv_mode;
+  constexpr int mode = MODE;
   const int kj = KJ;                                // coordinates per thread: 128 / blockDim
 
-  // ---- static tables for this group ----
-  for (int i = tid; i < 128; i += bd) sPerm[i] = P.perm[g * 128 + i];
-  for (int i = tid; i < F * NZ; i += bd) {
-    int f = i / NZ, d = i - f * NZ;
-    sPred[f * (NZ + 1) + d] = h2f(P.predictor[((long long)g * F + f) * NZ + d]);
-  }
-  for (int i = tid; i < NZ; i += bd) {
-    sBasis[i] = h2f(P.basis[(g * NZ + i) * 2 + 0]);
-    sBasis[NZ + i] = h2f(P.basis[(g * NZ + i) * 2 + 1]);
-  }
-  // ---- stage packed rows (coalesced 32-bit copies; every region is a 4-byte multiple) ----
+  // ---- stage static tables and packed rows with asynchronous 16-byte copies ----
+  // (every region below is a multiple of 16 bytes at a 16-byte aligned offset)
   unsigned char* pLo = sPack;
   unsigned char* pHi = pLo + rows * W8;
   unsigned char* pQ4 = pHi + rows * W8;
   unsigned char* pLat = pQ4 + rows * W4;
   uint16_t* pS8 = reinterpret_cast<uint16_t*>(pLat + rows * 2);
   uint16_t* pS4 = pS8 + rows;
-  auto copy_words = [&](unsigned char* dst, const unsigned char* src, int bytes) {
-    const uint32_t* s = reinterpret_cast<const uint32_t*>(src);
-    uint32_t* d = reinterpret_cast<uint32_t*>(dst);
-    for (int i = tid; i < bytes / 4; i += bd) d[i] = s[i];
-  };
-  copy_words(pLo, P.lo + row0 * W8, rows * W8);
-  copy_words(pHi, P.hi + row0 * W8, rows * W8);
-  copy_words(pQ4, P.q4 + row0 * W4, rows * W4);
-  copy_words(pLat, P.latent + row0 * 2, rows * 2);
-  copy_words(reinterpret_cast<unsigned char*>(pS8), reinterpret_cast<const unsigned char*>(P.s8 + row0), rows * 2);
-  copy_words(reinterpret_cast<unsigned char*>(pS4), reinterpret_cast<const unsigned char*>(P.s4 + row0), rows * 2);
+  stage16(rawPred, P.predictor + (long long)g * F * NZ, F * NZ * 2, tid, bd);
+  stage16(rawBasis, P.basis + (long long)g * NZ * 2, NZ * 4, tid, bd);
+  stage16(rawPerm, P.perm + g * 128, 128, tid, bd);
+  stage16(pLo, P.lo + row0 * W8, rows * W8, tid, bd);
+  stage16(pHi, P.hi + row0 * W8, rows * W8, tid, bd);
+  stage16(pQ4, P.q4 + row0 * W4, rows * W4, tid, bd);
+  stage16(pLat, P.latent + row0 * 2, rows * 2, tid, bd);
+  stage16(pS8, P.s8 + row0, rows * 2, tid, bd);
+  stage16(pS4, P.s4 + row0, rows * 2, tid, bd);
+  cp_async_wait_all();
+  __syncthreads();
+  for (int i = tid; i < F * NZ; i += bd) {
+    const int f = i / NZ, d = i - f * NZ;
+    sPred[f * (NZ + 1) + d] = h2f(rawPred[i]);
+  }
+  for (int i = tid; i < NZ; i += bd) {
+    sBasis[i] = h2f(rawBasis[2 * i + 0]);
+    sBasis[NZ + i] = h2f(rawBasis[2 * i + 1]);
+  }
+  for (int i = tid; i < 128; i += bd) sPerm[i] = rawPerm[i];
   __syncthreads();
 
   // ---- decode own row (:81-114) ----
@@ -369,17 +373,19 @@ ssu_sq325_kernel(const ScanParams P) {
     uint16_t* ring = P.conv_cache + (long long)b * P.conv_cache_sb;
     const int last = P.conv_pos + P.length - 1;       // absolute position of the newest token
     const int nwrite = mode == 2 ? 1 : min(4, P.length);
-    for (int i = 0; i < nwrite; ++i) {
-      const int pos = last - i;
-      const int slot = pos & 3;
-      ring[slot * 10240 + chx] = f2h(hx[3 - i]);
-      if (group_leader) {
 #pragma unroll
-        for (int k = 0; k < KJ; ++k)
-          if (k < kj && tid + k * bd < 128) {
-            ring[slot * 10240 + chb[k]] = f2h(hb[k][3 - i]);
-            ring[slot * 10240 + chc[k]] = f2h(hc[k][3 - i]);
-          }
+    for (int i = 0; i < 4; ++i) {
+      if (i < nwrite) {
+        const int slot = (last - i) & 3;
+        ring[slot * 10240 + chx] = f2h(hx[3 - i]);
+        if (group_leader) {
+#pragma unroll
+          for (int k = 0; k < KJ; ++k)
+            if (k < kj && tid + k * bd < 128) {
+              ring[slot * 10240 + chb[k]] = f2h(hb[k][3 - i]);
+              ring[slot * 10240 + chc[k]] = f2h(hc[k][3 - i]);
+            }
+        }
       }
     }
   }
@@ -408,23 +414,29 @@ ssu_sq325_kernel(const ScanParams P) {
     pS4[tid] = f2h(s4);
   }
   __syncthreads();
-  copy_words(P.lo + row0 * W8, pLo, rows * W8);
-  copy_words(P.hi + row0 * W8, pHi, rows * W8);
-  copy_words(P.q4 + row0 * W4, pQ4, rows * W4);
-  copy_words(P.latent + row0 * 2, pLat, rows * 2);
-  copy_words(reinterpret_cast<unsigned char*>(P.s8 + row0), reinterpret_cast<unsigned char*>(pS8), rows * 2);
-  copy_words(reinterpret_cast<unsigned char*>(P.s4 + row0), reinterpret_cast<unsigned char*>(pS4), rows * 2);
+  auto copy_out = [&](unsigned char* dst, const unsigned char* src, int bytes) {
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (int i = tid; i < bytes / 16; i += bd) d[i] = s[i];
+  };
+  copy_out(P.lo + row0 * W8, pLo, rows * W8);
+  copy_out(P.hi + row0 * W8, pHi, rows * W8);
+  copy_out(P.q4 + row0 * W4, pQ4, rows * W4);
+  copy_out(P.latent + row0 * 2, pLat, rows * 2);
+  copy_out(reinterpret_cast<unsigned char*>(P.s8 + row0), reinterpret_cast<unsigned char*>(pS8), rows * 2);
+  copy_out(reinterpret_cast<unsigned char*>(P.s4 + row0), reinterpret_cast<unsigned char*>(pS4), rows * 2);
 }
 
-template <int N8, int N4, int KJ>
+template <int N8, int N4, int KJ, int MODE>
 int launch_kj(const ScanParams& P, int hpc, cudaStream_t stream) {
   constexpr int NZ = 128 - N8 - N4;
   constexpr int F = N8 + N4 + 2;
   const int bd = hpc * P.dim;
   const size_t smem = (size_t)kTC * 64 * 16 + (size_t)kTC * 64 * 8 + (size_t)kTC * 8 * 4 +
-                      (size_t)kTC * kMaxHpc * 2 * 4 + (size_t)kTC * 128 * 4 + (size_t)F * (NZ + 1) * 4 +
-                      2 * NZ * 4 + 128 * 4 + (size_t)bd * 52;
-  auto kern = ssu_sq325_kernel<N8, N4, KJ>;
+                      (size_t)kTC * kMaxHpc * 2 * 4 + (size_t)kTC * 128 * 4 + 128 * 52 +
+                      (size_t)F * (NZ + 1) * 4 + 2 * NZ * 4 + 128 * 4;
+  (void)bd;
+  auto kern = ssu_sq325_kernel<N8, N4, KJ, MODE>;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) != cudaSuccess)
@@ -439,9 +451,11 @@ int launch_kj(const ScanParams& P, int hpc, cudaStream_t stream) {
 template <int N8, int N4>
 int launch_t(const ScanParams& P, int hpc, cudaStream_t stream) {
   const int bd = hpc * P.dim;
-  if (bd >= 128) return launch_kj<N8, N4, 1>(P, hpc, stream);
-  if (bd >= 64) return launch_kj<N8, N4, 2>(P, hpc, stream);
-  return launch_kj<N8, N4, 4>(P, hpc, stream);
+  if (P.conv_mode == 1) return bd == 128 ? launch_kj<N8, N4, 1, 1>(P, hpc, stream) : kEInval;
+  if (P.conv_mode == 2) return bd == 128 ? launch_kj<N8, N4, 1, 2>(P, hpc, stream) : kEInval;
+  if (bd >= 128) return launch_kj<N8, N4, 1, 0>(P, hpc, stream);
+  if (bd >= 64) return launch_kj<N8, N4, 2, 0>(P, hpc, stream);
+  return launch_kj<N8, N4, 4, 0>(P, hpc, stream);
 }
 
 }  // namespace
