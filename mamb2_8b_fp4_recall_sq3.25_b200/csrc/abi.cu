@@ -89,7 +89,7 @@ void free_ws(sq_model* m) {
 int linear(sq_model* m, const sq_fp4_matrix& W, const uint16_t* X, long long ldx, int M, uint16_t* Y,
            long long ldy, cudaStream_t st) {
   const Fp4Weight w = fw(W);
-  if (M <= 64) return check(launch_fp4_gemv(w, X, ldx, M, Y, ldy, st), "fp4 gemv");
+  if (M <= 64) return check(launch_fp4_gemv_stream(w, X, ldx, M, Y, ldy, m->d_err, st), "fp4 gemv");
   if ((size_t)W.rows * W.cols > m->stage_elems) return fail(SQ_EINVAL, "staging buffer too small");
   SQ_TRY(launch_fp4_decode(w, m->stage, W.cols, st), "fp4 decode");
   return check(launch_gemm_f16(X, ldx, m->stage, W.cols, Y, ldy, M, W.rows, W.cols, 0, nullptr, m->d_err, st),
@@ -180,14 +180,18 @@ int sq_fp4_linear(const uint8_t* codes, const uint8_t* block_scales, const float
   if (!aligned(codes, 16) || !aligned(x, 16)) return fail(SQ_EINVAL, "fp4_linear: misaligned buffers");
   Fp4Weight w{codes, block_scales, global_scale, n, k};
   cudaStream_t st = (cudaStream_t)stream;
-  if (m <= 64) return check(launch_fp4_gemv(w, x, ldx, m, y, ldy, st), "fp4 gemv");
-  if (!workspace || workspace_bytes < sq_fp4_linear_workspace(m, n, k) || !aligned(workspace, 16))
-    return fail(SQ_EINVAL, "fp4_linear: workspace too small");
   static int* d_err = nullptr;
   if (!d_err) {
     if (cudaMalloc(&d_err, sizeof(int)) != cudaSuccess) return cuda_fail("cudaMalloc");
     cudaMemset(d_err, 0, sizeof(int));
   }
+  if (m <= 64) {
+    if (k % 256 == 0 && aligned(block_scales, 16))
+      return check(launch_fp4_gemv_stream(w, x, ldx, m, y, ldy, d_err, st), "fp4 gemv");
+    return check(launch_fp4_gemv(w, x, ldx, m, y, ldy, st), "fp4 gemv");
+  }
+  if (!workspace || workspace_bytes < sq_fp4_linear_workspace(m, n, k) || !aligned(workspace, 16))
+    return fail(SQ_EINVAL, "fp4_linear: workspace too small");
   uint16_t* stg = (uint16_t*)workspace;
   SQ_TRY(launch_fp4_decode(w, stg, k, st), "fp4 decode");
   return check(launch_gemm_f16(x, ldx, stg, k, y, ldy, m, n, k, 0, nullptr, d_err, st), "tcgen05 gemm");
@@ -400,7 +404,7 @@ int sq_model_greedy(sq_model* m, const uint16_t* hidden, int rows, uint16_t* log
   if (!m->logits) return fail(SQ_ESTATE, "greedy: reserve() first");
   cudaStream_t st = (cudaStream_t)stream;
   uint16_t* lg = logits_out ? logits_out : m->logits;
-  SQ_TRY(launch_fp4_gemv(fw(m->head), hidden, kDModel, rows, lg, m->cfg.vocab, st), "lm_head gemv");
+  SQ_TRY(launch_fp4_gemv_stream(fw(m->head), hidden, kDModel, rows, lg, m->cfg.vocab, m->d_err, st), "lm_head gemv");
   return check(launch_argmax(lg, rows, m->cfg.vocab, m->cfg.vocab, (long long*)tokens_out, m->partials, st),
                "argmax");
 }

@@ -191,6 +191,205 @@ fp4_gemv_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ s
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Streaming skinny GEMM for M <= 8*MT, the decode-time projection kernel.
+// Warp 0 (one lane) streams row tiles of 16 weight rows x KC columns (codes + block
+// scales) into a STAGES-deep shared-memory ring with cp.async.bulk (non-multicast) and
+// mbarrier transaction counts; warps 1..4 decode each stage exactly into mma.sync A
+// fragments and multiply with X.  Every mbarrier wait is bounded (%globaltimer); on
+// expiry the warp records an error bit and leaves.
+constexpr int kGvRows = 16, kGvKC = 1024, kGvStages = 6, kGvConsumers = 4;
+constexpr int kGvCodeBytes = kGvRows * kGvKC / 2;          // 8 KB
+constexpr int kGvScaleBytes = kGvRows * kGvKC / 16;        // 1 KB
+constexpr int kGvStageBytes = kGvCodeBytes + kGvScaleBytes;
+constexpr unsigned long long kGvWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t gv_time() { uint64_t t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); return t; }
+__device__ __forceinline__ bool gv_try(uint32_t a, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool gv_wait(uint32_t a, uint32_t parity) {
+  if (gv_try(a, parity)) return true;
+  const uint64_t t0 = gv_time();
+  for (;;) {
+    for (int i = 0; i < 32; ++i) if (gv_try(a, parity)) return true;
+    if (gv_time() - t0 > kGvWaitNs) return false;
+  }
+}
+__device__ __forceinline__ void gv_bulk(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+               :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+
+template <int MT>
+__global__ void __launch_bounds__(32 * (1 + kGvConsumers))
+fp4_gemv_stream_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales,
+                       const float* __restrict__ gptr, int N, int K, int KC,
+                       const uint16_t* __restrict__ X, long long ldx, int M,
+                       uint16_t* __restrict__ Y, long long ldy, int* err) {
+  extern __shared__ __align__(128) unsigned char gsm[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(gsm + kGvStages * kGvStageBytes);
+  uint64_t* empty = full + kGvStages;
+  float* red = reinterpret_cast<float*>(empty + kGvStages);          // [consumers][MT][32][4]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(gsm);
+  const uint32_t fbar = (uint32_t)__cvta_generic_to_shared(full);
+  const uint32_t ebar = (uint32_t)__cvta_generic_to_shared(empty);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kGvStages; ++i) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(fbar + 8 * i) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(ebar + 8 * i), "r"(kGvConsumers) : "memory");
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const int tiles = (N + kGvRows - 1) / kGvRows;
+  const int kchunks = K / KC;
+  const int code_row = KC / 2, scale_row = KC / 16;
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0; uint32_t phase = 0; int issued = 0; bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        for (int kc = 0; kc < kchunks; ++kc) {
+          if (!gv_wait(ebar + 8 * stage, phase ^ 1)) { ok = false; break; }
+          const uint32_t fb = fbar + 8 * stage;
+          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                       :: "r"(fb), "r"((uint32_t)(kGvRows * (code_row + scale_row))) : "memory");
+          const uint32_t cdst = sbase + stage * kGvStageBytes, sdst = cdst + kGvCodeBytes;
+          for (int r = 0; r < kGvRows; ++r) {
+            const long long row = min(tile * kGvRows + r, N - 1);
+            gv_bulk(cdst + r * code_row, codes + row * (K / 2) + (long long)kc * code_row, code_row, fb);
+            gv_bulk(sdst + r * scale_row, scales + row * (K / 16) + (long long)kc * scale_row, scale_row, fb);
+          }
+          ++issued;
+          if (++stage == kGvStages) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        atomicOr(err, (int)kDevTimeoutProducer);
+        for (int i = 0; i < kGvStages && issued > 0; ++i, --issued) {   // drain own copies
+          if (--stage < 0) { stage = kGvStages - 1; phase ^= 1; }
+          gv_wait(fbar + 8 * stage, phase);
+        }
+      }
+    }
+    return;
+  }
+  // ------------------------------------------------------------------ consumers
+  const int cw = warp - 1;
+  const int gq = lane >> 2, tq = lane & 3;
+  const float gsc = *gptr;
+  const float2 g2 = make_float2(gsc, gsc);
+  const int subs = KC / 128;                      // 128-column sub-chunks per stage
+  int stage = 0; uint32_t phase = 0; bool ok = true;
+  for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    float acc[MT][4];
+#pragma unroll
+    for (int i = 0; i < MT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    for (int kc = 0; kc < kchunks; ++kc) {
+      if (ok && !gv_wait(fbar + 8 * stage, phase)) ok = false;
+      if (ok) {
+        const unsigned char* cs = gsm + stage * kGvStageBytes;
+        const unsigned char* ss = cs + kGvCodeBytes;
+        for (int sub = cw; sub < subs; sub += kGvConsumers) {
+          const uint4 ca = *reinterpret_cast<const uint4*>(cs + gq * code_row + sub * 64 + tq * 16);
+          const uint4 cb = *reinterpret_cast<const uint4*>(cs + (gq + 8) * code_row + sub * 64 + tq * 16);
+          const uint16_t sa = *reinterpret_cast<const uint16_t*>(ss + gq * scale_row + sub * 8 + tq * 2);
+          const uint16_t sb = *reinterpret_cast<const uint16_t*>(ss + (gq + 8) * scale_row + sub * 8 + tq * 2);
+          const uint32_t wa[4] = {ca.x, ca.y, ca.z, ca.w};
+          const uint32_t wb[4] = {cb.x, cb.y, cb.z, cb.w};
+          const uint32_t bsa0 = e4m3_splat_f16x2(sa & 0xFF), bsa1 = e4m3_splat_f16x2(sa >> 8);
+          const uint32_t bsb0 = e4m3_splat_f16x2(sb & 0xFF), bsb1 = e4m3_splat_f16x2(sb >> 8);
+          const int kbase = kc * KC + sub * 128 + tq * 32;
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {
+            uint32_t ma[4], mb[4];
+            e2m1x8_to_f16x2(wa[w4], ma);
+            e2m1x8_to_f16x2(wb[w4], mb);
+            const uint32_t bsA = (w4 < 2) ? bsa0 : bsa1, bsB = (w4 < 2) ? bsb0 : bsb1;
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+              const int j = w4 * 2 + jj;
+              uint32_t a[4];
+              a[0] = scale_pair(ma[2 * jj], bsA, g2);
+              a[1] = scale_pair(mb[2 * jj], bsB, g2);
+              a[2] = scale_pair(ma[2 * jj + 1], bsA, g2);
+              a[3] = scale_pair(mb[2 * jj + 1], bsB, g2);
+#pragma unroll
+              for (int mt = 0; mt < MT; ++mt) {
+                const int m = mt * 8 + gq;
+                uint32_t b0 = 0, b1 = 0;
+                if (m < M) {
+                  const uint2 xv = __ldg(reinterpret_cast<const uint2*>(X + (long long)m * ldx + kbase + 4 * j));
+                  b0 = xv.x; b1 = xv.y;
+                }
+                mma16816(acc[mt], a, b0, b1);
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(ebar + 8 * stage) : "memory");
+      }
+      if (++stage == kGvStages) { stage = 0; phase ^= 1; }
+    }
+    // cross-warp reduction of the tile (consumers only: named barrier 1)
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) red[((cw * MT + mt) * 32 + lane) * 4 + i] = acc[mt][i];
+    asm volatile("bar.sync 1, %0;" :: "r"(32 * kGvConsumers) : "memory");
+    if (cw == 0) {
+      const int n0 = tile * kGvRows;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int w = 0; w < kGvConsumers; ++w)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sacc[i] += red[((w * MT + mt) * 32 + lane) * 4 + i];
+        const int m0 = mt * 8 + 2 * tq;
+        const int na = n0 + gq, nb = n0 + gq + 8;
+        if (m0 < M && na < N) Y[(long long)m0 * ldy + na] = f2h(sacc[0]);
+        if (m0 + 1 < M && na < N) Y[(long long)(m0 + 1) * ldy + na] = f2h(sacc[1]);
+        if (m0 < M && nb < N) Y[(long long)m0 * ldy + nb] = f2h(sacc[2]);
+        if (m0 + 1 < M && nb < N) Y[(long long)(m0 + 1) * ldy + nb] = f2h(sacc[3]);
+      }
+    }
+    asm volatile("bar.sync 1, %0;" :: "r"(32 * kGvConsumers) : "memory");
+  }
+  if (!ok && lane == 0) atomicOr(err, (int)kDevTimeoutEpilogue);
+}
+
+int g_gv_sms = 0;
+
+template <int MT>
+int gemv_stream(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy, int* err,
+                cudaStream_t st) {
+  const int KC = (W.cols % kGvKC == 0) ? kGvKC : (W.cols % 512 == 0 ? 512 : (W.cols % 256 == 0 ? 256 : 0));
+  if (!KC) return kEInval;
+  if (!g_gv_sms) {
+    int d = 0; cudaGetDevice(&d);
+    cudaDeviceGetAttribute(&g_gv_sms, cudaDevAttrMultiProcessorCount, d);
+    if (g_gv_sms <= 0) g_gv_sms = 148;
+  }
+  const size_t smem = (size_t)kGvStages * kGvStageBytes + 2 * kGvStages * 8 + (size_t)kGvConsumers * MT * 32 * 16;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(fp4_gemv_stream_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return kECuda;
+    attr = true;
+  }
+  const int tiles = (W.rows + kGvRows - 1) / kGvRows;
+  const int grid = tiles < 3 * g_gv_sms ? tiles : 3 * g_gv_sms;
+  fp4_gemv_stream_kernel<MT><<<grid, 32 * (1 + kGvConsumers), smem, st>>>(
+      W.codes, W.scales, W.global_scale, W.rows, W.cols, KC, X, ldx, M, Y, ldy, err);
+  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+}
+
 template <int MT>
 int gemv_mt(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,
             cudaStream_t st) {
@@ -219,6 +418,16 @@ int launch_fp4_embed(const Fp4Weight& E, const long long* ids, int ntok, uint16_
   if (E.cols % 16 || ntok <= 0) return kEInval;
   fp4_embed_kernel<<<ntok, 256, 0, st>>>(E.codes, E.scales, E.global_scale, E.rows, E.cols, ids, ntok, out, err);
   return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+}
+
+int launch_fp4_gemv_stream(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,
+                           int* err, cudaStream_t st) {
+  if (M <= 0 || M > 64 || W.cols % 256 || ldx % 4 || !err) return kEInval;
+  if (((uintptr_t)W.codes % 16) || ((uintptr_t)W.scales % 16) || ((W.cols / 16) % 16)) return kEInval;
+  if (M <= 8) return gemv_stream<1>(W, X, ldx, M, Y, ldy, err, st);
+  if (M <= 16) return gemv_stream<2>(W, X, ldx, M, Y, ldy, err, st);
+  if (M <= 32) return gemv_stream<4>(W, X, ldx, M, Y, ldy, err, st);
+  return gemv_stream<8>(W, X, ldx, M, Y, ldy, err, st);
 }
 
 int launch_fp4_gemv(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,

@@ -19,6 +19,10 @@ int launch_fp4_decode(const Fp4Weight& W, uint16_t* out, long long ldo, cudaStre
 int launch_fp4_embed(const Fp4Weight& E, const long long* ids, int ntok, uint16_t* out, int* err, cudaStream_t st);
 int launch_fp4_gemv(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,
                     cudaStream_t st);
+// Same product through the bulk-copy pipelined kernel (cols % 256 == 0, 16-byte aligned rows);
+// `err` receives an error bit if a bounded wait expires.
+int launch_fp4_gemv_stream(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,
+                           int* err, cudaStream_t st);
 
 // tcgen05 GEMM: C[M,N] = A[M,K] . B[N,K]^T, fp16 in, fp32 accumulate in TMEM.
 // mode 0: store fp16 C.  mode 1: cross-entropy partials of fp16-rounded logits
