@@ -304,27 +304,26 @@ def main():
     gemm_s, gemm_flop = time_gemm_kernel(model, B * T, device)
     achieved = gemm_flop / gemm_s / 1e12
 
-    # batch-1 decode (greedy generation token step) on this GPU
+    # batch-1 decode (greedy generation token step, CUDA-graph replay) on this GPU
     decode = None
     if rank == 0 and args.decode_steps > 0:
         prompt = torch.from_numpy(wins[0, :64][None]).to(device)
         h = ex.backbone(prompt, reset=True)[:, -1]
-        tok = ex.greedy(h)
-        for _ in range(4):
-            h = ex.backbone(tok[:, None])[:, 0]
-            tok = ex.greedy(h)
+        tok = ex.greedy(h).clone()
+        ex.capture_decode(tok)
+        ex.replay_decode(4)
         torch.cuda.synchronize()
         d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         d0.record(s)
-        for _ in range(args.decode_steps):
-            h = ex.backbone(tok[:, None])[:, 0]
-            tok = ex.greedy(h)
+        ex.replay_decode(args.decode_steps)
         d1.record(s)
         torch.cuda.synchronize()
+        ex.check()
         dt = d0.elapsed_time(d1) / 1e3 / args.decode_steps
         roof = pk['hbm'] * 1e9 / DECODE_BYTES_B1
         decode = dict(tokens_per_s=1.0 / dt, ms_per_token=dt * 1e3, roofline_tokens_per_s=roof,
-                      frac=(1.0 / dt) / roof, bytes_per_token=DECODE_BYTES_B1, note='no CUDA graph; batch 1')
+                      frac=(1.0 / dt) / roof, bytes_per_token=DECODE_BYTES_B1,
+                      note='batch 1, 64-token prompt, CUDA-graph replay per token')
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -227,6 +227,13 @@ int sq_model_create(const sq_model_config* cfg, sq_model** out) {
   m->states.resize(cfg->n_layer);
   if (cudaMalloc(&m->d_err, sizeof(int)) != cudaSuccess) { delete m; return cuda_fail("cudaMalloc"); }
   cudaMemset(m->d_err, 0, sizeof(int));
+  // kernel attributes are set here, so later launches (and graph captures) never change them
+  if (prepare_scan_kernels() != kOk || prepare_fp4_kernels() != kOk || prepare_gemm_kernel() != kOk ||
+      prepare_layer_kernels() != kOk) {
+    cudaFree(m->d_err);
+    delete m;
+    return cuda_fail("kernel attribute setup");
+  }
   *out = m;
   return SQ_OK;
 }

@@ -286,15 +286,28 @@ fp4_gemv_stream_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restr
   const int subs = KC / 128;                      // 128-column sub-chunks per stage
   int stage = 0; uint32_t phase = 0; bool ok = true;
   for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-    float acc[MT][4];
+    float acc[MT][4], acc2[MT][4];          // two accumulator chains (even / odd k-steps)
 #pragma unroll
-    for (int i = 0; i < MT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    for (int i = 0; i < MT; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[i][e] = acc2[i][e] = 0.f;
     for (int kc = 0; kc < kchunks; ++kc) {
       if (ok && !gv_wait(fbar + 8 * stage, phase)) ok = false;
       if (ok) {
         const unsigned char* cs = gsm + stage * kGvStageBytes;
         const unsigned char* ss = cs + kGvCodeBytes;
         for (int sub = cw; sub < subs; sub += kGvConsumers) {
+          // all X (B-fragment) data of this sub-chunk first: 32 consecutive k per lane per m
+          const int kb0 = kc * KC + sub * 128 + tq * 32;
+          uint4 xr[MT][4];
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const int m = mt * 8 + gq;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              xr[mt][q] = (m < M) ? __ldg(reinterpret_cast<const uint4*>(X + (long long)m * ldx + kb0 + 8 * q))
+                                  : make_uint4(0, 0, 0, 0);
+          }
           const uint4 ca = *reinterpret_cast<const uint4*>(cs + gq * code_row + sub * 64 + tq * 16);
           const uint4 cb = *reinterpret_cast<const uint4*>(cs + (gq + 8) * code_row + sub * 64 + tq * 16);
           const uint16_t sa = *reinterpret_cast<const uint16_t*>(ss + gq * scale_row + sub * 8 + tq * 2);
@@ -303,7 +316,6 @@ fp4_gemv_stream_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restr
           const uint32_t wb[4] = {cb.x, cb.y, cb.z, cb.w};
           const uint32_t bsa0 = e4m3_splat_f16x2(sa & 0xFF), bsa1 = e4m3_splat_f16x2(sa >> 8);
           const uint32_t bsb0 = e4m3_splat_f16x2(sb & 0xFF), bsb1 = e4m3_splat_f16x2(sb >> 8);
-          const int kbase = kc * KC + sub * 128 + tq * 32;
 #pragma unroll
           for (int w4 = 0; w4 < 4; ++w4) {
             uint32_t ma[4], mb[4];
@@ -320,13 +332,10 @@ fp4_gemv_stream_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restr
               a[3] = scale_pair(mb[2 * jj + 1], bsB, g2);
 #pragma unroll
               for (int mt = 0; mt < MT; ++mt) {
-                const int m = mt * 8 + gq;
-                uint32_t b0 = 0, b1 = 0;
-                if (m < M) {
-                  const uint2 xv = __ldg(reinterpret_cast<const uint2*>(X + (long long)m * ldx + kbase + 4 * j));
-                  b0 = xv.x; b1 = xv.y;
-                }
-                mma16816(acc[mt], a, b0, b1);
+                // x[m][kb0 + 4j .. +3] = 16-byte word j/2, half (j&1)
+                const uint4 xq = xr[mt][j >> 1];
+                const uint32_t b0 = (j & 1) ? xq.z : xq.x, b1 = (j & 1) ? xq.w : xq.y;
+                mma16816((j & 1) ? acc2[mt] : acc[mt], a, b0, b1);
               }
             }
           }
@@ -340,7 +349,7 @@ fp4_gemv_stream_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restr
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) red[((cw * MT + mt) * 32 + lane) * 4 + i] = acc[mt][i];
+      for (int i = 0; i < 4; ++i) red[((cw * MT + mt) * 32 + lane) * 4 + i] = acc[mt][i] + acc2[mt][i];
     asm volatile("bar.sync 1, %0;" :: "r"(32 * kGvConsumers) : "memory");
     if (cw == 0) {
       const int n0 = tile * kGvRows;
@@ -369,7 +378,7 @@ template <int MT>
 int gemv_stream(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy, int* err,
                 cudaStream_t st) {
   const int KC = (W.cols % kGvKC == 0) ? kGvKC : (W.cols % 512 == 0 ? 512 : (W.cols % 256 == 0 ? 256 : 0));
-  if (!KC) return kEInval;
+  if (!KC && W.codes) return kEInval;
   if (!g_gv_sms) {
     int d = 0; cudaGetDevice(&d);
     cudaDeviceGetAttribute(&g_gv_sms, cudaDevAttrMultiProcessorCount, d);
@@ -383,6 +392,7 @@ int gemv_stream(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uin
       return kECuda;
     attr = true;
   }
+  if (!W.codes) return kOk;                          // prepare-only call
   const int tiles = (W.rows + kGvRows - 1) / kGvRows;
   const int grid = tiles < 3 * g_gv_sms ? tiles : 3 * g_gv_sms;
   fp4_gemv_stream_kernel<MT><<<grid, 32 * (1 + kGvConsumers), smem, st>>>(
@@ -420,10 +430,18 @@ int launch_fp4_embed(const Fp4Weight& E, const long long* ids, int ntok, uint16_
   return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
 }
 
+int prepare_fp4_kernels() {
+  Fp4Weight none{nullptr, nullptr, nullptr, 0, 1024};
+  int st = gemv_stream<1>(none, nullptr, 0, 1, nullptr, 0, nullptr, 0) | gemv_stream<2>(none, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
+           gemv_stream<4>(none, nullptr, 0, 1, nullptr, 0, nullptr, 0) | gemv_stream<8>(none, nullptr, 0, 1, nullptr, 0, nullptr, 0);
+  return st ? kECuda : kOk;
+}
+
 int launch_fp4_gemv_stream(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,
                            int* err, cudaStream_t st) {
-  if (M <= 0 || M > 64 || W.cols % 256 || ldx % 4 || !err) return kEInval;
-  if (((uintptr_t)W.codes % 16) || ((uintptr_t)W.scales % 16) || ((W.cols / 16) % 16)) return kEInval;
+  if (M <= 0 || M > 64 || W.cols % 256 || ldx % 8 || !err) return kEInval;
+  if (((uintptr_t)W.codes % 16) || ((uintptr_t)W.scales % 16) || ((uintptr_t)X % 16) || ((W.cols / 16) % 16))
+    return kEInval;
   if (M <= 8) return gemv_stream<1>(W, X, ldx, M, Y, ldy, err, st);
   if (M <= 16) return gemv_stream<2>(W, X, ldx, M, Y, ldy, err, st);
   if (M <= 32) return gemv_stream<4>(W, X, ldx, M, Y, ldy, err, st);

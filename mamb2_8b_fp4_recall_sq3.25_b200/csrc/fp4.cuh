@@ -39,5 +39,8 @@ int launch_gemm_f16(const uint16_t* A, long long lda, const uint16_t* B, long lo
                     uint16_t* C, long long ldc, int M, int N, int K, int mode, const GemmCE* ce,
                     int* dev_err, cudaStream_t st);
 int gemm_num_ntiles(int N);
+int prepare_fp4_kernels();
+int prepare_gemm_kernel();
+int prepare_layer_kernels();
 
 }  // namespace sq

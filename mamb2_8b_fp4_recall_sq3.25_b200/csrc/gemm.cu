@@ -322,6 +322,16 @@ int g_num_sms = 0;
 
 int gemm_num_ntiles(int N) { return (N + BN - 1) / BN; }
 
+static bool g_gemm_attr = false;
+int prepare_gemm_kernel() {
+  if (g_gemm_attr) return kOk;
+  const size_t smem = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+  if (cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return kECuda;
+  g_gemm_attr = true;
+  return kOk;
+}
+
 int launch_gemm_f16(const uint16_t* A, long long lda, const uint16_t* B, long long ldb,
                     uint16_t* C, long long ldc, int M, int N, int K, int mode, const GemmCE* ce,
                     int* dev_err, cudaStream_t st) {
@@ -338,12 +348,7 @@ int launch_gemm_f16(const uint16_t* A, long long lda, const uint16_t* B, long lo
     if (g_num_sms <= 0) g_num_sms = 148;
   }
   const size_t smem = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return kECuda;
-    attr = true;
-  }
+  if (prepare_gemm_kernel() != kOk) return kECuda;
   GemmArgs a;
   a.M = M; a.N = N; a.K = K; a.C = C; a.ldc = ldc; a.mode = mode;
   a.targets = ce ? ce->targets : nullptr; a.partials = ce ? ce->partials : nullptr;

@@ -140,83 +140,97 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], u
                : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__global__ void __launch_bounds__(256)
+template <int GPB>
+__global__ void __launch_bounds__(32 * GPB)
 resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __restrict__ z, long long z_st,
                            const uint16_t* __restrict__ u, long long u_st, AdapterPtrs ad, int has_ad,
                            const uint16_t* __restrict__ nw, float eps, uint16_t* __restrict__ out, int T) {
   extern __shared__ __align__(16) unsigned char smraw[];
-  const int gpb = blockDim.x >> 5;
-  uint16_t* Ys = reinterpret_cast<uint16_t*>(smraw);                  // [128][kYPitch]
-  uint16_t* Vs = Ys + 128 * kYPitch;                                  // [gpb*16][kVPitch]
-  __shared__ float spart[8];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint16_t* Ys = reinterpret_cast<uint16_t*>(smraw);                  // [128][kYPitch]   this token's y
+  uint16_t* Vs = Ys + 128 * kYPitch;                                  // [GPB*16][kVPitch] V rows
+  uint16_t* Zs = Vs + GPB * 16 * kVPitch;                             // [GPB][1024]      this token's z
+  uint16_t* Ns = Zs + GPB * 1024;                                     // [GPB][1024]      norm weights
+  uint16_t* Us = Ns + GPB * 1024;                                     // [4096]           mixer input u
+  uint16_t* Ws = Us + 4096;                                           // [4096]           gate weights
+  __shared__ float spart[GPB];
+  const int tid = threadIdx.x, nth = 32 * GPB;
+  const int warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, tq = lane & 3;
-  const int grp = blockIdx.x * gpb + warp;                            // norm group of this warp
-  const int vrow0 = blockIdx.x * gpb * 16;                            // first V row staged here
-  if (has_ad)
-    for (int i = threadIdx.x; i < gpb * 16 * 16; i += blockDim.x) {  // 16-byte chunks of V rows
+  const int grp0 = blockIdx.x * GPB;
+  const int grp = grp0 + warp;                                        // norm group of this warp
+  // per-CTA constants: V rows of the CTA's groups, gate weights, norm weights
+  if (has_ad) {
+    for (int i = tid; i < GPB * 16 * 16; i += nth) {
       const int r = i >> 4, c = (i & 15) * 8;
-      cp_async16(Vs + r * kVPitch + c, ad.V + (vrow0 + r) * 128 + c);
+      cp_async16(Vs + r * kVPitch + c, ad.V + (grp0 * 16 + r) * 128 + c);
     }
+    stage16(Ws, ad.w, 4096 * 2, tid, nth);
+  }
+  stage16(Ns, nw + grp0 * 1024, GPB * 1024 * 2, tid, nth);
   for (int t = blockIdx.y; t < T; t += gridDim.y) {
-    __syncthreads();                                   // previous token done with Ys / spart
+    __syncthreads();                                   // previous token done with the staged rows
     const uint16_t* yr = y + (long long)t * 8192;
-    for (int i = threadIdx.x; i < 128 * 8; i += blockDim.x) {        // stage y[j][p] (16 B chunks)
+    for (int i = tid; i < 128 * 8; i += nth) {         // y[j][p] in 16-byte chunks
       const int r = i >> 3, c = (i & 7) * 8;
       cp_async16(Ys + r * kYPitch + c, yr + r * 64 + c);
     }
+    stage16(Zs, z + (long long)t * z_st + grp0 * 1024, GPB * 1024 * 2, tid, nth);
+    if (has_ad) stage16(Us, u + (long long)t * u_st, 4096 * 2, tid, nth);
+    cp_async_wait_all();
+    __syncthreads();
+    float gate = 0.f;
     if (has_ad) {
-      // gate logit partials: fp16(u . w) + b (fp16), deterministic gpb-way split
+      // gate logit = fp16(fp16(u . w) + b): deterministic GPB-way split, then the same sum in every warp
+      constexpr int span = 4096 / GPB;
       float s = 0.f;
-      const int span = 4096 / gpb;
-      const uint16_t* ur = u + (long long)t * u_st + warp * span;
-      const uint16_t* wr = ad.w + warp * span;
-      for (int i = lane * 8; i < span; i += 256) {
-        const uint4 uv = *reinterpret_cast<const uint4*>(ur + i);
-        const uint4 wv = *reinterpret_cast<const uint4*>(wr + i);
+#pragma unroll 4
+      for (int i = warp * span + lane * 8; i < (warp + 1) * span; i += 256) {
+        const uint4 uv = *reinterpret_cast<const uint4*>(Us + i);
+        const uint4 wv = *reinterpret_cast<const uint4*>(Ws + i);
         const uint16_t* up = reinterpret_cast<const uint16_t*>(&uv);
         const uint16_t* wp = reinterpret_cast<const uint16_t*>(&wv);
 #pragma unroll
         for (int k = 0; k < 8; ++k) s = fmaf(h2f(up[k]), h2f(wp[k]), s);
       }
       s = warp_sum(s);
-      if (lane == 0) spart[warp] = s;
+      if (GPB > 1) {
+        if (lane == 0) spart[warp] = s;
+        __syncthreads();
+        s = 0.f;
+#pragma unroll
+        for (int w = 0; w < GPB; ++w) s += spart[w];
+      }
+      const float lg = h2f(f2h(h2f(f2h(s)) + h2f(ad.b[0])));
+      gate = h2f(f2h(ad.hard ? (lg > 0.f ? 1.f : 0.f) : 1.0f / (1.0f + expf(-lg))));
     }
-    cp_async_wait_all();
-    __syncthreads();
     float acc[8][4];
 #pragma unroll
     for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-    float gate = 0.f;
     if (has_ad) {
-      float tot = 0.f;
-#pragma unroll
-      for (int w = 0; w < gpb; ++w) tot += spart[w];
-      const float lg = h2f(f2h(h2f(f2h(tot)) + h2f(ad.b[0])));
-      gate = h2f(f2h(ad.hard ? (lg > 0.f ? 1.f : 0.f) : 1.0f / (1.0f + expf(-lg))));
       const int i0 = warp * 16;                        // local V row of this warp's heads
+      const int mi = lane >> 3, rr = lane & 7;
 #pragma unroll
       for (int k0 = 0; k0 < 128; k0 += 16) {
         uint32_t a[4];
         // matrices: (rows i0..+7, k0), (i0+8.., k0), (i0.., k0+8), (i0+8.., k0+8)
-        const int mi = lane >> 3, rr = lane & 7;
         ldsm_x4(a, Vs + (i0 + rr + (mi & 1) * 8) * kVPitch + k0 + (mi >> 1) * 8);
 #pragma unroll
         for (int n2 = 0; n2 < 4; ++n2) {
           uint32_t bfr[4];
           // matrices: (j k0..+7, p n), (j k0+8.., p n), (j k0.., p n+8), (j k0+8.., p n+8)
-          const int pn = n2 * 16 + (mi >> 1) * 8;
-          ldsm_x4_t(bfr, Ys + (k0 + rr + (mi & 1) * 8) * kYPitch + pn);
+          ldsm_x4_t(bfr, Ys + (k0 + rr + (mi & 1) * 8) * kYPitch + n2 * 16 + (mi >> 1) * 8);
           mma_f16(acc[2 * n2], a, bfr[0], bfr[1]);
           mma_f16(acc[2 * n2 + 1], a, bfr[2], bfr[3]);
         }
       }
     }
     // epilogue: correction, gated RMSNorm over this warp's group (1024 channels)
-    const uint16_t* zr = z + (long long)t * z_st;
+    const uint16_t* zs = Zs + warp * 1024;
+    const uint16_t* ns = Ns + warp * 1024;
     float xv[8][4];
     float ss = 0.f;
-    const int ia = grp * 16 + gq, ib = ia + 8;
+    const int ia = grp * 16 + gq, ib = ia + 8;          // heads (global)
+    const int la = gq, lb = gq + 8;                      // heads within the group
     const float ga = has_ad ? h2f(f2h(gate * h2f(ad.g[ia]))) : 0.f;
     const float gb = has_ad ? h2f(f2h(gate * h2f(ad.g[ib]))) : 0.f;
 #pragma unroll
@@ -224,7 +238,7 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
       const int p0 = n * 8 + 2 * tq;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int i = (e < 2) ? ia : ib;
+        const int i = (e < 2) ? ia : ib, li = (e < 2) ? la : lb;
         const int pp = p0 + (e & 1);
         float yv = h2f(Ys[i * kYPitch + pp]);
         if (has_ad) {
@@ -232,7 +246,7 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
           const float corr = h2f(f2h(((e < 2) ? ga : gb) * mix));
           yv = h2f(f2h(yv + corr));
         }
-        const float zz = h2f(zr[i * 64 + pp]);
+        const float zz = h2f(zs[li * 64 + pp]);
         const float x = yv * (zz * (1.0f / (1.0f + expf(-zz))));
         xv[n][e] = x;
         ss += x * x;
@@ -245,12 +259,11 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
       const int p0 = n * 8 + 2 * tq;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
-        const int i = half ? ib : ia;
-        const int ch = i * 64 + p0;
-        const float o0 = (xv[n][2 * half] * rstd) * h2f(nw[ch]);
-        const float o1 = (xv[n][2 * half + 1] * rstd) * h2f(nw[ch + 1]);
+        const int li = half ? lb : la;
+        const float o0 = (xv[n][2 * half] * rstd) * h2f(ns[li * 64 + p0]);
+        const float o1 = (xv[n][2 * half + 1] * rstd) * h2f(ns[li * 64 + p0 + 1]);
         __half2 hv = __floats2half2_rn(o0, o1);
-        *reinterpret_cast<__half2*>(out + (long long)t * 8192 + ch) = hv;
+        *reinterpret_cast<__half2*>(out + (long long)t * 8192 + grp * 1024 + li * 64 + p0) = hv;
       }
     }
   }
@@ -352,28 +365,49 @@ int launch_conv_prefill(const uint16_t* raw, long long raw_sb, long long raw_st,
   return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
 }
 
+template <int GPB>
+int launch_rg(const uint16_t* y, const uint16_t* z, long long z_st, const uint16_t* u, long long u_st,
+              const AdapterPtrs& a, int has_ad, const uint16_t* norm_w, float eps, uint16_t* out, int T, int ty,
+              cudaStream_t st) {
+  const size_t smem = (size_t)(128 * kYPitch + GPB * 16 * kVPitch + 2 * GPB * 1024 + 2 * 4096) * 2;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(resurface_gatednorm_kernel<GPB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return kECuda;
+    attr = true;
+  }
+  if (!y) return kOk;                                // prepare-only call
+  dim3 grid(8 / GPB, ty);
+  resurface_gatednorm_kernel<GPB><<<grid, 32 * GPB, smem, st>>>(y, z, z_st, u, u_st, a, has_ad, norm_w, eps, out, T);
+  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+}
+
+int prepare_layer_kernels() {
+  AdapterPtrs a{};
+  int st = launch_rg<1>(nullptr, nullptr, 0, nullptr, 0, a, 0, nullptr, 0.f, nullptr, 0, 0, 0) |
+           launch_rg<8>(nullptr, nullptr, 0, nullptr, 0, a, 0, nullptr, 0.f, nullptr, 0, 0, 0);
+  return st ? kECuda : kOk;
+}
+
 int launch_resurface_gatednorm(const uint16_t* y, const uint16_t* z, long long z_st, const uint16_t* u,
                                long long u_st, const AdapterPtrs* ad, const uint16_t* norm_w, float eps,
                                uint16_t* out, int T, cudaStream_t st) {
   if (T <= 0) return kEInval;
+  if (((uintptr_t)y % 16) || ((uintptr_t)z % 16) || ((uintptr_t)u % 16) || ((uintptr_t)norm_w % 16) ||
+      (z_st % 8) || (u_st % 8))
+    return kEInval;
   const int has_ad = ad && ad->V;
   AdapterPtrs a{};
-  if (has_ad) a = *ad;
+  if (has_ad) {
+    a = *ad;
+    if (((uintptr_t)a.V % 16) || ((uintptr_t)a.w % 16)) return kEInval;
+  }
   // few tokens: one warp (one norm group) per CTA spreads a token over 8 SMs;
   // many tokens: 8 warps per CTA share one staged copy of each token's y
-  const int gpb = T < 64 ? 1 : 8;
-  const size_t smem = (size_t)(128 * kYPitch + gpb * 16 * kVPitch) * 2;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(resurface_gatednorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (128 * kYPitch + 128 * kVPitch) * 2) != cudaSuccess)
-      return kECuda;
-    attr = true;
-  }
-  const int ty = gpb == 8 ? (T < 3 * num_sms() ? T : 3 * num_sms()) : T;
-  dim3 grid(8 / gpb, ty);
-  resurface_gatednorm_kernel<<<grid, 32 * gpb, smem, st>>>(y, z, z_st, u, u_st, a, has_ad, norm_w, eps, out, T);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  if (T < 64) return launch_rg<1>(y, z, z_st, u, u_st, a, has_ad, norm_w, eps, out, T, T, st);
+  const int ty = T < 2 * num_sms() ? T : 2 * num_sms();
+  return launch_rg<8>(y, z, z_st, u, u_st, a, has_ad, norm_w, eps, out, T, ty, st);
 }
 
 int launch_ce_finalize(const float2* partials, int ntiles, const float* tlogit, int rows, float* nll,

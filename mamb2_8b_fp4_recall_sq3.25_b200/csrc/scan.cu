@@ -16,6 +16,8 @@
 // the TC recurrence steps on its row with packed fp32x2 arithmetic.  The next chunk's
 // raw inputs are prefetched into registers while the current one is computed.  Packed
 // rows are read once at the start and written once at the end of the call.
+#include <algorithm>
+
 #include "common.cuh"
 #include "scan.cuh"
 
@@ -60,20 +62,22 @@ __device__ __forceinline__ float requant(float q, float lim) {
   return fminf(fmaxf(round_half_away(q), -lim), lim);
 }
 
-template <int N8, int N4, int KJ, int MODE>
+template <int N8, int N4, int KJ, int MODE, int TC>
 __global__ void __launch_bounds__(128)
 ssu_sq325_kernel(const ScanParams P) {
   constexpr int NZ = 128 - N8 - N4;
   constexpr int F = N8 + N4 + 2;
   constexpr int W8 = N8 / 2, W4 = N4 / 2;
   constexpr int NP = (N8 + N4) / 2;            // stored coordinate pairs
-  constexpr int TC = kTC;
   static_assert(N8 % 2 == 0 && N4 % 2 == 0, "tiers are nibble pairs");
 
   extern __shared__ __align__(16) unsigned char smem[];
+  constexpr int kTables = (TC * 64 * 16 > F * NZ * 2 + 16 + NZ * 4) ? TC * 64 * 16 : F * NZ * 2 + 16 + NZ * 4;
+  constexpr int kTablesA = (kTables + 15) / 16 * 16;
+  constexpr int kV2 = (TC * 64 * 8 > 128) ? TC * 64 * 8 : 128;
   float4* sP4 = reinterpret_cast<float4*>(smem);                     // [TC][64] {b_j,b_j+1,c_j,c_j+1}
-  float2* sV2 = reinterpret_cast<float2*>(sP4 + TC * 64);            // [TC][64] {cvec_j,cvec_j+1}
-  float* sDots = reinterpret_cast<float*>(sV2 + TC * 64);            // [TC][8]
+  float2* sV2 = reinterpret_cast<float2*>(smem + kTablesA);          // [TC][64] {cvec_j,cvec_j+1}
+  float* sDots = reinterpret_cast<float*>(smem + kTablesA + kV2);    // [TC][8]
   float* sDD = sDots + TC * 8;                                       // [TC][kMaxHpc][2] (dt, decay)
   float* sX = sDD + TC * kMaxHpc * 2;                                // [TC][blockDim] own x value
   unsigned char* sPack = reinterpret_cast<unsigned char*>(sX + TC * 128);   // rows*52 (16-B aligned)
@@ -200,7 +204,7 @@ ssu_sq325_kernel(const ScanParams P) {
 
   // ---- raw-input prefetch (registers) ----
   // packed raw prefetch: x of token pairs, and (B | C << 16) per owned coordinate
-  uint32_t pre_x[TC / 2], pre_bc[TC][KJ];
+  uint32_t pre_x[(TC + 1) / 2], pre_bc[TC][KJ];
   uint16_t pre_dt = 0;
   auto prefetch = [&](int c0) {
     const int nt = min(TC, P.length - c0);
@@ -427,22 +431,25 @@ ssu_sq325_kernel(const ScanParams P) {
   copy_out(reinterpret_cast<unsigned char*>(P.s4 + row0), reinterpret_cast<unsigned char*>(pS4), rows * 2);
 }
 
-template <int N8, int N4, int KJ, int MODE>
+template <int N8, int N4, int KJ, int MODE, int TC = (MODE == 2 ? 1 : kTC)>
 int launch_kj(const ScanParams& P, int hpc, cudaStream_t stream) {
   constexpr int NZ = 128 - N8 - N4;
   constexpr int F = N8 + N4 + 2;
   const int bd = hpc * P.dim;
-  const size_t smem = (size_t)kTC * 64 * 16 + (size_t)kTC * 64 * 8 + (size_t)kTC * 8 * 4 +
-                      (size_t)kTC * kMaxHpc * 2 * 4 + (size_t)kTC * 128 * 4 + 128 * 52 +
+  // token tables are also the raw staging area of the predictor table (F*NZ fp16 + basis)
+  const size_t tables = (std::max((size_t)TC * 64 * 16, (size_t)F * NZ * 2 + 16 + NZ * 4) + 15) / 16 * 16;
+  const size_t smem = tables + std::max((size_t)TC * 64 * 8, (size_t)128) + (size_t)TC * 8 * 4 +
+                      (size_t)TC * kMaxHpc * 2 * 4 + (size_t)TC * 128 * 4 + 128 * 52 +
                       (size_t)F * (NZ + 1) * 4 + 2 * NZ * 4 + 128 * 4;
   (void)bd;
-  auto kern = ssu_sq325_kernel<N8, N4, KJ, MODE>;
+  auto kern = ssu_sq325_kernel<N8, N4, KJ, MODE, TC>;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) != cudaSuccess)
       return kECuda;
     attr = true;
   }
+  if (hpc == 0) return kOk;                         // prepare-only call (attributes set, no launch)
   dim3 grid(P.heads / hpc, P.batch);
   kern<<<grid, bd, smem, stream>>>(P);
   return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
@@ -459,6 +466,26 @@ int launch_t(const ScanParams& P, int hpc, cudaStream_t stream) {
 }
 
 }  // namespace
+
+template <int N8, int N4>
+int prepare_t() {
+  ScanParams P{};
+  int st = kOk;
+  st |= launch_kj<N8, N4, 1, 0>(P, 0, 0);
+  st |= launch_kj<N8, N4, 2, 0>(P, 0, 0);
+  st |= launch_kj<N8, N4, 4, 0>(P, 0, 0);
+  st |= launch_kj<N8, N4, 1, 1>(P, 0, 0);
+  st |= launch_kj<N8, N4, 1, 2>(P, 0, 0);
+  return st;
+}
+
+// Sets the shared-memory attributes of every scan instantiation up front (a graph capture
+// must not be the first launch of a kernel that needs an attribute change).
+int prepare_scan_kernels() {
+  int st = prepare_t<32, 28>() | prepare_t<16, 60>() | prepare_t<8, 76>() | prepare_t<24, 44>() |
+           prepare_t<36, 20>() | prepare_t<40, 12>() | prepare_t<44, 4>();
+  return st ? kECuda : kOk;
+}
 
 int launch_scan(const ScanParams& P, cudaStream_t stream) {
   if (P.layout < 0 || P.layout > 6) return kEInval;

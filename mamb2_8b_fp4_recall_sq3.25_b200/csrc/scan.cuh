@@ -44,5 +44,6 @@ struct ScanParams {
 };
 
 int launch_scan(const ScanParams& p, cudaStream_t stream);
+int prepare_scan_kernels();
 
 }  // namespace sq

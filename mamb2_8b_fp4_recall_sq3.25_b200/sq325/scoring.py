@@ -84,13 +84,27 @@ def evaluate_ppl(execution, windows, batch_windows=16, rank=0, world=1, group=No
 
 
 @torch.no_grad()
-def generate(execution, prompt_ids, max_new_tokens, eos_token_id=None):
-    """Greedy decode: returns int64 [batch, n_generated] (n <= max_new_tokens)."""
+def generate(execution, prompt_ids, max_new_tokens, eos_token_id=None, graphs=False):
+    """Greedy decode: returns int64 [batch, n_generated] (n <= max_new_tokens).
+
+    graphs=True replays a captured CUDA graph per token (no host synchronisation inside
+    the loop; an EOS stop is then applied after the fact by truncation)."""
     dev = execution.device
     prompt = torch.as_tensor(prompt_ids, dtype=torch.long).to(dev)
     if prompt.ndim == 1:
         prompt = prompt[None]
     hidden = execution.backbone(prompt.contiguous(), reset=True)[:, -1]
+    if graphs:
+        tok = execution.greedy(hidden).clone()
+        first = tok.clone()
+        execution.capture_decode(tok)
+        rest = execution.replay_decode(max_new_tokens - 1) if max_new_tokens > 1 else None
+        seq = first[:, None] if rest is None else torch.cat([first[:, None], rest.T], 1)
+        if eos_token_id is not None:
+            hit = (seq == eos_token_id).all(0).nonzero()
+            if hit.numel():
+                seq = seq[:, :int(hit[0]) + 1]
+        return seq
     out = []
     for step in range(max_new_tokens):
         tok = execution.greedy(hidden)

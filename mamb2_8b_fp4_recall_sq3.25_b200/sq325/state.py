@@ -221,6 +221,50 @@ class PredictorState:
                   _lib.stream_ptr())
         return tok
 
+    # ------------------------------------------------------------------ graphed decode
+    @torch.no_grad()
+    def capture_decode(self, tokens):
+        """Capture the one-token greedy step (forward + lm_head + argmax) as CUDA graphs.
+
+        `tokens` is an int64 [batch] device tensor that the graph reads as this step's input
+        and overwrites with the argmax token, so replays chain without host round trips.
+        The conv ring slot depends on position % 4, so four graphs are captured (one per
+        residue) and replayed in turn.  Requires a prefilled request (tokens > 0)."""
+        if not self._cache or self._cache[0].tokens == 0:
+            raise RuntimeError('Prefill the request before capturing decode graphs')
+        B = self._batch_size
+        if tokens.shape != (B,) or tokens.dtype != torch.long or tokens.device != self.device:
+            raise ValueError('tokens must be CUDA int64 [batch]')
+        self.reserve(B)
+        self._graph_tokens = tokens
+        self._graph_hidden = torch.empty((B, 1, D_MODEL), device=self.device, dtype=torch.float16)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        self._graphs = []
+        with torch.cuda.stream(side):
+            for r in range(4):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=side):
+                    sp = C.c_void_p(side.cuda_stream)
+                    _lib.call('sq_model_forward', self._handle, _lib.ptr(tokens), B, 1, 4 + r,
+                              _lib.ptr(self._graph_hidden), sp)
+                    _lib.call('sq_model_greedy', self._handle, _lib.ptr(self._graph_hidden), B, None,
+                              _lib.ptr(tokens), sp)
+                self._graphs.append(g)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        return self._graphs
+
+    @torch.no_grad()
+    def replay_decode(self, steps):
+        """Advance `steps` greedy tokens by graph replay; returns int64 [steps, batch]."""
+        out = torch.empty((steps, self._batch_size), device=self.device, dtype=torch.long)
+        for i in range(steps):
+            self._graphs[self._cache[0].tokens % 4].replay()
+            for e in self._cache:
+                e.tokens += 1
+            out[i].copy_(self._graph_tokens)
+        return out
+
     def check(self):
         """Synchronise and raise if a device-side check failed (bad token id, expired wait)."""
         _lib.call('sq_model_check', self._handle, _lib.stream_ptr())

@@ -121,3 +121,17 @@ def test_scoring_driver_pooled_ppl(pair):
         total += ref
     assert math.isclose(res['nll'], total, rel_tol=NLL_RTOL)
     assert res['target_tokens'] == sum(len(w) - 1 for _, w in windows)
+
+
+def test_graphed_decode_matches_eager(pair):
+    """Greedy tokens from CUDA-graph replays (four residue graphs) equal the eager loop."""
+    from sq325 import PredictorState, generate
+    gm, _, statics = pair
+    prompt = np.random.default_rng(21).integers(0, gm.vocab, (2, 9))
+    with PredictorState(gm, *statics) as ex:
+        eager = generate(ex, prompt, 11)
+        graphed = generate(ex, prompt, 11, graphs=True)
+        torch.cuda.synchronize()
+        ex.check()
+    assert eager.shape == (2, 11)
+    assert torch.equal(eager.cpu(), graphed.cpu())
