@@ -59,6 +59,8 @@ struct sq_model {
   sq_model_config cfg;
   std::vector<sq_layer_desc> layers;
   std::vector<AdapterPtrs> adapters;
+  std::vector<Fp4Maps> in_maps, out_maps;     // streaming-GEMV TMA descriptors per layer
+  Fp4Maps head_maps{};
   struct St { int batch = 0; uint8_t *lo = 0, *hi = 0, *q4 = 0, *latent = 0; uint16_t *s8 = 0, *s4 = 0, *ring = 0; };
   std::vector<St> states;
   sq_fp4_matrix embed{}, head{};
@@ -86,10 +88,10 @@ void free_ws(sq_model* m) {
   m->max_tokens = 0;
 }
 
-int linear(sq_model* m, const sq_fp4_matrix& W, const uint16_t* X, long long ldx, int M, uint16_t* Y,
-           long long ldy, cudaStream_t st) {
+int linear(sq_model* m, const sq_fp4_matrix& W, const Fp4Maps* maps, const uint16_t* X, long long ldx, int M,
+           uint16_t* Y, long long ldy, cudaStream_t st) {
   const Fp4Weight w = fw(W);
-  if (M <= 64) return check(launch_fp4_gemv_stream(w, X, ldx, M, Y, ldy, m->d_err, st), "fp4 gemv");
+  if (M <= 64) return check(launch_fp4_gemv_stream(w, maps, X, ldx, M, Y, ldy, m->d_err, st), "fp4 gemv");
   if ((size_t)W.rows * W.cols > m->stage_elems) return fail(SQ_EINVAL, "staging buffer too small");
   SQ_TRY(launch_fp4_decode(w, m->stage, W.cols, st), "fp4 decode");
   return check(launch_gemm_f16(X, ldx, m->stage, W.cols, Y, ldy, M, W.rows, W.cols, 0, nullptr, m->d_err, st),
@@ -186,8 +188,8 @@ int sq_fp4_linear(const uint8_t* codes, const uint8_t* block_scales, const float
     cudaMemset(d_err, 0, sizeof(int));
   }
   if (m <= 64) {
-    if (k % 256 == 0 && aligned(block_scales, 16))
-      return check(launch_fp4_gemv_stream(w, x, ldx, m, y, ldy, d_err, st), "fp4 gemv");
+    if (k % 256 == 0 && aligned(block_scales, 16) && aligned(x, 16) && ldx % 8 == 0)
+      return check(launch_fp4_gemv_stream(w, nullptr, x, ldx, m, y, ldy, d_err, st), "fp4 gemv");
     return check(launch_fp4_gemv(w, x, ldx, m, y, ldy, st), "fp4 gemv");
   }
   if (!workspace || workspace_bytes < sq_fp4_linear_workspace(m, n, k) || !aligned(workspace, 16))
@@ -224,6 +226,8 @@ int sq_model_create(const sq_model_config* cfg, sq_model** out) {
   m->layers.resize(cfg->n_layer);
   std::memset(m->layers.data(), 0, sizeof(sq_layer_desc) * cfg->n_layer);
   m->adapters.assign(cfg->n_layer, AdapterPtrs{});
+  m->in_maps.assign(cfg->n_layer, Fp4Maps{});
+  m->out_maps.assign(cfg->n_layer, Fp4Maps{});
   m->states.resize(cfg->n_layer);
   if (cudaMalloc(&m->d_err, sizeof(int)) != cudaSuccess) { delete m; return cuda_fail("cudaMalloc"); }
   cudaMemset(m->d_err, 0, sizeof(int));
@@ -262,6 +266,8 @@ int sq_model_set_layer(sq_model* m, int layer, const sq_layer_desc* d) {
   if (!aligned(d->permutation, 16) || !aligned(d->basis, 16) || !aligned(d->predictor, 16))
     return fail(SQ_EINVAL, "set_layer: permutation / basis / predictor must be 16-byte aligned");
   m->layers[layer] = *d;
+  if (!make_fp4_maps(fw(d->in_proj), &m->in_maps[layer]) || !make_fp4_maps(fw(d->out_proj), &m->out_maps[layer]))
+    return fail(SQ_EINVAL, "set_layer: projection rows must be 16-byte aligned for the TMA streams");
   return SQ_OK;
 }
 
@@ -270,6 +276,7 @@ int sq_model_set_globals(sq_model* m, const sq_fp4_matrix* e, const sq_fp4_matri
   if (!fp4_ok(*e, m->cfg.vocab, kDModel) || !fp4_ok(*h, m->cfg.vocab, kDModel))
     return fail(SQ_EINVAL, "set_globals: embedding / lm_head must be [vocab,4096]");
   m->embed = *e; m->head = *h; m->norm_f = nf;
+  if (!make_fp4_maps(fw(*h), &m->head_maps)) return fail(SQ_EINVAL, "set_globals: lm_head rows must be 16-byte aligned");
   return SQ_OK;
 }
 
@@ -345,7 +352,7 @@ int sq_model_forward(sq_model* m, const int64_t* ids, int batch, int tokens, int
     if (!L.in_proj.codes) return fail(SQ_ESTATE, "forward: layer weights not set");
     if (S.batch != batch) return fail(SQ_ESTATE, "forward: state batch differs from the call (reset required)");
     SQ_TRY(launch_add_rmsnorm(m->h, m->res, l > 0, L.norm_weight, m->cfg.eps, m->hn, M, kDModel, st), "add_rmsnorm");
-    int s = linear(m, L.in_proj, m->hn, kDModel, M, m->zx, kZx, st);
+    int s = linear(m, L.in_proj, &m->in_maps[l], m->hn, kDModel, M, m->zx, kZx, st);
     if (s != SQ_OK) return s;
     ScanParams P{};
     P.batch = batch; P.length = tokens; P.heads = kHeads; P.dim = kHeadDim; P.groups = kGroups; P.layout = L.layout;
@@ -374,7 +381,7 @@ int sq_model_forward(sq_model* m, const int64_t* ids, int batch, int tokens, int
     const AdapterPtrs& ad = m->adapters[l];
     SQ_TRY(launch_resurface_gatednorm(m->y, m->zx, kZx, m->hn, kDModel, ad.V ? &ad : nullptr, L.gated_norm_weight,
                                       m->cfg.eps, m->yn, M, st), "resurface + gated norm");
-    s = linear(m, L.out_proj, m->yn, kDInner, M, m->h, kDModel, st);
+    s = linear(m, L.out_proj, &m->out_maps[l], m->yn, kDInner, M, m->h, kDModel, st);
     if (s != SQ_OK) return s;
   }
   SQ_TRY(launch_add_rmsnorm(m->h, m->res, 1, m->norm_f, m->cfg.eps, hidden_out, M, kDModel, st), "norm_f");
@@ -411,7 +418,8 @@ int sq_model_greedy(sq_model* m, const uint16_t* hidden, int rows, uint16_t* log
   if (!m->logits) return fail(SQ_ESTATE, "greedy: reserve() first");
   cudaStream_t st = (cudaStream_t)stream;
   uint16_t* lg = logits_out ? logits_out : m->logits;
-  SQ_TRY(launch_fp4_gemv_stream(fw(m->head), hidden, kDModel, rows, lg, m->cfg.vocab, m->d_err, st), "lm_head gemv");
+  SQ_TRY(launch_fp4_gemv_stream(fw(m->head), &m->head_maps, hidden, kDModel, rows, lg, m->cfg.vocab, m->d_err, st),
+         "lm_head gemv");
   return check(launch_argmax(lg, rows, m->cfg.vocab, m->cfg.vocab, (long long*)tokens_out, m->partials, st),
                "argmax");
 }

@@ -219,14 +219,16 @@ __device__ __forceinline__ bool gv_wait(uint32_t a, uint32_t parity) {
     if (gv_time() - t0 > kGvWaitNs) return false;
   }
 }
-__device__ __forceinline__ void gv_bulk(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
-               :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+
+__device__ __forceinline__ void gv_tma2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      :: "r"(dst), "l"(map), "r"(bar), "r"(x), "r"(y) : "memory");
 }
 
 template <int MT>
 __global__ void __launch_bounds__(32 * (1 + kGvConsumers))
-fp4_gemv_stream_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales,
+fp4_gemv_stream_kernel(const __grid_constant__ CUtensorMap mcodes, const __grid_constant__ CUtensorMap mscales,
                        const float* __restrict__ gptr, int N, int K, int KC,
                        const uint16_t* __restrict__ X, long long ldx, int M,
                        uint16_t* __restrict__ Y, long long ldy, int* err) {
@@ -259,11 +261,9 @@ fp4_gemv_stream_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restr
           asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
                        :: "r"(fb), "r"((uint32_t)(kGvRows * (code_row + scale_row))) : "memory");
           const uint32_t cdst = sbase + stage * kGvStageBytes, sdst = cdst + kGvCodeBytes;
-          for (int r = 0; r < kGvRows; ++r) {
-            const long long row = min(tile * kGvRows + r, N - 1);
-            gv_bulk(cdst + r * code_row, codes + row * (K / 2) + (long long)kc * code_row, code_row, fb);
-            gv_bulk(sdst + r * scale_row, scales + row * (K / 16) + (long long)kc * scale_row, scale_row, fb);
-          }
+          // one 16-row box each; x in u32 units (16-byte multiples), rows past N read zeros
+          gv_tma2d(cdst, &mcodes, fb, kc * (code_row / 4), tile * kGvRows);
+          gv_tma2d(sdst, &mscales, fb, kc * (scale_row / 4), tile * kGvRows);
           ++issued;
           if (++stage == kGvStages) { stage = 0; phase ^= 1; }
         }
@@ -374,10 +374,14 @@ fp4_gemv_stream_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restr
 
 int g_gv_sms = 0;
 
+int gemv_kc(int cols) {
+  return (cols % kGvKC == 0) ? kGvKC : (cols % 512 == 0 ? 512 : (cols % 256 == 0 ? 256 : 0));
+}
+
 template <int MT>
-int gemv_stream(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy, int* err,
-                cudaStream_t st) {
-  const int KC = (W.cols % kGvKC == 0) ? kGvKC : (W.cols % 512 == 0 ? 512 : (W.cols % 256 == 0 ? 256 : 0));
+int gemv_stream(const Fp4Weight& W, const Fp4Maps* maps, const uint16_t* X, long long ldx, int M, uint16_t* Y,
+                long long ldy, int* err, cudaStream_t st) {
+  const int KC = gemv_kc(W.cols);
   if (!KC && W.codes) return kEInval;
   if (!g_gv_sms) {
     int d = 0; cudaGetDevice(&d);
@@ -395,8 +399,13 @@ int gemv_stream(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uin
   if (!W.codes) return kOk;                          // prepare-only call
   const int tiles = (W.rows + kGvRows - 1) / kGvRows;
   const int grid = tiles < 3 * g_gv_sms ? tiles : 3 * g_gv_sms;
+  Fp4Maps local;
+  if (!maps || !maps->valid || maps->kc != KC) {
+    if (!make_fp4_maps(W, &local)) return kECuda;
+    maps = &local;
+  }
   fp4_gemv_stream_kernel<MT><<<grid, 32 * (1 + kGvConsumers), smem, st>>>(
-      W.codes, W.scales, W.global_scale, W.rows, W.cols, KC, X, ldx, M, Y, ldy, err);
+      maps->codes, maps->scales, W.global_scale, W.rows, W.cols, KC, X, ldx, M, Y, ldy, err);
   return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
 }
 
@@ -430,22 +439,36 @@ int launch_fp4_embed(const Fp4Weight& E, const long long* ids, int ntok, uint16_
   return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
 }
 
+bool make_fp4_maps(const Fp4Weight& W, Fp4Maps* maps) {
+  maps->valid = 0;
+  const int KC = gemv_kc(W.cols);
+  if (!KC || !W.codes || ((uintptr_t)W.codes % 16) || ((uintptr_t)W.scales % 16) || ((W.cols / 16) % 16))
+    return false;
+  maps->kc = KC;
+  if (!encode_u32_map(&maps->codes, W.codes, W.rows, W.cols / 8, W.cols / 2, KC / 8, kGvRows)) return false;
+  if (!encode_u32_map(&maps->scales, W.scales, W.rows, W.cols / 64, W.cols / 16, KC / 64, kGvRows)) return false;
+  maps->valid = 1;
+  return true;
+}
+
 int prepare_fp4_kernels() {
   Fp4Weight none{nullptr, nullptr, nullptr, 0, 1024};
-  int st = gemv_stream<1>(none, nullptr, 0, 1, nullptr, 0, nullptr, 0) | gemv_stream<2>(none, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
-           gemv_stream<4>(none, nullptr, 0, 1, nullptr, 0, nullptr, 0) | gemv_stream<8>(none, nullptr, 0, 1, nullptr, 0, nullptr, 0);
+  int st = gemv_stream<1>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
+           gemv_stream<2>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
+           gemv_stream<4>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
+           gemv_stream<8>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0);
   return st ? kECuda : kOk;
 }
 
-int launch_fp4_gemv_stream(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,
-                           int* err, cudaStream_t st) {
+int launch_fp4_gemv_stream(const Fp4Weight& W, const Fp4Maps* maps, const uint16_t* X, long long ldx, int M,
+                           uint16_t* Y, long long ldy, int* err, cudaStream_t st) {
   if (M <= 0 || M > 64 || W.cols % 256 || ldx % 8 || !err) return kEInval;
   if (((uintptr_t)W.codes % 16) || ((uintptr_t)W.scales % 16) || ((uintptr_t)X % 16) || ((W.cols / 16) % 16))
     return kEInval;
-  if (M <= 8) return gemv_stream<1>(W, X, ldx, M, Y, ldy, err, st);
-  if (M <= 16) return gemv_stream<2>(W, X, ldx, M, Y, ldy, err, st);
-  if (M <= 32) return gemv_stream<4>(W, X, ldx, M, Y, ldy, err, st);
-  return gemv_stream<8>(W, X, ldx, M, Y, ldy, err, st);
+  if (M <= 8) return gemv_stream<1>(W, maps, X, ldx, M, Y, ldy, err, st);
+  if (M <= 16) return gemv_stream<2>(W, maps, X, ldx, M, Y, ldy, err, st);
+  if (M <= 32) return gemv_stream<4>(W, maps, X, ldx, M, Y, ldy, err, st);
+  return gemv_stream<8>(W, maps, X, ldx, M, Y, ldy, err, st);
 }
 
 int launch_fp4_gemv(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,

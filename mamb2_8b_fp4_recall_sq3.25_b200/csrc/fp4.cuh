@@ -1,5 +1,6 @@
 // Packed FP4-E2M1 G16 weight descriptor and kernel launchers.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -19,10 +20,21 @@ int launch_fp4_decode(const Fp4Weight& W, uint16_t* out, long long ldo, cudaStre
 int launch_fp4_embed(const Fp4Weight& E, const long long* ids, int ntok, uint16_t* out, int* err, cudaStream_t st);
 int launch_fp4_gemv(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,
                     cudaStream_t st);
-// Same product through the bulk-copy pipelined kernel (cols % 256 == 0, 16-byte aligned rows);
-// `err` receives an error bit if a bounded wait expires.
-int launch_fp4_gemv_stream(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,
-                           int* err, cudaStream_t st);
+// TMA descriptors of one packed matrix for the streaming GEMV (codes and block scales as
+// u32 matrices, 16-row boxes).  Built once per matrix.
+struct Fp4Maps {
+  CUtensorMap codes;
+  CUtensorMap scales;
+  int kc;          // columns per pipeline stage
+  int valid;
+};
+bool make_fp4_maps(const Fp4Weight& W, Fp4Maps* maps);
+bool encode_u32_map(CUtensorMap* m, const void* base, long long rows, long long cols_u32, long long row_bytes,
+                    int box_cols, int box_rows);
+// Same product through the TMA-pipelined kernel (cols % 256 == 0, 16-byte aligned rows);
+// `maps` may be null (built on the fly); `err` receives an error bit if a bounded wait expires.
+int launch_fp4_gemv_stream(const Fp4Weight& W, const Fp4Maps* maps, const uint16_t* X, long long ldx, int M,
+                           uint16_t* Y, long long ldy, int* err, cudaStream_t st);
 
 // tcgen05 GEMM: C[M,N] = A[M,K] . B[N,K]^T, fp16 in, fp32 accumulate in TMEM.
 // mode 0: store fp16 C.  mode 1: cross-entropy partials of fp16-rounded logits

@@ -320,6 +320,21 @@ int g_num_sms = 0;
 
 }  // namespace
 
+// 2-D tiled tensor map over a row-major matrix of 4-byte elements (used by the FP4 GEMV
+// to stream code / block-scale tiles): dims {cols, rows}, box {box_cols, box_rows}.
+bool encode_u32_map(CUtensorMap* m, const void* base, long long rows, long long cols_u32, long long row_bytes,
+                    int box_cols, int box_rows) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols_u32, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int gemm_num_ntiles(int N) { return (N + BN - 1) / BN; }
 
 static bool g_gemm_attr = false;
