@@ -102,6 +102,22 @@ int64_t sq_fp4_linear_workspace(int m, int n, int k);
 int sq_fp4_linear(const uint8_t* codes, const uint8_t* block_scales, const float* global_scale,
                   int n, int k, const uint16_t* x, int64_t ldx, int m, uint16_t* y, int64_t ldy,
                   void* workspace, int64_t workspace_bytes, void* stream);
+/* sq_fp4_linear without any device allocation (no counterpart in the reference): for
+ * callers that cannot allocate, i.e. FFI bindings that own no device allocator, and
+ * serving processes whose device memory is fixed at start-up (a cudaMalloc synchronises
+ * the device and can fail mid-run).  Same result as sq_fp4_linear; for m > 64 the decoded
+ * weight rows are staged, in chunks of whole 256-row tiles, in a static device array of
+ * SQ_FP4_LINEAR_STATIC_STAGE_BYTES inside this library, so k <= 32768 there
+ * (sq_fp4_linear_static_max_k()); larger k returns SQ_EINVAL.
+ * The first call on each device does set-up (resolves the array's address, which may load
+ * the module, and sets kernel attributes): make it before any stream capture.  The call is
+ * synchronous on `stream`.  The array is shared by all callers in the process: calls that
+ * overlap in time (two host threads, or two streams) race on it and must be serialised. */
+#define SQ_FP4_LINEAR_STATIC_STAGE_BYTES (16u << 20)
+int64_t sq_fp4_linear_static_max_k(void);
+int sq_fp4_linear_static(const uint8_t* codes, const uint8_t* block_scales, const float* global_scale,
+                         int n, int k, const uint16_t* x, int64_t ldx, int m, uint16_t* y, int64_t ldy,
+                         void* stream);
 /* tcgen05 fp16 GEMM C[m,n] = A[m,k] . B[n,k]^T (fp32 accumulate), k % 64 == 0. */
 int sq_gemm_f16(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb,
                 uint16_t* c, int64_t ldc, int m, int n, int k, void* stream);

@@ -100,6 +100,11 @@ int linear(sq_model* m, const sq_fp4_matrix& W, const Fp4Maps* maps, const uint1
 
 }  // namespace
 
+namespace sq {
+// Records `msg` as the calling thread's last error (used by entry points in other files).
+int set_last_error(int code, const char* msg) { return fail(code, msg); }
+}  // namespace sq
+
 extern "C" {
 
 int sq_abi_version(void) { return SQ325_ABI_VERSION; }

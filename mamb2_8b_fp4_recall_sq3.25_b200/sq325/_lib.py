@@ -68,6 +68,8 @@ _PROTOS = {
     'sq_fp4_decode': (C.c_int, [p, p, p, C.c_int, C.c_int, p, i64, p]),
     'sq_fp4_linear_workspace': (i64, [C.c_int, C.c_int, C.c_int]),
     'sq_fp4_linear': (C.c_int, [p, p, p, C.c_int, C.c_int, p, i64, C.c_int, p, i64, p, i64, p]),
+    'sq_fp4_linear_static_max_k': (i64, []),
+    'sq_fp4_linear_static': (C.c_int, [p, p, p, C.c_int, C.c_int, p, i64, C.c_int, p, i64, p]),
     'sq_gemm_f16': (C.c_int, [p, i64, p, i64, p, i64, C.c_int, C.c_int, C.c_int, p]),
     'sq_model_create': (C.c_int, [C.POINTER(ModelConfig), C.POINTER(p)]),
     'sq_model_destroy': (C.c_int, [p]),
