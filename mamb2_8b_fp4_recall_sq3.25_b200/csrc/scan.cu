@@ -14,8 +14,10 @@
 // order, dt/decay per (token, head), the predictor readout vector cvec (= the reference's
 // `correction`) and the five zero-tier dots for all TC tokens, then every thread runs
 // the TC recurrence steps on its row with packed fp32x2 arithmetic.  The next chunk's
-// raw inputs are prefetched into registers while the current one is computed.  Packed
-// rows are read once at the start and written once at the end of the call.
+// raw inputs are copied asynchronously (cp.async) into a shared-memory ring of raw tokens
+// while the current one is computed; the same ring carries the conv history, so no input
+// or conv state is held in registers across the recurrence.  Packed rows are read once at
+// the start and written once at the end of the call.
 #include <algorithm>
 
 #include "common.cuh"
@@ -25,7 +27,7 @@ namespace sq {
 
 namespace {
 
-constexpr int kTC = 16;        // tokens per chunk
+constexpr int kTC = 8;         // tokens per chunk
 constexpr int kMaxHpc = 8;     // heads per CTA (dim >= 16)
 
 // Exactly rounded fp32 quotient a/s given inv = RN(1/s): one FMA remainder and one FMA
@@ -58,37 +60,87 @@ __device__ __forceinline__ float conv_step_value(const float (&w)[5], float x0, 
   s = h2f(f2h(s + w[4]));
   return silu16(s);
 }
-__device__ __forceinline__ float requant(float q, float lim) {
-  return fminf(fmaxf(round_half_away(q), -lim), lim);
+// Stored-tier requant of a coordinate pair (:155-162): v = clip(round_half_away(S/s), +-lim) * s
+// with S/s the correctly rounded quotient.  Computed on the magnitude: the clip moves in
+// front of the rounding (lim is an integer), floor(a + 0.5) is taken exactly with two
+// round-down adds (RD(a + 0.5) never crosses the integer below a + 0.5, and RD(t + 2^23)
+// = floor(t) + 2^23 for 0 <= t < 2^23), the product (u - 2^23) * s is one FMA against the
+// exact -2^23 * s, and the sign of S is put back last.  Bit-identical to the scalar chain.
+constexpr float kMagic = 8388608.0f;   // 2^23
+__device__ __forceinline__ void requant_pair(float& sa, float& sb, float2 ns, float2 inv, float lim, float2 s,
+                                             float2 nms) {
+  const float2 q = div_exact2(make_float2(sa, sb), ns, inv);
+  float2 a = make_float2(fminf(fabsf(q.x), lim), fminf(fabsf(q.y), lim));
+  a = __fadd2_rd(__fadd2_rd(a, make_float2(0.5f, 0.5f)), make_float2(kMagic, kMagic));
+  const float2 v = __ffma2_rn(a, s, nms);
+  sa = copysignf(v.x, sa);
+  sb = copysignf(v.y, sb);
 }
 
+// Shared-memory plan of one CTA (byte offsets; every region 16-byte aligned).
+//   ring   R slots of raw inputs per token: x[128] | B[128] | C[128] fp16 (x holds the
+//          CTA's own channels, B/C the whole group row in channel order).  Slot of token t
+//          (relative to the call, may be negative) = t mod R.  Slots -3..-1 carry the conv
+//          history: zeros after a reset (mode 1) or the conv cache (mode 2).
+//   T      token tables of one chunk: B/C in tier order (float4 pairs), cvec, conv'd x.
+//          Before the first chunk the same bytes stage the raw static tables and packed rows;
+//          after the last chunk they stage the repacked rows.
+//   dots, dd, pred, basis, perm, conv weights.
+template <int N8, int N4, int TC>
+struct ScanSmem {
+  static constexpr int NZ = 128 - N8 - N4, F = N8 + N4 + 2;
+  static constexpr int R = (2 * TC >= TC + 3) ? 2 * TC : 4;     // power of two >= TC + 3 and 2 TC
+  static constexpr int kSlotElems = 384;
+  static constexpr int a16(int v) { return (v + 15) / 16 * 16; }
+  static constexpr int oRawBasis = a16(F * NZ * 2);
+  static constexpr int oRawPerm = oRawBasis + a16(NZ * 4);
+  static constexpr int oPackStart = oRawPerm + 128;
+  static constexpr int kTok = TC * 64 * 16 + TC * 64 * 8 + TC * 128 * 4;
+  static constexpr int kT = (kTok > oPackStart + 128 * 52) ? kTok : oPackStart + 128 * 52;
+  static constexpr int oRing = 0;
+  static constexpr int oT = oRing + R * kSlotElems * 2;
+  static constexpr int oDots = oT + kT;
+  static constexpr int oDD = oDots + TC * 8 * 4;
+  static constexpr int oPred = oDD + TC * kMaxHpc * 2 * 4;
+  static constexpr int oBasis = oPred + a16(F * (NZ + 1) * 4);
+  static constexpr int oPerm = oBasis + a16(2 * NZ * 4);
+  static constexpr int oW = oPerm + 128 * 4;
+  static constexpr int kBytes = oW + 3 * 128 * 5 * 4;
+};
+
+// Resident CTAs per SM the register budget is sized for: 4 (<= 128 registers) while the
+// stored row fits, 3 for the widest layouts.
+template <int N8, int N4>
+constexpr int scan_min_blocks() { return N8 + N4 > 68 ? 3 : 4; }
+
 template <int N8, int N4, int KJ, int MODE, int TC>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128, scan_min_blocks<N8, N4>())
 ssu_sq325_kernel(const ScanParams P) {
-  constexpr int NZ = 128 - N8 - N4;
-  constexpr int F = N8 + N4 + 2;
+  using L = ScanSmem<N8, N4, TC>;
+  constexpr int NZ = L::NZ;
+  constexpr int F = L::F;
+  constexpr int R = L::R;
+  constexpr int SE = L::kSlotElems;
   constexpr int W8 = N8 / 2, W4 = N4 / 2;
   constexpr int NP = (N8 + N4) / 2;            // stored coordinate pairs
   static_assert(N8 % 2 == 0 && N4 % 2 == 0, "tiers are nibble pairs");
 
   extern __shared__ __align__(16) unsigned char smem[];
-  constexpr int kTables = (TC * 64 * 16 > F * NZ * 2 + 16 + NZ * 4) ? TC * 64 * 16 : F * NZ * 2 + 16 + NZ * 4;
-  constexpr int kTablesA = (kTables + 15) / 16 * 16;
-  constexpr int kV2 = (TC * 64 * 8 > 128) ? TC * 64 * 8 : 128;
-  float4* sP4 = reinterpret_cast<float4*>(smem);                     // [TC][64] {b_j,b_j+1,c_j,c_j+1}
-  float2* sV2 = reinterpret_cast<float2*>(smem + kTablesA);          // [TC][64] {cvec_j,cvec_j+1}
-  float* sDots = reinterpret_cast<float*>(smem + kTablesA + kV2);    // [TC][8]
-  float* sDD = sDots + TC * 8;                                       // [TC][kMaxHpc][2] (dt, decay)
-  float* sX = sDD + TC * kMaxHpc * 2;                                // [TC][blockDim] own x value
-  unsigned char* sPack = reinterpret_cast<unsigned char*>(sX + TC * 128);   // rows*52 (16-B aligned)
-  float* sPred = reinterpret_cast<float*>(sPack + 128 * 52);         // [F][NZ+1]
-  float* sBasis = sPred + F * (NZ + 1);                              // [2][NZ]
-  int* sPerm = reinterpret_cast<int*>(sBasis + 2 * NZ);              // [128]
+  uint16_t* ring = reinterpret_cast<uint16_t*>(smem + L::oRing);
+  float4* sP4 = reinterpret_cast<float4*>(smem + L::oT);                  // [TC][64] {b_j,b_j+1,c_j,c_j+1}
+  float2* sV2 = reinterpret_cast<float2*>(smem + L::oT + TC * 64 * 16);   // [TC][64] {cvec_j,cvec_j+1}
+  float* sX = reinterpret_cast<float*>(smem + L::oT + TC * 64 * 24);      // [TC][128] conv'd own x
+  float* sDots = reinterpret_cast<float*>(smem + L::oDots);               // [TC][8]
+  float* sDD = reinterpret_cast<float*>(smem + L::oDD);                   // [TC][kMaxHpc][2] (dt, decay)
+  float* sPred = reinterpret_cast<float*>(smem + L::oPred);               // [F][NZ+1]
+  float* sBasis = reinterpret_cast<float*>(smem + L::oBasis);             // [2][NZ]
+  int* sPerm = reinterpret_cast<int*>(smem + L::oPerm);                   // [128]
+  float* sW = reinterpret_cast<float*>(smem + L::oW);                     // [3][128][5] x / B / C taps + bias
   float* sPf = reinterpret_cast<float*>(sP4);
-  // raw fp16 staging of the static tables lives in the (not yet used) token tables
-  uint16_t* rawPred = reinterpret_cast<uint16_t*>(sP4);              // F*NZ fp16  (<= 8.6 KB)
-  uint16_t* rawBasis = rawPred + F * NZ + 8;                         // NZ*2 fp16
-  uint8_t* rawPerm = reinterpret_cast<uint8_t*>(sV2);                // 128 B
+  uint16_t* rawPred = reinterpret_cast<uint16_t*>(smem + L::oT);
+  uint16_t* rawBasis = reinterpret_cast<uint16_t*>(smem + L::oT + L::oRawBasis);
+  uint8_t* rawPerm = smem + L::oT + L::oRawPerm;
+  unsigned char* sPack = smem + L::oT + L::oPackStart;
 
   const int tid = threadIdx.x;
   const int bd = blockDim.x;
@@ -101,14 +153,47 @@ ssu_sq325_kernel(const ScanParams P) {
   const int h = h0 + hl;
   const int hpg = P.heads / P.groups;
   const int g = h0 / hpg;
-  const bool group_leader = (h0 % hpg) == 0;       // writes the group's B/C conv ring entries
+  const bool group_leader = (h0 % hpg) == 0;       // writes the group's B/C conv cache entries
   const long long row0 = ((long long)b * P.heads + h0) * dim;
   const int rows = bd;
-  constexpr int mode = MODE;
   const int kj = KJ;                                // coordinates per thread: 128 / blockDim
 
+  const uint16_t* xb = P.x + (long long)b * P.x_sb + (long long)h0 * dim;
+  const uint16_t* Bb = P.B + (long long)b * P.b_sb + g * 128;
+  const uint16_t* Cb = P.C + (long long)b * P.c_sb + g * 128;
+  // 16-byte asynchronous copies need 16-byte aligned rows; otherwise the raw inputs are
+  // staged with element loads (same layout, synchronous).
+  const bool vec = ((((uintptr_t)xb | (uintptr_t)Bb | (uintptr_t)Cb) & 15) == 0) &&
+                   ((P.x_st | P.b_st | P.c_st) & 7) == 0;
+  const int px = bd / 8;                            // 16-byte pieces of x per token
+  const int per_tok = px + 32;
+
+  // raw x/B/C of tokens [c0, c0 + nt) into their ring slots
+  uint16_t pre_dt = 0;
+  auto prefetch = [&](int c0) {
+    const int nt = min(TC, P.length - c0);
+    for (int i = tid; i < nt * per_tok; i += bd) {
+      const int t = i / per_tok, r = i - t * per_tok;
+      const long long tt = c0 + t;
+      uint16_t* slot = ring + ((c0 + t) & (R - 1)) * SE;
+      const uint16_t* src;
+      uint16_t* dst;
+      if (r < px) { src = xb + tt * P.x_st + r * 8; dst = slot + r * 8; }
+      else if (r < px + 16) { src = Bb + tt * P.b_st + (r - px) * 8; dst = slot + 128 + (r - px) * 8; }
+      else { src = Cb + tt * P.c_st + (r - px - 16) * 8; dst = slot + 256 + (r - px - 16) * 8; }
+      if (vec) cp_async16(dst, src);
+      else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dst[e] = src[e];
+      }
+    }
+    if (tid < nt * hpc) {
+      const int t = tid / hpc, hh = h0 + tid % hpc;
+      pre_dt = P.dt[(long long)b * P.dt_sb + (long long)(c0 + t) * P.dt_st + hh];
+    }
+  };
+
   // ---- stage static tables and packed rows with asynchronous 16-byte copies ----
-  // (every region below is a multiple of 16 bytes at a 16-byte aligned offset)
   unsigned char* pLo = sPack;
   unsigned char* pHi = pLo + rows * W8;
   unsigned char* pQ4 = pHi + rows * W8;
@@ -124,6 +209,18 @@ ssu_sq325_kernel(const ScanParams P) {
   stage16(pLat, P.latent + row0 * 2, rows * 2, tid, bd);
   stage16(pS8, P.s8 + row0, rows * 2, tid, bd);
   stage16(pS4, P.s4 + row0, rows * 2, tid, bd);
+  if (MODE == 2) {
+    // conv history: the cache's three previous positions into the slots of tokens -3..-1
+    const uint16_t* cache = P.conv_cache + (long long)b * P.conv_cache_sb;
+    for (int i = tid; i < 3 * per_tok; i += bd) {
+      const int k = i / per_tok, r = i - k * per_tok;
+      const uint16_t* cs = cache + ((P.conv_pos - 3 + k) & 3) * 10240;
+      uint16_t* slot = ring + ((k - 3) & (R - 1)) * SE;
+      if (r < px) cp_async16(slot + r * 8, cs + h0 * dim + r * 8);
+      else if (r < px + 16) cp_async16(slot + 128 + (r - px) * 8, cs + 8192 + g * 128 + (r - px) * 8);
+      else cp_async16(slot + 256 + (r - px - 16) * 8, cs + 9216 + g * 128 + (r - px - 16) * 8);
+    }
+  }
   cp_async_wait_all();
   __syncthreads();
   for (int i = tid; i < F * NZ; i += bd) {
@@ -135,7 +232,29 @@ ssu_sq325_kernel(const ScanParams P) {
     sBasis[NZ + i] = h2f(rawBasis[2 * i + 1]);
   }
   for (int i = tid; i < 128; i += bd) sPerm[i] = rawPerm[i];
+  if (MODE == 1) {
+    for (int i = tid; i < 3 * SE; i += bd) ring[((i / SE - 3) & (R - 1)) * SE + i % SE] = 0;
+  }
   __syncthreads();
+  if (MODE != 0) {
+    for (int c = tid; c < bd; c += bd) {
+      const int ch = h0 * dim + c;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sW[c * 5 + i] = h2f(P.conv_w[ch * 4 + i]);
+      sW[c * 5 + 4] = h2f(P.conv_b[ch]);
+    }
+    for (int j = tid; j < 128; j += bd) {
+      const int chb = 8192 + g * 128 + sPerm[j], chc = 9216 + g * 128 + sPerm[j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        sW[(128 + j) * 5 + i] = h2f(P.conv_w[chb * 4 + i]);
+        sW[(256 + j) * 5 + i] = h2f(P.conv_w[chc * 4 + i]);
+      }
+      sW[(128 + j) * 5 + 4] = h2f(P.conv_b[chb]);
+      sW[(256 + j) * 5 + 4] = h2f(P.conv_b[chc]);
+    }
+  }
+  prefetch(0);
 
   // ---- decode own row (:81-114) ----
   float S[N8 + N4];
@@ -159,77 +278,6 @@ ssu_sq325_kernel(const ScanParams P) {
   float z0 = e4m3_to_f32(pLat[tid * 2 + 0]) * ls0;
   float z1 = e4m3_to_f32(pLat[tid * 2 + 1]) * ls1;
   const float dv = P.d_is_f32 ? reinterpret_cast<const float*>(P.D)[h] : h2f(reinterpret_cast<const uint16_t*>(P.D)[h]);
-
-  // ---- conv weights / history for the channels this thread converts ----
-  const int chx = h * dim + p;                                      // own x channel
-  float wx[5] = {0, 0, 0, 0, 0}, hx[4] = {0, 0, 0, 0};             // hx: raw x at t-3..t (hx[3] newest)
-  float wb[KJ][5], wc[KJ][5], hb[KJ][4], hc[KJ][4];
-  int chb[KJ], chc[KJ];
-#pragma unroll
-  for (int k = 0; k < KJ; ++k) {
-    const int j = tid + k * bd;
-    chb[k] = chc[k] = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) hb[k][i] = hc[k][i] = 0.f;
-#pragma unroll
-    for (int i = 0; i < 5; ++i) wb[k][i] = wc[k][i] = 0.f;
-    if (mode != 0 && k < kj && j < 128) {
-      chb[k] = 8192 + g * 128 + sPerm[j];
-      chc[k] = 9216 + g * 128 + sPerm[j];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) { wb[k][i] = h2f(P.conv_w[chb[k] * 4 + i]); wc[k][i] = h2f(P.conv_w[chc[k] * 4 + i]); }
-      wb[k][4] = h2f(P.conv_b[chb[k]]); wc[k][4] = h2f(P.conv_b[chc[k]]);
-    }
-  }
-  if (mode != 0) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) wx[i] = h2f(P.conv_w[chx * 4 + i]);
-    wx[4] = h2f(P.conv_b[chx]);
-  }
-  if (mode == 2) {
-    // one-token step: history = the ring's previous three positions
-    const uint16_t* ring = P.conv_cache + (long long)b * P.conv_cache_sb;
-#pragma unroll
-    for (int i = 0; i < 3; ++i) {
-      const int slot = (P.conv_pos - 3 + i) & 3;
-      hx[i + 1] = h2f(ring[slot * 10240 + chx]);
-#pragma unroll
-      for (int k = 0; k < KJ; ++k)
-        if (k < kj && tid + k * bd < 128) {
-          hb[k][i + 1] = h2f(ring[slot * 10240 + chb[k]]);
-          hc[k][i + 1] = h2f(ring[slot * 10240 + chc[k]]);
-        }
-    }
-  }
-
-  // ---- raw-input prefetch (registers) ----
-  // packed raw prefetch: x of token pairs, and (B | C << 16) per owned coordinate
-  uint32_t pre_x[(TC + 1) / 2], pre_bc[TC][KJ];
-  uint16_t pre_dt = 0;
-  auto prefetch = [&](int c0) {
-    const int nt = min(TC, P.length - c0);
-#pragma unroll
-    for (int t = 0; t < TC; ++t) {
-      if (t < nt) {
-        const long long tt = c0 + t;
-        const uint32_t xr = P.x[(long long)b * P.x_sb + tt * P.x_st + (long long)h * dim + p];
-        pre_x[t / 2] = (t & 1) ? ((pre_x[t / 2] & 0xFFFFu) | (xr << 16)) : xr;
-        const uint16_t* Bt = P.B + (long long)b * P.b_sb + tt * P.b_st + g * 128;
-        const uint16_t* Ct = P.C + (long long)b * P.c_sb + tt * P.c_st + g * 128;
-#pragma unroll
-        for (int k = 0; k < KJ; ++k) {
-          const int j = tid + k * bd;
-          if (k < kj && j < 128) { const int n = sPerm[j]; pre_bc[t][k] = (uint32_t)Bt[n] | ((uint32_t)Ct[n] << 16); }
-        }
-      }
-    }
-    if (tid < nt * hpc) {
-      const int t = tid / hpc, hh = h0 + tid % hpc;
-      pre_dt = P.dt[(long long)b * P.dt_sb + (long long)(c0 + t) * P.dt_st + hh];
-    }
-  };
-  prefetch(0);
-
   const float bias_own = P.dt_bias_is_f32 ? reinterpret_cast<const float*>(P.dt_bias)[h0 + (tid % max(hpc, 1))]
                                           : h2f(reinterpret_cast<const uint16_t*>(P.dt_bias)[h0 + (tid % max(hpc, 1))]);
   const float A_own = P.A[h0 + (tid % max(hpc, 1))];
@@ -238,38 +286,63 @@ ssu_sq325_kernel(const ScanParams P) {
 
   for (int c0 = 0; c0 < P.length; c0 += TC) {
     const int nt = min(TC, P.length - c0);
-    __syncthreads();                                   // previous chunk finished reading shared tables
-    // -- publish B/C (tier order), dt/decay, and own x values for this chunk --
+    cp_async_wait_all();
+    __syncthreads();                                   // raw chunk landed; previous chunk's tables free
+    // -- publish conv'd x, B/C (tier order) and dt/decay for this chunk --
+    {
+      float w[5];
+      const uint16_t* rx = ring + tid;
+      float h1 = 0.f, h2 = 0.f, h3 = 0.f;             // raw x at t-3, t-2, t-1
+      if (MODE != 0) {
 #pragma unroll
-    for (int t = 0; t < TC; ++t) {
-      if (t < nt) {
+        for (int i = 0; i < 5; ++i) w[i] = sW[tid * 5 + i];
+        h1 = h2f(rx[((c0 - 3) & (R - 1)) * SE]);
+        h2 = h2f(rx[((c0 - 2) & (R - 1)) * SE]);
+        h3 = h2f(rx[((c0 - 1) & (R - 1)) * SE]);
+      }
 #pragma unroll
-        for (int k = 0; k < KJ; ++k) {
-          const int j = tid + k * bd;
-          if (k < kj && j < 128) {
-            float bv = h2f((uint16_t)(pre_bc[t][k] & 0xFFFFu)), cv = h2f((uint16_t)(pre_bc[t][k] >> 16));
-            if (mode != 0) {
-              hb[k][0] = hb[k][1]; hb[k][1] = hb[k][2]; hb[k][2] = hb[k][3]; hb[k][3] = bv;
-              hc[k][0] = hc[k][1]; hc[k][1] = hc[k][2]; hc[k][2] = hc[k][3]; hc[k][3] = cv;
-              if (mode == 1) {
-                bv = conv_prefill_value(wb[k], hb[k][0], hb[k][1], hb[k][2], hb[k][3]);
-                cv = conv_prefill_value(wc[k], hc[k][0], hc[k][1], hc[k][2], hc[k][3]);
-              } else {
-                bv = conv_step_value(wb[k], hb[k][0], hb[k][1], hb[k][2], hb[k][3]);
-                cv = conv_step_value(wc[k], hc[k][0], hc[k][1], hc[k][2], hc[k][3]);
-              }
-            }
+      for (int t = 0; t < TC; ++t) {
+        if (t < nt) {
+          const float raw = h2f(rx[((c0 + t) & (R - 1)) * SE]);
+          float xv = raw;
+          if (MODE == 1) xv = conv_prefill_value(w, h1, h2, h3, raw);
+          if (MODE == 2) xv = conv_step_value(w, h1, h2, h3, raw);
+          h1 = h2; h2 = h3; h3 = raw;
+          sX[t * 128 + tid] = xv;
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < KJ; ++k) {
+      const int j = tid + k * bd;
+      if (k < kj && j < 128) {
+        const int n = sPerm[j];
+        float wb[5], wc[5];
+        float b1 = 0.f, b2 = 0.f, b3 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
+        if (MODE != 0) {
+#pragma unroll
+          for (int i = 0; i < 5; ++i) { wb[i] = sW[(128 + j) * 5 + i]; wc[i] = sW[(256 + j) * 5 + i]; }
+          b1 = h2f(ring[((c0 - 3) & (R - 1)) * SE + 128 + n]);
+          b2 = h2f(ring[((c0 - 2) & (R - 1)) * SE + 128 + n]);
+          b3 = h2f(ring[((c0 - 1) & (R - 1)) * SE + 128 + n]);
+          c1 = h2f(ring[((c0 - 3) & (R - 1)) * SE + 256 + n]);
+          c2 = h2f(ring[((c0 - 2) & (R - 1)) * SE + 256 + n]);
+          c3 = h2f(ring[((c0 - 1) & (R - 1)) * SE + 256 + n]);
+        }
+#pragma unroll
+        for (int t = 0; t < TC; ++t) {
+          if (t < nt) {
+            const uint16_t* slot = ring + ((c0 + t) & (R - 1)) * SE;
+            const float rb = h2f(slot[128 + n]), rc = h2f(slot[256 + n]);
+            float bv = rb, cv = rc;
+            if (MODE == 1) { bv = conv_prefill_value(wb, b1, b2, b3, rb); cv = conv_prefill_value(wc, c1, c2, c3, rc); }
+            if (MODE == 2) { bv = conv_step_value(wb, b1, b2, b3, rb); cv = conv_step_value(wc, c1, c2, c3, rc); }
+            b1 = b2; b2 = b3; b3 = rb;
+            c1 = c2; c2 = c3; c3 = rc;
             sPf[t * 256 + (j >> 1) * 4 + (j & 1)] = bv;
             sPf[t * 256 + (j >> 1) * 4 + 2 + (j & 1)] = cv;
           }
         }
-        float x = h2f((uint16_t)((t & 1) ? (pre_x[t / 2] >> 16) : (pre_x[t / 2] & 0xFFFFu)));
-        if (mode != 0) {
-          hx[0] = hx[1]; hx[1] = hx[2]; hx[2] = hx[3]; hx[3] = x;
-          x = (mode == 1) ? conv_prefill_value(wx, hx[0], hx[1], hx[2], hx[3])
-                          : conv_step_value(wx, hx[0], hx[1], hx[2], hx[3]);
-        }
-        sX[t * 128 + tid] = x;
       }
     }
     if (tid < nt * hpc) {
@@ -277,8 +350,8 @@ ssu_sq325_kernel(const ScanParams P) {
       sDD[((tid / hpc) * kMaxHpc + tid % hpc) * 2 + 0] = dtv;
       sDD[((tid / hpc) * kMaxHpc + tid % hpc) * 2 + 1] = expf(A_own * dtv);
     }
+    __syncthreads();                                   // tables visible; this chunk's raw slots consumed
     if (c0 + TC < P.length) prefetch(c0 + TC);
-    __syncthreads();                                   // B/C of the chunk visible
     // -- group-level dots for every token of the chunk --
     for (int task = tid; task < nt * (F + 5); task += bd) {
       const int t = task / (F + 5), f = task - t * (F + 5);
@@ -359,38 +432,31 @@ ssu_sq325_kernel(const ScanParams P) {
       const float i4 = s4 > 0.f ? __frcp_rn(s4) : 0.f;
       const float2 s82 = make_float2(s8, s8), ns82 = make_float2(-s8, -s8), i82 = make_float2(i8, i8);
       const float2 s42 = make_float2(s4, s4), ns42 = make_float2(-s4, -s4), i42 = make_float2(i4, i4);
+      const float m8s = -kMagic * s8, m4s = -kMagic * s4;            // exact (power-of-two scaling)
+      const float2 nm82 = make_float2(m8s, m8s), nm42 = make_float2(m4s, m4s);
 #pragma unroll
       for (int jp = 0; jp < NP; ++jp) {
         const bool t8 = 2 * jp < N8;
-        float2 q = div_exact2(make_float2(S[2 * jp], S[2 * jp + 1]), t8 ? ns82 : ns42, t8 ? i82 : i42);
-        const float lim = t8 ? 127.f : 7.f;
-        q.x = requant(q.x, lim);
-        q.y = requant(q.y, lim);
-        const float2 v = __fmul2_rn(q, t8 ? s82 : s42);
-        S[2 * jp] = v.x; S[2 * jp + 1] = v.y;
+        requant_pair(S[2 * jp], S[2 * jp + 1], t8 ? ns82 : ns42, t8 ? i82 : i42, t8 ? 127.f : 7.f,
+                     t8 ? s82 : s42, t8 ? nm82 : nm42);
       }
     }
   }
 
-  // ---- conv ring update (raw columns of the last positions) ----
-  if (mode != 0) {
-    uint16_t* ring = P.conv_cache + (long long)b * P.conv_cache_sb;
-    const int last = P.conv_pos + P.length - 1;       // absolute position of the newest token
-    const int nwrite = mode == 2 ? 1 : min(4, P.length);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (i < nwrite) {
-        const int slot = (last - i) & 3;
-        ring[slot * 10240 + chx] = f2h(hx[3 - i]);
-        if (group_leader) {
-#pragma unroll
-          for (int k = 0; k < KJ; ++k)
-            if (k < kj && tid + k * bd < 128) {
-              ring[slot * 10240 + chb[k]] = f2h(hb[k][3 - i]);
-              ring[slot * 10240 + chc[k]] = f2h(hc[k][3 - i]);
-            }
+  // ---- conv cache update: raw columns of the newest positions, channel order ----
+  if (MODE != 0) {
+    uint16_t* cache = P.conv_cache + (long long)b * P.conv_cache_sb;
+    const int nwrite = MODE == 2 ? 1 : min(4, P.length);
+    for (int i = 0; i < nwrite; ++i) {
+      const int t = P.length - 1 - i;                  // relative token
+      const int slot = (P.conv_pos + t) & 3;           // absolute position mod 4
+      const uint16_t* src = ring + (t & (R - 1)) * SE;
+      cache[slot * 10240 + h0 * dim + tid] = src[tid];
+      if (group_leader)
+        for (int n = tid; n < 128; n += bd) {
+          cache[slot * 10240 + 8192 + g * 128 + n] = src[128 + n];
+          cache[slot * 10240 + 9216 + g * 128 + n] = src[256 + n];
         }
-      }
     }
   }
 
@@ -433,25 +499,18 @@ ssu_sq325_kernel(const ScanParams P) {
 
 template <int N8, int N4, int KJ, int MODE, int TC = (MODE == 2 ? 1 : kTC)>
 int launch_kj(const ScanParams& P, int hpc, cudaStream_t stream) {
-  constexpr int NZ = 128 - N8 - N4;
-  constexpr int F = N8 + N4 + 2;
-  const int bd = hpc * P.dim;
-  // token tables are also the raw staging area of the predictor table (F*NZ fp16 + basis)
-  const size_t tables = (std::max((size_t)TC * 64 * 16, (size_t)F * NZ * 2 + 16 + NZ * 4) + 15) / 16 * 16;
-  const size_t smem = tables + std::max((size_t)TC * 64 * 8, (size_t)128) + (size_t)TC * 8 * 4 +
-                      (size_t)TC * kMaxHpc * 2 * 4 + (size_t)TC * 128 * 4 + 128 * 52 +
-                      (size_t)F * (NZ + 1) * 4 + 2 * NZ * 4 + 128 * 4;
-  (void)bd;
+  const size_t smem = ScanSmem<N8, N4, TC>::kBytes;
   auto kern = ssu_sq325_kernel<N8, N4, KJ, MODE, TC>;
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
       return kECuda;
     attr = true;
   }
   if (hpc == 0) return kOk;                         // prepare-only call (attributes set, no launch)
   dim3 grid(P.heads / hpc, P.batch);
-  kern<<<grid, bd, smem, stream>>>(P);
+  kern<<<grid, hpc * P.dim, smem, stream>>>(P);
   return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
 }
 
@@ -496,6 +555,7 @@ int launch_scan(const ScanParams& P, cudaStream_t stream) {
     return kEInval;
   if (P.conv_mode == 1 && P.conv_pos != 0) return kEInval;     // fused prefill only from a reset state
   if (P.conv_mode == 2 && (P.length != 1 || P.conv_pos <= 0)) return kEInval;
+  if (P.conv_mode != 0 && ((((uintptr_t)P.conv_cache) & 15) || (P.conv_cache_sb & 7))) return kEInval;
   const int hpg = P.heads / P.groups;
   int hpc = 1;
   for (int c = 1; c <= hpg && c <= kMaxHpc; ++c)
