@@ -176,7 +176,7 @@ def build_workload(rank, device):
 
 def launches_per_step(M_rows, n_layer=N_LAYER, vocab=VOCAB):
     lin = 1 if M_rows <= 64 else 2
-    per_layer = 1 + lin + 1 + 1 + 1 + lin          # add_rmsnorm, in_proj, conv, scan, resurface+norm, out_proj
+    per_layer = 1 + lin + 1 + 1 + 1 + lin          # add_rmsnorm, in_proj, scan prep, scan, resurface+norm, out_proj
     score = 2 * ((vocab + 32767) // 32768) + 1     # per 32768-row chunk: decode + gemm; finalize
     return 1 + n_layer * per_layer + 1 + score     # embed, layers, norm_f, head
 

@@ -51,7 +51,10 @@ int64_t sq_state_bytes(int batch, int heads, int dim);                  /* 52 B/
  * All arrays are device pointers.  fp16 arrays are uint16_t bit patterns.
  * Activation element (b,t,h,p) of x / y lives at ptr + b*batch_stride + t*token_stride
  * + h*dim + p; dt (b,t,h) at dt + b*sb + t*st + h; B/C (b,t,g,n) at ptr + b*sb + t*st +
- * g*128 + n.  The state is mutated in place and y is written for every token. */
+ * g*128 + n.  The state is mutated in place and y is written for every token.
+ * workspace (optional, >= sq_scan_workspace(...) bytes, 256-byte aligned) enables the
+ * two-kernel multi-token path (group-level dots computed once per group instead of once
+ * per CTA); with NULL the single fused kernel runs.  Results are identical. */
 typedef struct sq_scan_args {
   int32_t batch, length, heads, dim, groups, layout;
   const uint16_t* x;  int64_t x_batch_stride, x_token_stride;
@@ -67,7 +70,9 @@ typedef struct sq_scan_args {
   const uint16_t* predictor;                          /* [G,n8+n4+2,nzero] fp16 */
   uint8_t* lo; uint8_t* hi; uint8_t* q4; uint8_t* latent; uint16_t* s8; uint16_t* s4; /* PackedState */
   uint16_t* y; int64_t y_batch_stride, y_token_stride;
+  void* workspace; int64_t workspace_bytes;           /* optional, may be NULL / 0 */
 } sq_scan_args;
+int64_t sq_scan_workspace(int batch, int length, int heads, int groups, int layout);
 int sq_scan(const sq_scan_args* args, void* stream);
 
 /* ---------------------------------------------------------------- standalone codec

@@ -70,6 +70,7 @@ struct sq_model {
   uint16_t *h = 0, *res = 0, *hn = 0, *zx = 0, *xbc = 0, *y = 0, *yn = 0, *stage = 0, *logits = 0;
   float2* partials = 0;
   float* tlogit = 0;
+  void* prep = 0;                             // two-kernel scan workspace (any layout)
   int* d_err = 0;
   size_t stage_elems = 0;
   std::atomic<int> busy{0};
@@ -80,11 +81,12 @@ namespace {
 Fp4Weight fw(const sq_fp4_matrix& m) { return Fp4Weight{m.codes, m.block_scales, m.global_scale, m.rows, m.cols}; }
 
 void free_ws(sq_model* m) {
-  void* ptrs[] = {m->h, m->res, m->hn, m->zx, m->xbc, m->y, m->yn, m->stage, m->logits, m->partials, m->tlogit};
+  void* ptrs[] = {m->h, m->res, m->hn, m->zx, m->xbc, m->y, m->yn, m->stage, m->logits, m->partials, m->tlogit,
+                  m->prep};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   m->h = m->res = m->hn = m->zx = m->xbc = m->y = m->yn = m->stage = m->logits = nullptr;
-  m->partials = nullptr; m->tlogit = nullptr;
+  m->partials = nullptr; m->tlogit = nullptr; m->prep = nullptr;
   m->max_tokens = 0;
 }
 
@@ -127,6 +129,10 @@ int sq_layout_counts(int layout, int* n8, int* n4, int* nzero) {
 
 int64_t sq_state_bytes(int batch, int heads, int dim) { return (int64_t)batch * heads * dim * 52; }
 
+int64_t sq_scan_workspace(int batch, int length, int heads, int groups, int layout) {
+  return scan_prep_bytes(batch, length, heads, groups, layout);
+}
+
 int sq_scan(const sq_scan_args* a, void* stream) {
   if (!a) return fail(SQ_EINVAL, "null scan args");
   const void* req[] = {a->x, a->dt, a->A, a->B, a->C, a->D, a->dt_bias, a->permutation, a->basis,
@@ -148,6 +154,12 @@ int sq_scan(const sq_scan_args* a, void* stream) {
   P.perm = a->permutation; P.basis = a->basis; P.latent_scale = a->latent_scale; P.predictor = a->predictor;
   P.lo = a->lo; P.hi = a->hi; P.q4 = a->q4; P.latent = a->latent; P.s8 = a->s8; P.s4 = a->s4;
   P.y = a->y; P.y_sb = a->y_batch_stride; P.y_st = a->y_token_stride;
+  if (a->workspace) {
+    const long long need = scan_prep_bytes(a->batch, a->length, a->heads, a->groups, a->layout);
+    if (need < 0 || a->workspace_bytes < need || !aligned(a->workspace, 256))
+      return fail(SQ_EINVAL, "scan: workspace smaller than sq_scan_workspace() or not 256-byte aligned");
+    scan_prep_bind(P, a->workspace);
+  }
   return check(launch_scan(P, (cudaStream_t)stream), "sq_scan");
 }
 
@@ -319,7 +331,8 @@ int sq_model_reserve(sq_model* m, int max_tokens) {
       {(void**)&m->yn, T * kDInner * 2}, {(void**)&m->stage, stage * 2},
       {(void**)&m->logits, (size_t)64 * m->cfg.vocab * 2},
       {(void**)&m->partials, std::max(T * nt * sizeof(float2), (size_t)argmax_workspace_bytes(64, m->cfg.vocab))},
-      {(void**)&m->tlogit, T * sizeof(float)}};
+      {(void**)&m->tlogit, T * sizeof(float)},
+      {(void**)&m->prep, (size_t)scan_prep_bytes_any_layout(1, max_tokens, kHeads, kGroups)}};
   for (auto& a : allocs) {
     if (cudaMalloc(a.p, a.bytes) != cudaSuccess) {
       cudaGetLastError();
@@ -382,6 +395,7 @@ int sq_model_forward(sq_model* m, const int64_t* ids, int batch, int tokens, int
       P.x = m->xbc; P.B = m->xbc + kDInner; P.C = m->xbc + kDInner + 1024;
       P.x_sb = P.b_sb = P.c_sb = (long long)tokens * kXbc; P.x_st = P.b_st = P.c_st = kXbc;
     }
+    if (!step) scan_prep_bind(P, m->prep);
     SQ_TRY(launch_scan(P, st), "ssu scan");
     const AdapterPtrs& ad = m->adapters[l];
     SQ_TRY(launch_resurface_gatednorm(m->y, m->zx, kZx, m->hn, kDModel, ad.V ? &ad : nullptr, L.gated_norm_weight,

@@ -497,6 +497,452 @@ ssu_sq325_kernel(const ScanParams P) {
   copy_out(reinterpret_cast<unsigned char*>(P.s4 + row0), reinterpret_cast<unsigned char*>(pS4), rows * 2);
 }
 
+// ============================================================================================
+// Two-kernel path for multi-token calls (modes 0 and 1, 64 <= dim, 128 threads per CTA).
+//
+// scan_prep_kernel does the per-(batch, token, group) work once instead of once per CTA of
+// the group: the B/C conv (mode 1), the predictor readout vector cvec, the pcz pair and the
+// five zero-tier dots, and dt/decay per head.  Its outputs go to a caller workspace:
+//   bc   [B][T][G][256] fp16   conv'd B (tier order) then conv'd C (tier order)
+//   pv   [B][T][G][FP]  fp32   cvec[0..NS) | pcz0 pcz1 | B.C, b0.C, b1.C, b0.B, b1.B | pad
+//   ddt  [B][T][H]      float2 (dt after softplus, exp(A dt))
+// ssu_chunk_kernel then streams x (raw in mode 1), bc, pv and ddt through a cp.async ring and
+// runs the recurrence with B*dt precomputed per head.  Same arithmetic, operation for
+// operation, as the fused kernel above: results are bit-identical.
+// ============================================================================================
+
+constexpr int kPrepTokens = 16;   // tokens per prep CTA
+constexpr int kChunkTC = 8;       // tokens per chunk in the chunk kernel
+
+template <int N8, int N4>
+struct PrepLayout {
+  static constexpr int NS = N8 + N4, NZ = 128 - NS, F = NS + 2;
+  static constexpr int FP = (F + 5 + 3) / 4 * 4;       // pv floats per (b,t,g), 16-byte rows
+};
+
+template <int N8, int N4, int MODE>
+__global__ void __launch_bounds__(256)
+scan_prep_kernel(const ScanParams P) {
+  using PL = PrepLayout<N8, N4>;
+  constexpr int NS = PL::NS, NZ = PL::NZ, F = PL::F, FP = PL::FP;
+  constexpr int TT = kPrepTokens;
+  constexpr int oPred = TT * 256 * 4;
+  constexpr int oBasis = oPred + (F * (NZ + 1) * 4 + 15) / 16 * 16;
+  constexpr int oPerm = oBasis + (2 * NZ * 4 + 15) / 16 * 16;
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* sBC = reinterpret_cast<float*>(smem);                       // [TT][256] conv'd B | C (tier order)
+  float* sPred = reinterpret_cast<float*>(smem + oPred);             // [F][NZ+1]
+  float* sBasis = reinterpret_cast<float*>(smem + oBasis);           // [2][NZ]
+  int* sPerm = reinterpret_cast<int*>(smem + oPerm);                 // [128]
+  uint16_t* rawPred = reinterpret_cast<uint16_t*>(smem);             // staging in sBC
+  uint16_t* rawBasis = rawPred + (F * NZ * 2 + 15) / 16 * 8;
+  uint8_t* rawPerm = reinterpret_cast<uint8_t*>(rawBasis + (NZ * 4 + 15) / 16 * 8);
+
+  const int tid = threadIdx.x;
+  const int t0 = blockIdx.x * TT, g = blockIdx.y, b = blockIdx.z;
+  const int nt = min(TT, P.length - t0);
+  stage16(rawPred, P.predictor + (long long)g * F * NZ, F * NZ * 2, tid, 256);
+  stage16(rawBasis, P.basis + (long long)g * NZ * 2, NZ * 4, tid, 256);
+  stage16(rawPerm, P.perm + g * 128, 128, tid, 256);
+  cp_async_wait_all();
+  __syncthreads();
+  for (int i = tid; i < F * NZ; i += 256) {
+    const int f = i / NZ, d = i - f * NZ;
+    sPred[f * (NZ + 1) + d] = h2f(rawPred[i]);
+  }
+  for (int i = tid; i < NZ; i += 256) {
+    sBasis[i] = h2f(rawBasis[2 * i + 0]);
+    sBasis[NZ + i] = h2f(rawBasis[2 * i + 1]);
+  }
+  if (tid < 128) sPerm[tid] = rawPerm[tid];
+  __syncthreads();
+
+  // ---- B/C of tier coordinate j = tid % 128 (B for tid < 128, C above), conv'd in mode 1 ----
+  {
+    const int j = tid & 127;
+    const bool isC = tid >= 128;
+    const int n = sPerm[j];
+    const uint16_t* src = (isC ? P.C + (long long)b * P.c_sb : P.B + (long long)b * P.b_sb) + g * 128 + n;
+    const long long st = isC ? P.c_st : P.b_st;
+    float w[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+    float h1 = 0.f, h2 = 0.f, h3 = 0.f;
+    if (MODE == 1) {
+      const int ch = (isC ? 9216 : 8192) + g * 128 + n;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = h2f(P.conv_w[ch * 4 + i]);
+      w[4] = h2f(P.conv_b[ch]);
+      if (t0 >= 3) h1 = h2f(src[(long long)(t0 - 3) * st]);
+      if (t0 >= 2) h2 = h2f(src[(long long)(t0 - 2) * st]);
+      if (t0 >= 1) h3 = h2f(src[(long long)(t0 - 1) * st]);
+    }
+    uint16_t* out = P.prep_bc + (((long long)b * P.length + t0) * P.groups + g) * 256 + tid;
+    for (int t = 0; t < nt; ++t) {
+      const float raw = h2f(src[(long long)(t0 + t) * st]);
+      const float v = MODE == 1 ? conv_prefill_value(w, h1, h2, h3, raw) : raw;
+      h1 = h2; h2 = h3; h3 = raw;
+      sBC[t * 256 + tid] = v;
+      out[(long long)t * P.groups * 256] = f2h(v);     // v is an fp16 value: exact
+    }
+  }
+  // ---- dt / decay for the group's heads ----
+  {
+    const int hpg = P.heads / P.groups;
+    for (int i = tid; i < nt * hpg; i += 256) {
+      const int t = i / hpg, h = g * hpg + i % hpg;
+      const float bias = P.dt_bias_is_f32 ? reinterpret_cast<const float*>(P.dt_bias)[h]
+                                          : h2f(reinterpret_cast<const uint16_t*>(P.dt_bias)[h]);
+      const float dtv = softplus_ref(h2f(P.dt[(long long)b * P.dt_sb + (long long)(t0 + t) * P.dt_st + h]) + bias);
+      P.prep_ddt[((long long)b * P.length + t0 + t) * P.heads + h] = make_float2(dtv, expf(P.A[h] * dtv));
+    }
+  }
+  __syncthreads();
+  // ---- group dots (same accumulation order as the fused kernel) ----
+  float* pv = P.prep_pv + (((long long)b * P.length + t0) * P.groups + g) * FP;
+  for (int task = tid; task < nt * FP; task += 256) {
+    const int t = task / FP, f = task - t * FP;
+    const float* tb = sBC + t * 256;
+    float r = 0.f;
+    if (f < F) {
+      const float* pr = sPred + f * (NZ + 1);
+      float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 4
+      for (int d = 0; d < NZ; d += 2) {
+        acc0 = fmaf(tb[128 + NS + d], pr[d], acc0);
+        acc1 = fmaf(tb[128 + NS + d + 1], pr[d + 1], acc1);
+      }
+      r = acc0 + acc1;
+    } else if (f < F + 5) {
+      const int k = f - F;   // 0: B.C, 1: basis0.C, 2: basis1.C, 3: basis0.B, 4: basis1.B
+      const float* us = (k == 0) ? nullptr : sBasis + ((k - 1) & 1) * NZ;
+      const int voff = (k >= 3 || k == 0) ? 0 : 128;   // 0 -> B, 128 -> C
+      float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 4
+      for (int d = 0; d < NZ; d += 2) {
+        const float u0 = (k == 0) ? tb[NS + d] : us[d], u1 = (k == 0) ? tb[NS + d + 1] : us[d + 1];
+        const float v0 = (k == 0) ? tb[128 + NS + d] : tb[voff + NS + d];
+        const float v1 = (k == 0) ? tb[128 + NS + d + 1] : tb[voff + NS + d + 1];
+        acc0 = fmaf(u0, v0, acc0);
+        acc1 = fmaf(u1, v1, acc1);
+      }
+      r = acc0 + acc1;
+    }
+    pv[(long long)t * P.groups * FP + f] = r;
+  }
+}
+
+// Shared-memory plan of the chunk kernel (byte offsets, 16-byte aligned regions).
+//   ring  R = 2 TC slots per token: raw (mode 1) or conv'd x[128] fp16 | bc[256] fp16 |
+//         pv[FP] fp32 | ddt[hpc] float2.  Slot of token t (call-relative, may be negative)
+//         = t mod R; slots of tokens -3..-1 hold the x conv history (zeros after a reset).
+//   T     sP4 [TC][hpc][64] float4 {B*dt pair, C pair} per head, sX [TC][128] conv'd x;
+//         before the first / after the last chunk: the packed rows.
+//   W     x conv taps + bias [128][5] fp32.
+template <int N8, int N4>
+struct ChunkSmem {
+  static constexpr int FP = PrepLayout<N8, N4>::FP;
+  static constexpr int TC = kChunkTC, R = 2 * kChunkTC;
+  static constexpr int oX = 0, oBC = 256, oPV = 768, oDD = 768 + FP * 4;
+  static constexpr int kSlot = (oDD + 2 * 8 + 15) / 16 * 16;   // hpc <= 2
+  static constexpr int oRing = 0;
+  static constexpr int oT = R * kSlot;
+  static constexpr int kTok = TC * 2 * 64 * 16 + TC * 128 * 4;
+  static constexpr int kT = kTok > 128 * 52 ? kTok : 128 * 52;
+  static constexpr int oW = oT + kT;
+  static constexpr int kBytes = oW + 128 * 5 * 4;
+};
+
+__device__ __forceinline__ void cp_async8(void* smem_dst, const void* gsrc) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" :: "r"(d), "l"(gsrc) : "memory");
+}
+
+template <int N8, int N4, int MODE>
+__global__ void __launch_bounds__(128, scan_min_blocks<N8, N4>())
+ssu_chunk_kernel(const ScanParams P) {
+  using L = ChunkSmem<N8, N4>;
+  constexpr int NS = N8 + N4, F = NS + 2, FP = L::FP;
+  constexpr int TC = L::TC, R = L::R, SB = L::kSlot;
+  constexpr int W8 = N8 / 2, W4 = N4 / 2;
+  constexpr int NP = NS / 2;
+  static_assert(N8 % 2 == 0 && N4 % 2 == 0, "tiers are nibble pairs");
+
+  extern __shared__ __align__(16) unsigned char smem[];
+  unsigned char* ring = smem + L::oRing;
+  float4* sP4 = reinterpret_cast<float4*>(smem + L::oT);                    // [TC][hpc][64]
+  float* sX = reinterpret_cast<float*>(smem + L::oT + TC * 2 * 64 * 16);    // [TC][128]
+  float* sW = reinterpret_cast<float*>(smem + L::oW);                       // [128][5]
+  float* sPf = reinterpret_cast<float*>(sP4);
+  unsigned char* sPack = smem + L::oT;
+
+  const int tid = threadIdx.x;
+  const int dim = P.dim;
+  const int hpc = 128 / dim;
+  const int b = blockIdx.y;
+  const int h0 = blockIdx.x * hpc;
+  const int hl = tid / dim;
+  const int p = tid - hl * dim;
+  const int h = h0 + hl;
+  const int hpg = P.heads / P.groups;
+  const int g = h0 / hpg;
+  const bool group_leader = (h0 % hpg) == 0;
+  const long long row0 = ((long long)b * P.heads + h0) * dim;
+  constexpr int rows = 128;
+
+  auto slot_of = [&](int t) { return ring + (t & (R - 1)) * SB; };
+  const uint16_t* xb = P.x + (long long)b * P.x_sb + (long long)h0 * dim;
+  const bool vec = ((((uintptr_t)xb) & 15) == 0) && (P.x_st & 7) == 0;
+  const long long btg = (long long)b * P.length;       // token row base of this batch entry
+  constexpr int kPcs = 16 + 32 + FP / 4;               // 16-byte pieces per token (x, bc, pv)
+
+  auto prefetch = [&](int c0) {
+    const int nt = min(TC, P.length - c0);
+    for (int i = tid; i < nt * (kPcs + hpc); i += 128) {
+      const int t = i / (kPcs + hpc), r = i - t * (kPcs + hpc);
+      const long long tt = c0 + t;
+      unsigned char* slot = slot_of(c0 + t);
+      if (r < 16) {
+        const uint16_t* src = xb + tt * P.x_st + r * 8;
+        uint16_t* dst = reinterpret_cast<uint16_t*>(slot + L::oX) + r * 8;
+        if (vec) cp_async16(dst, src);
+        else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) dst[e] = src[e];
+        }
+      } else if (r < 48) {
+        cp_async16(slot + L::oBC + (r - 16) * 16, P.prep_bc + ((btg + tt) * P.groups + g) * 256 + (r - 16) * 8);
+      } else if (r < kPcs) {
+        cp_async16(slot + L::oPV + (r - 48) * 16, P.prep_pv + ((btg + tt) * P.groups + g) * FP + (r - 48) * 4);
+      } else {
+        cp_async8(slot + L::oDD + (r - kPcs) * 8, P.prep_ddt + (btg + tt) * P.heads + h0 + (r - kPcs));
+      }
+    }
+  };
+
+  // ---- stage packed rows; x conv taps; zero history ----
+  unsigned char* pLo = sPack;
+  unsigned char* pHi = pLo + rows * W8;
+  unsigned char* pQ4 = pHi + rows * W8;
+  unsigned char* pLat = pQ4 + rows * W4;
+  uint16_t* pS8 = reinterpret_cast<uint16_t*>(pLat + rows * 2);
+  uint16_t* pS4 = pS8 + rows;
+  stage16(pLo, P.lo + row0 * W8, rows * W8, tid, 128);
+  stage16(pHi, P.hi + row0 * W8, rows * W8, tid, 128);
+  stage16(pQ4, P.q4 + row0 * W4, rows * W4, tid, 128);
+  stage16(pLat, P.latent + row0 * 2, rows * 2, tid, 128);
+  stage16(pS8, P.s8 + row0, rows * 2, tid, 128);
+  stage16(pS4, P.s4 + row0, rows * 2, tid, 128);
+  if (MODE == 1) {
+    const int ch = h0 * dim + tid;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sW[tid * 5 + i] = h2f(P.conv_w[ch * 4 + i]);
+    sW[tid * 5 + 4] = h2f(P.conv_b[ch]);
+#pragma unroll
+    for (int k = -3; k < 0; ++k) reinterpret_cast<uint16_t*>(slot_of(k) + L::oX)[tid] = 0;
+  }
+  prefetch(0);
+  cp_async_wait_all();
+  __syncthreads();
+
+  // ---- decode own row (:81-114) ----
+  float S[NS];
+  {
+    const float s8 = h2f(pS8[tid]), s4 = h2f(pS4[tid]);
+#pragma unroll
+    for (int j = 0; j < N8; ++j) {
+      int lo = (pLo[tid * W8 + j / 2] >> (4 * (j & 1))) & 15;
+      int hi = (pHi[tid * W8 + j / 2] >> (4 * (j & 1))) & 15;
+      int ub = (hi << 4) | lo;
+      S[j] = (float)(ub - 256 * (ub > 127)) * s8;
+    }
+#pragma unroll
+    for (int j = 0; j < N4; ++j) {
+      int nib = (pQ4[tid * W4 + j / 2] >> (4 * (j & 1))) & 15;
+      S[N8 + j] = (float)(nib - 16 * (nib > 7)) * s4;
+    }
+  }
+  const float ls0 = h2f(P.latent_scale[g * 2 + 0]), ls1 = h2f(P.latent_scale[g * 2 + 1]);
+  const float ils0 = __frcp_rn(ls0), ils1 = __frcp_rn(ls1);
+  float z0 = e4m3_to_f32(pLat[tid * 2 + 0]) * ls0;
+  float z1 = e4m3_to_f32(pLat[tid * 2 + 1]) * ls1;
+  const float dv = P.d_is_f32 ? reinterpret_cast<const float*>(P.D)[h] : h2f(reinterpret_cast<const uint16_t*>(P.D)[h]);
+  const float inv127 = 1.0f / 127.0f, inv7 = 1.0f / 7.0f;
+  float s8 = 0.f, s4 = 0.f;
+
+  for (int c0 = 0; c0 < P.length; c0 += TC) {
+    const int nt = min(TC, P.length - c0);
+    cp_async_wait_all();
+    __syncthreads();                                   // chunk landed; previous tables (or the
+                                                       // packed rows read by the decode) free
+    // -- publish conv'd x and, per head, {B*dt, C} pairs in tier order --
+    {
+      float w[5];
+      const uint16_t* rx = reinterpret_cast<const uint16_t*>(ring + L::oX) + tid;
+      float h1 = 0.f, h2 = 0.f, h3 = 0.f;
+      if (MODE == 1) {
+#pragma unroll
+        for (int i = 0; i < 5; ++i) w[i] = sW[tid * 5 + i];
+        h1 = h2f(rx[((c0 - 3) & (R - 1)) * (SB / 2)]);
+        h2 = h2f(rx[((c0 - 2) & (R - 1)) * (SB / 2)]);
+        h3 = h2f(rx[((c0 - 1) & (R - 1)) * (SB / 2)]);
+      }
+      const int j = tid;
+#pragma unroll
+      for (int t = 0; t < TC; ++t) {
+        if (t < nt) {
+          const unsigned char* slot = slot_of(c0 + t);
+          const float raw = h2f(rx[((c0 + t) & (R - 1)) * (SB / 2)]);
+          float xv = raw;
+          if (MODE == 1) xv = conv_prefill_value(w, h1, h2, h3, raw);
+          h1 = h2; h2 = h3; h3 = raw;
+          sX[t * 128 + tid] = xv;
+          const uint16_t* bc = reinterpret_cast<const uint16_t*>(slot + L::oBC);
+          const float2* dd = reinterpret_cast<const float2*>(slot + L::oDD);
+          const float bv = h2f(bc[j]), cv = h2f(bc[128 + j]);
+          for (int hh = 0; hh < hpc; ++hh) {
+            float* q = sPf + ((t * hpc + hh) * 64 + (j >> 1)) * 4 + (j & 1);
+            q[0] = bv * dd[hh].x;
+            q[2] = cv;
+          }
+        }
+      }
+    }
+    __syncthreads();                                   // tables visible; raw x of the chunk consumed
+    if (c0 + TC < P.length) prefetch(c0 + TC);
+
+    // -- per-row recurrence, readout and requant (:115-162) for the chunk's tokens --
+#pragma unroll 1
+    for (int t = 0; t < nt; ++t) {
+      const unsigned char* slot = slot_of(c0 + t);
+      const float2 ddv = reinterpret_cast<const float2*>(slot + L::oDD)[hl];
+      const float dtv = ddv.x, dec = ddv.y;
+      const float x = sX[t * 128 + tid];
+      const float2 dd = make_float2(dec, dec), xx = make_float2(x, x);
+      const float4* cp = sP4 + (t * hpc + hl) * 64;
+      const float* pv = reinterpret_cast<const float*>(slot + L::oPV);
+      const float2* vp = reinterpret_cast<const float2*>(pv);
+      float2 ya = make_float2(0.f, 0.f), yb = ya, ca = ya, cb = ya;
+      float m8a = 0.f, m8b = 0.f, m4a = 0.f, m4b = 0.f;
+#pragma unroll
+      for (int jp = 0; jp < NP; ++jp) {
+        const float4 bc = cp[jp];
+        const float2 cv = vp[jp];
+        const float2 pr = make_float2(S[2 * jp], S[2 * jp + 1]);
+        const float2 upd = __fmul2_rn(make_float2(bc.x, bc.y), xx);                   // (B*dt)*x
+        const float2 sn = __ffma2_rn(pr, dd, upd);                                      // prior*decay + upd
+        S[2 * jp] = sn.x; S[2 * jp + 1] = sn.y;
+        if (jp & 1) { yb = __ffma2_rn(sn, make_float2(bc.z, bc.w), yb); cb = __ffma2_rn(pr, cv, cb); }
+        else        { ya = __ffma2_rn(sn, make_float2(bc.z, bc.w), ya); ca = __ffma2_rn(pr, cv, ca); }
+        if (2 * jp < N8) { m8a = fmaxf(m8a, fabsf(sn.x)); m8b = fmaxf(m8b, fabsf(sn.y)); }
+        else             { m4a = fmaxf(m4a, fabsf(sn.x)); m4b = fmaxf(m4b, fabsf(sn.y)); }
+      }
+      const float pcz0 = pv[NS], pcz1 = pv[NS + 1];
+      const float dbc = pv[F + 0], dc0 = pv[F + 1], dc1 = pv[F + 2], db0 = pv[F + 3], db1 = pv[F + 4];
+      const float ysum = (ya.x + ya.y) + (yb.x + yb.y);
+      const float ycorr = (ca.x + ca.y) + (cb.x + cb.y);
+      const float xdt = x * dtv;
+      float out = ysum + (dec * (z0 * dc0 + z1 * dc1) + xdt * dbc + x * dv);
+      out = out + dec * (ycorr + z0 * pcz0 + z1 * pcz1);
+      P.y[(long long)b * P.y_sb + (long long)(c0 + t) * P.y_st + (long long)h * dim + p] = f2h(out);
+      // latent FP8 requant (:149-154)
+      z0 = z0 * dec + xdt * db0;
+      z1 = z1 * dec + xdt * db1;
+      z0 = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(div_exact(z0, ls0, ils0), -448.f), 448.f))) * ls0;
+      z1 = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(div_exact(z1, ls1, ils1), -448.f), 448.f))) * ls1;
+      // INT8 / INT4 requant (:155-162, scripts/state_ppl_codec_v6.py:52-61)
+      const float m8 = fmaxf(m8a, m8b), m4 = fmaxf(m4a, m4b);
+      s8 = h2f(f2h(fmaxf(div_exact(m8, 127.f, inv127), 1e-8f)));
+      s4 = h2f(f2h(fmaxf(div_exact(m4, 7.f, inv7), 1e-8f)));
+      const float i8 = s8 > 0.f ? __frcp_rn(s8) : 0.f;
+      const float i4 = s4 > 0.f ? __frcp_rn(s4) : 0.f;
+      const float2 s82 = make_float2(s8, s8), ns82 = make_float2(-s8, -s8), i82 = make_float2(i8, i8);
+      const float2 s42 = make_float2(s4, s4), ns42 = make_float2(-s4, -s4), i42 = make_float2(i4, i4);
+      const float m8s = -kMagic * s8, m4s = -kMagic * s4;
+      const float2 nm82 = make_float2(m8s, m8s), nm42 = make_float2(m4s, m4s);
+#pragma unroll
+      for (int jp = 0; jp < NP; ++jp) {
+        const bool t8 = 2 * jp < N8;
+        requant_pair(S[2 * jp], S[2 * jp + 1], t8 ? ns82 : ns42, t8 ? i82 : i42, t8 ? 127.f : 7.f,
+                     t8 ? s82 : s42, t8 ? nm82 : nm42);
+      }
+    }
+  }
+
+  // ---- conv cache update (mode 1): raw columns of the newest positions ----
+  if (MODE == 1) {
+    uint16_t* cache = P.conv_cache + (long long)b * P.conv_cache_sb;
+    const int nwrite = min(4, P.length);
+    for (int i = 0; i < nwrite; ++i) {
+      const int t = P.length - 1 - i;
+      const int cs = (P.conv_pos + t) & 3;
+      cache[cs * 10240 + h0 * dim + tid] = reinterpret_cast<const uint16_t*>(slot_of(t) + L::oX)[tid];
+      if (group_leader) {
+        cache[cs * 10240 + 8192 + g * 128 + tid] = P.B[(long long)b * P.b_sb + (long long)t * P.b_st + g * 128 + tid];
+        cache[cs * 10240 + 9216 + g * 128 + tid] = P.C[(long long)b * P.c_sb + (long long)t * P.c_st + g * 128 + tid];
+      }
+    }
+  }
+
+  // ---- pack once (:163-181) and store coalesced ----
+  __syncthreads();
+  {
+    const float i8 = s8 > 0.f ? __frcp_rn(s8) : 0.f;
+    const float i4 = s4 > 0.f ? __frcp_rn(s4) : 0.f;
+#pragma unroll
+    for (int j = 0; j < N8; j += 2) {
+      const int qa = __float2int_rn(div_exact(S[j], s8, i8));
+      const int qb = __float2int_rn(div_exact(S[j + 1], s8, i8));
+      pLo[tid * W8 + j / 2] = (unsigned char)((qa & 15) | ((qb & 15) << 4));
+      pHi[tid * W8 + j / 2] = (unsigned char)(((qa >> 4) & 15) | (((qb >> 4) & 15) << 4));
+    }
+#pragma unroll
+    for (int j = 0; j < N4; j += 2) {
+      const int qa = __float2int_rn(div_exact(S[N8 + j], s4, i4));
+      const int qb = __float2int_rn(div_exact(S[N8 + j + 1], s4, i4));
+      pQ4[tid * W4 + j / 2] = (unsigned char)((qa & 15) | ((qb & 15) << 4));
+    }
+    pLat[tid * 2 + 0] = f32_to_e4m3(fminf(fmaxf(div_exact(z0, ls0, ils0), -448.f), 448.f));
+    pLat[tid * 2 + 1] = f32_to_e4m3(fminf(fmaxf(div_exact(z1, ls1, ils1), -448.f), 448.f));
+    pS8[tid] = f2h(s8);
+    pS4[tid] = f2h(s4);
+  }
+  __syncthreads();
+  auto copy_out = [&](unsigned char* dst, const unsigned char* src, int bytes) {
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (int i = tid; i < bytes / 16; i += 128) d[i] = s[i];
+  };
+  copy_out(P.lo + row0 * W8, pLo, rows * W8);
+  copy_out(P.hi + row0 * W8, pHi, rows * W8);
+  copy_out(P.q4 + row0 * W4, pQ4, rows * W4);
+  copy_out(P.latent + row0 * 2, pLat, rows * 2);
+  copy_out(reinterpret_cast<unsigned char*>(P.s8 + row0), reinterpret_cast<unsigned char*>(pS8), rows * 2);
+  copy_out(reinterpret_cast<unsigned char*>(P.s4 + row0), reinterpret_cast<unsigned char*>(pS4), rows * 2);
+}
+
+template <int N8, int N4, int MODE>
+int launch_chunked(const ScanParams& P, bool prepare_only, cudaStream_t stream) {
+  using PL = PrepLayout<N8, N4>;
+  constexpr int prep_smem = kPrepTokens * 256 * 4 + (PL::F * (PL::NZ + 1) * 4 + 15) / 16 * 16 +
+                            (2 * PL::NZ * 4 + 15) / 16 * 16 + 128 * 4;
+  constexpr int chunk_smem = ChunkSmem<N8, N4>::kBytes;
+  auto kp = scan_prep_kernel<N8, N4, MODE>;
+  auto kc = ssu_chunk_kernel<N8, N4, MODE>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kp, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem) != cudaSuccess ||
+        cudaFuncSetAttribute(kc, cudaFuncAttributeMaxDynamicSharedMemorySize, chunk_smem) != cudaSuccess ||
+        cudaFuncSetAttribute(kc, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+      return kECuda;
+    attr = true;
+  }
+  if (prepare_only) return kOk;
+  dim3 gp((P.length + kPrepTokens - 1) / kPrepTokens, P.groups, P.batch);
+  kp<<<gp, 256, prep_smem, stream>>>(P);
+  dim3 gc(P.heads / (128 / P.dim), P.batch);
+  kc<<<gc, 128, chunk_smem, stream>>>(P);
+  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+}
+
 template <int N8, int N4, int KJ, int MODE, int TC = (MODE == 2 ? 1 : kTC)>
 int launch_kj(const ScanParams& P, int hpc, cudaStream_t stream) {
   const size_t smem = ScanSmem<N8, N4, TC>::kBytes;
@@ -517,6 +963,8 @@ int launch_kj(const ScanParams& P, int hpc, cudaStream_t stream) {
 template <int N8, int N4>
 int launch_t(const ScanParams& P, int hpc, cudaStream_t stream) {
   const int bd = hpc * P.dim;
+  if (P.conv_mode != 2 && P.prep_bc && P.prep_pv && P.prep_ddt && bd == 128 && hpc <= 2)
+    return P.conv_mode == 1 ? launch_chunked<N8, N4, 1>(P, false, stream) : launch_chunked<N8, N4, 0>(P, false, stream);
   if (P.conv_mode == 1) return bd == 128 ? launch_kj<N8, N4, 1, 1>(P, hpc, stream) : kEInval;
   if (P.conv_mode == 2) return bd == 128 ? launch_kj<N8, N4, 1, 2>(P, hpc, stream) : kEInval;
   if (bd >= 128) return launch_kj<N8, N4, 1, 0>(P, hpc, stream);
@@ -535,6 +983,8 @@ int prepare_t() {
   st |= launch_kj<N8, N4, 4, 0>(P, 0, 0);
   st |= launch_kj<N8, N4, 1, 1>(P, 0, 0);
   st |= launch_kj<N8, N4, 1, 2>(P, 0, 0);
+  st |= launch_chunked<N8, N4, 0>(P, true, 0);
+  st |= launch_chunked<N8, N4, 1>(P, true, 0);
   return st;
 }
 
@@ -544,6 +994,36 @@ int prepare_scan_kernels() {
   int st = prepare_t<32, 28>() | prepare_t<16, 60>() | prepare_t<8, 76>() | prepare_t<24, 44>() |
            prepare_t<36, 20>() | prepare_t<40, 12>() | prepare_t<44, 4>();
   return st ? kECuda : kOk;
+}
+
+namespace {
+int prep_fp(int layout) {
+  const int f = kLayouts[layout].n8 + kLayouts[layout].n4 + 2;
+  return (f + 5 + 3) / 4 * 4;
+}
+long long round256(long long v) { return (v + 255) / 256 * 256; }
+}  // namespace
+
+long long scan_prep_bytes(int batch, int length, int heads, int groups, int layout) {
+  if (layout < 0 || layout > 6 || batch <= 0 || length <= 0 || heads <= 0 || groups <= 0) return -1;
+  const long long bt = (long long)batch * length;
+  return round256(bt * groups * 512) + round256(bt * groups * prep_fp(layout) * 4) + round256(bt * heads * 8);
+}
+
+long long scan_prep_bytes_any_layout(int batch, int length, int heads, int groups) {
+  long long m = 0;
+  for (int l = 0; l < 7; ++l) m = std::max(m, scan_prep_bytes(batch, length, heads, groups, l));
+  return m;
+}
+
+void scan_prep_bind(ScanParams& P, void* ws) {
+  unsigned char* w = static_cast<unsigned char*>(ws);
+  const long long bt = (long long)P.batch * P.length;
+  P.prep_bc = reinterpret_cast<uint16_t*>(w);
+  w += round256(bt * P.groups * 512);
+  P.prep_pv = reinterpret_cast<float*>(w);
+  w += round256(bt * P.groups * prep_fp(P.layout) * 4);
+  P.prep_ddt = reinterpret_cast<float2*>(w);
 }
 
 int launch_scan(const ScanParams& P, cudaStream_t stream) {

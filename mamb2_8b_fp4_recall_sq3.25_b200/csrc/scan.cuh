@@ -41,9 +41,20 @@ struct ScanParams {
   uint16_t* conv_cache;     // [B,4,10240] fp16 ring, slot = position % 4
   int conv_pos;             // absolute position of the first token of this call
   long long conv_cache_sb;  // batch stride of the ring (elements)
+  // Optional workspace of the two-kernel multi-token path (modes 0/1, 128-thread CTAs):
+  // per-(batch, token, group) conv'd B/C, predictor/zero-tier dots and per-head dt/decay,
+  // computed once by a prep kernel.  Null pointers select the single fused kernel.
+  uint16_t* prep_bc;        // [B][T][G][256] fp16
+  float* prep_pv;           // [B][T][G][FP] fp32
+  float2* prep_ddt;         // [B][T][H]
 };
 
 int launch_scan(const ScanParams& p, cudaStream_t stream);
+// Workspace of the two-kernel path (bytes) and the binding of its three arrays into P
+// (P.batch/length/groups/layout set); -1 for invalid sizes.
+long long scan_prep_bytes(int batch, int length, int heads, int groups, int layout);
+long long scan_prep_bytes_any_layout(int batch, int length, int heads, int groups);
+void scan_prep_bind(ScanParams& P, void* ws);
 int prepare_scan_kernels();
 
 }  // namespace sq

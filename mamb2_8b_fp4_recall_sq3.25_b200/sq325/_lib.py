@@ -38,7 +38,8 @@ class ScanArgs(C.Structure):
                 ('D', p), ('d_is_f32', i32), ('dt_bias', p), ('dt_bias_is_f32', i32),
                 ('permutation', p), ('basis', p), ('latent_scale', p), ('predictor', p),
                 ('lo', p), ('hi', p), ('q4', p), ('latent', p), ('s8', p), ('s4', p),
-                ('y', p), ('y_batch_stride', i64), ('y_token_stride', i64)]
+                ('y', p), ('y_batch_stride', i64), ('y_token_stride', i64),
+                ('workspace', p), ('workspace_bytes', i64)]
 
 
 class ModelConfig(C.Structure):
@@ -66,6 +67,7 @@ _PROTOS = {
     'sq_state_decode': (C.c_int, [C.c_int] * 5 + [p] * 9 + [p]),
     'sq_state_encode': (C.c_int, [C.c_int] * 6 + [p] * 9 + [p]),
     'sq_fp4_decode': (C.c_int, [p, p, p, C.c_int, C.c_int, p, i64, p]),
+    'sq_scan_workspace': (i64, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
     'sq_fp4_linear_workspace': (i64, [C.c_int, C.c_int, C.c_int]),
     'sq_fp4_linear': (C.c_int, [p, p, p, C.c_int, C.c_int, p, i64, C.c_int, p, i64, p, i64, p]),
     'sq_fp4_linear_static_max_k': (i64, []),

@@ -112,11 +112,14 @@ def _state_ptrs(state):
 
 
 @torch.no_grad()
-def scan(x, dt, A, B, C_, D, dt_bias, state, permutation, basis, latent_scale, predictor, *, layout):
+def scan(x, dt, A, B, C_, D, dt_bias, state, permutation, basis, latent_scale, predictor, *, layout,
+         fused=False):
     """Mutate `state` for every token and return (y fp16 [batch,L,H,P], None).
 
     Same contract and checks as the reference scan (:184-236); the predictor readout
-    correction is computed inside the kernel.
+    correction is computed on the device.  By default a workspace from the torch allocator
+    selects the two-kernel path (group-level dots once per group); fused=True runs the single
+    fused kernel instead.  Both give identical bytes.
     """
     spec = layout_descriptor(layout)
     if x.ndim != 4 or x.dtype != torch.float16 or not x.is_cuda:
@@ -165,6 +168,12 @@ def scan(x, dt, A, B, C_, D, dt_bias, state, permutation, basis, latent_scale, p
     t = state.tensors
     a.lo, a.hi, a.q4, a.latent, a.s8, a.s4 = (t[k].data_ptr() for k in ('lo', 'hi', 'q4', 'latent', 's8', 's4'))
     a.y, a.y_batch_stride, a.y_token_stride = y.data_ptr(), length * heads * dim, heads * dim
+    ws = None
+    if not fused:
+        need = _lib.load().sq_scan_workspace(batch, length, heads, groups, layout_index(layout))
+        if need > 0:
+            ws = torch.empty(need, device=x.device, dtype=torch.uint8)
+            a.workspace, a.workspace_bytes = ws.data_ptr(), need
     with torch.cuda.device(x.device):
         _lib.call('sq_scan', C.byref(a), _lib.stream_ptr())
     return y, None

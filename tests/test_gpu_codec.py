@@ -137,3 +137,42 @@ def test_codec_round_trip_many_steps():
     scale = np.abs(yo).max()
     assert err.max() <= 0.05 * scale, (err.max(), scale)
     assert np.sqrt((err ** 2).mean()) <= 5e-3 * scale
+
+
+def _random_scan_inputs(layout, B, L, H, P, G, seed):
+    from sq325 import codec
+    g = torch.Generator(device='cuda').manual_seed(seed)
+    n8, n4, nz = oc.layout_counts(layout)
+    x = torch.randn(B, L, H, P, device='cuda', generator=g).half()
+    dt = (torch.randn(B, L, H, device='cuda', generator=g) * 0.5).half()
+    A = -(torch.rand(H, device='cuda', generator=g) * 3 + 0.1)
+    Bm = torch.randn(B, L, G, 128, device='cuda', generator=g).half()
+    Cm = torch.randn(B, L, G, 128, device='cuda', generator=g).half()
+    D = torch.randn(H, device='cuda', generator=g).half()
+    db = (torch.rand(H, device='cuda', generator=g) * 3 - 4).half()
+    perm = torch.stack([torch.randperm(128, device='cuda', generator=g) for _ in range(G)]).to(torch.uint8)
+    basis = torch.randn(G, nz, 2, device='cuda', generator=g).half()
+    ls = (torch.rand(G, 2, device='cuda', generator=g) + 0.1).half()
+    pred = (torch.randn(G, n8 + n4 + 2, nz, device='cuda', generator=g) / np.sqrt(n8 + n4 + 2)).half()
+    st = codec.allocate_state(B, H, P, 128, 'cuda', layout=layout)
+    for k in ('lo', 'hi', 'q4'):
+        st.tensors[k].copy_(torch.randint(0, 256, st.tensors[k].shape, device='cuda', generator=g).to(torch.uint8))
+    for k in ('s8', 's4'):
+        st.tensors[k].copy_((torch.rand(st.tensors[k].shape, device='cuda', generator=g) * 0.05).half())
+    return (x, dt, A, Bm, Cm, D, db), st, (perm, basis, ls, pred)
+
+
+@pytest.mark.parametrize('layout', oc.LAYOUTS)
+@pytest.mark.parametrize('length', [1, 7, 8, 37])
+def test_two_kernel_path_matches_fused_kernel_bytes(layout, length):
+    """Model geometry (128-thread CTAs): the prep + chunk kernels and the single fused kernel
+    must produce the same y and the same packed state bytes, for ragged chunk counts."""
+    from sq325 import codec
+    args, st, tables = _random_scan_inputs(layout, 2, length, 128, 64, 8, seed=length)
+    st2 = st.clone()
+    y1, _ = codec.scan(*args, st, *tables, layout=layout, fused=True)
+    y2, _ = codec.scan(*args, st2, *tables, layout=layout)
+    torch.cuda.synchronize()
+    assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
+    for k in st.tensors:
+        assert torch.equal(st.tensors[k].view(torch.uint8), st2.tensors[k].view(torch.uint8)), k
