@@ -77,6 +77,50 @@ __device__ __forceinline__ void requant_pair(float& sa, float& sb, float2 ns, fl
   sb = copysignf(v.y, sb);
 }
 
+// Per-token scalar tail shared by both scan kernels, so their arithmetic is identical by
+// construction: the readout (:139-147), the FP8 requant of both latent coefficients
+// (:149-154) and the INT8/INT4 scales of the new state (:155-160), pairs in fp32x2.
+// dots = {B.C, b0.C, b1.C, b0.B, b1.B, pcz0, pcz1}.
+struct TokenScales { float s8, s4, i8, i4; };
+__device__ __forceinline__ float token_tail(float2 ya, float2 yb, float2 ca, float2 cb, float m8, float m4,
+                                            float x, float dtv, float dec, float dv, const float (&dots)[7],
+                                            float2& z, float2 ls, float2 nls, float2 ils, TokenScales& ts) {
+  const float ysum = (ya.x + ya.y) + (yb.x + yb.y);
+  const float ycorr = (ca.x + ca.y) + (cb.x + cb.y);
+  const float xdt = x * dtv;
+  const float zc = fmaf(z.x, dots[1], z.y * dots[2]);
+  float out = ysum + fmaf(dec, zc, fmaf(xdt, dots[0], x * dv));
+  out = fmaf(dec, fmaf(z.y, dots[6], fmaf(z.x, dots[5], ycorr)), out);
+  // latent: z = z*dec + xdt*db, then RN-satfinite E4M3 of clip(z/ls) and back
+  z = __ffma2_rn(z, make_float2(dec, dec), __fmul2_rn(make_float2(xdt, xdt), make_float2(dots[3], dots[4])));
+  float2 q = div_exact2(z, nls, ils);
+  q = make_float2(fminf(fmaxf(q.x, -448.f), 448.f), fminf(fmaxf(q.y, -448.f), 448.f));
+  const __half2_raw hz = __nv_cvt_fp8x2_to_halfraw2(__nv_cvt_float2_to_fp8x2(q, __NV_SATFINITE, __NV_E4M3), __NV_E4M3);
+  z = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&hz)), ls);
+  // scales: fp16(max(max|S| / {127, 7}, 1e-8))
+  float2 sc = div_exact2(make_float2(m8, m4), make_float2(-127.f, -7.f), make_float2(1.0f / 127.0f, 1.0f / 7.0f));
+  sc = __half22float2(__float22half2_rn(make_float2(fmaxf(sc.x, 1e-8f), fmaxf(sc.y, 1e-8f))));
+  ts.s8 = sc.x; ts.s4 = sc.y;
+  ts.i8 = sc.x > 0.f ? __frcp_rn(sc.x) : 0.f;
+  ts.i4 = sc.y > 0.f ? __frcp_rn(sc.y) : 0.f;
+  return out;
+}
+
+// Requant of every stored pair with the row's new scales.
+template <int N8, int NP>
+__device__ __forceinline__ void requant_row(float (&S)[2 * NP], const TokenScales& ts) {
+  const float2 s82 = make_float2(ts.s8, ts.s8), ns82 = make_float2(-ts.s8, -ts.s8), i82 = make_float2(ts.i8, ts.i8);
+  const float2 s42 = make_float2(ts.s4, ts.s4), ns42 = make_float2(-ts.s4, -ts.s4), i42 = make_float2(ts.i4, ts.i4);
+  const float m8s = -kMagic * ts.s8, m4s = -kMagic * ts.s4;          // exact (power-of-two scaling)
+  const float2 nm82 = make_float2(m8s, m8s), nm42 = make_float2(m4s, m4s);
+#pragma unroll
+  for (int jp = 0; jp < NP; ++jp) {
+    const bool t8 = 2 * jp < N8;
+    requant_pair(S[2 * jp], S[2 * jp + 1], t8 ? ns82 : ns42, t8 ? i82 : i42, t8 ? 127.f : 7.f,
+                 t8 ? s82 : s42, t8 ? nm82 : nm42);
+  }
+}
+
 // Shared-memory plan of one CTA (byte offsets; every region 16-byte aligned).
 //   ring   R slots of raw inputs per token: x[128] | B[128] | C[128] fp16 (x holds the
 //          CTA's own channels, B/C the whole group row in channel order).  Slot of token t
@@ -114,7 +158,7 @@ template <int N8, int N4>
 constexpr int scan_min_blocks() { return N8 + N4 > 68 ? 3 : 4; }
 
 template <int N8, int N4, int KJ, int MODE, int TC>
-__global__ void __launch_bounds__(128, scan_min_blocks<N8, N4>())
+__global__ void __launch_bounds__(128, MODE == 2 ? 1 : scan_min_blocks<N8, N4>())   // decode grids are small
 ssu_sq325_kernel(const ScanParams P) {
   using L = ScanSmem<N8, N4, TC>;
   constexpr int NZ = L::NZ;
@@ -275,13 +319,12 @@ ssu_sq325_kernel(const ScanParams P) {
   }
   const float ls0 = h2f(P.latent_scale[g * 2 + 0]), ls1 = h2f(P.latent_scale[g * 2 + 1]);
   const float ils0 = __frcp_rn(ls0), ils1 = __frcp_rn(ls1);
-  float z0 = e4m3_to_f32(pLat[tid * 2 + 0]) * ls0;
-  float z1 = e4m3_to_f32(pLat[tid * 2 + 1]) * ls1;
+  const float2 ls2 = make_float2(ls0, ls1), nls2 = make_float2(-ls0, -ls1), ils2 = make_float2(ils0, ils1);
+  float2 zz = make_float2(e4m3_to_f32(pLat[tid * 2 + 0]) * ls0, e4m3_to_f32(pLat[tid * 2 + 1]) * ls1);
   const float dv = P.d_is_f32 ? reinterpret_cast<const float*>(P.D)[h] : h2f(reinterpret_cast<const uint16_t*>(P.D)[h]);
   const float bias_own = P.dt_bias_is_f32 ? reinterpret_cast<const float*>(P.dt_bias)[h0 + (tid % max(hpc, 1))]
                                           : h2f(reinterpret_cast<const uint16_t*>(P.dt_bias)[h0 + (tid % max(hpc, 1))]);
   const float A_own = P.A[h0 + (tid % max(hpc, 1))];
-  const float inv127 = 1.0f / 127.0f, inv7 = 1.0f / 7.0f;
   float s8 = 0.f, s4 = 0.f;
 
   for (int c0 = 0; c0 < P.length; c0 += TC) {
@@ -410,36 +453,16 @@ ssu_sq325_kernel(const ScanParams P) {
         if (2 * jp < N8) { m8a = fmaxf(m8a, fabsf(sn.x)); m8b = fmaxf(m8b, fabsf(sn.y)); }
         else             { m4a = fmaxf(m4a, fabsf(sn.x)); m4b = fmaxf(m4b, fabsf(sn.y)); }
       }
-      const float* dots = sDots + t * 8;
-      const float dbc = dots[0], dc0 = dots[1], dc1 = dots[2], db0 = dots[3], db1 = dots[4];
-      const float pcz0 = dots[5], pcz1 = dots[6];
-      const float ysum = (ya.x + ya.y) + (yb.x + yb.y);
-      const float ycorr = (ca.x + ca.y) + (cb.x + cb.y);
-      const float xdt = x * dtv;
-      float out = ysum + (dec * (z0 * dc0 + z1 * dc1) + xdt * dbc + x * dv);
-      out = out + dec * (ycorr + z0 * pcz0 + z1 * pcz1);
-      P.y[(long long)b * P.y_sb + (long long)(c0 + t) * P.y_st + (long long)h * dim + p] = f2h(out);
-      // latent FP8 requant (:149-154)
-      z0 = z0 * dec + xdt * db0;
-      z1 = z1 * dec + xdt * db1;
-      z0 = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(div_exact(z0, ls0, ils0), -448.f), 448.f))) * ls0;
-      z1 = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(div_exact(z1, ls1, ils1), -448.f), 448.f))) * ls1;
-      // INT8 / INT4 requant (:155-162, scripts/state_ppl_codec_v6.py:52-61)
-      const float m8 = fmaxf(m8a, m8b), m4 = fmaxf(m4a, m4b);
-      s8 = h2f(f2h(fmaxf(div_exact(m8, 127.f, inv127), 1e-8f)));
-      s4 = h2f(f2h(fmaxf(div_exact(m4, 7.f, inv7), 1e-8f)));
-      const float i8 = s8 > 0.f ? __frcp_rn(s8) : 0.f;
-      const float i4 = s4 > 0.f ? __frcp_rn(s4) : 0.f;
-      const float2 s82 = make_float2(s8, s8), ns82 = make_float2(-s8, -s8), i82 = make_float2(i8, i8);
-      const float2 s42 = make_float2(s4, s4), ns42 = make_float2(-s4, -s4), i42 = make_float2(i4, i4);
-      const float m8s = -kMagic * s8, m4s = -kMagic * s4;            // exact (power-of-two scaling)
-      const float2 nm82 = make_float2(m8s, m8s), nm42 = make_float2(m4s, m4s);
+      float dots[7];
 #pragma unroll
-      for (int jp = 0; jp < NP; ++jp) {
-        const bool t8 = 2 * jp < N8;
-        requant_pair(S[2 * jp], S[2 * jp + 1], t8 ? ns82 : ns42, t8 ? i82 : i42, t8 ? 127.f : 7.f,
-                     t8 ? s82 : s42, t8 ? nm82 : nm42);
-      }
+      for (int i = 0; i < 7; ++i) dots[i] = sDots[t * 8 + i];
+      TokenScales ts;
+      const float out = token_tail(ya, yb, ca, cb, fmaxf(m8a, m8b), fmaxf(m4a, m4b), x, dtv, dec, dv, dots, zz,
+                                   ls2, nls2, ils2, ts);
+      P.y[(long long)b * P.y_sb + (long long)(c0 + t) * P.y_st + (long long)h * dim + p] = f2h(out);
+      // INT8 / INT4 requant (:155-162, scripts/state_ppl_codec_v6.py:52-61)
+      s8 = ts.s8; s4 = ts.s4;
+      requant_row<N8, NP>(S, ts);
     }
   }
 
@@ -478,8 +501,8 @@ ssu_sq325_kernel(const ScanParams P) {
       const int qb = __float2int_rn(div_exact(S[N8 + j + 1], s4, i4));
       pQ4[tid * W4 + j / 2] = (unsigned char)((qa & 15) | ((qb & 15) << 4));
     }
-    pLat[tid * 2 + 0] = f32_to_e4m3(fminf(fmaxf(div_exact(z0, ls0, ils0), -448.f), 448.f));
-    pLat[tid * 2 + 1] = f32_to_e4m3(fminf(fmaxf(div_exact(z1, ls1, ils1), -448.f), 448.f));
+    pLat[tid * 2 + 0] = f32_to_e4m3(fminf(fmaxf(div_exact(zz.x, ls0, ils0), -448.f), 448.f));
+    pLat[tid * 2 + 1] = f32_to_e4m3(fminf(fmaxf(div_exact(zz.y, ls1, ils1), -448.f), 448.f));
     pS8[tid] = f2h(s8);
     pS4[tid] = f2h(s4);
   }
@@ -762,10 +785,9 @@ ssu_chunk_kernel(const ScanParams P) {
   }
   const float ls0 = h2f(P.latent_scale[g * 2 + 0]), ls1 = h2f(P.latent_scale[g * 2 + 1]);
   const float ils0 = __frcp_rn(ls0), ils1 = __frcp_rn(ls1);
-  float z0 = e4m3_to_f32(pLat[tid * 2 + 0]) * ls0;
-  float z1 = e4m3_to_f32(pLat[tid * 2 + 1]) * ls1;
+  const float2 ls2 = make_float2(ls0, ls1), nls2 = make_float2(-ls0, -ls1), ils2 = make_float2(ils0, ils1);
+  float2 zz = make_float2(e4m3_to_f32(pLat[tid * 2 + 0]) * ls0, e4m3_to_f32(pLat[tid * 2 + 1]) * ls1);
   const float dv = P.d_is_f32 ? reinterpret_cast<const float*>(P.D)[h] : h2f(reinterpret_cast<const uint16_t*>(P.D)[h]);
-  const float inv127 = 1.0f / 127.0f, inv7 = 1.0f / 7.0f;
   float s8 = 0.f, s4 = 0.f;
 
   for (int c0 = 0; c0 < P.length; c0 += TC) {
@@ -835,35 +857,20 @@ ssu_chunk_kernel(const ScanParams P) {
         if (2 * jp < N8) { m8a = fmaxf(m8a, fabsf(sn.x)); m8b = fmaxf(m8b, fabsf(sn.y)); }
         else             { m4a = fmaxf(m4a, fabsf(sn.x)); m4b = fmaxf(m4b, fabsf(sn.y)); }
       }
-      const float pcz0 = pv[NS], pcz1 = pv[NS + 1];
-      const float dbc = pv[F + 0], dc0 = pv[F + 1], dc1 = pv[F + 2], db0 = pv[F + 3], db1 = pv[F + 4];
-      const float ysum = (ya.x + ya.y) + (yb.x + yb.y);
-      const float ycorr = (ca.x + ca.y) + (cb.x + cb.y);
-      const float xdt = x * dtv;
-      float out = ysum + (dec * (z0 * dc0 + z1 * dc1) + xdt * dbc + x * dv);
-      out = out + dec * (ycorr + z0 * pcz0 + z1 * pcz1);
-      P.y[(long long)b * P.y_sb + (long long)(c0 + t) * P.y_st + (long long)h * dim + p] = f2h(out);
-      // latent FP8 requant (:149-154)
-      z0 = z0 * dec + xdt * db0;
-      z1 = z1 * dec + xdt * db1;
-      z0 = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(div_exact(z0, ls0, ils0), -448.f), 448.f))) * ls0;
-      z1 = e4m3_to_f32(f32_to_e4m3(fminf(fmaxf(div_exact(z1, ls1, ils1), -448.f), 448.f))) * ls1;
-      // INT8 / INT4 requant (:155-162, scripts/state_ppl_codec_v6.py:52-61)
-      const float m8 = fmaxf(m8a, m8b), m4 = fmaxf(m4a, m4b);
-      s8 = h2f(f2h(fmaxf(div_exact(m8, 127.f, inv127), 1e-8f)));
-      s4 = h2f(f2h(fmaxf(div_exact(m4, 7.f, inv7), 1e-8f)));
-      const float i8 = s8 > 0.f ? __frcp_rn(s8) : 0.f;
-      const float i4 = s4 > 0.f ? __frcp_rn(s4) : 0.f;
-      const float2 s82 = make_float2(s8, s8), ns82 = make_float2(-s8, -s8), i82 = make_float2(i8, i8);
-      const float2 s42 = make_float2(s4, s4), ns42 = make_float2(-s4, -s4), i42 = make_float2(i4, i4);
-      const float m8s = -kMagic * s8, m4s = -kMagic * s4;
-      const float2 nm82 = make_float2(m8s, m8s), nm42 = make_float2(m4s, m4s);
-#pragma unroll
-      for (int jp = 0; jp < NP; ++jp) {
-        const bool t8 = 2 * jp < N8;
-        requant_pair(S[2 * jp], S[2 * jp + 1], t8 ? ns82 : ns42, t8 ? i82 : i42, t8 ? 127.f : 7.f,
-                     t8 ? s82 : s42, t8 ? nm82 : nm42);
+      float dots[7];
+      {
+        const float2 d01 = *reinterpret_cast<const float2*>(pv + F), d23 = *reinterpret_cast<const float2*>(pv + F + 2);
+        const float2 pz = *reinterpret_cast<const float2*>(pv + NS);
+        dots[0] = d01.x; dots[1] = d01.y; dots[2] = d23.x; dots[3] = d23.y; dots[4] = pv[F + 4];
+        dots[5] = pz.x; dots[6] = pz.y;
       }
+      TokenScales ts;
+      const float out = token_tail(ya, yb, ca, cb, fmaxf(m8a, m8b), fmaxf(m4a, m4b), x, dtv, dec, dv, dots, zz,
+                                   ls2, nls2, ils2, ts);
+      P.y[(long long)b * P.y_sb + (long long)(c0 + t) * P.y_st + (long long)h * dim + p] = f2h(out);
+      // INT8 / INT4 requant (:155-162, scripts/state_ppl_codec_v6.py:52-61)
+      s8 = ts.s8; s4 = ts.s4;
+      requant_row<N8, NP>(S, ts);
     }
   }
 
@@ -900,8 +907,8 @@ ssu_chunk_kernel(const ScanParams P) {
       const int qb = __float2int_rn(div_exact(S[N8 + j + 1], s4, i4));
       pQ4[tid * W4 + j / 2] = (unsigned char)((qa & 15) | ((qb & 15) << 4));
     }
-    pLat[tid * 2 + 0] = f32_to_e4m3(fminf(fmaxf(div_exact(z0, ls0, ils0), -448.f), 448.f));
-    pLat[tid * 2 + 1] = f32_to_e4m3(fminf(fmaxf(div_exact(z1, ls1, ils1), -448.f), 448.f));
+    pLat[tid * 2 + 0] = f32_to_e4m3(fminf(fmaxf(div_exact(zz.x, ls0, ils0), -448.f), 448.f));
+    pLat[tid * 2 + 1] = f32_to_e4m3(fminf(fmaxf(div_exact(zz.y, ls1, ils1), -448.f), 448.f));
     pS8[tid] = f2h(s8);
     pS4[tid] = f2h(s4);
   }
