@@ -192,6 +192,13 @@ int sq_model_greedy(sq_model* model, const uint16_t* hidden, int rows, uint16_t*
                     int64_t* tokens_out, void* stream);
 /* Synchronises the stream and reports a device-side failure (bad token id, expired wait). */
 int sq_model_check(sq_model* model, void* stream);
+/* Numerics of the one-token decode-step projections and of the greedy head (at most 64
+ * rows).  exact = 0 (default): the exact fp16 products E2M1*E4M3 enter the tensor-core
+ * product and the fp32 global scale multiplies each fp32 output once (factored scale), the
+ * bandwidth-bound form.  exact = 1: every weight is first rounded to fp16 as the reference's
+ * decoded FP16 weights (fp4.py:100-103), about three ALU instructions per weight.  Prompts,
+ * scoring windows and the scoring head always use the exactly decoded weights. */
+int sq_model_set_exact_skinny(sq_model* model, int exact);
 
 #ifdef __cplusplus
 }

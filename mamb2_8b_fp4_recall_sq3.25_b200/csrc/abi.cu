@@ -71,6 +71,7 @@ struct sq_model {
   float2* partials = 0;
   float* tlogit = 0;
   void* prep = 0;                             // two-kernel scan workspace (any layout)
+  bool exact_skinny = false;                  // decode steps / greedy head: per-weight fp16 decode
   int* d_err = 0;
   size_t stage_elems = 0;
   std::atomic<int> busy{0};
@@ -90,10 +91,11 @@ void free_ws(sq_model* m) {
   m->max_tokens = 0;
 }
 
+// exact: per-weight fp16 decode in the skinny kernel; false only for one-token decode steps.
 int linear(sq_model* m, const sq_fp4_matrix& W, const Fp4Maps* maps, const uint16_t* X, long long ldx, int M,
-           uint16_t* Y, long long ldy, cudaStream_t st) {
+           uint16_t* Y, long long ldy, bool exact, cudaStream_t st) {
   const Fp4Weight w = fw(W);
-  if (M <= 64) return check(launch_fp4_gemv_stream(w, maps, X, ldx, M, Y, ldy, m->d_err, st), "fp4 gemv");
+  if (M <= 64) return check(launch_fp4_gemv_stream(w, maps, X, ldx, M, Y, ldy, m->d_err, st, exact), "fp4 gemv");
   if ((size_t)W.rows * W.cols > m->stage_elems) return fail(SQ_EINVAL, "staging buffer too small");
   SQ_TRY(launch_fp4_decode(w, m->stage, W.cols, st), "fp4 decode");
   return check(launch_gemm_f16(X, ldx, m->stage, W.cols, Y, ldy, M, W.rows, W.cols, 0, nullptr, m->d_err, st),
@@ -370,7 +372,7 @@ int sq_model_forward(sq_model* m, const int64_t* ids, int batch, int tokens, int
     if (!L.in_proj.codes) return fail(SQ_ESTATE, "forward: layer weights not set");
     if (S.batch != batch) return fail(SQ_ESTATE, "forward: state batch differs from the call (reset required)");
     SQ_TRY(launch_add_rmsnorm(m->h, m->res, l > 0, L.norm_weight, m->cfg.eps, m->hn, M, kDModel, st), "add_rmsnorm");
-    int s = linear(m, L.in_proj, &m->in_maps[l], m->hn, kDModel, M, m->zx, kZx, st);
+    int s = linear(m, L.in_proj, &m->in_maps[l], m->hn, kDModel, M, m->zx, kZx, !step || m->exact_skinny, st);
     if (s != SQ_OK) return s;
     ScanParams P{};
     P.batch = batch; P.length = tokens; P.heads = kHeads; P.dim = kHeadDim; P.groups = kGroups; P.layout = L.layout;
@@ -400,7 +402,7 @@ int sq_model_forward(sq_model* m, const int64_t* ids, int batch, int tokens, int
     const AdapterPtrs& ad = m->adapters[l];
     SQ_TRY(launch_resurface_gatednorm(m->y, m->zx, kZx, m->hn, kDModel, ad.V ? &ad : nullptr, L.gated_norm_weight,
                                       m->cfg.eps, m->yn, M, st), "resurface + gated norm");
-    s = linear(m, L.out_proj, &m->out_maps[l], m->yn, kDInner, M, m->h, kDModel, st);
+    s = linear(m, L.out_proj, &m->out_maps[l], m->yn, kDInner, M, m->h, kDModel, !step || m->exact_skinny, st);
     if (s != SQ_OK) return s;
   }
   SQ_TRY(launch_add_rmsnorm(m->h, m->res, 1, m->norm_f, m->cfg.eps, hidden_out, M, kDModel, st), "norm_f");
@@ -437,10 +439,17 @@ int sq_model_greedy(sq_model* m, const uint16_t* hidden, int rows, uint16_t* log
   if (!m->logits) return fail(SQ_ESTATE, "greedy: reserve() first");
   cudaStream_t st = (cudaStream_t)stream;
   uint16_t* lg = logits_out ? logits_out : m->logits;
-  SQ_TRY(launch_fp4_gemv_stream(fw(m->head), &m->head_maps, hidden, kDModel, rows, lg, m->cfg.vocab, m->d_err, st),
+  SQ_TRY(launch_fp4_gemv_stream(fw(m->head), &m->head_maps, hidden, kDModel, rows, lg, m->cfg.vocab, m->d_err, st,
+                                m->exact_skinny),
          "lm_head gemv");
   return check(launch_argmax(lg, rows, m->cfg.vocab, m->cfg.vocab, (long long*)tokens_out, m->partials, st),
                "argmax");
+}
+
+int sq_model_set_exact_skinny(sq_model* m, int exact) {
+  if (!m) return fail(SQ_EINVAL, "set_exact_skinny: null model");
+  m->exact_skinny = exact != 0;
+  return SQ_OK;
 }
 
 int sq_model_check(sq_model* m, void* stream) {

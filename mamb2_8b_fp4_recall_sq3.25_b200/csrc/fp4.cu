@@ -31,6 +31,10 @@ __device__ __forceinline__ uint32_t e4m3_splat_f16x2(uint32_t byte) {
 // Exact decode of one code pair: FP16(FP32(FP32(m*b)*g)).  m*b is exact in fp16 (<= 6
 // significant bits, |m*b| <= 2688, >= 2^-10), so HMUL2 gives it exactly; the product with
 // the fp32 global scale is then rounded once to fp32 and once to fp16, as the reference.
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  __half2 p = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&p);
+}
 __device__ __forceinline__ uint32_t scale_pair(uint32_t m16x2, uint32_t b16x2, float2 g2) {
   __half2 p = __hmul2(*reinterpret_cast<__half2*>(&m16x2), *reinterpret_cast<__half2*>(&b16x2));
   const float2 f = __fmul2_rn(__half22float2(p), g2);
@@ -226,7 +230,12 @@ __device__ __forceinline__ void gv_tma2d(uint32_t dst, const CUtensorMap* map, u
       :: "r"(dst), "l"(map), "r"(bar), "r"(x), "r"(y) : "memory");
 }
 
-template <int MT>
+// EXACT: every weight is decoded to FP16(FP32(m*b)*g) before the product (the reference's
+// decoded-weight numerics).  Otherwise the exact fp16 products m*b enter the MMA and the
+// fp32 global scale multiplies each fp32 accumulator once (factored scale): the weight seen
+// by the product is then m*b*g unrounded instead of its fp16 rounding, one instruction per
+// weight instead of about three.
+template <int MT, bool EXACT>
 __global__ void __launch_bounds__(32 * (1 + kGvConsumers))
 fp4_gemv_stream_kernel(const __grid_constant__ CUtensorMap mcodes, const __grid_constant__ CUtensorMap mscales,
                        const float* __restrict__ gptr, int N, int K, int KC,
@@ -326,10 +335,17 @@ fp4_gemv_stream_kernel(const __grid_constant__ CUtensorMap mcodes, const __grid_
             for (int jj = 0; jj < 2; ++jj) {
               const int j = w4 * 2 + jj;
               uint32_t a[4];
-              a[0] = scale_pair(ma[2 * jj], bsA, g2);
-              a[1] = scale_pair(mb[2 * jj], bsB, g2);
-              a[2] = scale_pair(ma[2 * jj + 1], bsA, g2);
-              a[3] = scale_pair(mb[2 * jj + 1], bsB, g2);
+              if (EXACT) {
+                a[0] = scale_pair(ma[2 * jj], bsA, g2);
+                a[1] = scale_pair(mb[2 * jj], bsB, g2);
+                a[2] = scale_pair(ma[2 * jj + 1], bsA, g2);
+                a[3] = scale_pair(mb[2 * jj + 1], bsB, g2);
+              } else {
+                a[0] = hmul2_u32(ma[2 * jj], bsA);
+                a[1] = hmul2_u32(mb[2 * jj], bsB);
+                a[2] = hmul2_u32(ma[2 * jj + 1], bsA);
+                a[3] = hmul2_u32(mb[2 * jj + 1], bsB);
+              }
 #pragma unroll
               for (int mt = 0; mt < MT; ++mt) {
                 // x[m][kb0 + 4j .. +3] = 16-byte word j/2, half (j&1)
@@ -359,6 +375,9 @@ fp4_gemv_stream_kernel(const __grid_constant__ CUtensorMap mcodes, const __grid_
         for (int w = 0; w < kGvConsumers; ++w)
 #pragma unroll
           for (int i = 0; i < 4; ++i) sacc[i] += red[((w * MT + mt) * 32 + lane) * 4 + i];
+        if (!EXACT)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sacc[i] *= gsc;
         const int m0 = mt * 8 + 2 * tq;
         const int na = n0 + gq, nb = n0 + gq + 8;
         if (m0 < M && na < N) Y[(long long)m0 * ldy + na] = f2h(sacc[0]);
@@ -378,7 +397,7 @@ int gemv_kc(int cols) {
   return (cols % kGvKC == 0) ? kGvKC : (cols % 512 == 0 ? 512 : (cols % 256 == 0 ? 256 : 0));
 }
 
-template <int MT>
+template <int MT, bool EXACT>
 int gemv_stream(const Fp4Weight& W, const Fp4Maps* maps, const uint16_t* X, long long ldx, int M, uint16_t* Y,
                 long long ldy, int* err, cudaStream_t st) {
   const int KC = gemv_kc(W.cols);
@@ -391,7 +410,7 @@ int gemv_stream(const Fp4Weight& W, const Fp4Maps* maps, const uint16_t* X, long
   const size_t smem = (size_t)kGvStages * kGvStageBytes + 2 * kGvStages * 8 + (size_t)kGvConsumers * MT * 32 * 16;
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(fp4_gemv_stream_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    if (cudaFuncSetAttribute(fp4_gemv_stream_kernel<MT, EXACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
       return kECuda;
     attr = true;
@@ -404,7 +423,7 @@ int gemv_stream(const Fp4Weight& W, const Fp4Maps* maps, const uint16_t* X, long
     if (!make_fp4_maps(W, &local)) return kECuda;
     maps = &local;
   }
-  fp4_gemv_stream_kernel<MT><<<grid, 32 * (1 + kGvConsumers), smem, st>>>(
+  fp4_gemv_stream_kernel<MT, EXACT><<<grid, 32 * (1 + kGvConsumers), smem, st>>>(
       maps->codes, maps->scales, W.global_scale, W.rows, W.cols, KC, X, ldx, M, Y, ldy, err);
   return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
 }
@@ -453,22 +472,32 @@ bool make_fp4_maps(const Fp4Weight& W, Fp4Maps* maps) {
 
 int prepare_fp4_kernels() {
   Fp4Weight none{nullptr, nullptr, nullptr, 0, 1024};
-  int st = gemv_stream<1>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
-           gemv_stream<2>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
-           gemv_stream<4>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
-           gemv_stream<8>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0);
+  int st = gemv_stream<1, true>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
+           gemv_stream<2, true>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
+           gemv_stream<4, true>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
+           gemv_stream<8, true>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
+           gemv_stream<1, false>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
+           gemv_stream<2, false>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
+           gemv_stream<4, false>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
+           gemv_stream<8, false>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0);
   return st ? kECuda : kOk;
 }
 
 int launch_fp4_gemv_stream(const Fp4Weight& W, const Fp4Maps* maps, const uint16_t* X, long long ldx, int M,
-                           uint16_t* Y, long long ldy, int* err, cudaStream_t st) {
+                           uint16_t* Y, long long ldy, int* err, cudaStream_t st, bool exact) {
   if (M <= 0 || M > 64 || W.cols % 256 || ldx % 8 || !err) return kEInval;
   if (((uintptr_t)W.codes % 16) || ((uintptr_t)W.scales % 16) || ((uintptr_t)X % 16) || ((W.cols / 16) % 16))
     return kEInval;
-  if (M <= 8) return gemv_stream<1>(W, maps, X, ldx, M, Y, ldy, err, st);
-  if (M <= 16) return gemv_stream<2>(W, maps, X, ldx, M, Y, ldy, err, st);
-  if (M <= 32) return gemv_stream<4>(W, maps, X, ldx, M, Y, ldy, err, st);
-  return gemv_stream<8>(W, maps, X, ldx, M, Y, ldy, err, st);
+  if (exact) {
+    if (M <= 8) return gemv_stream<1, true>(W, maps, X, ldx, M, Y, ldy, err, st);
+    if (M <= 16) return gemv_stream<2, true>(W, maps, X, ldx, M, Y, ldy, err, st);
+    if (M <= 32) return gemv_stream<4, true>(W, maps, X, ldx, M, Y, ldy, err, st);
+    return gemv_stream<8, true>(W, maps, X, ldx, M, Y, ldy, err, st);
+  }
+  if (M <= 8) return gemv_stream<1, false>(W, maps, X, ldx, M, Y, ldy, err, st);
+  if (M <= 16) return gemv_stream<2, false>(W, maps, X, ldx, M, Y, ldy, err, st);
+  if (M <= 32) return gemv_stream<4, false>(W, maps, X, ldx, M, Y, ldy, err, st);
+  return gemv_stream<8, false>(W, maps, X, ldx, M, Y, ldy, err, st);
 }
 
 int launch_fp4_gemv(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,

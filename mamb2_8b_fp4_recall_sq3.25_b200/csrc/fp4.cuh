@@ -33,8 +33,9 @@ bool encode_u32_map(CUtensorMap* m, const void* base, long long rows, long long 
                     int box_cols, int box_rows);
 // Same product through the TMA-pipelined kernel (cols % 256 == 0, 16-byte aligned rows);
 // `maps` may be null (built on the fly); `err` receives an error bit if a bounded wait expires.
+// exact = false applies the fp32 global scale once per output instead of per weight.
 int launch_fp4_gemv_stream(const Fp4Weight& W, const Fp4Maps* maps, const uint16_t* X, long long ldx, int M,
-                           uint16_t* Y, long long ldy, int* err, cudaStream_t st);
+                           uint16_t* Y, long long ldy, int* err, cudaStream_t st, bool exact = true);
 
 // tcgen05 GEMM: C[M,N] = A[M,K] . B[N,K]^T, fp16 in, fp32 accumulate in TMEM.
 // mode 0: store fp16 C.  mode 1: cross-entropy partials of fp16-rounded logits

@@ -155,7 +155,7 @@ struct ScanSmem {
 // Resident CTAs per SM the register budget is sized for: 4 (<= 128 registers) while the
 // stored row fits, 3 for the widest layouts.
 template <int N8, int N4>
-constexpr int scan_min_blocks() { return N8 + N4 > 68 ? 3 : 4; }
+constexpr int scan_min_blocks() { return N8 + N4 >= 68 ? 3 : 4; }
 
 template <int N8, int N4, int KJ, int MODE, int TC>
 __global__ void __launch_bounds__(128, MODE == 2 ? 1 : scan_min_blocks<N8, N4>())   // decode grids are small

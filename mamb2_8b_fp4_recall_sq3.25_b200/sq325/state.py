@@ -66,6 +66,7 @@ class PredictorState:
         self._installed = False
         self._inside_backbone = False
         self._reserved = 0
+        self._exact_projections = False
 
     # ------------------------------------------------------------------ lifecycle
     def install(self):
@@ -80,6 +81,7 @@ class PredictorState:
             cfg = _lib.ModelConfig(self.model.n_layer, self.model.vocab, self.model.eps)
             _lib.call('sq_model_create', C.byref(cfg), C.byref(h))
             self._handle = h
+            _lib.call('sq_model_set_exact_skinny', h, int(self._exact_projections))
             for i, (L, layout) in enumerate(zip(self.model.layers, self.layouts)):
                 d = _lib.LayerDesc()
                 d.in_proj, d.out_proj = L.in_proj.cabi(), L.out_proj.cabi()
@@ -99,6 +101,17 @@ class PredictorState:
         except Exception:
             self.close()
             raise
+        return self
+
+    def set_exact_projections(self, exact=True):
+        """One-token decode steps and the greedy head use the factored global scale by
+        default (fp16 products E2M1*E4M3 on the tensor cores, fp32 global scale once per
+        output).  exact=True rounds every weight to fp16 first, the reference's decoded-weight
+        numerics, at about three ALU instructions per weight.  Prompts and scoring always use
+        the exactly decoded weights."""
+        self._exact_projections = bool(exact)
+        if self._handle is not None:
+            _lib.call('sq_model_set_exact_skinny', self._handle, int(self._exact_projections))
         return self
 
     def _sync_adapter(self):

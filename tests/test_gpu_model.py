@@ -42,13 +42,17 @@ def test_prefill_hidden_and_nll(pair, B, T):
     assert torch.allclose(got, exp, rtol=NLL_RTOL, atol=0), (got, exp)
 
 
-def test_decode_steps_and_greedy(pair):
+@pytest.mark.parametrize('exact', [False, True])
+def test_decode_steps_and_greedy(pair, exact):
+    """Decode-time projections (<= 64 rows) in both numerics: factored global scale (default)
+    and per-weight fp16 decode; both against the oracle's decoded-FP16-weight model."""
     from sq325 import PredictorState
     gm, ora, statics = pair
     rng = np.random.default_rng(5)
     B, T = 2, 12
     ids = _ids(rng, B, T, gm.vocab)
     with PredictorState(gm, *statics) as ex:
+        ex.set_exact_projections(exact)
         h = ex.backbone(torch.from_numpy(ids).cuda(), reset=True)
         ora.reset(B)
         hr = ora.backbone(ids)
@@ -135,3 +139,26 @@ def test_graphed_decode_matches_eager(pair):
         ex.check()
     assert eager.shape == (2, 11)
     assert torch.equal(eager.cpu(), graphed.cpu())
+
+
+def test_factored_scale_projections_track_exact(pair):
+    """The factored-scale decode-step projections differ from the per-weight fp16 decode only
+    by the fp16 rounding of each weight: hidden states and logits agree closely."""
+    from sq325 import PredictorState
+    gm, _, statics = pair
+    rng = np.random.default_rng(9)
+    prompt = torch.from_numpy(_ids(rng, 1, 20, gm.vocab)).cuda()
+    steps = [torch.from_numpy(_ids(rng, 1, 1, gm.vocab)).cuda() for _ in range(3)]
+    outs = {}
+    for exact in (True, False):
+        with PredictorState(gm, *statics) as ex:
+            ex.set_exact_projections(exact)
+            ex.backbone(prompt, reset=True)
+            for s in steps:
+                h = ex.backbone(s)
+            logits = torch.empty(1, gm.vocab, device='cuda', dtype=torch.float16)
+            ex.greedy(h[:, -1], logits=logits)
+            torch.cuda.synchronize()
+            outs[exact] = (h.float(), logits.float())
+    assert rel_l2(outs[False][0], outs[True][0]) < 5e-3
+    assert rel_l2(outs[False][1], outs[True][1]) < 5e-3
