@@ -11,6 +11,7 @@ already resident on the device; `e2e` = the same through the public scoring API 
 pinned host buffers (H2D of the windows, D2H of the per-window NLLs, every step).
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+  python bench.py --case gemm|scan [--layout L] --steps K     (one kernel, for ncu)
   torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU, NCCL)
 """
 from __future__ import annotations
@@ -38,6 +39,9 @@ UNIT = 'tokens/s'
 WINDOWS_PER_GPU, SEQLEN, VOCAB, N_LAYER = 16, 2048, 256000, 56
 FLOP_PER_TOKEN = 2 * (56 * (18560 * 4096 + 4096 * 8192) + 256000 * 4096)   # 14,369,685,504
 DECODE_BYTES_B1 = 4_111_674_420
+# dram__bytes_read.sum + dram__bytes_write.sum of one in_proj GEMM launch (M=32768), from
+# one ncu --set full capture of `python bench.py --case gemm --steps 2` on this build.
+GEMM_TRAFFIC_BYTES = 2_715_832_000 + 1_196_445_000
 
 
 def peaks():
@@ -209,6 +213,57 @@ def time_gemm_kernel(model, rows, device, reps=5):
     return statistics.median(ts), 2.0 * rows * w.rows * w.cols
 
 
+@torch.no_grad()
+def run_case(args):
+    """One kernel on a small case, for ncu captures (a few GB on the device, steps + 3
+    launches).  Prints one JSON line with CUDA-event timings; not a bench line."""
+    from sq325 import _lib, codec
+    torch.cuda.set_device(0)
+    gen = torch.Generator(device='cuda').manual_seed(0)
+    s = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    if args.case == 'gemm':                       # tcgen05 in_proj GEMM at the scoring shape
+        M, N, K = 32768, 18560, 4096
+        a = torch.randn(M, K, device='cuda', generator=gen).half()
+        b = (torch.randn(N, K, device='cuda', generator=gen) * 0.02).half()
+        c = torch.empty(M, N, device='cuda', dtype=torch.float16)
+        call = lambda: _lib.call('sq_gemm_f16', _lib.ptr(a), K, _lib.ptr(b), K, _lib.ptr(c), N, M, N, K,
+                                 _lib.stream_ptr())
+        unit, work = 'TFLOP/s', 2.0 * M * N * K
+    else:                                         # SQ3.25 scan: prep + chunk kernels, 16 x 128 x 64 rows
+        B, L, H, P, G = 16, 512, 128, 64, 8
+        spec = codec.layout_descriptor(args.layout)
+        n8, n4, nz = spec['n8'], spec['n4'], spec['nzero']
+        x = torch.randn(B, L, H, P, device='cuda', generator=gen).half()
+        dt = (torch.randn(B, L, H, device='cuda', generator=gen) * 0.5).half()
+        A = -(torch.rand(H, device='cuda', generator=gen) * 3 + 0.1)
+        Bm = torch.randn(B, L, G, 128, device='cuda', generator=gen).half()
+        Cm = torch.randn(B, L, G, 128, device='cuda', generator=gen).half()
+        D = torch.randn(H, device='cuda', generator=gen).half()
+        db = (torch.rand(H, device='cuda', generator=gen) * 3 - 4).half()
+        perm = torch.stack([torch.randperm(128, device='cuda', generator=gen) for _ in range(G)]).to(torch.uint8)
+        basis = torch.randn(G, nz, 2, device='cuda', generator=gen).half()
+        ls = (torch.rand(G, 2, device='cuda', generator=gen) + 0.1).half()
+        pred = (torch.randn(G, n8 + n4 + 2, nz, device='cuda', generator=gen) / np.sqrt(n8 + n4 + 2)).half()
+        st = codec.allocate_state(B, H, P, 128, 'cuda', layout=args.layout)
+        call = lambda: codec.scan(x, dt, A, Bm, Cm, D, db, st, perm, basis, ls, pred, layout=args.layout)
+        unit, work = 'us/token', float(L)
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(args.steps):
+        ev[0].record(s)
+        call()
+        ev[1].record(s)
+        torch.cuda.synchronize()
+        ts.append(ev[0].elapsed_time(ev[1]) / 1e3)
+    t = statistics.median(ts)
+    val = work / t / 1e12 if unit == 'TFLOP/s' else t * 1e6 / work
+    print(json.dumps(dict(case=args.case, layout=args.layout if args.case == 'scan' else None, seconds=t,
+                          value=val, unit=unit, steps=args.steps)))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
@@ -218,7 +273,13 @@ def main():
     ap.add_argument('--ref-tokens', type=int, default=16)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--decode-steps', type=int, default=32)
+    ap.add_argument('--case', choices=['gemm', 'scan'], default=None,
+                    help='time one kernel on a small case (for ncu captures) instead of the bench')
+    ap.add_argument('--layout', default='32_32_64', help='scan layout of --case scan')
     args = ap.parse_args()
+    if args.case:
+        run_case(args)
+        return
     args.steps_ref = min(args.steps, 3)
     args.warmup_ref = 1 if args.warmup > 0 else 0
     if args.impl == 'reference':
@@ -342,7 +403,7 @@ def main():
                         parallelism=f'dp{world} (window-sharded, one NLL all-reduce)', l2='inputs larger than L2'),
             e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h),
             roofline=dict(bound='tensor', kernel='tcgen05 in_proj GEMM (M=%d,N=18560,K=4096)' % (B * T),
-                          achieved=achieved, peak=pk['tf'], unit='TFLOP/s', frac=achieved / pk['tf'], traffic=None,
+                          achieved=achieved, peak=pk['tf'], unit='TFLOP/s', frac=achieved / pk['tf'], traffic=GEMM_TRAFFIC_BYTES,
                           peak_source=pk['src'] + ' bf16_tflops (burst)'),
             step_roofline=dict(flop_per_token=FLOP_PER_TOKEN,
                                achieved_tflops=FLOP_PER_TOKEN * B * T * world / elapsed * args.steps / 1e12 / world,
