@@ -11,7 +11,7 @@ already resident on the device; `e2e` = the same through the public scoring API 
 pinned host buffers (H2D of the windows, D2H of the per-window NLLs, every step).
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
-  python bench.py --case gemm|scan [--layout L] --steps K     (one kernel, for ncu)
+  python bench.py --case gemm|scan|decode [--layout L] [--layers N --vocab V] --steps K   (one kernel, for ncu)
   torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU, NCCL)
 """
 from __future__ import annotations
@@ -222,7 +222,19 @@ def run_case(args):
     gen = torch.Generator(device='cuda').manual_seed(0)
     s = torch.cuda.current_stream()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    if args.case == 'gemm':                       # tcgen05 in_proj GEMM at the scoring shape
+    if args.case == 'decode':                     # persistent batch-1 decode step on a shortened model
+        from sq325 import model as M, resurface as R
+        from sq325.state import PredictorState
+        model = M.synthetic_model(seed=4, n_layer=args.layers, vocab=args.vocab, device='cuda')
+        model.adapter = R.random_bank(args.layers, seed=5, device='cuda')
+        statics = M.synthetic_statics(M.RELEASED_LAYOUTS[:args.layers], seed=4, device='cuda')
+        ex = PredictorState(model, *statics).install()
+        ex.reserve(64)
+        prompt = torch.from_numpy(zipf_tokens(64, np.random.default_rng(3)) % args.vocab)[None].cuda()
+        tok = ex.greedy(ex.backbone(prompt, reset=True)[:, -1]).clone()
+        call = lambda: ex.decode_persistent(tok, 1)
+        unit, work = 'us/token', 1.0
+    elif args.case == 'gemm':                     # tcgen05 in_proj GEMM at the scoring shape
         M, N, K = 32768, 18560, 4096
         a = torch.randn(M, K, device='cuda', generator=gen).half()
         b = (torch.randn(N, K, device='cuda', generator=gen) * 0.02).half()
@@ -261,7 +273,8 @@ def run_case(args):
     t = statistics.median(ts)
     val = work / t / 1e12 if unit == 'TFLOP/s' else t * 1e6 / work
     print(json.dumps(dict(case=args.case, layout=args.layout if args.case == 'scan' else None, seconds=t,
-                          value=val, unit=unit, steps=args.steps)))
+                          value=val, unit=unit, steps=args.steps,
+                          layers=args.layers if args.case == 'decode' else None)))
 
 
 def main():
@@ -273,9 +286,11 @@ def main():
     ap.add_argument('--ref-tokens', type=int, default=16)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--decode-steps', type=int, default=32)
-    ap.add_argument('--case', choices=['gemm', 'scan'], default=None,
+    ap.add_argument('--case', choices=['gemm', 'scan', 'decode'], default=None,
                     help='time one kernel on a small case (for ncu captures) instead of the bench')
     ap.add_argument('--layout', default='32_32_64', help='scan layout of --case scan')
+    ap.add_argument('--layers', type=int, default=4, help='layers of --case decode')
+    ap.add_argument('--vocab', type=int, default=32768, help='vocabulary of --case decode')
     args = ap.parse_args()
     if args.case:
         run_case(args)
@@ -371,20 +386,27 @@ def main():
         prompt = torch.from_numpy(wins[0, :64][None]).to(device)
         h = ex.backbone(prompt, reset=True)[:, -1]
         tok = ex.greedy(h).clone()
-        ex.capture_decode(tok)
-        ex.replay_decode(4)
-        torch.cuda.synchronize()
         d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        d0.record(s)
-        ex.replay_decode(args.decode_steps)
-        d1.record(s)
-        torch.cuda.synchronize()
-        ex.check()
-        dt = d0.elapsed_time(d1) / 1e3 / args.decode_steps
+
+        def timed(run):
+            run(4)
+            torch.cuda.synchronize()
+            d0.record(s)
+            run(args.decode_steps)
+            d1.record(s)
+            torch.cuda.synchronize()
+            ex.check()
+            return d0.elapsed_time(d1) / 1e3 / args.decode_steps
+
+        dt = timed(lambda n: ex.decode_persistent(tok, n))      # one cooperative launch per token
+        ex.capture_decode(tok)
+        dt_graph = timed(ex.replay_decode)                      # multi-kernel step, CUDA-graph replay
         roof = pk['hbm'] * 1e9 / DECODE_BYTES_B1
         decode = dict(tokens_per_s=1.0 / dt, ms_per_token=dt * 1e3, roofline_tokens_per_s=roof,
                       frac=(1.0 / dt) / roof, bytes_per_token=DECODE_BYTES_B1,
-                      note='batch 1, 64-token prompt, CUDA-graph replay per token')
+                      graph_replay_tokens_per_s=1.0 / dt_graph,
+                      note='batch 1, 64-token prompt, persistent kernel (one cooperative launch per token); '
+                           'graph_replay = the multi-kernel step replayed as CUDA graphs')
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -192,6 +192,15 @@ int sq_model_greedy(sq_model* model, const uint16_t* hidden, int rows, uint16_t*
                     int64_t* tokens_out, void* stream);
 /* Synchronises the stream and reports a device-side failure (bad token id, expired wait). */
 int sq_model_check(sq_model* model, void* stream);
+/* Greedy decode at batch 1 with one persistent launch per token (the loop of
+ * infer_fp4_ridge_resurface_v1.py:100-110 after the prompt): step s feeds tokens[0] at
+ * position pos + s, runs all layers, the final norm, lm_head and argmax, overwrites
+ * tokens[0] with the pick and stores it in out_tokens[s] (device, may be NULL).  Requires
+ * batch-1 states (pos > 0: prompt already consumed), reserve(), and the factored-scale
+ * projections (sq_model_set_exact_skinny(model, 0)); the logits of the last step are left
+ * in the model's greedy workspace.  Same tokens and states as sq_model_forward +
+ * sq_model_greedy per step. */
+int sq_model_decode(sq_model* model, int64_t* tokens, int pos, int steps, int64_t* out_tokens, void* stream);
 /* Numerics of the one-token decode-step projections and of the greedy head (at most 64
  * rows).  exact = 0 (default): the exact fp16 products E2M1*E4M3 enter the tensor-core
  * product and the fp32 global scale multiplies each fp32 output once (factored scale), the

@@ -9,6 +9,7 @@
 
 #include "../../include/sq325.h"
 #include "common.cuh"
+#include "decode.cuh"
 #include "fp4.cuh"
 #include "layer.cuh"
 #include "scan.cuh"
@@ -72,6 +73,13 @@ struct sq_model {
   float* tlogit = 0;
   void* prep = 0;                             // two-kernel scan workspace (any layout)
   bool exact_skinny = false;                  // decode steps / greedy head: per-weight fp16 decode
+  // persistent batch-1 decode: device copies of the layer table and TMA maps, step buffers
+  DecLayer* d_dlayers = 0;
+  DecLayerRows* d_drows = 0;
+  CUtensorMap* d_dmaps = 0;
+  unsigned char* d_dbuf = 0;                  // h | res[2] | zx | y | argmax partials | sync
+  bool dec_dirty = true;
+  int dec_grid = 0;
   int* d_err = 0;
   size_t stage_elems = 0;
   std::atomic<int> busy{0};
@@ -264,6 +272,9 @@ int sq_model_create(const sq_model_config* cfg, sq_model** out) {
 int sq_model_destroy(sq_model* m) {
   if (!m) return SQ_OK;
   free_ws(m);
+  void* dec[] = {m->d_dlayers, m->d_drows, m->d_dmaps, m->d_dbuf};
+  for (void* p : dec)
+    if (p) cudaFree(p);
   if (m->d_err) cudaFree(m->d_err);
   delete m;
   return SQ_OK;
@@ -285,6 +296,7 @@ int sq_model_set_layer(sq_model* m, int layer, const sq_layer_desc* d) {
   if (!aligned(d->permutation, 16) || !aligned(d->basis, 16) || !aligned(d->predictor, 16))
     return fail(SQ_EINVAL, "set_layer: permutation / basis / predictor must be 16-byte aligned");
   m->layers[layer] = *d;
+  m->dec_dirty = true;
   if (!make_fp4_maps(fw(d->in_proj), &m->in_maps[layer]) || !make_fp4_maps(fw(d->out_proj), &m->out_maps[layer]))
     return fail(SQ_EINVAL, "set_layer: projection rows must be 16-byte aligned for the TMA streams");
   return SQ_OK;
@@ -295,6 +307,7 @@ int sq_model_set_globals(sq_model* m, const sq_fp4_matrix* e, const sq_fp4_matri
   if (!fp4_ok(*e, m->cfg.vocab, kDModel) || !fp4_ok(*h, m->cfg.vocab, kDModel))
     return fail(SQ_EINVAL, "set_globals: embedding / lm_head must be [vocab,4096]");
   m->embed = *e; m->head = *h; m->norm_f = nf;
+  m->dec_dirty = true;
   if (!make_fp4_maps(fw(*h), &m->head_maps)) return fail(SQ_EINVAL, "set_globals: lm_head rows must be 16-byte aligned");
   return SQ_OK;
 }
@@ -304,6 +317,7 @@ int sq_model_set_adapter(sq_model* m, int layer, const uint16_t* V, const uint16
   if (!m || layer < 0 || layer >= m->cfg.n_layer) return fail(SQ_EINVAL, "set_adapter: bad layer");
   if (V && (!g || !w || !b)) return fail(SQ_EINVAL, "set_adapter: null pointer");
   m->adapters[layer] = AdapterPtrs{V, g, w, b, hard};
+  m->dec_dirty = true;
   return SQ_OK;
 }
 
@@ -315,6 +329,7 @@ int sq_model_bind_state(sq_model* m, int layer, int batch, uint8_t* lo, uint8_t*
     if (!q || !aligned(q, 16)) return fail(SQ_EINVAL, "bind_state: null or misaligned (16 B) buffer");
   sq_model::St& s = m->states[layer];
   s.batch = batch; s.lo = lo; s.hi = hi; s.q4 = q4; s.latent = latent; s.s8 = s8; s.s4 = s4; s.ring = ring;
+  m->dec_dirty = true;
   return SQ_OK;
 }
 
@@ -444,6 +459,99 @@ int sq_model_greedy(sq_model* m, const uint16_t* hidden, int rows, uint16_t* log
          "lm_head gemv");
   return check(launch_argmax(lg, rows, m->cfg.vocab, m->cfg.vocab, (long long*)tokens_out, m->partials, st),
                "argmax");
+}
+
+namespace {
+constexpr size_t kDecH = 0, kDecRes = kDecH + 4096 * 2, kDecZx = kDecRes + 2 * 4096 * 2, kDecY = kDecZx + kZx * 2,
+                 kDecPv = kDecY + kDInner * 2, kDecPi = kDecPv + 1024 * 4, kDecSync = kDecPi + 1024 * 4,
+                 kDecBytes = kDecSync + 256;
+
+// Device copies of everything the persistent decode kernel reads through pointers.
+int decode_setup(sq_model* m) {
+  const int L = m->cfg.n_layer;
+  if (!m->d_dlayers) {
+    if (cudaMalloc(&m->d_dlayers, sizeof(DecLayer) * L) != cudaSuccess ||
+        cudaMalloc(&m->d_drows, sizeof(DecLayerRows) * L) != cudaSuccess ||
+        cudaMalloc(&m->d_dmaps, sizeof(CUtensorMap) * (2 * L + 1) * 2) != cudaSuccess ||
+        cudaMalloc(&m->d_dbuf, kDecBytes) != cudaSuccess)
+      return fail(SQ_ENOMEM, "decode: cudaMalloc failed");
+    if (cudaMemset(m->d_dbuf, 0, kDecBytes) != cudaSuccess) return cuda_fail("decode: cudaMemset");
+  }
+  std::vector<DecLayer> dl(L);
+  std::vector<DecLayerRows> rows(L);
+  std::vector<CUtensorMap> maps((2 * L + 1) * 2);
+  for (int l = 0; l < L; ++l) {
+    const sq_layer_desc& d = m->layers[l];
+    const sq_model::St& st = m->states[l];
+    const AdapterPtrs& ad = m->adapters[l];
+    if (!d.in_proj.codes) return fail(SQ_ESTATE, "decode: layer weights not set");
+    if (st.batch != 1) return fail(SQ_ESTATE, "decode: the persistent kernel decodes batch 1 (bind batch-1 states)");
+    // every tensor the kernel bulk-copies must start on a 16-byte boundary
+    const void* a16[] = {d.conv_weight, d.conv_bias, d.norm_weight, d.gated_norm_weight, d.latent_scale, d.D,
+                         d.dt_bias, d.A, ad.w, ad.V, ad.g};
+    for (const void* q : a16)
+      if (q && !aligned(q, 16)) return fail(SQ_EINVAL, "decode: layer tensors must be 16-byte aligned");
+    if (!m->in_maps[l].valid || !m->out_maps[l].valid || m->in_maps[l].kc != 1024 || m->out_maps[l].kc != 1024)
+      return fail(SQ_ESTATE, "decode: projection stream maps missing");
+    DecLayer& x = dl[l];
+    std::memset(&x, 0, sizeof(x));
+    x.norm_w = d.norm_weight; x.conv_w = d.conv_weight; x.conv_b = d.conv_bias; x.A = d.A; x.D = d.D;
+    x.dt_bias = d.dt_bias; x.gnorm_w = d.gated_norm_weight;
+    x.in_g = d.in_proj.global_scale; x.out_g = d.out_proj.global_scale;
+    x.perm = d.permutation; x.basis = d.basis; x.latent_scale = d.latent_scale; x.predictor = d.predictor;
+    x.ad_V = ad.V; x.ad_g = ad.g; x.ad_w = ad.w; x.ad_b = ad.b; x.hard = ad.hard;
+    x.lo = st.lo; x.hi = st.hi; x.q4 = st.q4; x.latent = st.latent; x.s8 = st.s8; x.s4 = st.s4; x.ring = st.ring;
+    x.layout = d.layout;
+    rows[l] = DecLayerRows{d.in_proj.codes, d.in_proj.block_scales, d.out_proj.codes, d.out_proj.block_scales};
+    maps[(2 * l) * 2 + 0] = m->in_maps[l].codes; maps[(2 * l) * 2 + 1] = m->in_maps[l].scales;
+    maps[(2 * l + 1) * 2 + 0] = m->out_maps[l].codes; maps[(2 * l + 1) * 2 + 1] = m->out_maps[l].scales;
+  }
+  if (!m->head.codes || !m->head_maps.valid || m->head_maps.kc != 1024) return fail(SQ_ESTATE, "decode: lm_head not set");
+  if (!aligned(m->norm_f, 16) || !aligned(m->embed.codes, 4)) return fail(SQ_EINVAL, "decode: norm_f must be 16-byte aligned");
+  maps[(2 * L) * 2 + 0] = m->head_maps.codes; maps[(2 * L) * 2 + 1] = m->head_maps.scales;
+  if (cudaMemcpy(m->d_dlayers, dl.data(), sizeof(DecLayer) * L, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(m->d_drows, rows.data(), sizeof(DecLayerRows) * L, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(m->d_dmaps, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+    return cuda_fail("decode: table upload");
+  if (!m->dec_grid) m->dec_grid = decode_grid();
+  if (m->dec_grid < 128) return fail(SQ_ECUDA, "decode: cooperative launch of one CTA per SM (>= 128 SMs) unavailable");
+  m->dec_dirty = false;
+  return SQ_OK;
+}
+}  // namespace
+
+int sq_model_decode(sq_model* m, int64_t* tokens, int pos, int steps, int64_t* out_tokens, void* stream) {
+  if (!m || !tokens || steps <= 0 || pos <= 0) return fail(SQ_EINVAL, "decode: bad arguments (pos > 0: prefill first)");
+  Busy busy(m);
+  if (!busy.ok) return fail(SQ_ESTATE, "decode: concurrent/reentrant use of one model context");
+  if (m->exact_skinny)
+    return fail(SQ_EINVAL, "decode: the persistent kernel runs the factored-scale projections (exact mode is off)");
+  if (!m->logits || !m->norm_f) return fail(SQ_ESTATE, "decode: reserve() and set_globals() first");
+  if (m->dec_dirty) {
+    const int s = decode_setup(m);
+    if (s != SQ_OK) return s;
+  }
+  DecodeParams P{};
+  P.layers = m->d_dlayers; P.maps = m->d_dmaps; P.rows = m->d_drows;
+  P.head_codes = m->head.codes; P.head_scales = m->head.block_scales;
+  P.emb_codes = m->embed.codes; P.emb_scales = m->embed.block_scales; P.emb_g = m->embed.global_scale;
+  P.head_g = m->head.global_scale; P.norm_f = m->norm_f;
+  P.h = reinterpret_cast<uint16_t*>(m->d_dbuf + kDecH); P.res = reinterpret_cast<uint16_t*>(m->d_dbuf + kDecRes);
+  P.zx = reinterpret_cast<uint16_t*>(m->d_dbuf + kDecZx); P.y = reinterpret_cast<uint16_t*>(m->d_dbuf + kDecY);
+  P.logits = m->logits;
+  P.part_v = reinterpret_cast<float*>(m->d_dbuf + kDecPv); P.part_i = reinterpret_cast<int*>(m->d_dbuf + kDecPi);
+  P.sync = reinterpret_cast<DecodeSync*>(m->d_dbuf + kDecSync);
+  P.err = m->d_err; P.tok = (long long*)tokens; P.out_tokens = (long long*)out_tokens;
+  P.n_layer = m->cfg.n_layer; P.vocab = m->cfg.vocab; P.eps = m->cfg.eps;
+  // fresh barrier words (an aborted launch leaves its count and abort flag behind)
+  if (cudaMemsetAsync(P.sync, 0, sizeof(DecodeSync), (cudaStream_t)stream) != cudaSuccess)
+    return cuda_fail("decode: barrier reset");
+  for (int s = 0; s < steps; ++s) {
+    P.pos = pos + s;
+    P.step = s;
+    SQ_TRY(launch_decode_step(P, m->dec_grid, (cudaStream_t)stream), "persistent decode step");
+  }
+  return SQ_OK;
 }
 
 int sq_model_set_exact_skinny(sq_model* m, int exact) {

@@ -9,16 +9,12 @@
 //                       (scripts/run_fp4_ridge_resurface_v3.py:105-109,
 //                        scripts/infer_fp4_ridge_resurface_v1.py:103-105)
 #include "common.cuh"
+#include "device_util.cuh"
 #include "layer.cuh"
 
 namespace sq {
 namespace {
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
 
 // one CTA (256 threads) per row; D % 8 == 0, D <= 8192
 __global__ void add_rmsnorm_kernel(const uint16_t* __restrict__ h, uint16_t* __restrict__ res, int has_res,
@@ -123,22 +119,6 @@ __global__ void conv_prefill_kernel(const uint16_t* __restrict__ raw, long long 
 constexpr int kVPitch = 136;   // fp16 elements per staged V row (128 + 8 pad, 272 B)
 constexpr int kYPitch = 72;    // fp16 elements per staged y row (64 + 8 pad, 144 B)
 
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-  uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
-  uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
-}
-__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-               "{%0,%1,%2,%3};\n"
-               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
 
 template <int GPB>
 __global__ void __launch_bounds__(32 * GPB)
@@ -219,8 +199,8 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
           uint32_t bfr[4];
           // matrices: (j k0..+7, p n), (j k0+8.., p n), (j k0.., p n+8), (j k0+8.., p n+8)
           ldsm_x4_t(bfr, Ys + (k0 + rr + (mi & 1) * 8) * kYPitch + n2 * 16 + (mi >> 1) * 8);
-          mma_f16(acc[2 * n2], a, bfr[0], bfr[1]);
-          mma_f16(acc[2 * n2 + 1], a, bfr[2], bfr[3]);
+          mma16816(acc[2 * n2], a, bfr[0], bfr[1]);
+          mma16816(acc[2 * n2 + 1], a, bfr[2], bfr[3]);
         }
       }
     }
@@ -303,9 +283,6 @@ __global__ void window_sum_kernel(const float* __restrict__ nll, int per, const 
 
 // first-occurrence argmax in two stages: per (row, slice) partials, then per row
 constexpr int kArgSlice = 4096;
-__device__ __forceinline__ void argmax_merge(float& bv, int& bi, float v2, int i2) {
-  if (v2 > bv || (v2 == bv && i2 < bi)) { bv = v2; bi = i2; }
-}
 __global__ void argmax_partial_kernel(const uint16_t* __restrict__ logits, int V, long long ld,
                                       float* __restrict__ pv, int* __restrict__ pi, int nslice) {
   __shared__ float sv[256];

@@ -69,6 +69,7 @@ _PROTOS = {
     'sq_fp4_decode': (C.c_int, [p, p, p, C.c_int, C.c_int, p, i64, p]),
     'sq_scan_workspace': (i64, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
     'sq_model_set_exact_skinny': (C.c_int, [p, C.c_int]),
+    'sq_model_decode': (C.c_int, [p, p, C.c_int, C.c_int, p, p]),
     'sq_fp4_linear_workspace': (i64, [C.c_int, C.c_int, C.c_int]),
     'sq_fp4_linear': (C.c_int, [p, p, p, C.c_int, C.c_int, p, i64, C.c_int, p, i64, p, i64, p]),
     'sq_fp4_linear_static_max_k': (i64, []),

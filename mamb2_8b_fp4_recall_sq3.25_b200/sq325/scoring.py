@@ -84,11 +84,13 @@ def evaluate_ppl(execution, windows, batch_windows=16, rank=0, world=1, group=No
 
 
 @torch.no_grad()
-def generate(execution, prompt_ids, max_new_tokens, eos_token_id=None, graphs=False):
+def generate(execution, prompt_ids, max_new_tokens, eos_token_id=None, graphs=False, persistent=True):
     """Greedy decode: returns int64 [batch, n_generated] (n <= max_new_tokens).
 
-    graphs=True replays a captured CUDA graph per token (no host synchronisation inside
-    the loop; an EOS stop is then applied after the fact by truncation)."""
+    graphs=True runs the token loop without host synchronisation (an EOS stop is then
+    applied after the fact by truncation): at batch 1 with the factored-scale projections
+    one persistent kernel launch per token (persistent=True), otherwise a captured CUDA
+    graph per token."""
     dev = execution.device
     prompt = torch.as_tensor(prompt_ids, dtype=torch.long).to(dev)
     if prompt.ndim == 1:
@@ -97,8 +99,14 @@ def generate(execution, prompt_ids, max_new_tokens, eos_token_id=None, graphs=Fa
     if graphs:
         tok = execution.greedy(hidden).clone()
         first = tok.clone()
-        execution.capture_decode(tok)
-        rest = execution.replay_decode(max_new_tokens - 1) if max_new_tokens > 1 else None
+        use_kernel = (persistent and prompt.shape[0] == 1 and max_new_tokens > 1 and
+                      not getattr(execution, '_exact_projections', False))
+        rest = None
+        if use_kernel:
+            rest = execution.decode_persistent(tok, max_new_tokens - 1)
+        elif max_new_tokens > 1:
+            execution.capture_decode(tok)
+            rest = execution.replay_decode(max_new_tokens - 1)
         seq = first[:, None] if rest is None else torch.cat([first[:, None], rest.T], 1)
         if eos_token_id is not None:
             hit = (seq == eos_token_id).all(0).nonzero()

@@ -278,6 +278,30 @@ class PredictorState:
             out[i].copy_(self._graph_tokens)
         return out
 
+    @torch.no_grad()
+    def decode_persistent(self, tokens, steps):
+        """Greedy decode at batch 1 with one persistent kernel launch per token (all layers,
+        final norm, lm_head and argmax in one cooperative kernel).  `tokens` is an int64 [1]
+        device tensor holding the token to feed first; it is overwritten with every pick.
+        Returns int64 [steps, 1] picks.  Same tokens and states as `replay_decode`; uses the
+        factored-scale projections."""
+        if not self._cache or self._cache[0].tokens == 0:
+            raise RuntimeError('Prefill the request before decoding')
+        if self._batch_size != 1:
+            raise ValueError('The persistent decode kernel runs batch 1')
+        if tokens.shape != (1,) or tokens.dtype != torch.long or tokens.device != self.device:
+            raise ValueError('tokens must be CUDA int64 [1]')
+        if steps <= 0:
+            raise ValueError('steps must be positive')
+        self.reserve(1)
+        out = torch.empty((steps, 1), device=self.device, dtype=torch.long)
+        with torch.cuda.device(self.device):
+            _lib.call('sq_model_decode', self._handle, _lib.ptr(tokens), self._cache[0].tokens, steps,
+                      _lib.ptr(out), _lib.stream_ptr())
+        for e in self._cache:
+            e.tokens += steps
+        return out
+
     def check(self):
         """Synchronise and raise if a device-side check failed (bad token id, expired wait)."""
         _lib.call('sq_model_check', self._handle, _lib.stream_ptr())

@@ -162,3 +162,27 @@ def test_factored_scale_projections_track_exact(pair):
             outs[exact] = (h.float(), logits.float())
     assert rel_l2(outs[False][0], outs[True][0]) < 5e-3
     assert rel_l2(outs[False][1], outs[True][1]) < 5e-3
+
+
+def test_persistent_decode_matches_graph_replay(pair):
+    """The one-launch-per-token decode kernel reproduces the multi-kernel graph replay:
+    identical greedy tokens, identical packed states and conv rings, identical last logits."""
+    from sq325 import PredictorState, generate
+    gm, _, statics = pair
+    prompt = np.random.default_rng(31).integers(0, gm.vocab, (1, 9))
+    runs = {}
+    for persistent in (False, True):
+        with PredictorState(gm, *statics) as ex:
+            seq = generate(ex, prompt, 13, graphs=True, persistent=persistent)
+            torch.cuda.synchronize()
+            ex.check()
+            states = [{k: v.view(torch.uint8).clone() for k, v in e.state.tensors.items()} for e in ex._cache]
+            rings = [ex.conv_chronological(l).clone() for l in range(gm.n_layer)]
+            runs[persistent] = (seq.cpu(), states, rings)
+    assert runs[True][0].shape == (1, 13)
+    assert torch.equal(runs[True][0], runs[False][0])
+    for a, b in zip(runs[True][1], runs[False][1]):
+        for k in a:
+            assert torch.equal(a[k], b[k]), k
+    for a, b in zip(runs[True][2], runs[False][2]):
+        assert torch.equal(a, b)
