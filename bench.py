@@ -398,14 +398,14 @@ def main():
             ex.check()
             return d0.elapsed_time(d1) / 1e3 / args.decode_steps
 
-        dt = timed(lambda n: ex.decode_persistent(tok, n))      # one cooperative launch per token
+        dt = timed(lambda n: ex.decode_persistent(tok, n))      # one cooperative launch for n tokens
         ex.capture_decode(tok)
         dt_graph = timed(ex.replay_decode)                      # multi-kernel step, CUDA-graph replay
         roof = pk['hbm'] * 1e9 / DECODE_BYTES_B1
         decode = dict(tokens_per_s=1.0 / dt, ms_per_token=dt * 1e3, roofline_tokens_per_s=roof,
                       frac=(1.0 / dt) / roof, bytes_per_token=DECODE_BYTES_B1,
                       graph_replay_tokens_per_s=1.0 / dt_graph,
-                      note='batch 1, 64-token prompt, persistent kernel (one cooperative launch per token); '
+                      note='batch 1, 64-token prompt, persistent kernel (one cooperative launch runs all timed tokens); '
                            'graph_replay = the multi-kernel step replayed as CUDA graphs')
 
     cpu = None

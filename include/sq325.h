@@ -192,8 +192,8 @@ int sq_model_greedy(sq_model* model, const uint16_t* hidden, int rows, uint16_t*
                     int64_t* tokens_out, void* stream);
 /* Synchronises the stream and reports a device-side failure (bad token id, expired wait). */
 int sq_model_check(sq_model* model, void* stream);
-/* Greedy decode at batch 1 with one persistent launch per token (the loop of
- * infer_fp4_ridge_resurface_v1.py:100-110 after the prompt): step s feeds tokens[0] at
+/* Greedy decode at batch 1 with one persistent cooperative launch for all `steps` tokens
+ * (the loop of infer_fp4_ridge_resurface_v1.py:100-110 after the prompt): step s feeds tokens[0] at
  * position pos + s, runs all layers, the final norm, lm_head and argmax, overwrites
  * tokens[0] with the pick and stores it in out_tokens[s] (device, may be NULL).  Requires
  * batch-1 states (pos > 0: prompt already consumed), reserve(), and the factored-scale

@@ -546,11 +546,9 @@ int sq_model_decode(sq_model* m, int64_t* tokens, int pos, int steps, int64_t* o
   // fresh barrier words (an aborted launch leaves its count and abort flag behind)
   if (cudaMemsetAsync(P.sync, 0, sizeof(DecodeSync), (cudaStream_t)stream) != cudaSuccess)
     return cuda_fail("decode: barrier reset");
-  for (int s = 0; s < steps; ++s) {
-    P.pos = pos + s;
-    P.step = s;
-    SQ_TRY(launch_decode_step(P, m->dec_grid, (cudaStream_t)stream), "persistent decode step");
-  }
+  P.pos = pos;
+  P.steps = steps;
+  SQ_TRY(launch_decode_step(P, m->dec_grid, (cudaStream_t)stream), "persistent decode");
   return SQ_OK;
 }
 

@@ -1,4 +1,4 @@
-// Persistent batch-1 greedy decode step (one cooperative launch per generated token).
+// Persistent batch-1 greedy decode (one cooperative launch runs all requested tokens).
 //
 // Same arithmetic, operation for operation, as the multi-kernel decode step it replaces
 // (fp4_embed, add_rmsnorm, the factored-scale streaming GEMV, the one-token scan step with
@@ -93,6 +93,14 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
+}
+// Time-bounded wait that ignores the abort flag: before a CTA exits, every copy it issued
+// must have landed in its shared memory.
+__device__ __forceinline__ bool mb_drain(uint32_t a, uint32_t parity) {
+  const uint64_t t0 = now_ns();
+  while (!mb_try(a, parity))
+    if (now_ns() - t0 > kWaitNs) return false;
+  return true;
 }
 __device__ __forceinline__ void tma2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y,
                                       uint64_t policy) {
@@ -389,6 +397,7 @@ __device__ void producer(const DecodeParams& P, const Ring& R) {
     }
     ++ctr;
   };
+  for (int step = 0; step < P.steps && ok; ++step) {
   prefetch_rows(lp[0].in_codes, lp[0].in_scales, kDModel, rin);
   for (int l = 0; l < P.n_layer && ok; ++l) {
     prefetch_rows(lp[l].out_codes, lp[l].out_scales, kDInner, rout);
@@ -407,14 +416,12 @@ __device__ void producer(const DecodeParams& P, const Ring& R) {
       prefetch_rows(head_codes, head_scales, kDModel, TileRange{t + 8, min(rhead.t1, t + 16)});
     for (int kc = 0; kc < kDModel / kKc; ++kc) issue(mh, mh + 1, t, kc);
   }
+  }
   // every issued copy has landed before the CTA may exit
   const int issued = ctr;
   for (int i = 0; i < kNst && i < issued; ++i) {
     const int c = issued - 1 - i;
-    if (!mb_wait(R.full + 8 * (c % kNst), (uint32_t)(c / kNst) & 1u, P.sync)) {
-      // a copy that never completes leaves nothing to wait for; stop after the bound
-      break;
-    }
+    if (!mb_drain(R.full + 8 * (c % kNst), (uint32_t)(c / kNst) & 1u)) break;
   }
 }
 
@@ -462,7 +469,8 @@ __device__ __forceinline__ unsigned scan_stage_bytes(const Geo& G) {
   return G.f * G.nz * 2 + G.nz * 4 + 128 + 64 * (2 * G.w8 + G.w4) + 3 * 128 + 512 + 128 + 2048 + 512 + 3 * 640 + 32 +
          256 + 256 + 512;
 }
-__device__ void scan_stage(const DecodeParams& P, const DecLayer& L, int hh, unsigned char* sc, uint32_t bar) {
+__device__ void scan_stage(const DecodeParams& P, const DecLayer& L, int hh, unsigned char* sc, uint32_t bar,
+                           int pos) {
   const Geo G = geo_of(L.layout);
   const int g = hh / (kHeads / kGroups);
   const long long row0 = (long long)hh * 64;
@@ -484,7 +492,7 @@ __device__ void scan_stage(const DecodeParams& P, const DecLayer& L, int hh, uns
   cp(sc + sBbc, L.conv_b + 8192 + g * 128, 256);
   cp(sc + sBbc + 256, L.conv_b + 9216 + g * 128, 256);
   for (int k = 0; k < 3; ++k) {
-    const uint16_t* rs = L.ring + ((P.pos - 3 + k) & 3) * 10240;
+    const uint16_t* rs = L.ring + ((pos - 3 + k) & 3) * 10240;
     unsigned char* hk = sc + sHist + k * 640;
     cp(hk, rs + hh * 64, 128);
     cp(hk + 128, rs + 8192 + g * 128, 256);
@@ -497,7 +505,7 @@ __device__ void scan_stage(const DecodeParams& P, const DecLayer& L, int hh, uns
 }
 
 __device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsigned char* sc, float2* S2,
-                          int layer) {
+                          int layer, int pos) {
   const Geo G = geo_of(L.layout);
   const int NS = G.ns, NZ = G.nz, F = G.f, W8 = G.w8, W4 = G.w4, NP = G.np, N8 = G.n8;
   const int tid = threadIdx.x, g = hh / (kHeads / kGroups);
@@ -511,7 +519,7 @@ __device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsi
   float* sX = reinterpret_cast<float*>(sc + sXo);
   float* sDots = reinterpret_cast<float*>(sc + sDotso);
   float* sDD = reinterpret_cast<float*>(sc + sDDo);
-  const int slot = P.pos & 3;
+  const int slot = pos & 3;
   uint16_t* ring_new = L.ring + slot * 10240;
   // -- conv step (state_quant.py:291-297) of B/C in tier order, x of own channels, dt --
   {
@@ -718,7 +726,7 @@ __device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsi
 // V (staged at the start of the layer) and y (staged after the scan) sit in shared memory.
 __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const uint16_t* Us, const uint16_t* Ys,
                                const uint16_t* Vs, const uint16_t* Ws, const uint16_t* Gs, const uint16_t* Ns,
-                               uint16_t* zout) {
+                               uint16_t* zout, int layer) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gq = lane >> 2, tq = lane & 3;
   const int grp = warp;
@@ -739,6 +747,7 @@ __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const u
     const float lg = h2f(f2h(h2f(f2h(s)) + h2f(L.ad_b[0])));
     gate = h2f(f2h(L.hard ? (lg > 0.f ? 1.f : 0.f) : 1.0f / (1.0f + expf(-lg))));
   }
+  DTRACE(layer, 10);
   float acc[8][4];
 #pragma unroll
   for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
@@ -758,6 +767,7 @@ __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const u
       }
     }
   }
+  DTRACE(layer, 11);
   const uint16_t* zs = zout + grp * 1024;               // z of this group, staged where yn goes
   const uint16_t* ns = Ns + grp * 1024;
   float xv[8][4];
@@ -838,15 +848,8 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
   const TileRange rin = tile_range(kZx / kRows, cta, ncta), rout = tile_range(kDModel / kRows, cta, ncta);
   const TileRange rhead = tile_range(P.vocab / kRows, cta, ncta);
   const int item = cta < kHeads ? cta : -1;           // scan head of this CTA (batch 1)
-  long long id = *P.tok;
-  if (id < 0 || id >= P.vocab) {
-    if (tid == 0 && cta == 0) atomicOr(P.err, (int)kDevBadArgs);
-    id = 0;
-  }
   bool ok = true;
   int ctr = 0;
-  float best = -INFINITY;
-  int bidx = 0x7fffffff;
   uint16_t* Vs = reinterpret_cast<uint16_t*>(sm + oV);
   float2* S2 = reinterpret_cast<float2*>(sm + oV);      // scan row state, same bytes as V
   uint16_t* Ws = reinterpret_cast<uint16_t*>(sm + oAdw);
@@ -864,35 +867,54 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     mb_expect(sbNw, kDModel * 2);
     bulk_g2s(Nw, P.layers[0].norm_w, kDModel * 2, sbNw);
   }
-  int vuse = 0;
+  int vuse = 0, nw_phase = 0, in_phase = 0;
+  unsigned arms_in = 0, arms_nw = 1, arms_v = 0;        // bulk-copy phases armed by thread 0
+  for (int step = 0; step < P.steps; ++step) {
+  // the token of this step: the caller's for the first, then the previous step's pick
+  long long id = __ldcg(P.tok);
+  if (id < 0 || id >= P.vocab) {
+    if (tid == 0 && cta == 0) atomicOr(P.err, (int)kDevBadArgs);
+    id = 0;
+  }
+  const int pos = P.pos + step;
+  float best = -INFINITY;
+  int bidx = 0x7fffffff;
   for (int l = 0; l < P.n_layer; ++l) {
     const DecLayer& L = P.layers[l];
     DTRACE(l, 0);
     DARRIVE(l, 3);
     // per-layer inputs that do not depend on this token: one thread issues bulk copies that
-    // land while in_proj runs (earlier generic accesses of these bytes are fenced first)
+    // land while in_proj runs.  The proxy fence orders the generic accesses before it (this
+    // CTA's shared memory, and the state rows / conv ring written by the previous step, made
+    // visible by the grid barriers) ahead of the copies.
     if (tid == 0) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("fence.proxy.async;" ::: "memory");
       unsigned bytes = kDInner * 2;
       if (L.ad_V) bytes += kDModel * 2 + kHeads * 2;
       if (item >= 0) bytes += scan_stage_bytes(geo_of(L.layout));
       mb_expect(sbIn, bytes);
+      ++arms_in;
       bulk_g2s(Gn, L.gnorm_w, kDInner * 2, sbIn);
       if (L.ad_V) {
         bulk_g2s(Ws, L.ad_w, kDModel * 2, sbIn);
         bulk_g2s(Ag, L.ad_g, kHeads * 2, sbIn);
       }
-      if (item >= 0) scan_stage(P, L, item, sc, sbIn);
+      if (item >= 0) scan_stage(P, L, item, sc, sbIn, pos);
+      // V is copied into shared memory only after the scan: bring it into L2 now (4 KB piece
+      // per CTA, the pieces spread over the grid)
+      if (L.ad_V && cta < 8) prefetch_l2(reinterpret_cast<const uint8_t*>(L.ad_V) + cta * 4096, 4096);
     }
     // this layer's norm weight was staged one layer ahead (layer 0: at the start)
-    stage_wait(sbNw, (uint32_t)(l & 1));
+    stage_wait(sbNw, (uint32_t)nw_phase);
+    nw_phase ^= 1;
     uint16_t* res_out = cta == 0 ? P.res + ((l + 1) & 1) * kDModel : nullptr;
     block_norm(P, P.h, l > 0 ? P.res + (l & 1) * kDModel : nullptr, res_out, Nw + (l & 1) * kDModel,
                l == 0 ? id : -1, hn, misc);
     // next layer's norm weight (norm_f after the last layer) into the other half
     if (tid == 0) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("fence.proxy.async;" ::: "memory");
       mb_expect(sbNw, kDModel * 2);
+      ++arms_nw;
       bulk_g2s(Nw + ((l + 1) & 1) * kDModel, l + 1 < P.n_layer ? P.layers[l + 1].norm_w : P.norm_f, kDModel * 2, sbNw);
     }
     DTRACE(l, 1);
@@ -908,9 +930,9 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     for (int i = tid; i < kDInner / 8; i += kCompute) cp_async16(yn + i * 8, P.zx + i * 8);
     asm volatile("cp.async.commit_group;\n" ::: "memory");
     if (item >= 0) {
-      stage_wait(sbIn, (uint32_t)(l & 1));
+      stage_wait(sbIn, (uint32_t)in_phase);
       DTRACE(l, 9);
-      scan_step(P, L, item, sc, S2, l);
+      scan_step(P, L, item, sc, S2, l, pos);
     }
     DTRACE(l, 4);
     DARRIVE(l, 1);
@@ -919,8 +941,9 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     {
       uint16_t* Ys = reinterpret_cast<uint16_t*>(sc);
       if (L.ad_V && tid == 0) {                          // V into the row-state bytes, now free
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("fence.proxy.async;" ::: "memory");
         mb_expect(sbV, 128 * 128 * 2);
+        ++arms_v;
         bulk_g2s(Vs, L.ad_V, 128 * 128 * 2, sbV);
       }
       for (int i = tid; i < 128 * 8; i += kCompute) {
@@ -928,13 +951,15 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
         cp_async16(Ys + r * kYPitch + c, P.y + r * 64 + c);
       }
       cp_async_wait_all();
-      stage_wait(sbIn, (uint32_t)(l & 1));
+      stage_wait(sbIn, (uint32_t)in_phase);
+      in_phase ^= 1;
       if (L.ad_V) {
         stage_wait(sbV, (uint32_t)(vuse & 1));
         ++vuse;
       }
       bar_sync(1, kCompute);
-      resurface_norm(P, L, hn, Ys, Vs, Ws, Ag, Gn, yn);
+      DTRACE(l, 9);
+      resurface_norm(P, L, hn, Ys, Vs, Ws, Ag, Gn, yn, l);
       bar_sync(1, kCompute);
     }
     DTRACE(l, 6);
@@ -948,10 +973,18 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     DTRACE(l, 8);
   }
   DTRACE(63, 0);
-  stage_wait(sbNw, (uint32_t)(P.n_layer & 1));                   // norm_f
+  stage_wait(sbNw, (uint32_t)nw_phase);                          // norm_f
+  nw_phase ^= 1;
   // final norm (norm_f) and the greedy head
   block_norm(P, P.h, P.res + (P.n_layer & 1) * kDModel, nullptr, Nw + (P.n_layer & 1) * kDModel, -1, hn, misc);
+  if (step + 1 < P.steps && tid == 0) {                          // next token's layer-0 norm weight
+    asm volatile("fence.proxy.async;" ::: "memory");
+    mb_expect(sbNw, kDModel * 2);
+    ++arms_nw;
+    bulk_g2s(Nw, P.layers[0].norm_w, kDModel * 2, sbNw);
+  }
   gemv_phase(P, R, sm, ctr, rhead.t0, rhead.t1, kDModel / kKc, hn, P.head_g, P.logits, red, true, best, bidx, ok);
+  ctr += (rhead.t1 - rhead.t0) * (kDModel / kKc);
   // CTA candidate: warps 0 and 4 hold the per-lane picks of their group
   if ((warp & 3) == 0) {
 #pragma unroll
@@ -989,8 +1022,17 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     if (tid == 0) {
       const long long pick = bi == 0x7fffffff ? 0 : bi;
       *P.tok = pick;
-      if (P.out_tokens) P.out_tokens[P.step] = pick;
+      if (P.out_tokens) P.out_tokens[step] = pick;
     }
+  }
+  if (step + 1 < P.steps) grid_sync(P, flag);                    // every CTA reads the pick next
+  }
+  // after an abort some staged copies were never waited for: let them land before exiting
+  cp_async_wait_all();
+  if (tid == 0) {
+    if (arms_in) mb_drain(sbIn, (arms_in - 1) & 1u);
+    if (arms_nw) mb_drain(sbNw, (arms_nw - 1) & 1u);
+    if (arms_v) mb_drain(sbV, (arms_v - 1) & 1u);
   }
   (void)ok;
 }

@@ -55,14 +55,15 @@ struct DecodeParams {
   float* part_v; int* part_i;    // [grid] argmax candidates
   DecodeSync* sync;
   int* err;
-  long long* tok;                // [1] token fed to this step, replaced by the greedy pick
+  long long* tok;                // [1] token fed to the first step, replaced by every greedy pick
   long long* out_tokens;         // [steps] picks (may be null)
-  int n_layer, vocab, pos, step;
+  int n_layer, vocab, pos, steps; // pos: position of the first step's token
   float eps;
 };
 
 // Dynamic shared memory of the kernel; decode_grid() = CTAs of one cooperative launch (one
-// per SM) or -1 when this device cannot run it; launch_decode_step enqueues one token step.
+// per SM) or -1 when this device cannot run it; launch_decode_step enqueues one launch that
+// runs p.steps greedy token steps.
 int decode_smem_bytes();
 int prepare_decode_kernel();
 int decode_grid();

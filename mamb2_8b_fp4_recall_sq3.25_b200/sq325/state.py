@@ -280,8 +280,8 @@ class PredictorState:
 
     @torch.no_grad()
     def decode_persistent(self, tokens, steps):
-        """Greedy decode at batch 1 with one persistent kernel launch per token (all layers,
-        final norm, lm_head and argmax in one cooperative kernel).  `tokens` is an int64 [1]
+        """Greedy decode at batch 1 with one persistent cooperative kernel launch for all
+        `steps` tokens (every layer, the final norm, lm_head and argmax per token).  `tokens` is an int64 [1]
         device tensor holding the token to feed first; it is overwritten with every pick.
         Returns int64 [steps, 1] picks.  Same tokens and states as `replay_decode`; uses the
         factored-scale projections."""

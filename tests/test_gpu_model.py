@@ -186,3 +186,24 @@ def test_persistent_decode_matches_graph_replay(pair):
             assert torch.equal(a[k], b[k]), k
     for a, b in zip(runs[True][2], runs[False][2]):
         assert torch.equal(a, b)
+
+
+def test_persistent_decode_split_calls_match_one_call(pair):
+    """Several tokens in one persistent launch equal the same tokens from separate calls."""
+    from sq325 import PredictorState
+    gm, _, statics = pair
+    prompt = torch.from_numpy(np.random.default_rng(41).integers(0, gm.vocab, (1, 7))).cuda()
+    outs = []
+    for split in (False, True):
+        with PredictorState(gm, *statics) as ex:
+            tok = ex.greedy(ex.backbone(prompt, reset=True)[:, -1]).clone()
+            if split:
+                seq = torch.cat([ex.decode_persistent(tok, 3), ex.decode_persistent(tok, 2), ex.decode_persistent(tok, 4)])
+            else:
+                seq = ex.decode_persistent(tok, 9)
+            torch.cuda.synchronize()
+            ex.check()
+            outs.append((seq.cpu(), [e.state.tensors['lo'].clone() for e in ex._cache]))
+    assert torch.equal(outs[0][0], outs[1][0])
+    for a, b in zip(outs[0][1], outs[1][1]):
+        assert torch.equal(a, b)
