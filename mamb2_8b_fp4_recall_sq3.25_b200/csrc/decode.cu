@@ -27,7 +27,7 @@
 namespace sq {
 namespace {
 
-constexpr int kWarps = 9, kThreads = 32 * kWarps, kCompute = 256;
+constexpr int kWarps = 10, kThreads = 32 * kWarps, kCompute = 256;   // 8 compute, producer, stager
 constexpr int kNst = 11;                               // ring stages
 constexpr int kRows = 16, kKc = 1024;                  // tile rows, columns per chunk
 constexpr int kCodeBytes = kRows * kKc / 2, kScaleBytes = kRows * kKc / 16, kStageBytes = kCodeBytes + kScaleBytes;
@@ -40,7 +40,7 @@ constexpr unsigned long long kWaitNs = 500000000ull;   // 0.5 s per wait
 // more than one dependent memory round trip.
 constexpr int oRing = 0;
 constexpr int oBar = oRing + kNst * kStageBytes;       // full[kNst], empty[kNst]
-constexpr int oSBar = oBar + 2 * kNst * 8;             // staging mbarriers: layer inputs, norm weight, V
+constexpr int oSBar = oBar + 2 * kNst * 8;             // staging mbarriers: layer inputs, norm weight, V, inputs free
 constexpr int oRed = oSBar + 32;                       // GEMV cross-warp sums [2][4][32][4] f32
 constexpr int oHn = oRed + 2 * 4 * 32 * 4 * 4;         // normed layer input [4096] fp16
 constexpr int oYn = oHn + kDModel * 2;                 // z staging, then the gated-norm output [8192] fp16
@@ -116,7 +116,7 @@ __device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes) {
 // Phase timestamps of two CTAs for the first layers, compiled only with SQ_DECODE_TRACE
 // (a profiling build); the product build records nothing.
 #ifdef SQ_DECODE_TRACE
-__device__ unsigned long long g_decode_trace[2][64][12];
+__device__ unsigned long long g_decode_trace[2][64][16];
 #define DTRACE(layer, slot)                                                                         \
   do {                                                                                              \
     if (threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1) && (layer) < 64)       \
@@ -147,15 +147,27 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
   asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ bool grid_sync(const DecodeParams& P, int* flag) {
+// Split-phase form: grid_arrive adds this CTA's arrival and returns the count to wait for
+// (thread 0 only; 0 after an abort); work that does not depend on the other CTAs can run
+// before grid_wait.
+__device__ unsigned long long grid_arrive(const DecodeParams& P) {
   bar_sync(1, kCompute);
+  unsigned long long target = 0;
   if (threadIdx.x == 0) {
     DecodeSync* s = P.sync;
-    int ok = !ld_abort(s);
-    if (ok) {
+    if (!ld_abort(s)) {
       __threadfence();
       const unsigned long long old = atomicAdd(&s->count, 1ull);
-      const unsigned long long target = (old / gridDim.x + 1) * gridDim.x;
+      target = (old / gridDim.x + 1) * gridDim.x;
+    }
+  }
+  return target;
+}
+__device__ bool grid_wait(const DecodeParams& P, unsigned long long target, int* flag) {
+  if (threadIdx.x == 0) {
+    const DecodeSync* s = P.sync;
+    int ok = target != 0;
+    if (ok) {
       const uint64_t t0 = now_ns();
       int spins = 0;
       while (ld_acquire_u64(&s->count) < target) {
@@ -171,6 +183,7 @@ __device__ bool grid_sync(const DecodeParams& P, int* flag) {
   bar_sync(1, kCompute);
   return *flag != 0;
 }
+__device__ bool grid_sync(const DecodeParams& P, int* flag) { return grid_wait(P, grid_arrive(P), flag); }
 
 // Block residual + RMSNorm over 4096 channels with 256 threads, the add_rmsnorm_kernel
 // arithmetic: res = fp16(h + res) (or h), out = fp16((res * rstd) * w).  The layer-0 input
@@ -462,46 +475,53 @@ __device__ __forceinline__ void mb_expect(uint32_t bar, unsigned bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
 }
 
-// Bulk copies of the step's static inputs (one thread issues them; they complete on `bar`,
-// armed by the caller with scan_stage_bytes): predictor table, basis, permutation, the
-// head's packed rows, conv taps / biases, the conv ring history and the per-head scalars.
+// The step's static inputs in kScanPieces pieces (each a multiple of 16 bytes, both ends
+// 16-byte aligned): predictor table, basis, permutation, the head's packed rows, conv taps /
+// biases, the conv ring history and the per-head scalars.
+constexpr int kScanPieces = 28;
 __device__ __forceinline__ unsigned scan_stage_bytes(const Geo& G) {
   return G.f * G.nz * 2 + G.nz * 4 + 128 + 64 * (2 * G.w8 + G.w4) + 3 * 128 + 512 + 128 + 2048 + 512 + 3 * 640 + 32 +
          256 + 256 + 512;
 }
-__device__ void scan_stage(const DecodeParams& P, const DecLayer& L, int hh, unsigned char* sc, uint32_t bar,
-                           int pos) {
+struct Piece { void* d; const void* s; int bytes; };
+__device__ __forceinline__ Piece scan_stage_piece(const DecLayer& L, int hh, unsigned char* sc, int k, int pos) {
   const Geo G = geo_of(L.layout);
   const int g = hh / (kHeads / kGroups);
   const long long row0 = (long long)hh * 64;
-  auto cp = [&](void* d, const void* s, int bytes) { bulk_g2s(d, s, (unsigned)bytes, bar); };
   unsigned char* rows = sc + sRows;
-  cp(sc + sPred, L.predictor + (long long)g * G.f * G.nz, G.f * G.nz * 2);
-  cp(sc + sBasis, L.basis + (long long)g * G.nz * 2, G.nz * 4);
-  cp(sc + sPerm, L.perm + g * 128, 128);
-  cp(rows, L.lo + row0 * G.w8, 64 * G.w8);
-  cp(rows + 64 * G.w8, L.hi + row0 * G.w8, 64 * G.w8);
-  cp(rows + 128 * G.w8, L.q4 + row0 * G.w4, 64 * G.w4);
-  cp(rows + 128 * G.w8 + 64 * G.w4, L.latent + row0 * 2, 128);
-  cp(rows + 128 * G.w8 + 64 * G.w4 + 128, L.s8 + row0, 128);
-  cp(rows + 128 * G.w8 + 64 * G.w4 + 256, L.s4 + row0, 128);
-  cp(sc + sWx, L.conv_w + (long long)hh * 64 * 4, 512);
-  cp(sc + sBx, L.conv_b + hh * 64, 128);
-  cp(sc + sWbc, L.conv_w + (long long)(8192 + g * 128) * 4, 1024);
-  cp(sc + sWbc + 1024, L.conv_w + (long long)(9216 + g * 128) * 4, 1024);
-  cp(sc + sBbc, L.conv_b + 8192 + g * 128, 256);
-  cp(sc + sBbc + 256, L.conv_b + 9216 + g * 128, 256);
-  for (int k = 0; k < 3; ++k) {
-    const uint16_t* rs = L.ring + ((pos - 3 + k) & 3) * 10240;
-    unsigned char* hk = sc + sHist + k * 640;
-    cp(hk, rs + hh * 64, 128);
-    cp(hk + 128, rs + 8192 + g * 128, 256);
-    cp(hk + 384, rs + 9216 + g * 128, 256);
+  void* d = nullptr;
+  const void* src = nullptr;
+  int bytes = 0;
+  switch (k) {
+    case 0: d = sc + sPred; src = L.predictor + (long long)g * G.f * G.nz; bytes = G.f * G.nz * 2; break;
+    case 1: d = sc + sBasis; src = L.basis + (long long)g * G.nz * 2; bytes = G.nz * 4; break;
+    case 2: d = sc + sPerm; src = L.perm + g * 128; bytes = 128; break;
+    case 3: d = rows; src = L.lo + row0 * G.w8; bytes = 64 * G.w8; break;
+    case 4: d = rows + 64 * G.w8; src = L.hi + row0 * G.w8; bytes = 64 * G.w8; break;
+    case 5: d = rows + 128 * G.w8; src = L.q4 + row0 * G.w4; bytes = 64 * G.w4; break;
+    case 6: d = rows + 128 * G.w8 + 64 * G.w4; src = L.latent + row0 * 2; bytes = 128; break;
+    case 7: d = rows + 128 * G.w8 + 64 * G.w4 + 128; src = L.s8 + row0; bytes = 128; break;
+    case 8: d = rows + 128 * G.w8 + 64 * G.w4 + 256; src = L.s4 + row0; bytes = 128; break;
+    case 9: d = sc + sWx; src = L.conv_w + (long long)hh * 64 * 4; bytes = 512; break;
+    case 10: d = sc + sBx; src = L.conv_b + hh * 64; bytes = 128; break;
+    case 11: d = sc + sWbc; src = L.conv_w + (long long)(8192 + g * 128) * 4; bytes = 1024; break;
+    case 12: d = sc + sWbc + 1024; src = L.conv_w + (long long)(9216 + g * 128) * 4; bytes = 1024; break;
+    case 13: d = sc + sBbc; src = L.conv_b + 8192 + g * 128; bytes = 256; break;
+    case 14: d = sc + sBbc + 256; src = L.conv_b + 9216 + g * 128; bytes = 256; break;
+    case 24: d = sc + sLs; src = L.latent_scale; bytes = kGroups * 2 * 2; break;
+    case 25: d = sc + sDv; src = L.D; bytes = kHeads * 2; break;
+    case 26: d = sc + sDtb; src = L.dt_bias; bytes = kHeads * 2; break;
+    case 27: d = sc + sAv; src = L.A; bytes = kHeads * 4; break;
+    default: {                                        // 15..23: conv ring history, 3 slots x 3 pieces
+      const int hk = (k - 15) / 3, part = (k - 15) % 3;
+      const uint16_t* rs = L.ring + ((pos - 3 + hk) & 3) * 10240;
+      unsigned char* hd = sc + sHist + hk * 640;
+      if (part == 0) { d = hd; src = rs + hh * 64; bytes = 128; }
+      else if (part == 1) { d = hd + 128; src = rs + 8192 + g * 128; bytes = 256; }
+      else { d = hd + 384; src = rs + 9216 + g * 128; bytes = 256; }
+    }
   }
-  cp(sc + sLs, L.latent_scale, kGroups * 2 * 2);
-  cp(sc + sDv, L.D, kHeads * 2);
-  cp(sc + sDtb, L.dt_bias, kHeads * 2);
-  cp(sc + sAv, L.A, kHeads * 4);
+  return Piece{d, src, bytes};
 }
 
 __device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsigned char* sc, float2* S2,
@@ -720,13 +740,29 @@ __device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsi
   copy_out(reinterpret_cast<unsigned char*>(L.s4 + row0), reinterpret_cast<unsigned char*>(pS4), 128);
 }
 
+// Adapter gate partial of warp w: the dot u . w over channels [512 w, 512 w + 512), lane
+// stride 8, then the warp sum.  The gate logit is the sum of the eight partials in warp
+// order (the summation of the multi-kernel resurface_gatednorm_kernel).
+__device__ __forceinline__ float gate_partial(const uint16_t* Us, const uint16_t* Ws, int w, int lane) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = w * 512 + lane * 8; i < (w + 1) * 512; i += 256) {
+    const uint4 uv = *reinterpret_cast<const uint4*>(Us + i);
+    const uint4 wv = *reinterpret_cast<const uint4*>(Ws + i);
+    const uint16_t* up = reinterpret_cast<const uint16_t*>(&uv);
+    const uint16_t* wp = reinterpret_cast<const uint16_t*>(&wv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s = fmaf(h2f(up[k]), h2f(wp[k]), s);
+  }
+  return warp_sum(s);
+}
+
 // Resurface adapter + gated RMSNorm for one token, warp w = norm group w: the
-// resurface_gatednorm_kernel arithmetic with one group per CTA (gate dot by one warp,
-// head mix on the tensor cores, correction, x = y * silu(z), RMSNorm over 1024 channels).
-// V (staged at the start of the layer) and y (staged after the scan) sit in shared memory.
-__device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const uint16_t* Us, const uint16_t* Ys,
-                               const uint16_t* Vs, const uint16_t* Ws, const uint16_t* Gs, const uint16_t* Ns,
-                               uint16_t* zout, int layer) {
+// resurface_gatednorm_kernel arithmetic with one group per CTA (head mix on the tensor
+// cores, correction, x = y * silu(z), RMSNorm over 1024 channels).  The gate partials were
+// computed earlier (gpart[8]); V (staged after the scan) and y sit in shared memory.
+__device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const float* gpart, const uint16_t* Ys,
+                               const uint16_t* Vs, const uint16_t* Gs, const uint16_t* Ns, uint16_t* zout, int layer) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gq = lane >> 2, tq = lane & 3;
   const int grp = warp;
@@ -734,20 +770,12 @@ __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const u
   float gate = 0.f;
   if (has_ad) {
     float s = 0.f;
-#pragma unroll 4
-    for (int i = lane * 8; i < kDModel; i += 256) {
-      const uint4 uv = *reinterpret_cast<const uint4*>(Us + i);
-      const uint4 wv = *reinterpret_cast<const uint4*>(Ws + i);
-      const uint16_t* up = reinterpret_cast<const uint16_t*>(&uv);
-      const uint16_t* wp = reinterpret_cast<const uint16_t*>(&wv);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) s = fmaf(h2f(up[k]), h2f(wp[k]), s);
-    }
-    s = warp_sum(s);
+    for (int w = 0; w < 8; ++w) s += gpart[w];
     const float lg = h2f(f2h(h2f(f2h(s)) + h2f(L.ad_b[0])));
-    gate = h2f(f2h(L.hard ? (lg > 0.f ? 1.f : 0.f) : 1.0f / (1.0f + expf(-lg))));
+    gate = h2f(f2h(L.hard ? (lg > 0.f ? 1.f : 0.f) : __frcp_rn(1.0f + expf(-lg))));
   }
-  DTRACE(layer, 10);
+  DTRACE(layer, 13);
   float acc[8][4];
 #pragma unroll
   for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
@@ -767,7 +795,7 @@ __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const u
       }
     }
   }
-  DTRACE(layer, 11);
+  DTRACE(layer, 14);
   const uint16_t* zs = zout + grp * 1024;               // z of this group, staged where yn goes
   const uint16_t* ns = Ns + grp * 1024;
   float xv[8][4];
@@ -790,7 +818,7 @@ __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const u
         yv = h2f(f2h(yv + corr));
       }
       const float zv = h2f(zs[li * 64 + pp]);
-      const float x = yv * (zv * (1.0f / (1.0f + expf(-zv))));
+      const float x = yv * (zv * __frcp_rn(1.0f + expf(-zv)));
       xv[n][e] = x;
       ss += x * x;
     }
@@ -812,6 +840,55 @@ __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const u
 }
 
 
+// Stager (one lane of its own warp): the per-layer inputs that do not depend on the token
+// (gated-norm and adapter weights; for CTAs with a scan head the scan statics, the head's
+// packed rows and the conv ring history) as bulk copies on `full`, one layer ahead: layer g
+// (counted over all steps) is issued once the compute warps have released the buffers of
+// layer g - 1 (`free`, arrived after that layer's Resurface).  Issuing ~30 copies takes
+// microseconds while the weight stream occupies the copy engine, so it runs off the compute
+// warps' path.  The state rows and conv ring it reads were written by the previous step and
+// made visible by the grid barriers since; the proxy fence orders them before the copies.
+__device__ void stager(const DecodeParams& P, unsigned char* sm, uint32_t full, uint32_t free_bar, int item) {
+  unsigned char* sc = sm + oScan;
+  uint16_t* Ws = reinterpret_cast<uint16_t*>(sm + oAdw);
+  uint16_t* Gn = reinterpret_cast<uint16_t*>(sm + oGnw);
+  uint16_t* Ag = reinterpret_cast<uint16_t*>(sm + oAdg);
+  int armed = 0;
+  for (int step = 0; step < P.steps; ++step)
+    for (int l = 0; l < P.n_layer; ++l) {
+      const int g = step * P.n_layer + l;
+      if (g > 0 && !mb_wait(free_bar, (uint32_t)(g - 1) & 1u, P.sync)) {
+        set_abort(P, (int)kDevTimeoutProducer);
+        goto drain;
+      }
+      {
+        const DecLayer& L = P.layers[l];
+        asm volatile("fence.proxy.async;" ::: "memory");
+        unsigned bytes = kDInner * 2;
+        if (L.ad_V) bytes += kDModel * 2 + kHeads * 2;
+        if (item >= 0) bytes += scan_stage_bytes(geo_of(L.layout));
+        mb_expect(full, bytes);
+        ++armed;
+        bulk_g2s(Gn, L.gnorm_w, kDInner * 2, full);
+        if (L.ad_V) {
+          bulk_g2s(Ws, L.ad_w, kDModel * 2, full);
+          bulk_g2s(Ag, L.ad_g, kHeads * 2, full);
+          // V is copied into shared memory after the scan: bring it into L2 now (4 KB piece
+          // per CTA, the pieces spread over the grid)
+          if (blockIdx.x < 8) prefetch_l2(reinterpret_cast<const uint8_t*>(L.ad_V) + blockIdx.x * 4096, 4096);
+        }
+        if (item >= 0)
+          for (int k = 0; k < kScanPieces; ++k) {
+            const Piece pc = scan_stage_piece(L, item, sc, k, P.pos + step);
+            bulk_g2s(pc.d, pc.s, (unsigned)pc.bytes, full);
+          }
+      }
+    }
+drain:
+  // every issued copy has landed before the CTA may exit
+  if (armed) mb_drain(full, (uint32_t)(armed - 1) & 1u);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
 decode_step_kernel(const __grid_constant__ DecodeParams P) {
   extern __shared__ __align__(1024) unsigned char sm[];
@@ -823,7 +900,7 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
   R.tag = reinterpret_cast<volatile int*>(sm + oMisc + 320);
   if (tid == 0) {
     for (int i = 0; i < kNst; ++i) R.tag[i] = -1;
-    for (int i = 0; i < 3; ++i)
+    for (int i = 0; i < 4; ++i)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;"
                    :: "r"((uint32_t)__cvta_generic_to_shared(sm + oSBar) + 8 * i) : "memory");
     for (int i = 0; i < kNst; ++i) {
@@ -833,8 +910,14 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  if (warp == kWarps - 1) {
+  const uint32_t sbIn = (uint32_t)__cvta_generic_to_shared(sm + oSBar), sbNw = sbIn + 8, sbV = sbIn + 16,
+                 sbFree = sbIn + 24;
+  if (warp == kWarps - 2) {
     if ((tid & 31) == 0) producer(P, R);
+    return;
+  }
+  if (warp == kWarps - 1) {
+    if ((tid & 31) == 0) stager(P, sm, sbIn, sbFree, blockIdx.x < kHeads ? (int)blockIdx.x : -1);
     return;
   }
   // ------------------------------------------------------------ compute warps
@@ -856,19 +939,18 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
   uint16_t* Gn = reinterpret_cast<uint16_t*>(sm + oGnw);
   uint16_t* Ag = reinterpret_cast<uint16_t*>(sm + oAdg);
   uint16_t* Nw = reinterpret_cast<uint16_t*>(sm + oNw);
-  const uint32_t sbIn = (uint32_t)__cvta_generic_to_shared(sm + oSBar), sbNw = sbIn + 8, sbV = sbIn + 16;
   auto stage_wait = [&](uint32_t bar, uint32_t parity) {
     if (ok && !mb_wait(bar, parity, P.sync)) {
       ok = false;
       set_abort(P, (int)kDevTimeoutProducer);
     }
   };
+  int vuse = 0, nw_phase = 0, in_phase = 0;
+  unsigned arms_nw = 1, arms_v = 0;                    // bulk-copy phases armed by thread 0
   if (tid == 0) {
     mb_expect(sbNw, kDModel * 2);
     bulk_g2s(Nw, P.layers[0].norm_w, kDModel * 2, sbNw);
   }
-  int vuse = 0, nw_phase = 0, in_phase = 0;
-  unsigned arms_in = 0, arms_nw = 1, arms_v = 0;        // bulk-copy phases armed by thread 0
   for (int step = 0; step < P.steps; ++step) {
   // the token of this step: the caller's for the first, then the previous step's pick
   long long id = __ldcg(P.tok);
@@ -883,27 +965,6 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     const DecLayer& L = P.layers[l];
     DTRACE(l, 0);
     DARRIVE(l, 3);
-    // per-layer inputs that do not depend on this token: one thread issues bulk copies that
-    // land while in_proj runs.  The proxy fence orders the generic accesses before it (this
-    // CTA's shared memory, and the state rows / conv ring written by the previous step, made
-    // visible by the grid barriers) ahead of the copies.
-    if (tid == 0) {
-      asm volatile("fence.proxy.async;" ::: "memory");
-      unsigned bytes = kDInner * 2;
-      if (L.ad_V) bytes += kDModel * 2 + kHeads * 2;
-      if (item >= 0) bytes += scan_stage_bytes(geo_of(L.layout));
-      mb_expect(sbIn, bytes);
-      ++arms_in;
-      bulk_g2s(Gn, L.gnorm_w, kDInner * 2, sbIn);
-      if (L.ad_V) {
-        bulk_g2s(Ws, L.ad_w, kDModel * 2, sbIn);
-        bulk_g2s(Ag, L.ad_g, kHeads * 2, sbIn);
-      }
-      if (item >= 0) scan_stage(P, L, item, sc, sbIn, pos);
-      // V is copied into shared memory only after the scan: bring it into L2 now (4 KB piece
-      // per CTA, the pieces spread over the grid)
-      if (L.ad_V && cta < 8) prefetch_l2(reinterpret_cast<const uint8_t*>(L.ad_V) + cta * 4096, 4096);
-    }
     // this layer's norm weight was staged one layer ahead (layer 0: at the start)
     stage_wait(sbNw, (uint32_t)nw_phase);
     nw_phase ^= 1;
@@ -924,13 +985,21 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     ctr += (rin.t1 - rin.t0) * (kDModel / kKc);
     DTRACE(l, 2);
     DARRIVE(l, 0);
-    if (!grid_sync(P, flag)) ok = false;
+    {
+      const unsigned long long tk = grid_arrive(P);
+      stage_wait(sbIn, (uint32_t)in_phase);              // this layer's staged inputs
+      in_phase ^= 1;
+      if (L.ad_V) {                                      // adapter gate partials of this layer's input
+        const float gp = gate_partial(hn, Ws, warp, tid & 31);
+        if ((tid & 31) == 0) misc[24 + warp] = gp;
+      }
+      if (!grid_wait(P, tk, flag)) ok = false;
+    }
     DTRACE(l, 3);
     // z columns for the gated norm, staged where yn will be written
     for (int i = tid; i < kDInner / 8; i += kCompute) cp_async16(yn + i * 8, P.zx + i * 8);
     asm volatile("cp.async.commit_group;\n" ::: "memory");
     if (item >= 0) {
-      stage_wait(sbIn, (uint32_t)in_phase);
       DTRACE(l, 9);
       scan_step(P, L, item, sc, S2, l, pos);
     }
@@ -951,16 +1020,16 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
         cp_async16(Ys + r * kYPitch + c, P.y + r * 64 + c);
       }
       cp_async_wait_all();
-      stage_wait(sbIn, (uint32_t)in_phase);
-      in_phase ^= 1;
       if (L.ad_V) {
         stage_wait(sbV, (uint32_t)(vuse & 1));
         ++vuse;
       }
       bar_sync(1, kCompute);
-      DTRACE(l, 9);
-      resurface_norm(P, L, hn, Ys, Vs, Ws, Ag, Gn, yn, l);
+      DTRACE(l, 12);
+      resurface_norm(P, L, misc + 24, Ys, Vs, Ag, Gn, yn, l);
       bar_sync(1, kCompute);
+      // the staged layer inputs are no longer read: the stager may bring the next layer's
+      if (tid == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(sbFree) : "memory");
     }
     DTRACE(l, 6);
     DWARP(l, 2);
@@ -1030,7 +1099,6 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
   // after an abort some staged copies were never waited for: let them land before exiting
   cp_async_wait_all();
   if (tid == 0) {
-    if (arms_in) mb_drain(sbIn, (arms_in - 1) & 1u);
     if (arms_nw) mb_drain(sbNw, (arms_nw - 1) & 1u);
     if (arms_v) mb_drain(sbV, (arms_v - 1) & 1u);
   }

@@ -109,6 +109,21 @@ __global__ void conv_prefill_kernel(const uint16_t* __restrict__ raw, long long 
   }
 }
 
+// Adapter gate partial over channels [512 w, 512 w + 512): lane stride 8, warp sum.
+__device__ __forceinline__ float gate_span(const uint16_t* Us, const uint16_t* Ws, int w, int lane) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = w * 512 + lane * 8; i < (w + 1) * 512; i += 256) {
+    const uint4 uv = *reinterpret_cast<const uint4*>(Us + i);
+    const uint4 wv = *reinterpret_cast<const uint4*>(Ws + i);
+    const uint16_t* up = reinterpret_cast<const uint16_t*>(&uv);
+    const uint16_t* wp = reinterpret_cast<const uint16_t*>(&wv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s = fmaf(h2f(up[k]), h2f(wp[k]), s);
+  }
+  return warp_sum(s);
+}
+
 // A CTA of `gpb` warps (8 for long sequences, 1 for decode batches) covers gated-norm
 // groups blockIdx.x*gpb .. +gpb-1 (warp w owns heads 16g..16g+15 of its group g) and
 // processes tokens t = blockIdx.y, += gridDim.y.  The 128x128 head mix
@@ -118,7 +133,6 @@ __global__ void conv_prefill_kernel(const uint16_t* __restrict__ raw, long long 
 // group entirely in registers.
 constexpr int kVPitch = 136;   // fp16 elements per staged V row (128 + 8 pad, 272 B)
 constexpr int kYPitch = 72;    // fp16 elements per staged y row (64 + 8 pad, 144 B)
-
 
 template <int GPB>
 __global__ void __launch_bounds__(32 * GPB)
@@ -160,28 +174,22 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
     __syncthreads();
     float gate = 0.f;
     if (has_ad) {
-      // gate logit = fp16(fp16(u . w) + b): deterministic GPB-way split, then the same sum in every warp
-      constexpr int span = 4096 / GPB;
+      // gate logit = fp16(fp16(u . w) + b): eight 512-channel partials (lane stride 8, warp
+      // sum each), added in order; with GPB = 8 each warp computes one, with GPB = 1 one warp
+      // computes all eight
       float s = 0.f;
-#pragma unroll 4
-      for (int i = warp * span + lane * 8; i < (warp + 1) * span; i += 256) {
-        const uint4 uv = *reinterpret_cast<const uint4*>(Us + i);
-        const uint4 wv = *reinterpret_cast<const uint4*>(Ws + i);
-        const uint16_t* up = reinterpret_cast<const uint16_t*>(&uv);
-        const uint16_t* wp = reinterpret_cast<const uint16_t*>(&wv);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) s = fmaf(h2f(up[k]), h2f(wp[k]), s);
-      }
-      s = warp_sum(s);
       if (GPB > 1) {
-        if (lane == 0) spart[warp] = s;
+        const float p = gate_span(Us, Ws, warp, lane);
+        if (lane == 0) spart[warp] = p;
         __syncthreads();
-        s = 0.f;
 #pragma unroll
         for (int w = 0; w < GPB; ++w) s += spart[w];
+      } else {
+#pragma unroll 1
+        for (int w = 0; w < 8; ++w) s += gate_span(Us, Ws, w, lane);
       }
       const float lg = h2f(f2h(h2f(f2h(s)) + h2f(ad.b[0])));
-      gate = h2f(f2h(ad.hard ? (lg > 0.f ? 1.f : 0.f) : 1.0f / (1.0f + expf(-lg))));
+      gate = h2f(f2h(ad.hard ? (lg > 0.f ? 1.f : 0.f) : __frcp_rn(1.0f + expf(-lg))));
     }
     float acc[8][4];
 #pragma unroll
@@ -227,7 +235,7 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
           yv = h2f(f2h(yv + corr));
         }
         const float zz = h2f(zs[li * 64 + pp]);
-        const float x = yv * (zz * (1.0f / (1.0f + expf(-zz))));
+        const float x = yv * (zz * __frcp_rn(1.0f + expf(-zz)));
         xv[n][e] = x;
         ss += x * x;
       }
