@@ -472,14 +472,15 @@ int decode_setup(sq_model* m) {
   if (!m->d_dlayers) {
     if (cudaMalloc(&m->d_dlayers, sizeof(DecLayer) * L) != cudaSuccess ||
         cudaMalloc(&m->d_drows, sizeof(DecLayerRows) * L) != cudaSuccess ||
-        cudaMalloc(&m->d_dmaps, sizeof(CUtensorMap) * (2 * L + 1) * 2) != cudaSuccess ||
+        cudaMalloc(&m->d_dmaps, sizeof(CUtensorMap) * ((2 * L + 1) * 2 + 2 * L)) != cudaSuccess ||
         cudaMalloc(&m->d_dbuf, kDecBytes) != cudaSuccess)
       return fail(SQ_ENOMEM, "decode: cudaMalloc failed");
     if (cudaMemset(m->d_dbuf, 0, kDecBytes) != cudaSuccess) return cuda_fail("decode: cudaMemset");
   }
   std::vector<DecLayer> dl(L);
   std::vector<DecLayerRows> rows(L);
-  std::vector<CUtensorMap> maps((2 * L + 1) * 2);
+  std::vector<CUtensorMap> maps((2 * L + 1) * 2 + 2 * L);
+  CUtensorMap* aux = maps.data() + (2 * L + 1) * 2;
   for (int l = 0; l < L; ++l) {
     const sq_layer_desc& d = m->layers[l];
     const sq_model::St& st = m->states[l];
@@ -505,6 +506,10 @@ int decode_setup(sq_model* m) {
     rows[l] = DecLayerRows{d.in_proj.codes, d.in_proj.block_scales, d.out_proj.codes, d.out_proj.block_scales};
     maps[(2 * l) * 2 + 0] = m->in_maps[l].codes; maps[(2 * l) * 2 + 1] = m->in_maps[l].scales;
     maps[(2 * l + 1) * 2 + 0] = m->out_maps[l].codes; maps[(2 * l + 1) * 2 + 1] = m->out_maps[l].scales;
+    std::memset(aux + 2 * l, 0, 2 * sizeof(CUtensorMap));
+    if ((ad.V && !encode_f16_sw128_map(aux + 2 * l, ad.V, 128, 128, 128)) ||
+        !encode_f16_sw128_map(aux + 2 * l + 1, d.gated_norm_weight, 128, 64, 128))
+      return fail(SQ_ECUDA, "decode: tensor map encoding failed");
   }
   if (!m->head.codes || !m->head_maps.valid || m->head_maps.kc != 1024) return fail(SQ_ESTATE, "decode: lm_head not set");
   if (!aligned(m->norm_f, 16) || !aligned(m->embed.codes, 4)) return fail(SQ_EINVAL, "decode: norm_f must be 16-byte aligned");
@@ -533,6 +538,7 @@ int sq_model_decode(sq_model* m, int64_t* tokens, int pos, int steps, int64_t* o
   }
   DecodeParams P{};
   P.layers = m->d_dlayers; P.maps = m->d_dmaps; P.rows = m->d_drows;
+  P.aux_maps = m->d_dmaps + (2 * m->cfg.n_layer + 1) * 2;
   P.head_codes = m->head.codes; P.head_scales = m->head.block_scales;
   P.emb_codes = m->embed.codes; P.emb_scales = m->embed.block_scales; P.emb_g = m->embed.global_scale;
   P.head_g = m->head.global_scale; P.norm_f = m->norm_f;

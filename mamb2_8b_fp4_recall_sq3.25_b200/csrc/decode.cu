@@ -34,31 +34,36 @@ constexpr int kCodeBytes = kRows * kKc / 2, kScaleBytes = kRows * kKc / 16, kSta
 constexpr int kDModel = 4096, kDInner = 8192, kZx = 18560, kHeads = 128, kGroups = 8;
 constexpr unsigned long long kWaitNs = 500000000ull;   // 0.5 s per wait
 
-// shared-memory plan (bytes).  Per-layer tensors are staged with cp.async well before use
-// (adapter, gated-norm weights, scan tables at the start of the layer; the next layer's
-// norm weight one layer ahead; z right after the in_proj barrier), so no phase waits on
-// more than one dependent memory round trip.
-constexpr int oRing = 0;
-constexpr int oBar = oRing + kNst * kStageBytes;       // full[kNst], empty[kNst]
-constexpr int oSBar = oBar + 2 * kNst * 8;             // staging mbarriers: layer inputs, norm weight, V, inputs free
-constexpr int oRed = oSBar + 32;                       // GEMV cross-warp sums [2][4][32][4] f32
-constexpr int oHn = oRed + 2 * 4 * 32 * 4 * 4;         // normed layer input [4096] fp16
-constexpr int oYn = oHn + kDModel * 2;                 // z staging, then the gated-norm output [8192] fp16
-constexpr int oScan = oYn + kDInner * 2;               // scan item staging / y staging
+// shared-memory plan (bytes).  Per-layer tensors are staged well before use (the stager
+// brings adapter, gated-norm weights and scan tables one layer ahead; the next layer's norm
+// weight is copied one layer ahead; z right after the in_proj barrier; V after the scan).
+// V and the gated-norm weights arrive as SWIZZLE_128B TMA tiles and z / the gated-norm
+// output use the same layout (see swz), so the Resurface epilogue and the head mix read
+// shared memory without bank conflicts; both tiles start on 1024-byte boundaries.
 constexpr int kScanBytes = 20608;
-constexpr int kVPitch = 128;                           // adapter V rows (one bulk copy, unpadded)
-constexpr int oV = oScan + kScanBytes;                 // scan: row state [np][64] float2; then adapter V [128][128]
-constexpr int oAdw = oV + 128 * kVPitch * 2;           // adapter gate weights [4096] fp16
-constexpr int oGnw = oAdw + kDModel * 2;               // gated RMSNorm weights [8192] fp16
-constexpr int oAdg = oGnw + kDInner * 2;               // adapter g [128] fp16
-constexpr int oNw = oAdg + 256;                        // Block norm weights [2][4096] fp16 (layer parity)
-constexpr int oMisc = oNw + 2 * kDModel * 2;           // small scratch (reductions, flags)
+constexpr int oRing = 0;                               // kNst x 9216 (1024-byte multiples)
+constexpr int oV = oRing + kNst * kStageBytes;         // scan: row state [np][64] float2; then adapter V, 2 x [128][64] swizzled
+constexpr int oGnw = oV + 128 * 128 * 2;               // gated RMSNorm weights [128][64] swizzled
+constexpr int oYn = oGnw + kDInner * 2;                // z staging, then the gated-norm output [128][64] swizzled
+constexpr int oHn = oYn + kDInner * 2;                 // normed layer input [4096] fp16
+constexpr int oScan = oHn + kDModel * 2;               // scan item staging / y staging
+constexpr int oAdw = oScan + kScanBytes;               // adapter gate weights [4096] fp16
+constexpr int oNw = oAdw + kDModel * 2;                // Block norm weights [2][4096] fp16 (layer parity)
+constexpr int oAdg = oNw + 2 * kDModel * 2;            // adapter g [128] fp16
+constexpr int oRed = oAdg + 256;                       // GEMV cross-warp sums [2][4][32][4] f32
+constexpr int oBar = oRed + 2 * 4 * 32 * 4 * 4;        // full[kNst], empty[kNst]
+constexpr int oSBar = oBar + 2 * kNst * 8;             // staging mbarriers: layer inputs, norm weight, V, inputs free
+constexpr int oMisc = oSBar + 32;                      // small scratch (reductions, flags)
 constexpr int kSmem = oMisc + 512;
 // scan region
 constexpr int sPred = 0, sBasis = 8448, sPerm = 8768, sRows = 8896, sWx = 12224, sBx = 12736, sWbc = 12864,
               sBbc = 14912, sHist = 15424, sP4o = 17344, sV2o = 18368, sXo = 18880, sDotso = 19136, sDDo = 19168,
               sLs = 19200, sDv = 19232, sDtb = 19488, sAv = 19744;   // latent scales, D, dt_bias, A
 constexpr int kYPitch = 72;                            // y staging rows (64 + 8 pad) for ldmatrix
+static_assert(oV % 1024 == 0 && oGnw % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+// Element (h, p) of an [rows][64] fp16 tile in the SWIZZLE_128B layout: row h is 128 bytes,
+// its 16-byte chunk c sits at chunk c ^ (h & 7).
+__device__ __forceinline__ int swz(int h, int p) { return (h << 6) + ((((p >> 3) ^ h) & 7) << 3) + (p & 7); }
 
 __device__ __forceinline__ void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(n) : "memory"); }
 __device__ __forceinline__ uint64_t now_ns() { uint64_t t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); return t; }
@@ -108,6 +113,11 @@ __device__ __forceinline__ void tma2d(uint32_t dst, const CUtensorMap* map, uint
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1, {%3, %4}], [%2], %5;"
       :: "r"(dst), "l"(map), "r"(bar), "r"(x), "r"(y), "l"(policy) : "memory");
+}
+__device__ __forceinline__ void tma2d_plain(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      :: "r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(map), "r"(bar), "r"(x), "r"(y) : "memory");
 }
 __device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
@@ -270,71 +280,100 @@ __device__ __forceinline__ bool wait_chunk(const Ring& R, int c, const DecodeSyn
   }
 }
 
+// One chunk (16 rows x 1024 columns in ring stage `cs`) of a tile: warp cw of the group takes
+// 128-column sub-chunks cw and cw + 4, decodes them into mma.sync A fragments (factored
+// global scale) and accumulates even / odd k-steps in acc / acc2.  xoff[s2][qq]: offset of the
+// 8 input values k = sub * 128 + tq * 32 + 8 qq of the chunk (x_offsets).
+__device__ __forceinline__ void chunk_mma(const unsigned char* cs, const uint16_t* Xs, int kc, int cw, int lane,
+                                          const int (&xoff)[2][4], float (&acc)[4], float (&acc2)[4]) {
+  const int gq = lane >> 2, tq = lane & 3;
+  constexpr int code_row = kKc / 2, scale_row = kKc / 16;
+  const unsigned char* ss = cs + kCodeBytes;
+#pragma unroll
+  for (int s2 = 0; s2 < 2; ++s2) {
+    const int sub = cw + 4 * s2;
+    uint4 xr[4];
+#pragma unroll
+    for (int qq = 0; qq < 4; ++qq)
+      xr[qq] = (gq == 0) ? *reinterpret_cast<const uint4*>(Xs + kc * kKc + xoff[s2][qq]) : make_uint4(0, 0, 0, 0);
+    const uint4 ca = *reinterpret_cast<const uint4*>(cs + gq * code_row + sub * 64 + tq * 16);
+    const uint4 cb = *reinterpret_cast<const uint4*>(cs + (gq + 8) * code_row + sub * 64 + tq * 16);
+    const uint16_t sa = *reinterpret_cast<const uint16_t*>(ss + gq * scale_row + sub * 8 + tq * 2);
+    const uint16_t sb = *reinterpret_cast<const uint16_t*>(ss + (gq + 8) * scale_row + sub * 8 + tq * 2);
+    const uint32_t wa[4] = {ca.x, ca.y, ca.z, ca.w};
+    const uint32_t wb[4] = {cb.x, cb.y, cb.z, cb.w};
+    const uint32_t bsa0 = e4m3_splat_f16x2(sa & 0xFF), bsa1 = e4m3_splat_f16x2(sa >> 8);
+    const uint32_t bsb0 = e4m3_splat_f16x2(sb & 0xFF), bsb1 = e4m3_splat_f16x2(sb >> 8);
+#pragma unroll
+    for (int w4 = 0; w4 < 4; ++w4) {
+      uint32_t ma[4], mb[4];
+      e2m1x8_to_f16x2(wa[w4], ma);
+      e2m1x8_to_f16x2(wb[w4], mb);
+      const uint32_t bsA = (w4 < 2) ? bsa0 : bsa1, bsB = (w4 < 2) ? bsb0 : bsb1;
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int j = w4 * 2 + jj;
+        uint32_t a[4];
+        a[0] = hmul2_u32(ma[2 * jj], bsA);
+        a[1] = hmul2_u32(mb[2 * jj], bsB);
+        a[2] = hmul2_u32(ma[2 * jj + 1], bsA);
+        a[3] = hmul2_u32(mb[2 * jj + 1], bsB);
+        const uint4 xq = xr[j >> 1];
+        const uint32_t b0 = (j & 1) ? xq.z : xq.x, b1 = (j & 1) ? xq.w : xq.y;
+        mma16816((j & 1) ? acc2 : acc, a, b0, b1);
+      }
+    }
+  }
+}
+
+// Offsets (within a 1024-column chunk) of the input values a lane reads: linear, or for an
+// input stored as swizzled rows of 64 (swz) the same elements there.  Column k = sub * 128 +
+// tq * 32 + 8 qq lies in row 2 sub + (tq >> 1) + 16 kc, chunk (tq & 1) * 4 + qq; the row's low
+// three bits do not depend on kc, so the offsets are constant over a phase.
+template <bool XSWZ>
+__device__ __forceinline__ void x_offsets(int cw, int tq, int (&xoff)[2][4]) {
+#pragma unroll
+  for (int s2 = 0; s2 < 2; ++s2)
+#pragma unroll
+    for (int qq = 0; qq < 4; ++qq) {
+      const int sub = cw + 4 * s2, h = 2 * sub + (tq >> 1), c = (tq & 1) * 4 + qq;
+      xoff[s2][qq] = XSWZ ? h * 64 + (((c ^ h) & 7) << 3) : sub * 128 + tq * 32 + 8 * qq;
+    }
+}
+
 // One projection phase: this CTA's tiles [t0, t1) of a 16-row-tiled matrix, chunks of 1024
-// columns at ring counters ctr + (tile - t0) * cpt + kc.  Tiles alternate between the two
-// 4-warp consumer groups; per tile the fp4_gemv_stream_kernel arithmetic (factored global
-// scale): warp cw of the group takes 128-column sub-chunks cw and cw + 4 of every chunk,
-// even / odd k-steps accumulate separately, the four warps' sums are added in order.
+// columns at ring counters ctr + (tile - t0) * cpt + kc (cpt even).  Tiles alternate between
+// the two 4-warp consumer groups; per tile the fp4_gemv_stream_kernel arithmetic (factored
+// global scale), chunks taken two per wait, the four warps' sums added in order.
+template <bool XSWZ>
 __device__ void gemv_phase(const DecodeParams& P, const Ring& R, const unsigned char* sm, int ctr, int t0, int t1,
                            int cpt, const uint16_t* Xs, const float* gptr, uint16_t* Y, float* red, bool argmax,
                            float& best, int& bidx, bool& ok) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = warp >> 2, cw = warp & 3;
   const int gq = lane >> 2, tq = lane & 3;
-  constexpr int code_row = kKc / 2, scale_row = kKc / 16;
   const float gsc = *gptr;
+  int xoff[2][4];
+  x_offsets<XSWZ>(cw, tq, xoff);
   for (int i = q; i < t1 - t0; i += 2) {
     const int tile = t0 + i;
     float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int kc = 0; kc < cpt; ++kc) {
+    for (int kc = 0; kc < cpt; kc += 2) {
       const int c = ctr + i * cpt + kc;
-      const int stage = c % kNst;
-      if (ok && !wait_chunk(R, c, P.sync)) {
+      const int st0 = c % kNst, st1 = (c + 1) % kNst;
+      if (ok && !(wait_chunk(R, c, P.sync) && wait_chunk(R, c + 1, P.sync))) {
         ok = false;
         set_abort(P, (int)kDevTimeoutMma);
       }
       if (ok) {
-        const unsigned char* cs = sm + oRing + stage * kStageBytes;
-        const unsigned char* ss = cs + kCodeBytes;
-#pragma unroll
-        for (int s2 = 0; s2 < 2; ++s2) {
-          const int sub = cw + 4 * s2;
-          const int kb0 = kc * kKc + sub * 128 + tq * 32;
-          uint4 xr[4];
-#pragma unroll
-          for (int qq = 0; qq < 4; ++qq)
-            xr[qq] = (gq == 0) ? *reinterpret_cast<const uint4*>(Xs + kb0 + 8 * qq) : make_uint4(0, 0, 0, 0);
-          const uint4 ca = *reinterpret_cast<const uint4*>(cs + gq * code_row + sub * 64 + tq * 16);
-          const uint4 cb = *reinterpret_cast<const uint4*>(cs + (gq + 8) * code_row + sub * 64 + tq * 16);
-          const uint16_t sa = *reinterpret_cast<const uint16_t*>(ss + gq * scale_row + sub * 8 + tq * 2);
-          const uint16_t sb = *reinterpret_cast<const uint16_t*>(ss + (gq + 8) * scale_row + sub * 8 + tq * 2);
-          const uint32_t wa[4] = {ca.x, ca.y, ca.z, ca.w};
-          const uint32_t wb[4] = {cb.x, cb.y, cb.z, cb.w};
-          const uint32_t bsa0 = e4m3_splat_f16x2(sa & 0xFF), bsa1 = e4m3_splat_f16x2(sa >> 8);
-          const uint32_t bsb0 = e4m3_splat_f16x2(sb & 0xFF), bsb1 = e4m3_splat_f16x2(sb >> 8);
-#pragma unroll
-          for (int w4 = 0; w4 < 4; ++w4) {
-            uint32_t ma[4], mb[4];
-            e2m1x8_to_f16x2(wa[w4], ma);
-            e2m1x8_to_f16x2(wb[w4], mb);
-            const uint32_t bsA = (w4 < 2) ? bsa0 : bsa1, bsB = (w4 < 2) ? bsb0 : bsb1;
-#pragma unroll
-            for (int jj = 0; jj < 2; ++jj) {
-              const int j = w4 * 2 + jj;
-              uint32_t a[4];
-              a[0] = hmul2_u32(ma[2 * jj], bsA);
-              a[1] = hmul2_u32(mb[2 * jj], bsB);
-              a[2] = hmul2_u32(ma[2 * jj + 1], bsA);
-              a[3] = hmul2_u32(mb[2 * jj + 1], bsB);
-              const uint4 xq = xr[j >> 1];
-              const uint32_t b0 = (j & 1) ? xq.z : xq.x, b1 = (j & 1) ? xq.w : xq.y;
-              mma16816((j & 1) ? acc2 : acc, a, b0, b1);
-            }
-          }
-        }
+        chunk_mma(sm + oRing + st0 * kStageBytes, Xs, kc, cw, lane, xoff, acc, acc2);
+        chunk_mma(sm + oRing + st1 * kStageBytes, Xs, kc + 1, cw, lane, xoff, acc, acc2);
       }
       __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(R.empty + 8 * stage) : "memory");
+      if (lane == 0) {
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(R.empty + 8 * st0) : "memory");
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(R.empty + 8 * st1) : "memory");
+      }
     }
     float* rq = red + q * (4 * 32 * 4);
 #pragma unroll
@@ -785,7 +824,8 @@ __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const f
 #pragma unroll
     for (int k0 = 0; k0 < 128; k0 += 16) {
       uint32_t a[4];
-      ldsm_x4(a, Vs + (i0 + rr + (mi & 1) * 8) * kVPitch + k0 + (mi >> 1) * 8);
+      const int vr = i0 + rr + (mi & 1) * 8, vc = k0 + (mi >> 1) * 8;   // V row, first column of the 8
+      ldsm_x4(a, Vs + (vc >> 6) * 128 * 64 + swz(vr, vc & 63));
 #pragma unroll
       for (int n2 = 0; n2 < 4; ++n2) {
         uint32_t bfr[4];
@@ -796,45 +836,55 @@ __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const f
     }
   }
   DTRACE(layer, 14);
+  // The epilogue runs once per layer: it is written as short loops (the mix results and the
+  // x values go through this warp's 16 V rows, 4 KB, no longer read) so that its code stays
+  // small in the instruction caches.
+  float* scr0 = reinterpret_cast<float*>(const_cast<uint16_t*>(Vs) + grp * 16 * 64);      // 512 floats
+  float* scr1 = reinterpret_cast<float*>(const_cast<uint16_t*>(Vs) + 128 * 64 + grp * 16 * 64);
+  auto scr_at = [&](int n, int e) { return (n < 4 ? scr0 + (n * 4 + e) * 32 : scr1 + ((n - 4) * 4 + e) * 32) + lane; };
+  __syncwarp();
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) *scr_at(n, e) = acc[n][e];
   const uint16_t* zs = zout + grp * 1024;               // z of this group, staged where yn goes
   const uint16_t* ns = Ns + grp * 1024;
-  float xv[8][4];
   float ss = 0.f;
   const int ia = grp * 16 + gq, ib = ia + 8;
   const int la = gq, lb = gq + 8;
   const float ga = has_ad ? h2f(f2h(gate * h2f(Gs[ia]))) : 0.f;
   const float gb = has_ad ? h2f(f2h(gate * h2f(Gs[ib]))) : 0.f;
-#pragma unroll
+  const __half2 ga2 = __float2half2_rn(ga), gb2 = __float2half2_rn(gb);
+#pragma unroll 1
   for (int n = 0; n < 8; ++n) {
     const int p0 = n * 8 + 2 * tq;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int i = (e < 2) ? ia : ib, li = (e < 2) ? la : lb;
-      const int pp = p0 + (e & 1);
-      float yv = h2f(Ys[i * kYPitch + pp]);
-      if (has_ad) {
-        const float mix = h2f(f2h(acc[n][e]));
-        const float corr = h2f(f2h(((e < 2) ? ga : gb) * mix));
-        yv = h2f(f2h(yv + corr));
-      }
-      const float zv = h2f(zs[li * 64 + pp]);
-      const float x = yv * (zv * __frcp_rn(1.0f + expf(-zv)));
-      xv[n][e] = x;
-      ss += x * x;
+    for (int half = 0; half < 2; ++half) {
+      const int i = half ? ib : ia, li = half ? lb : la;
+      float* sp = scr_at(n, 2 * half);
+      const float2 x2 = resurface_pair(*reinterpret_cast<const uint32_t*>(Ys + i * kYPitch + p0),
+                                       *reinterpret_cast<const uint32_t*>(zs + swz(li, p0)), sp[0], sp[32],
+                                       half ? gb2 : ga2, has_ad);
+      sp[0] = x2.x;
+      sp[32] = x2.y;
+      ss += x2.x * x2.x;
+      ss += x2.y * x2.y;
     }
   }
   ss = warp_sum(ss);
   const float rstd = 1.0f / sqrtf(ss / 1024.0f + P.eps);
-#pragma unroll
+#pragma unroll 1
   for (int n = 0; n < 8; ++n) {
     const int p0 = n * 8 + 2 * tq;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int li = half ? lb : la;
-      const float o0 = (xv[n][2 * half] * rstd) * h2f(ns[li * 64 + p0]);
-      const float o1 = (xv[n][2 * half + 1] * rstd) * h2f(ns[li * 64 + p0 + 1]);
+      const float* sp = scr_at(n, 2 * half);
+      const float2 w2 = __half22float2(*reinterpret_cast<const __half2*>(ns + swz(li, p0)));
+      const float o0 = (sp[0] * rstd) * w2.x;
+      const float o1 = (sp[32] * rstd) * w2.y;
       __half2 hv = __floats2half2_rn(o0, o1);
-      *reinterpret_cast<__half2*>(zout + grp * 1024 + li * 64 + p0) = hv;   // each lane's own z slots
+      *reinterpret_cast<__half2*>(zout + grp * 1024 + swz(li, p0)) = hv;   // each lane's own z slots
     }
   }
 }
@@ -869,7 +919,7 @@ __device__ void stager(const DecodeParams& P, unsigned char* sm, uint32_t full, 
         if (item >= 0) bytes += scan_stage_bytes(geo_of(L.layout));
         mb_expect(full, bytes);
         ++armed;
-        bulk_g2s(Gn, L.gnorm_w, kDInner * 2, full);
+        tma2d_plain(Gn, P.aux_maps + 2 * l + 1, full, 0, 0);          // [128][64] swizzled
         if (L.ad_V) {
           bulk_g2s(Ws, L.ad_w, kDModel * 2, full);
           bulk_g2s(Ag, L.ad_g, kHeads * 2, full);
@@ -893,6 +943,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 decode_step_kernel(const __grid_constant__ DecodeParams P) {
   extern __shared__ __align__(1024) unsigned char sm[];
   const int tid = threadIdx.x, warp = tid >> 5;
+  if ((__cvta_generic_to_shared(sm) & 1023u) != 0) {    // the swizzled tiles assume a 1024-byte aligned base
+    if (tid == 0) atomicOr(P.err, (int)kDevBadArgs);
+    return;
+  }
   Ring R;
   R.base = (uint32_t)__cvta_generic_to_shared(sm + oRing);
   R.full = (uint32_t)__cvta_generic_to_shared(sm + oBar);
@@ -980,7 +1034,7 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     }
     DTRACE(l, 1);
     DWARP(l, 0);
-    gemv_phase(P, R, sm, ctr, rin.t0, rin.t1, kDModel / kKc, hn, L.in_g, P.zx, red, false, best, bidx, ok);
+    gemv_phase<false>(P, R, sm, ctr, rin.t0, rin.t1, kDModel / kKc, hn, L.in_g, P.zx, red, false, best, bidx, ok);
     DWARP(l, 1);
     ctr += (rin.t1 - rin.t0) * (kDModel / kKc);
     DTRACE(l, 2);
@@ -996,8 +1050,8 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
       if (!grid_wait(P, tk, flag)) ok = false;
     }
     DTRACE(l, 3);
-    // z columns for the gated norm, staged where yn will be written
-    for (int i = tid; i < kDInner / 8; i += kCompute) cp_async16(yn + i * 8, P.zx + i * 8);
+    // z columns for the gated norm (swizzled rows of 64), staged where yn will be written
+    for (int i = tid; i < kDInner / 8; i += kCompute) cp_async16(yn + swz(i >> 3, (i & 7) * 8), P.zx + i * 8);
     asm volatile("cp.async.commit_group;\n" ::: "memory");
     if (item >= 0) {
       DTRACE(l, 9);
@@ -1013,7 +1067,8 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
         asm volatile("fence.proxy.async;" ::: "memory");
         mb_expect(sbV, 128 * 128 * 2);
         ++arms_v;
-        bulk_g2s(Vs, L.ad_V, 128 * 128 * 2, sbV);
+        tma2d_plain(Vs, P.aux_maps + 2 * l, sbV, 0, 0);
+        tma2d_plain(Vs + 128 * 64, P.aux_maps + 2 * l, sbV, 64, 0);
       }
       for (int i = tid; i < 128 * 8; i += kCompute) {
         const int r = i >> 3, c = (i & 7) * 8;
@@ -1033,7 +1088,7 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     }
     DTRACE(l, 6);
     DWARP(l, 2);
-    gemv_phase(P, R, sm, ctr, rout.t0, rout.t1, kDInner / kKc, yn, L.out_g, P.h, red, false, best, bidx, ok);
+    gemv_phase<true>(P, R, sm, ctr, rout.t0, rout.t1, kDInner / kKc, yn, L.out_g, P.h, red, false, best, bidx, ok);
     DWARP(l, 3);
     ctr += (rout.t1 - rout.t0) * (kDInner / kKc);
     DTRACE(l, 7);
@@ -1052,7 +1107,7 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     ++arms_nw;
     bulk_g2s(Nw, P.layers[0].norm_w, kDModel * 2, sbNw);
   }
-  gemv_phase(P, R, sm, ctr, rhead.t0, rhead.t1, kDModel / kKc, hn, P.head_g, P.logits, red, true, best, bidx, ok);
+  gemv_phase<false>(P, R, sm, ctr, rhead.t0, rhead.t1, kDModel / kKc, hn, P.head_g, P.logits, red, true, best, bidx, ok);
   ctr += (rhead.t1 - rhead.t0) * (kDModel / kKc);
   // CTA candidate: warps 0 and 4 hold the per-lane picks of their group
   if ((warp & 3) == 0) {

@@ -59,6 +59,25 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
 }
 
+// z * sigmoid(z) in fp32 with the hardware exponential and reciprocal approximations
+// (ex2.approx and rcp.approx, a few ulp; torch's silu on the reference side differs from a
+// correctly rounded result by a similar amount).  1 + e^-z >= 1, so the reciprocal never
+// sees a denormal; e^-z = inf gives 0.
+__device__ __forceinline__ float silu_fast(float z) { return z * __fdividef(1.0f, 1.0f + __expf(-z)); }
+
+// Resurface correction and gated-norm input of two adjacent channels of one head:
+// y' = fp16(y + fp16(g * fp16(mix))) on half2 (each half2 operation rounds its exact result
+// once to fp16, the value the fp32 operation followed by an fp16 rounding gives: products of
+// two fp16 values are exact in fp32, and a sum that fp32 must round has operands more than
+// 2^13 apart, far from an fp16 rounding boundary), then x = y' * silu(z) in fp32.
+__device__ __forceinline__ float2 resurface_pair(uint32_t y2, uint32_t z2, float m0, float m1, __half2 g2, bool has_ad) {
+  __half2 yh = *reinterpret_cast<__half2*>(&y2);
+  if (has_ad) yh = __hadd2(yh, __hmul2(g2, __floats2half2_rn(m0, m1)));
+  const float2 yf = __half22float2(yh);
+  const float2 zf = __half22float2(*reinterpret_cast<__half2*>(&z2));
+  return make_float2(yf.x * silu_fast(zf.x), yf.y * silu_fast(zf.y));
+}
+
 // first-occurrence merge of (value, index) argmax candidates
 __device__ __forceinline__ void argmax_merge(float& bv, int& bi, float v2, int i2) {
   if (v2 > bv || (v2 == bv && i2 < bi)) { bv = v2; bi = i2; }

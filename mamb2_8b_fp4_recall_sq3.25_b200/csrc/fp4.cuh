@@ -31,6 +31,7 @@ struct Fp4Maps {
 bool make_fp4_maps(const Fp4Weight& W, Fp4Maps* maps);
 bool encode_u32_map(CUtensorMap* m, const void* base, long long rows, long long cols_u32, long long row_bytes,
                     int box_cols, int box_rows);
+bool encode_f16_sw128_map(CUtensorMap* m, const void* base, long long rows, long long cols, int box_rows);
 // Same product through the TMA-pipelined kernel (cols % 256 == 0, 16-byte aligned rows);
 // `maps` may be null (built on the fly); `err` receives an error bit if a bounded wait expires.
 // exact = false applies the fp32 global scale once per output instead of per weight.

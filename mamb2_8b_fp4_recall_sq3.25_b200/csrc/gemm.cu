@@ -335,6 +335,21 @@ bool encode_u32_map(CUtensorMap* m, const void* base, long long rows, long long 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D tiled tensor map over a row-major fp16 matrix [rows][cols] whose box rows are 64
+// elements (128 bytes) wide, loaded with SWIZZLE_128B: 16-byte chunk c of box row r lands at
+// chunk c ^ (r & 7) of that row in shared memory (destination 1024-byte aligned).
+bool encode_f16_sw128_map(CUtensorMap* m, const void* base, long long rows, long long cols, int box_rows) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+  cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int gemm_num_ntiles(int N) { return (N + BN - 1) / BN; }
 
 static bool g_gemm_attr = false;

@@ -221,23 +221,20 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
     const int la = gq, lb = gq + 8;                      // heads within the group
     const float ga = has_ad ? h2f(f2h(gate * h2f(ad.g[ia]))) : 0.f;
     const float gb = has_ad ? h2f(f2h(gate * h2f(ad.g[ib]))) : 0.f;
+    const __half2 ga2 = __float2half2_rn(ga), gb2 = __float2half2_rn(gb);
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
       const int p0 = n * 8 + 2 * tq;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int i = (e < 2) ? ia : ib, li = (e < 2) ? la : lb;
-        const int pp = p0 + (e & 1);
-        float yv = h2f(Ys[i * kYPitch + pp]);
-        if (has_ad) {
-          const float mix = h2f(f2h(acc[n][e]));
-          const float corr = h2f(f2h(((e < 2) ? ga : gb) * mix));
-          yv = h2f(f2h(yv + corr));
-        }
-        const float zz = h2f(zs[li * 64 + pp]);
-        const float x = yv * (zz * __frcp_rn(1.0f + expf(-zz)));
-        xv[n][e] = x;
-        ss += x * x;
+      for (int half = 0; half < 2; ++half) {
+        const int i = half ? ib : ia, li = half ? lb : la;
+        const float2 x2 = resurface_pair(*reinterpret_cast<const uint32_t*>(Ys + i * kYPitch + p0),
+                                         *reinterpret_cast<const uint32_t*>(zs + li * 64 + p0), acc[n][2 * half],
+                                         acc[n][2 * half + 1], half ? gb2 : ga2, has_ad);
+        xv[n][2 * half] = x2.x;
+        xv[n][2 * half + 1] = x2.y;
+        ss += x2.x * x2.x;
+        ss += x2.y * x2.y;
       }
     }
     ss = warp_sum(ss);
