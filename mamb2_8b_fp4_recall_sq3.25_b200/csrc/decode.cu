@@ -149,27 +149,29 @@ __device__ unsigned long long g_decode_warp[4][16];
 #define DWARP(layer, which) do { } while (0)
 #endif
 
-// Grid barrier for the compute warps of every CTA (the producer warp never joins).
-// One release add on a 64-bit arrival counter (zeroed before the first step); barrier k
-// of the call completes when the counter reaches (k + 1) * gridDim.x.
+// Grid barrier for the compute warps of every CTA (the producer and stager warps never
+// join).  One release add on a 64-bit arrival counter (zeroed before the launch); every CTA
+// passes the same sequence of barriers, so barrier k of the launch completes when the counter
+// reaches (k + 1) * gridDim.x and the add needs no reply.
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-// Split-phase form: grid_arrive adds this CTA's arrival and returns the count to wait for
-// (thread 0 only; 0 after an abort); work that does not depend on the other CTAs can run
-// before grid_wait.
-__device__ unsigned long long grid_arrive(const DecodeParams& P) {
+__device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+// Split-phase form: grid_arrive adds this CTA's arrival (after a CTA barrier, so the release
+// covers every thread's earlier writes) and returns the count to wait for (0 after an abort);
+// work that does not depend on the other CTAs can run before grid_wait.  `nbar` counts the
+// barriers of the launch (the same in every thread).
+__device__ unsigned long long grid_arrive(const DecodeParams& P, unsigned& nbar) {
   bar_sync(1, kCompute);
-  unsigned long long target = 0;
+  const unsigned long long target = (unsigned long long)(++nbar) * gridDim.x;
   if (threadIdx.x == 0) {
     DecodeSync* s = P.sync;
-    if (!ld_abort(s)) {
-      __threadfence();
-      const unsigned long long old = atomicAdd(&s->count, 1ull);
-      target = (old / gridDim.x + 1) * gridDim.x;
-    }
+    if (ld_abort(s)) return 0;
+    red_release_add(&s->count, 1ull);
   }
   return target;
 }
@@ -180,12 +182,12 @@ __device__ bool grid_wait(const DecodeParams& P, unsigned long long target, int*
     if (ok) {
       const uint64_t t0 = now_ns();
       int spins = 0;
-      while (ld_acquire_u64(&s->count) < target) {
-        if (ld_abort(s)) { ok = 0; break; }
-        if (++spins > 64) {
+      while (ld_acquire_u64(&s->count) < target) {   // one load in flight per poll
+        if ((++spins & 15) == 0) {
+          if (ld_abort(s)) { ok = 0; break; }
           if (now_ns() - t0 > kWaitNs) { set_abort(P, (int)kDevTimeoutEpilogue); ok = 0; break; }
-          __nanosleep(20);
         }
+        if (spins > 64) __nanosleep(20);
       }
     }
     *flag = ok;
@@ -193,7 +195,9 @@ __device__ bool grid_wait(const DecodeParams& P, unsigned long long target, int*
   bar_sync(1, kCompute);
   return *flag != 0;
 }
-__device__ bool grid_sync(const DecodeParams& P, int* flag) { return grid_wait(P, grid_arrive(P), flag); }
+__device__ bool grid_sync(const DecodeParams& P, unsigned& nbar, int* flag) {
+  return grid_wait(P, grid_arrive(P, nbar), flag);
+}
 
 // Block residual + RMSNorm over 4096 channels with 256 threads, the add_rmsnorm_kernel
 // arithmetic: res = fp16(h + res) (or h), out = fp16((res * rstd) * w).  The layer-0 input
@@ -479,9 +483,11 @@ __device__ void producer(const DecodeParams& P, const Ring& R) {
 
 // ---------------------------------------------------------------- scan step of one head
 // The one-token codec step of ssu_sq325_kernel (MODE 2, TC 1) for the 64 rows of head
-// `hh`: conv step on the raw in_proj columns with the ring history, group dots, recurrence,
-// readout, latent and INT8/INT4 requant, pack.  256 threads: B/C conv one channel each,
-// dots one task each, rows on threads 0..63.  One code path for all seven layouts: the
+// `hh`, in three parts: scan_unpack decodes the stored pairs (before the token's inputs
+// exist), scan_step runs the conv step on the raw in_proj columns with the ring history, the
+// group dots, recurrence, readout and the token tail (scales), and publishes y; scan_finish
+// requantises and packs the state (after y is out).  256 threads: B/C conv one channel each,
+// dots one task each, rows on four lanes each.  One code path for all seven layouts: the
 // row's stored pairs live in shared memory (pair-major, [np][64] float2) and runtime loops
 // run the same per-pair operations, in the same order, as recur_row / requant_row, so the
 // step is compact enough to stay in the instruction caches.
@@ -564,7 +570,7 @@ __device__ __forceinline__ Piece scan_stage_piece(const DecLayer& L, int hh, uns
 }
 
 __device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsigned char* sc, float2* S2,
-                          int layer, int pos) {
+                          int layer, int pos, TokenScales& ts, float2& zlat) {
   const Geo G = geo_of(L.layout);
   const int NS = G.ns, NZ = G.nz, F = G.f, W8 = G.w8, W4 = G.w4, NP = G.np, N8 = G.n8;
   const int tid = threadIdx.x, g = hh / (kHeads / kGroups);
@@ -651,39 +657,13 @@ __device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsi
   }
   bar_sync(1, kCompute);
   DTRACE(layer, 11);
-  // -- per-row recurrence, readout, requant, pack: row p = tid / 4 on four adjacent lanes,
-  //    lane k = tid % 4 takes the pairs jp = k, k + 4, ... (readout stream k of recur_row4) --
-  unsigned char* pLo = sc + sRows;
-  unsigned char* pHi = pLo + 64 * W8;
-  unsigned char* pQ4 = pHi + 64 * W8;
-  unsigned char* pLat = pQ4 + 64 * W4;
-  uint16_t* pS8 = reinterpret_cast<uint16_t*>(pLat + 128);
-  uint16_t* pS4 = pS8 + 64;
+  // -- per-row recurrence and readout: row p = tid / 4 on four adjacent lanes, lane k = tid % 4
+  //    takes the pairs jp = k, k + 4, ... (readout stream k of recur_row4); the stored pairs
+  //    were decoded into S2 by scan_unpack --
+  const unsigned char* pLat = sc + sRows + 64 * (2 * W8 + W4);
   {
     const int p = tid >> 2, k = tid & 3;
     float2* Sr = S2 + p;                                // pair jp of row p at Sr[jp * 64]
-    {
-      const float s8 = h2f(pS8[p]), s4 = h2f(pS4[p]);
-#pragma unroll 1
-      for (int jp = k; jp < NP; jp += 4) {
-        float v[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int j = 2 * jp + e;
-          if (j < N8) {
-            const int lo = (pLo[p * W8 + j / 2] >> (4 * (j & 1))) & 15;
-            const int hi = (pHi[p * W8 + j / 2] >> (4 * (j & 1))) & 15;
-            const int ub = (hi << 4) | lo;
-            v[e] = (float)(ub - 256 * (ub > 127)) * s8;
-          } else {
-            const int j4 = j - N8;
-            const int nib = (pQ4[p * W4 + j4 / 2] >> (4 * (j4 & 1))) & 15;
-            v[e] = (float)(nib - 16 * (nib > 7)) * s4;
-          }
-        }
-        Sr[jp * 64] = make_float2(v[0], v[1]);
-      }
-    }
     const uint16_t* lsv = reinterpret_cast<const uint16_t*>(sc + sLs);
     const float ls0 = h2f(lsv[g * 2 + 0]), ls1 = h2f(lsv[g * 2 + 1]);
     const float ils0 = __frcp_rn(ls0), ils1 = __frcp_rn(ls1);
@@ -731,8 +711,64 @@ __device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsi
     float dots[7];
 #pragma unroll
     for (int i = 0; i < 7; ++i) dots[i] = sDots[i];
-    TokenScales ts;                                     // identical in the four lanes
-    const float out = token_tail_sums(ysum, ycorr, m8, m4, x, dtv, dec, dv, dots, zz, ls2, nls2, ils2, ts);
+    const float out = token_tail_sums(ysum, ycorr, m8, m4, x, dtv, dec, dv, dots, zz, ls2, nls2, ils2, ts);  // same in the four lanes
+    zlat = zz;
+    if (k == 0) P.y[hh * 64 + p] = f2h(out);
+  }
+}
+
+// The stored pairs of the head's 64 rows (packed rows staged in shared memory) as fp32 pairs
+// in S2 ([np][64] float2, pair-major): the INT8 / INT4 codes times the row scales.  Depends
+// only on the previous step's state, so it runs before the token's inputs exist.
+__device__ void scan_unpack(const DecLayer& L, const unsigned char* sc, float2* S2) {
+  const Geo G = geo_of(L.layout);
+  const int W8 = G.w8, W4 = G.w4, NP = G.np, N8 = G.n8;
+  const unsigned char* pLo = sc + sRows;
+  const unsigned char* pHi = pLo + 64 * W8;
+  const unsigned char* pQ4 = pHi + 64 * W8;
+  const uint16_t* pS8 = reinterpret_cast<const uint16_t*>(pQ4 + 64 * W4 + 128);
+  const uint16_t* pS4 = pS8 + 64;
+  const int p = threadIdx.x >> 2, k = threadIdx.x & 3;
+  float2* Sr = S2 + p;
+  const float s8 = h2f(pS8[p]), s4 = h2f(pS4[p]);
+#pragma unroll 1
+  for (int jp = k; jp < NP; jp += 4) {
+    float v[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int j = 2 * jp + e;
+      if (j < N8) {
+        const int lo = (pLo[p * W8 + j / 2] >> (4 * (j & 1))) & 15;
+        const int hi = (pHi[p * W8 + j / 2] >> (4 * (j & 1))) & 15;
+        const int ub = (hi << 4) | lo;
+        v[e] = (float)(ub - 256 * (ub > 127)) * s8;
+      } else {
+        const int j4 = j - N8;
+        const int nib = (pQ4[p * W4 + j4 / 2] >> (4 * (j4 & 1))) & 15;
+        v[e] = (float)(nib - 16 * (nib > 7)) * s4;
+      }
+    }
+    Sr[jp * 64] = make_float2(v[0], v[1]);
+  }
+}
+
+// The rest of the step, which only this CTA's next step reads: requant of the new pairs with
+// the row scales ts, the codes packed into the staged rows, the latent bytes and scales, and
+// the rows copied back to the layer state.  Runs after the readout y has been published.
+__device__ void scan_finish(const DecLayer& L, int hh, unsigned char* sc, float2* S2, const TokenScales& ts,
+                            float2 zz) {
+  const Geo G = geo_of(L.layout);
+  const int W8 = G.w8, W4 = G.w4, NP = G.np, N8 = G.n8;
+  const int tid = threadIdx.x, g = hh / (kHeads / kGroups);
+  unsigned char* pLo = sc + sRows;
+  unsigned char* pHi = pLo + 64 * W8;
+  unsigned char* pQ4 = pHi + 64 * W8;
+  unsigned char* pLat = pQ4 + 64 * W4;
+  uint16_t* pS8 = reinterpret_cast<uint16_t*>(pLat + 128);
+  uint16_t* pS4 = pS8 + 64;
+  {
+    const int p = tid >> 2, k = tid & 3;
+    float2* Sr = S2 + p;
     // requant + pack of this lane's pairs: v = requant(S), then the codes of v
     const float s8 = ts.s8, s4 = ts.s4;
     const float2 s82 = make_float2(s8, s8), ns82 = make_float2(-s8, -s8), i82 = make_float2(ts.i8, ts.i8);
@@ -758,7 +794,9 @@ __device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsi
       }
     }
     if (k == 0) {
-      P.y[hh * 64 + p] = f2h(out);
+      const uint16_t* lsv = reinterpret_cast<const uint16_t*>(sc + sLs);
+      const float ls0 = h2f(lsv[g * 2 + 0]), ls1 = h2f(lsv[g * 2 + 1]);
+      const float ils0 = __frcp_rn(ls0), ils1 = __frcp_rn(ls1);
       pLat[p * 2 + 0] = f32_to_e4m3(fminf(fmaxf(div_exact(zz.x, ls0, ils0), -448.f), 448.f));
       pLat[p * 2 + 1] = f32_to_e4m3(fminf(fmaxf(div_exact(zz.y, ls1, ils1), -448.f), 448.f));
       pS8[p] = f2h(s8);
@@ -1000,6 +1038,7 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     }
   };
   int vuse = 0, nw_phase = 0, in_phase = 0;
+  unsigned nbar = 0;                                   // grid barriers passed
   unsigned arms_nw = 1, arms_v = 0;                    // bulk-copy phases armed by thread 0
   if (tid == 0) {
     mb_expect(sbNw, kDModel * 2);
@@ -1040,26 +1079,33 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     DTRACE(l, 2);
     DARRIVE(l, 0);
     {
-      const unsigned long long tk = grid_arrive(P);
+      const unsigned long long tk = grid_arrive(P, nbar);
       stage_wait(sbIn, (uint32_t)in_phase);              // this layer's staged inputs
       in_phase ^= 1;
       if (L.ad_V) {                                      // adapter gate partials of this layer's input
         const float gp = gate_partial(hn, Ws, warp, tid & 31);
         if ((tid & 31) == 0) misc[24 + warp] = gp;
       }
+      if (item >= 0) scan_unpack(L, sc, S2);             // the previous step's state of the head
       if (!grid_wait(P, tk, flag)) ok = false;
     }
     DTRACE(l, 3);
     // z columns for the gated norm (swizzled rows of 64), staged where yn will be written
     for (int i = tid; i < kDInner / 8; i += kCompute) cp_async16(yn + swz(i >> 3, (i & 7) * 8), P.zx + i * 8);
     asm volatile("cp.async.commit_group;\n" ::: "memory");
-    if (item >= 0) {
-      DTRACE(l, 9);
-      scan_step(P, L, item, sc, S2, l, pos);
+    {
+      TokenScales ts;
+      float2 zlat;
+      if (item >= 0) {
+        DTRACE(l, 9);
+        scan_step(P, L, item, sc, S2, l, pos, ts, zlat);
+      }
+      DTRACE(l, 4);
+      DARRIVE(l, 1);
+      const unsigned long long tk = grid_arrive(P, nbar);      // y is published
+      if (item >= 0) scan_finish(L, item, sc, S2, ts, zlat);
+      if (!grid_wait(P, tk, flag)) ok = false;
     }
-    DTRACE(l, 4);
-    DARRIVE(l, 1);
-    if (!grid_sync(P, flag)) ok = false;
     DTRACE(l, 5);
     {
       uint16_t* Ys = reinterpret_cast<uint16_t*>(sc);
@@ -1093,7 +1139,7 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     ctr += (rout.t1 - rout.t0) * (kDInner / kKc);
     DTRACE(l, 7);
     DARRIVE(l, 2);
-    if (!grid_sync(P, flag)) ok = false;
+    if (!grid_sync(P, nbar, flag)) ok = false;
     DTRACE(l, 8);
   }
   DTRACE(63, 0);
@@ -1131,7 +1177,7 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     P.part_i[cta] = bi;
   }
   DTRACE(63, 1);
-  grid_sync(P, flag);
+  grid_sync(P, nbar, flag);
   DTRACE(63, 2);
   if (cta == 0 && warp == 0) {
     float bv = -INFINITY;
@@ -1149,7 +1195,7 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
       if (P.out_tokens) P.out_tokens[step] = pick;
     }
   }
-  if (step + 1 < P.steps) grid_sync(P, flag);                    // every CTA reads the pick next
+  if (step + 1 < P.steps) grid_sync(P, nbar, flag);                    // every CTA reads the pick next
   }
   // after an abort some staged copies were never waited for: let them land before exiting
   cp_async_wait_all();
