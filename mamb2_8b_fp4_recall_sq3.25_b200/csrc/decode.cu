@@ -35,14 +35,14 @@ constexpr int kDModel = 4096, kDInner = 8192, kZx = 18560, kHeads = 128, kGroups
 constexpr unsigned long long kWaitNs = 500000000ull;   // 0.5 s per wait
 
 // shared-memory plan (bytes).  Per-layer tensors are staged well before use (the stager
-// brings adapter, gated-norm weights and scan tables one layer ahead; the next layer's norm
-// weight is copied one layer ahead; z right after the in_proj barrier; V after the scan).
+// brings adapter V and weights, gated-norm weights and scan tables one layer ahead; the next
+// layer's norm weight is copied one layer ahead; z right after the in_proj barrier).
 // V and the gated-norm weights arrive as SWIZZLE_128B TMA tiles and z / the gated-norm
 // output use the same layout (see swz), so the Resurface epilogue and the head mix read
 // shared memory without bank conflicts; both tiles start on 1024-byte boundaries.
 constexpr int kScanBytes = 20608;
 constexpr int oRing = 0;                               // kNst x 9216 (1024-byte multiples)
-constexpr int oV = oRing + kNst * kStageBytes;         // scan: row state [np][64] float2; then adapter V, 2 x [128][64] swizzled
+constexpr int oV = oRing + kNst * kStageBytes;         // adapter V, 2 x [128][64] swizzled
 constexpr int oGnw = oV + 128 * 128 * 2;               // gated RMSNorm weights [128][64] swizzled
 constexpr int oYn = oGnw + kDInner * 2;                // z staging, then the gated-norm output [128][64] swizzled
 constexpr int oHn = oYn + kDInner * 2;                 // normed layer input [4096] fp16
@@ -52,7 +52,7 @@ constexpr int oNw = oAdw + kDModel * 2;                // Block norm weights [2]
 constexpr int oAdg = oNw + 2 * kDModel * 2;            // adapter g [128] fp16
 constexpr int oRed = oAdg + 256;                       // GEMV cross-warp sums [2][4][32][4] f32
 constexpr int oBar = oRed + 2 * 4 * 32 * 4 * 4;        // full[kNst], empty[kNst]
-constexpr int oSBar = oBar + 2 * kNst * 8;             // staging mbarriers: layer inputs, norm weight, V, inputs free
+constexpr int oSBar = oBar + 2 * kNst * 8;             // staging mbarriers: layer inputs, norm weight, (unused), inputs free
 constexpr int oMisc = oSBar + 32;                      // small scratch (reductions, flags)
 constexpr int kSmem = oMisc + 512;
 // scan region
@@ -569,7 +569,12 @@ __device__ __forceinline__ Piece scan_stage_piece(const DecLayer& L, int hh, uns
   return Piece{d, src, bytes};
 }
 
-__device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsigned char* sc, float2* S2,
+// A lane's stored pairs of its row: pair jp = k + 4 i in v[i] (k = lane of the row, at most
+// 11 pairs a lane for 42 pairs a row), in registers from the unpack to the requant.
+constexpr int kRowPairs = 11;
+struct RowState { float2 v[kRowPairs]; };
+
+__device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsigned char* sc, RowState& rs,
                           int layer, int pos, TokenScales& ts, float2& zlat) {
   const Geo G = geo_of(L.layout);
   const int NS = G.ns, NZ = G.nz, F = G.f, W8 = G.w8, W4 = G.w4, NP = G.np, N8 = G.n8;
@@ -659,11 +664,10 @@ __device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsi
   DTRACE(layer, 11);
   // -- per-row recurrence and readout: row p = tid / 4 on four adjacent lanes, lane k = tid % 4
   //    takes the pairs jp = k, k + 4, ... (readout stream k of recur_row4); the stored pairs
-  //    were decoded into S2 by scan_unpack --
+  //    were decoded into rs by scan_unpack --
   const unsigned char* pLat = sc + sRows + 64 * (2 * W8 + W4);
   {
     const int p = tid >> 2, k = tid & 3;
-    float2* Sr = S2 + p;                                // pair jp of row p at Sr[jp * 64]
     const uint16_t* lsv = reinterpret_cast<const uint16_t*>(sc + sLs);
     const float ls0 = h2f(lsv[g * 2 + 0]), ls1 = h2f(lsv[g * 2 + 1]);
     const float ils0 = __frcp_rn(ls0), ils1 = __frcp_rn(ls1);
@@ -677,18 +681,21 @@ __device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsi
     float m8a = 0.f, m8b = 0.f, m4a = 0.f, m4b = 0.f;
     const float4* cpp = reinterpret_cast<const float4*>(sPf);
     const float2* vpp = reinterpret_cast<const float2*>(sV);
-#pragma unroll 2
-    for (int jp = k; jp < NP; jp += 4) {
-      const float4 bc = cpp[jp];
-      const float2 cv = vpp[jp];
-      const float2 pr = Sr[jp * 64];
-      const float2 upd = __fmul2_rn(__fmul2_rn(make_float2(bc.x, bc.y), dt2), xx);   // (B*dt)*x
-      const float2 sn = __ffma2_rn(pr, dd, upd);                                      // prior*decay + upd
-      Sr[jp * 64] = sn;
-      ys = __ffma2_rn(sn, make_float2(bc.z, bc.w), ys);
-      cs = __ffma2_rn(pr, cv, cs);
-      if (2 * jp < N8) { m8a = fmaxf(m8a, fabsf(sn.x)); m8b = fmaxf(m8b, fabsf(sn.y)); }
-      else             { m4a = fmaxf(m4a, fabsf(sn.x)); m4b = fmaxf(m4b, fabsf(sn.y)); }
+#pragma unroll
+    for (int i = 0; i < kRowPairs; ++i) {
+      const int jp = k + 4 * i;
+      if (jp < NP) {
+        const float4 bc = cpp[jp];
+        const float2 cv = vpp[jp];
+        const float2 pr = rs.v[i];
+        const float2 upd = __fmul2_rn(__fmul2_rn(make_float2(bc.x, bc.y), dt2), xx);   // (B*dt)*x
+        const float2 sn = __ffma2_rn(pr, dd, upd);                                      // prior*decay + upd
+        rs.v[i] = sn;
+        ys = __ffma2_rn(sn, make_float2(bc.z, bc.w), ys);
+        cs = __ffma2_rn(pr, cv, cs);
+        if (2 * jp < N8) { m8a = fmaxf(m8a, fabsf(sn.x)); m8b = fmaxf(m8b, fabsf(sn.y)); }
+        else             { m4a = fmaxf(m4a, fabsf(sn.x)); m4b = fmaxf(m4b, fabsf(sn.y)); }
+      }
     }
     // combine the four lanes of the row: ((t0 + t1) + (t2 + t3)); max over the lanes
     const float ty = ys.x + ys.y, tc = cs.x + cs.y;
@@ -718,9 +725,9 @@ __device__ void scan_step(const DecodeParams& P, const DecLayer& L, int hh, unsi
 }
 
 // The stored pairs of the head's 64 rows (packed rows staged in shared memory) as fp32 pairs
-// in S2 ([np][64] float2, pair-major): the INT8 / INT4 codes times the row scales.  Depends
-// only on the previous step's state, so it runs before the token's inputs exist.
-__device__ void scan_unpack(const DecLayer& L, const unsigned char* sc, float2* S2) {
+// in the lanes' registers: the INT8 / INT4 codes times the row scales.  Depends only on the
+// previous step's state, so it runs before the token's inputs exist.
+__device__ void scan_unpack(const DecLayer& L, const unsigned char* sc, RowState& rs) {
   const Geo G = geo_of(L.layout);
   const int W8 = G.w8, W4 = G.w4, NP = G.np, N8 = G.n8;
   const unsigned char* pLo = sc + sRows;
@@ -729,33 +736,35 @@ __device__ void scan_unpack(const DecLayer& L, const unsigned char* sc, float2* 
   const uint16_t* pS8 = reinterpret_cast<const uint16_t*>(pQ4 + 64 * W4 + 128);
   const uint16_t* pS4 = pS8 + 64;
   const int p = threadIdx.x >> 2, k = threadIdx.x & 3;
-  float2* Sr = S2 + p;
   const float s8 = h2f(pS8[p]), s4 = h2f(pS4[p]);
-#pragma unroll 1
-  for (int jp = k; jp < NP; jp += 4) {
-    float v[2];
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int j = 2 * jp + e;
-      if (j < N8) {
-        const int lo = (pLo[p * W8 + j / 2] >> (4 * (j & 1))) & 15;
-        const int hi = (pHi[p * W8 + j / 2] >> (4 * (j & 1))) & 15;
-        const int ub = (hi << 4) | lo;
-        v[e] = (float)(ub - 256 * (ub > 127)) * s8;
-      } else {
-        const int j4 = j - N8;
-        const int nib = (pQ4[p * W4 + j4 / 2] >> (4 * (j4 & 1))) & 15;
-        v[e] = (float)(nib - 16 * (nib > 7)) * s4;
+  for (int i = 0; i < kRowPairs; ++i) {
+    const int jp = k + 4 * i;
+    if (jp < NP) {
+      float v[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = 2 * jp + e;
+        if (j < N8) {
+          const int lo = (pLo[p * W8 + j / 2] >> (4 * (j & 1))) & 15;
+          const int hi = (pHi[p * W8 + j / 2] >> (4 * (j & 1))) & 15;
+          const int ub = (hi << 4) | lo;
+          v[e] = (float)(ub - 256 * (ub > 127)) * s8;
+        } else {
+          const int j4 = j - N8;
+          const int nib = (pQ4[p * W4 + j4 / 2] >> (4 * (j4 & 1))) & 15;
+          v[e] = (float)(nib - 16 * (nib > 7)) * s4;
+        }
       }
+      rs.v[i] = make_float2(v[0], v[1]);
     }
-    Sr[jp * 64] = make_float2(v[0], v[1]);
   }
 }
 
 // The rest of the step, which only this CTA's next step reads: requant of the new pairs with
 // the row scales ts, the codes packed into the staged rows, the latent bytes and scales, and
 // the rows copied back to the layer state.  Runs after the readout y has been published.
-__device__ void scan_finish(const DecLayer& L, int hh, unsigned char* sc, float2* S2, const TokenScales& ts,
+__device__ void scan_finish(const DecLayer& L, int hh, unsigned char* sc, const RowState& rs, const TokenScales& ts,
                             float2 zz) {
   const Geo G = geo_of(L.layout);
   const int W8 = G.w8, W4 = G.w4, NP = G.np, N8 = G.n8;
@@ -768,7 +777,6 @@ __device__ void scan_finish(const DecLayer& L, int hh, unsigned char* sc, float2
   uint16_t* pS4 = pS8 + 64;
   {
     const int p = tid >> 2, k = tid & 3;
-    float2* Sr = S2 + p;
     // requant + pack of this lane's pairs: v = requant(S), then the codes of v
     const float s8 = ts.s8, s4 = ts.s4;
     const float2 s82 = make_float2(s8, s8), ns82 = make_float2(-s8, -s8), i82 = make_float2(ts.i8, ts.i8);
@@ -777,10 +785,12 @@ __device__ void scan_finish(const DecLayer& L, int hh, unsigned char* sc, float2
     const float2 nm82 = make_float2(m8s, m8s), nm42 = make_float2(m4s, m4s);
     const float i8 = s8 > 0.f ? __frcp_rn(s8) : 0.f;
     const float i4 = s4 > 0.f ? __frcp_rn(s4) : 0.f;
-#pragma unroll 2
-    for (int jp = k; jp < NP; jp += 4) {
+#pragma unroll
+    for (int i = 0; i < kRowPairs; ++i) {
+      const int jp = k + 4 * i;
+      if (jp >= NP) break;
       const bool t8 = 2 * jp < N8;
-      float2 v = Sr[jp * 64];
+      float2 v = rs.v[i];
       requant_pair(v.x, v.y, t8 ? ns82 : ns42, t8 ? i82 : i42, t8 ? 127.f : 7.f, t8 ? s82 : s42, t8 ? nm82 : nm42);
       if (t8) {
         const int qa = __float2int_rn(div_exact(v.x, s8, i8));
@@ -929,8 +939,9 @@ __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const f
 
 
 // Stager (one lane of its own warp): the per-layer inputs that do not depend on the token
-// (gated-norm and adapter weights; for CTAs with a scan head the scan statics, the head's
-// packed rows and the conv ring history) as bulk copies on `full`, one layer ahead: layer g
+// (gated-norm weights, adapter V / gate weights / g; for CTAs with a scan head the scan
+// statics, the head's packed rows and the conv ring history) as bulk / TMA copies on `full`,
+// one layer ahead: layer g
 // (counted over all steps) is issued once the compute warps have released the buffers of
 // layer g - 1 (`free`, arrived after that layer's Resurface).  Issuing ~30 copies takes
 // microseconds while the weight stream occupies the copy engine, so it runs off the compute
@@ -941,6 +952,7 @@ __device__ void stager(const DecodeParams& P, unsigned char* sm, uint32_t full, 
   uint16_t* Ws = reinterpret_cast<uint16_t*>(sm + oAdw);
   uint16_t* Gn = reinterpret_cast<uint16_t*>(sm + oGnw);
   uint16_t* Ag = reinterpret_cast<uint16_t*>(sm + oAdg);
+  uint16_t* Vs = reinterpret_cast<uint16_t*>(sm + oV);
   int armed = 0;
   for (int step = 0; step < P.steps; ++step)
     for (int l = 0; l < P.n_layer; ++l) {
@@ -953,7 +965,7 @@ __device__ void stager(const DecodeParams& P, unsigned char* sm, uint32_t full, 
         const DecLayer& L = P.layers[l];
         asm volatile("fence.proxy.async;" ::: "memory");
         unsigned bytes = kDInner * 2;
-        if (L.ad_V) bytes += kDModel * 2 + kHeads * 2;
+        if (L.ad_V) bytes += kDModel * 2 + kHeads * 2 + 128 * 128 * 2;
         if (item >= 0) bytes += scan_stage_bytes(geo_of(L.layout));
         mb_expect(full, bytes);
         ++armed;
@@ -961,9 +973,8 @@ __device__ void stager(const DecodeParams& P, unsigned char* sm, uint32_t full, 
         if (L.ad_V) {
           bulk_g2s(Ws, L.ad_w, kDModel * 2, full);
           bulk_g2s(Ag, L.ad_g, kHeads * 2, full);
-          // V is copied into shared memory after the scan: bring it into L2 now (4 KB piece
-          // per CTA, the pieces spread over the grid)
-          if (blockIdx.x < 8) prefetch_l2(reinterpret_cast<const uint8_t*>(L.ad_V) + blockIdx.x * 4096, 4096);
+          tma2d_plain(Vs, P.aux_maps + 2 * l, full, 0, 0);             // 2 x [128][64] swizzled
+          tma2d_plain(Vs + 128 * 64, P.aux_maps + 2 * l, full, 64, 0);
         }
         if (item >= 0)
           for (int k = 0; k < kScanPieces; ++k) {
@@ -1002,8 +1013,7 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  const uint32_t sbIn = (uint32_t)__cvta_generic_to_shared(sm + oSBar), sbNw = sbIn + 8, sbV = sbIn + 16,
-                 sbFree = sbIn + 24;
+  const uint32_t sbIn = (uint32_t)__cvta_generic_to_shared(sm + oSBar), sbNw = sbIn + 8, sbFree = sbIn + 24;
   if (warp == kWarps - 2) {
     if ((tid & 31) == 0) producer(P, R);
     return;
@@ -1026,7 +1036,6 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
   bool ok = true;
   int ctr = 0;
   uint16_t* Vs = reinterpret_cast<uint16_t*>(sm + oV);
-  float2* S2 = reinterpret_cast<float2*>(sm + oV);      // scan row state, same bytes as V
   uint16_t* Ws = reinterpret_cast<uint16_t*>(sm + oAdw);
   uint16_t* Gn = reinterpret_cast<uint16_t*>(sm + oGnw);
   uint16_t* Ag = reinterpret_cast<uint16_t*>(sm + oAdg);
@@ -1037,9 +1046,9 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
       set_abort(P, (int)kDevTimeoutProducer);
     }
   };
-  int vuse = 0, nw_phase = 0, in_phase = 0;
+  int nw_phase = 0, in_phase = 0;
   unsigned nbar = 0;                                   // grid barriers passed
-  unsigned arms_nw = 1, arms_v = 0;                    // bulk-copy phases armed by thread 0
+  unsigned arms_nw = 1;                                // bulk-copy phases armed by thread 0
   if (tid == 0) {
     mb_expect(sbNw, kDModel * 2);
     bulk_g2s(Nw, P.layers[0].norm_w, kDModel * 2, sbNw);
@@ -1078,6 +1087,7 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     ctr += (rin.t1 - rin.t0) * (kDModel / kKc);
     DTRACE(l, 2);
     DARRIVE(l, 0);
+    RowState rs;                                         // the head's row pairs (CTAs with a scan head)
     {
       const unsigned long long tk = grid_arrive(P, nbar);
       stage_wait(sbIn, (uint32_t)in_phase);              // this layer's staged inputs
@@ -1086,7 +1096,7 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
         const float gp = gate_partial(hn, Ws, warp, tid & 31);
         if ((tid & 31) == 0) misc[24 + warp] = gp;
       }
-      if (item >= 0) scan_unpack(L, sc, S2);             // the previous step's state of the head
+      if (item >= 0) scan_unpack(L, sc, rs);             // the previous step's state of the head
       if (!grid_wait(P, tk, flag)) ok = false;
     }
     DTRACE(l, 3);
@@ -1098,33 +1108,22 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
       float2 zlat;
       if (item >= 0) {
         DTRACE(l, 9);
-        scan_step(P, L, item, sc, S2, l, pos, ts, zlat);
+        scan_step(P, L, item, sc, rs, l, pos, ts, zlat);
       }
       DTRACE(l, 4);
       DARRIVE(l, 1);
       const unsigned long long tk = grid_arrive(P, nbar);      // y is published
-      if (item >= 0) scan_finish(L, item, sc, S2, ts, zlat);
+      if (item >= 0) scan_finish(L, item, sc, rs, ts, zlat);
       if (!grid_wait(P, tk, flag)) ok = false;
     }
     DTRACE(l, 5);
     {
       uint16_t* Ys = reinterpret_cast<uint16_t*>(sc);
-      if (L.ad_V && tid == 0) {                          // V into the row-state bytes, now free
-        asm volatile("fence.proxy.async;" ::: "memory");
-        mb_expect(sbV, 128 * 128 * 2);
-        ++arms_v;
-        tma2d_plain(Vs, P.aux_maps + 2 * l, sbV, 0, 0);
-        tma2d_plain(Vs + 128 * 64, P.aux_maps + 2 * l, sbV, 64, 0);
-      }
       for (int i = tid; i < 128 * 8; i += kCompute) {
         const int r = i >> 3, c = (i & 7) * 8;
         cp_async16(Ys + r * kYPitch + c, P.y + r * 64 + c);
       }
       cp_async_wait_all();
-      if (L.ad_V) {
-        stage_wait(sbV, (uint32_t)(vuse & 1));
-        ++vuse;
-      }
       bar_sync(1, kCompute);
       DTRACE(l, 12);
       resurface_norm(P, L, misc + 24, Ys, Vs, Ag, Gn, yn, l);
@@ -1201,7 +1200,6 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
   cp_async_wait_all();
   if (tid == 0) {
     if (arms_nw) mb_drain(sbNw, (arms_nw - 1) & 1u);
-    if (arms_v) mb_drain(sbV, (arms_v - 1) & 1u);
   }
   (void)ok;
 }
