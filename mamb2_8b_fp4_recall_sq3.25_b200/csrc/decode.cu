@@ -2,20 +2,23 @@
 //
 // Same arithmetic, operation for operation, as the multi-kernel decode step it replaces
 // (fp4_embed, add_rmsnorm, the factored-scale streaming GEMV, the one-token scan step with
-// the conv ring, resurface_gatednorm with one warp per norm group, argmax), so tokens,
-// logits and state bytes are identical; what changes is the schedule:
-//   * grid = one CTA per SM, 9 warps: warps 0-7 compute, warp 8 lane 0 is the weight
-//     producer.  Each CTA owns fixed 16-row tiles of in_proj, out_proj and lm_head and
-//     streams them (1024-column chunks of codes + block scales, 2-D TMA, no multicast)
-//     through a 14-stage mbarrier ring in the order the consumers use them, running ahead
-//     across phases and layers; the next tiles are also prefetched into L2.
-//   * per layer: norm (every CTA, redundant) -> in_proj -> grid barrier -> scan step (one
-//     head per CTA) -> grid barrier -> resurface + gated norm (every CTA, redundant: the
+// the conv ring, resurface_gatednorm, argmax), so tokens, logits and state bytes are
+// identical; what changes is the schedule:
+//   * grid = one CTA per SM, 10 warps: warps 0-7 compute, warp 8 lane 0 is the weight
+//     producer, warp 9 lane 0 the stager.  Each CTA owns fixed 16-row tiles of in_proj,
+//     out_proj and lm_head and streams them (1024-column chunks of codes + block scales,
+//     2-D TMA, no multicast) through an 11-stage mbarrier ring in the order the consumers
+//     use them, running ahead across phases and layers.  The stager brings each layer's
+//     token-independent inputs (norm / adapter weights, the scan head's tables, packed state
+//     rows and conv history) one layer ahead.
+//   * per layer: norm (every CTA, redundant) -> in_proj -> grid barrier (gate dot and the
+//     head's state unpack inside it) -> scan step (one head per CTA) -> grid barrier (state
+//     requant / write-back inside it) -> resurface + gated norm (every CTA, redundant: the
 //     128x128 head mix needs all heads) -> out_proj -> grid barrier.
 //   * data another CTA wrote during this launch is read through L2 only (ld.global.cg,
-//     cp.async.cg); every wait (ring slot, grid barrier) is bounded by %globaltimer and
-//     observes a shared abort flag, after which the launch finishes without waiting and
-//     reports through the error word.
+//     cp.async.cg); every wait (ring slot, staging copy, grid barrier) is bounded by
+//     %globaltimer and observes a shared abort flag, after which the launch finishes without
+//     waiting and reports through the error word.
 #include <cstring>
 
 #include "common.cuh"
@@ -118,9 +121,6 @@ __device__ __forceinline__ void tma2d_plain(void* dst, const CUtensorMap* map, u
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
       :: "r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(map), "r"(bar), "r"(x), "r"(y) : "memory");
-}
-__device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
 }
 
 // Phase timestamps of two CTAs for the first layers, compiled only with SQ_DECODE_TRACE
@@ -346,8 +346,10 @@ __device__ __forceinline__ void x_offsets(int cw, int tq, int (&xoff)[2][4]) {
 }
 
 // One projection phase: this CTA's tiles [t0, t1) of a 16-row-tiled matrix, chunks of 1024
-// columns at ring counters ctr + (tile - t0) * cpt + kc (cpt even).  Tiles alternate between
-// the two 4-warp consumer groups; per tile the fp4_gemv_stream_kernel arithmetic (factored
+// columns from ring counter ctr on (cpt per tile, cpt even); tiles alternate between the two
+// 4-warp consumer groups, and the producer issues each pair of tiles chunk-interleaved (tile
+// 2m chunk kc at ctr + 2m cpt + 2 kc, tile 2m + 1 one after it) so that both groups see the
+// whole ring ahead of them; per tile the fp4_gemv_stream_kernel arithmetic (factored
 // global scale), chunks taken two per wait, the four warps' sums added in order.
 template <bool XSWZ>
 __device__ void gemv_phase(const DecodeParams& P, const Ring& R, const unsigned char* sm, int ctr, int t0, int t1,
@@ -361,11 +363,14 @@ __device__ void gemv_phase(const DecodeParams& P, const Ring& R, const unsigned 
   x_offsets<XSWZ>(cw, tq, xoff);
   for (int i = q; i < t1 - t0; i += 2) {
     const int tile = t0 + i;
+    // ring position of chunk kc: tiles 2m and 2m + 1 (one per group) are issued interleaved
+    const int base = ctr + (i >> 1) * 2 * cpt, paired = (i | 1) < t1 - t0;
+    const int step = paired ? 2 : 1, off = paired ? (i & 1) : 0;
     float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
     for (int kc = 0; kc < cpt; kc += 2) {
-      const int c = ctr + i * cpt + kc;
-      const int st0 = c % kNst, st1 = (c + 1) % kNst;
-      if (ok && !(wait_chunk(R, c, P.sync) && wait_chunk(R, c + 1, P.sync))) {
+      const int c = base + kc * step + off, c1 = c + step;
+      const int st0 = c % kNst, st1 = c1 % kNst;
+      if (ok && !(wait_chunk(R, c, P.sync) && wait_chunk(R, c1, P.sync))) {
         ok = false;
         set_abort(P, (int)kDevTimeoutMma);
       }
@@ -406,29 +411,14 @@ __device__ void gemv_phase(const DecodeParams& P, const Ring& R, const unsigned 
 }
 
 // Producer: the CTA's chunks in consumption order (per layer: in_proj tiles x 4 chunks,
-// out_proj tiles x 8 chunks; then lm_head tiles x 4 chunks), plus L2 prefetch of the
-// next layer's rows.
+// out_proj tiles x 8 chunks; then lm_head tiles x 4 chunks).  No separate L2 prefetch: bulk
+// L2 prefetches of the next rows measured slower (they occupy the same copy engine).
 struct TileRange { int t0, t1; };
 __device__ __forceinline__ TileRange tile_range(int ntiles, int cta, int ncta) {
   return TileRange{(int)((long long)ntiles * cta / ncta), (int)((long long)ntiles * (cta + 1) / ncta)};
 }
 
-__device__ void prefetch_span(const uint8_t* p, long long bytes) {
-  constexpr long long kPiece = 4096;
-  for (long long o = 0; o < bytes; o += kPiece)
-    prefetch_l2(p + o, (unsigned)(bytes - o < kPiece ? bytes - o : kPiece));
-}
-__device__ void prefetch_rows(const uint8_t* codes, const uint8_t* scales, int K, TileRange r) {
-  if (r.t1 <= r.t0) return;
-  const long long cb = (long long)kRows * (K / 2), sb = (long long)kRows * (K / 16);
-  prefetch_span(codes + r.t0 * cb, (r.t1 - r.t0) * cb);
-  prefetch_span(scales + r.t0 * sb, (r.t1 - r.t0) * sb);
-}
-
 __device__ void producer(const DecodeParams& P, const Ring& R) {
-  const DecLayerRows* lp = P.rows;
-  const uint8_t* head_codes = P.head_codes;
-  const uint8_t* head_scales = P.head_scales;
   const int cta = blockIdx.x, ncta = gridDim.x;
   const TileRange rin = tile_range(kZx / kRows, cta, ncta), rout = tile_range(kDModel / kRows, cta, ncta);
   const TileRange rhead = tile_range(P.vocab / kRows, cta, ncta);
@@ -453,24 +443,22 @@ __device__ void producer(const DecodeParams& P, const Ring& R) {
     }
     ++ctr;
   };
+  // tiles [r.t0, r.t1) in the consumers' order: pairs of tiles chunk-interleaved
+  auto issue_tiles = [&](const CUtensorMap* m, TileRange r, int cpt) {
+    for (int t = r.t0; t < r.t1; t += 2)
+      for (int kc = 0; kc < cpt; ++kc)
+        for (int u = t; u < t + 2 && u < r.t1; ++u) issue(m, m + 1, u, kc);
+  };
   for (int step = 0; step < P.steps && ok; ++step) {
-  prefetch_rows(lp[0].in_codes, lp[0].in_scales, kDModel, rin);
   for (int l = 0; l < P.n_layer && ok; ++l) {
-    prefetch_rows(lp[l].out_codes, lp[l].out_scales, kDInner, rout);
     const CUtensorMap* mi = P.maps + (2 * l) * 2;
-    for (int t = rin.t0; t < rin.t1; ++t)
-      for (int kc = 0; kc < kDModel / kKc; ++kc) issue(mi, mi + 1, t, kc);
-    if (l + 1 < P.n_layer) prefetch_rows(lp[l + 1].in_codes, lp[l + 1].in_scales, kDModel, rin);
-    else prefetch_rows(head_codes, head_scales, kDModel, TileRange{rhead.t0, min(rhead.t1, rhead.t0 + 8)});
+    issue_tiles(mi, rin, kDModel / kKc);
     const CUtensorMap* mo = P.maps + (2 * l + 1) * 2;
-    for (int t = rout.t0; t < rout.t1; ++t)
-      for (int kc = 0; kc < kDInner / kKc; ++kc) issue(mo, mo + 1, t, kc);
+    issue_tiles(mo, rout, kDInner / kKc);
   }
   const CUtensorMap* mh = P.maps + (2 * P.n_layer) * 2;
-  for (int t = rhead.t0; t < rhead.t1 && ok; ++t) {
-    if ((t - rhead.t0) % 8 == 0)
-      prefetch_rows(head_codes, head_scales, kDModel, TileRange{t + 8, min(rhead.t1, t + 16)});
-    for (int kc = 0; kc < kDModel / kKc; ++kc) issue(mh, mh + 1, t, kc);
+  for (int t = rhead.t0; t < rhead.t1 && ok; t += 2) {
+    issue_tiles(mh, TileRange{t, min(rhead.t1, t + 2)}, kDModel / kKc);
   }
   }
   // every issued copy has landed before the CTA may exit
