@@ -872,9 +872,7 @@ __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const f
     }
   }
   DTRACE(layer, 14);
-  // The epilogue runs once per layer: it is written as short loops (the mix results and the
-  // x values go through this warp's 16 V rows, 4 KB, no longer read) so that its code stays
-  // small in the instruction caches.
+  // The mix results and the x values go through this warp's 16 V rows (4 KB, no longer read).
   float* scr0 = reinterpret_cast<float*>(const_cast<uint16_t*>(Vs) + grp * 16 * 64);      // 512 floats
   float* scr1 = reinterpret_cast<float*>(const_cast<uint16_t*>(Vs) + 128 * 64 + grp * 16 * 64);
   auto scr_at = [&](int n, int e) { return (n < 4 ? scr0 + (n * 4 + e) * 32 : scr1 + ((n - 4) * 4 + e) * 32) + lane; };
@@ -891,7 +889,7 @@ __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const f
   const float ga = has_ad ? h2f(f2h(gate * h2f(Gs[ia]))) : 0.f;
   const float gb = has_ad ? h2f(f2h(gate * h2f(Gs[ib]))) : 0.f;
   const __half2 ga2 = __float2half2_rn(ga), gb2 = __float2half2_rn(gb);
-#pragma unroll 1
+#pragma unroll
   for (int n = 0; n < 8; ++n) {
     const int p0 = n * 8 + 2 * tq;
 #pragma unroll
@@ -909,7 +907,7 @@ __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const f
   }
   ss = warp_sum(ss);
   const float rstd = 1.0f / sqrtf(ss / 1024.0f + P.eps);
-#pragma unroll 1
+#pragma unroll
   for (int n = 0; n < 8; ++n) {
     const int p0 = n * 8 + 2 * tq;
 #pragma unroll
