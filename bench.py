@@ -117,15 +117,22 @@ def dist_init(n):
 
 # ------------------------------------------------------------------ CPU reference arm
 
-def cpu_sample(tokens=16, layers=2, vocab_slice=32768, seed=0):
+_CPU_MODELS = {}
+
+
+def cpu_sample(tokens=512, layers=2, vocab_slice=32768, seed=0):
     """The CPU oracle port (oracle/) on a bounded slice of the workload: one window of
     `tokens` tokens through `layers` full-geometry layers plus the lm_head + CE over a
     `vocab_slice`-row slice of the vocabulary, all host threads.  Returns seconds per
-    scored token extrapolated to 56 layers and the full 256000-row head."""
+    scored token extrapolated to 56 layers and the full 256000-row head.  The oracle model
+    is built once per process and reused by later samples."""
     sys.path.insert(0, str(ROOT / 'tests'))
     from _models import build_pair
     torch.set_num_threads(os.cpu_count())
-    _, ora, _ = build_pair(n_layer=layers, vocab=vocab_slice, seed=seed, adapter=True, device='cpu')
+    key = (layers, vocab_slice, seed)
+    if key not in _CPU_MODELS:
+        _CPU_MODELS[key] = build_pair(n_layer=layers, vocab=vocab_slice, seed=seed, adapter=True, device='cpu')[1]
+    ora = _CPU_MODELS[key]
     rng = np.random.default_rng(seed)
     ids = zipf_tokens(tokens + 1, rng, vocab=vocab_slice)[None]
     ora.reset(1)
@@ -283,7 +290,7 @@ def main():
     ap.add_argument('--steps', type=int, default=4)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='native', choices=['native', 'reference'])
-    ap.add_argument('--ref-tokens', type=int, default=16)
+    ap.add_argument('--ref-tokens', type=int, default=512)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--decode-steps', type=int, default=32)
     ap.add_argument('--case', choices=['gemm', 'scan', 'decode'], default=None,
