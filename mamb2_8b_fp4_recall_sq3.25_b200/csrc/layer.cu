@@ -134,6 +134,13 @@ __device__ __forceinline__ float gate_span(const uint16_t* Us, const uint16_t* W
 constexpr int kVPitch = 136;   // fp16 elements per staged V row (128 + 8 pad, 272 B)
 constexpr int kYPitch = 72;    // fp16 elements per staged y row (64 + 8 pad, 144 B)
 
+// [rows][64] fp16 tiles in shared memory with 16-byte chunk c of row h at chunk c ^ (h & 7),
+// so that lanes reading the same column of eight consecutive rows hit different banks.
+__device__ __forceinline__ int swz64(int h, int p) { return (h << 6) + ((((p >> 3) ^ h) & 7) << 3) + (p & 7); }
+__device__ __forceinline__ void stage_swz64(uint16_t* dst, const uint16_t* src, int rows, int tid, int nth) {
+  for (int i = tid; i < rows * 8; i += nth) cp_async16(dst + swz64(i >> 3, (i & 7) * 8), src + i * 8);
+}
+
 template <int GPB>
 __global__ void __launch_bounds__(32 * GPB)
 resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __restrict__ z, long long z_st,
@@ -142,8 +149,8 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
   extern __shared__ __align__(16) unsigned char smraw[];
   uint16_t* Ys = reinterpret_cast<uint16_t*>(smraw);                  // [128][kYPitch]   this token's y
   uint16_t* Vs = Ys + 128 * kYPitch;                                  // [GPB*16][kVPitch] V rows
-  uint16_t* Zs = Vs + GPB * 16 * kVPitch;                             // [GPB][1024]      this token's z
-  uint16_t* Ns = Zs + GPB * 1024;                                     // [GPB][1024]      norm weights
+  uint16_t* Zs = Vs + GPB * 16 * kVPitch;                             // [GPB*16][64]     this token's z (swz64)
+  uint16_t* Ns = Zs + GPB * 1024;                                     // [GPB*16][64]     norm weights (swz64)
   uint16_t* Us = Ns + GPB * 1024;                                     // [4096]           mixer input u
   uint16_t* Ws = Us + 4096;                                           // [4096]           gate weights
   __shared__ float spart[GPB];
@@ -160,7 +167,7 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
     }
     stage16(Ws, ad.w, 4096 * 2, tid, nth);
   }
-  stage16(Ns, nw + grp0 * 1024, GPB * 1024 * 2, tid, nth);
+  stage_swz64(Ns, nw + grp0 * 1024, GPB * 16, tid, nth);
   for (int t = blockIdx.y; t < T; t += gridDim.y) {
     __syncthreads();                                   // previous token done with the staged rows
     const uint16_t* yr = y + (long long)t * 8192;
@@ -168,7 +175,7 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
       const int r = i >> 3, c = (i & 7) * 8;
       cp_async16(Ys + r * kYPitch + c, yr + r * 64 + c);
     }
-    stage16(Zs, z + (long long)t * z_st + grp0 * 1024, GPB * 1024 * 2, tid, nth);
+    stage_swz64(Zs, z + (long long)t * z_st + grp0 * 1024, GPB * 16, tid, nth);
     if (has_ad) stage16(Us, u + (long long)t * u_st, 4096 * 2, tid, nth);
     cp_async_wait_all();
     __syncthreads();
@@ -213,7 +220,7 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
       }
     }
     // epilogue: correction, gated RMSNorm over this warp's group (1024 channels)
-    const uint16_t* zs = Zs + warp * 1024;
+    uint16_t* zs = Zs + warp * 1024;                    // this warp's z rows, then its output rows
     const uint16_t* ns = Ns + warp * 1024;
     float xv[8][4];
     float ss = 0.f;
@@ -229,7 +236,7 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
       for (int half = 0; half < 2; ++half) {
         const int i = half ? ib : ia, li = half ? lb : la;
         const float2 x2 = resurface_pair(*reinterpret_cast<const uint32_t*>(Ys + i * kYPitch + p0),
-                                         *reinterpret_cast<const uint32_t*>(zs + li * 64 + p0), acc[n][2 * half],
+                                         *reinterpret_cast<const uint32_t*>(zs + swz64(li, p0)), acc[n][2 * half],
                                          acc[n][2 * half + 1], half ? gb2 : ga2, has_ad);
         xv[n][2 * half] = x2.x;
         xv[n][2 * half + 1] = x2.y;
@@ -245,12 +252,16 @@ resurface_gatednorm_kernel(const uint16_t* __restrict__ y, const uint16_t* __res
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int li = half ? lb : la;
-        const float o0 = (xv[n][2 * half] * rstd) * h2f(ns[li * 64 + p0]);
-        const float o1 = (xv[n][2 * half + 1] * rstd) * h2f(ns[li * 64 + p0 + 1]);
-        __half2 hv = __floats2half2_rn(o0, o1);
-        *reinterpret_cast<__half2*>(out + (long long)t * 8192 + grp * 1024 + li * 64 + p0) = hv;
+        const float2 w2 = __half22float2(*reinterpret_cast<const __half2*>(ns + swz64(li, p0)));
+        const float o0 = (xv[n][2 * half] * rstd) * w2.x;
+        const float o1 = (xv[n][2 * half + 1] * rstd) * w2.y;
+        *reinterpret_cast<__half2*>(zs + swz64(li, p0)) = __floats2half2_rn(o0, o1);   // z already read
       }
     }
+    __syncwarp();
+    uint4* og = reinterpret_cast<uint4*>(out + (long long)t * 8192 + grp * 1024);
+#pragma unroll
+    for (int i = lane; i < 128; i += 32) og[i] = *reinterpret_cast<const uint4*>(zs + swz64(i >> 3, (i & 7) * 8));
   }
 }
 
@@ -377,6 +388,7 @@ int launch_resurface_gatednorm(const uint16_t* y, const uint16_t* z, long long z
                                uint16_t* out, int T, cudaStream_t st) {
   if (T <= 0) return kEInval;
   if (((uintptr_t)y % 16) || ((uintptr_t)z % 16) || ((uintptr_t)u % 16) || ((uintptr_t)norm_w % 16) ||
+      ((uintptr_t)out % 16) ||
       (z_st % 8) || (u_st % 8))
     return kEInval;
   const int has_ad = ad && ad->V;
