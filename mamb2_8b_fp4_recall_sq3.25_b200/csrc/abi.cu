@@ -75,7 +75,6 @@ struct sq_model {
   bool exact_skinny = false;                  // decode steps / greedy head: per-weight fp16 decode
   // persistent batch-1 decode: device copies of the layer table and TMA maps, step buffers
   DecLayer* d_dlayers = 0;
-  DecLayerRows* d_drows = 0;
   CUtensorMap* d_dmaps = 0;
   unsigned char* d_dbuf = 0;                  // h | res[2] | zx | y | argmax partials | sync
   bool dec_dirty = true;
@@ -272,7 +271,7 @@ int sq_model_create(const sq_model_config* cfg, sq_model** out) {
 int sq_model_destroy(sq_model* m) {
   if (!m) return SQ_OK;
   free_ws(m);
-  void* dec[] = {m->d_dlayers, m->d_drows, m->d_dmaps, m->d_dbuf};
+  void* dec[] = {m->d_dlayers, m->d_dmaps, m->d_dbuf};
   for (void* p : dec)
     if (p) cudaFree(p);
   if (m->d_err) cudaFree(m->d_err);
@@ -471,14 +470,12 @@ int decode_setup(sq_model* m) {
   const int L = m->cfg.n_layer;
   if (!m->d_dlayers) {
     if (cudaMalloc(&m->d_dlayers, sizeof(DecLayer) * L) != cudaSuccess ||
-        cudaMalloc(&m->d_drows, sizeof(DecLayerRows) * L) != cudaSuccess ||
         cudaMalloc(&m->d_dmaps, sizeof(CUtensorMap) * ((2 * L + 1) * 2 + 2 * L)) != cudaSuccess ||
         cudaMalloc(&m->d_dbuf, kDecBytes) != cudaSuccess)
       return fail(SQ_ENOMEM, "decode: cudaMalloc failed");
     if (cudaMemset(m->d_dbuf, 0, kDecBytes) != cudaSuccess) return cuda_fail("decode: cudaMemset");
   }
   std::vector<DecLayer> dl(L);
-  std::vector<DecLayerRows> rows(L);
   std::vector<CUtensorMap> maps((2 * L + 1) * 2 + 2 * L);
   CUtensorMap* aux = maps.data() + (2 * L + 1) * 2;
   for (int l = 0; l < L; ++l) {
@@ -503,7 +500,6 @@ int decode_setup(sq_model* m) {
     x.ad_V = ad.V; x.ad_g = ad.g; x.ad_w = ad.w; x.ad_b = ad.b; x.hard = ad.hard;
     x.lo = st.lo; x.hi = st.hi; x.q4 = st.q4; x.latent = st.latent; x.s8 = st.s8; x.s4 = st.s4; x.ring = st.ring;
     x.layout = d.layout;
-    rows[l] = DecLayerRows{d.in_proj.codes, d.in_proj.block_scales, d.out_proj.codes, d.out_proj.block_scales};
     maps[(2 * l) * 2 + 0] = m->in_maps[l].codes; maps[(2 * l) * 2 + 1] = m->in_maps[l].scales;
     maps[(2 * l + 1) * 2 + 0] = m->out_maps[l].codes; maps[(2 * l + 1) * 2 + 1] = m->out_maps[l].scales;
     std::memset(aux + 2 * l, 0, 2 * sizeof(CUtensorMap));
@@ -515,7 +511,6 @@ int decode_setup(sq_model* m) {
   if (!aligned(m->norm_f, 16) || !aligned(m->embed.codes, 4)) return fail(SQ_EINVAL, "decode: norm_f must be 16-byte aligned");
   maps[(2 * L) * 2 + 0] = m->head_maps.codes; maps[(2 * L) * 2 + 1] = m->head_maps.scales;
   if (cudaMemcpy(m->d_dlayers, dl.data(), sizeof(DecLayer) * L, cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemcpy(m->d_drows, rows.data(), sizeof(DecLayerRows) * L, cudaMemcpyHostToDevice) != cudaSuccess ||
       cudaMemcpy(m->d_dmaps, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice) != cudaSuccess)
     return cuda_fail("decode: table upload");
   if (!m->dec_grid) m->dec_grid = decode_grid();
@@ -537,7 +532,7 @@ int sq_model_decode(sq_model* m, int64_t* tokens, int pos, int steps, int64_t* o
     if (s != SQ_OK) return s;
   }
   DecodeParams P{};
-  P.layers = m->d_dlayers; P.maps = m->d_dmaps; P.rows = m->d_drows;
+  P.layers = m->d_dlayers; P.maps = m->d_dmaps;
   P.aux_maps = m->d_dmaps + (2 * m->cfg.n_layer + 1) * 2;
   P.head_codes = m->head.codes; P.head_scales = m->head.block_scales;
   P.emb_codes = m->embed.codes; P.emb_scales = m->embed.block_scales; P.emb_g = m->embed.global_scale;

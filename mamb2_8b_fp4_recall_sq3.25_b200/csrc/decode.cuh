@@ -36,13 +36,10 @@ struct DecLayer {
 
 struct DecodeSync { unsigned long long count; int abort, pad; };
 
-// Raw packed rows of a layer's projections (for L2 prefetch ahead of the TMA stream).
-struct DecLayerRows { const uint8_t *in_codes, *in_scales, *out_codes, *out_scales; };
 
 struct DecodeParams {
   const DecLayer* layers;        // [n_layer] (device)
   const CUtensorMap* maps;       // [(2 * n_layer + 1) * 2] codes / scales maps (device, 64-B aligned)
-  const DecLayerRows* rows;      // [n_layer] (device)
   const CUtensorMap* aux_maps;   // [n_layer][2]: adapter V [128][128], gated-norm weights [128][64]; fp16, SWIZZLE_128B
   const uint8_t* head_codes; const uint8_t* head_scales;
   const uint8_t* emb_codes; const uint8_t* emb_scales; const float* emb_g;
