@@ -7,7 +7,7 @@
 //   * grid = one CTA per SM, 10 warps: warps 0-7 compute, warp 8 lane 0 is the weight
 //     producer, warp 9 lane 0 the stager.  Each CTA owns fixed 16-row tiles of in_proj,
 //     out_proj and lm_head and streams them (1024-column chunks of codes + block scales,
-//     2-D TMA, no multicast) through an 11-stage mbarrier ring in the order the consumers
+//     2-D TMA, no multicast) through a 12-stage mbarrier ring in the order the consumers
 //     use them, running ahead across phases and layers.  The stager brings each layer's
 //     token-independent inputs (norm / adapter weights, the scan head's tables, packed state
 //     rows and conv history) one layer ahead.
@@ -31,7 +31,7 @@ namespace sq {
 namespace {
 
 constexpr int kWarps = 10, kThreads = 32 * kWarps, kCompute = 256;   // 8 compute, producer, stager
-constexpr int kNst = 11;                               // ring stages
+constexpr int kNst = 12;                               // ring stages
 constexpr int kRows = 16, kKc = 1024;                  // tile rows, columns per chunk
 constexpr int kCodeBytes = kRows * kKc / 2, kScaleBytes = kRows * kKc / 16, kStageBytes = kCodeBytes + kScaleBytes;
 constexpr int kDModel = 4096, kDInner = 8192, kZx = 18560, kHeads = 128, kGroups = 8;
@@ -51,8 +51,8 @@ constexpr int oYn = oGnw + kDInner * 2;                // z staging, then the ga
 constexpr int oHn = oYn + kDInner * 2;                 // normed layer input [4096] fp16
 constexpr int oScan = oHn + kDModel * 2;               // scan item staging / y staging
 constexpr int oAdw = oScan + kScanBytes;               // adapter gate weights [4096] fp16
-constexpr int oNw = oAdw + kDModel * 2;                // Block norm weights [2][4096] fp16 (layer parity)
-constexpr int oAdg = oNw + 2 * kDModel * 2;            // adapter g [128] fp16
+constexpr int oNw = oAdw + kDModel * 2;                // Block norm weights [4096] fp16 (the next layer's copied in after each norm)
+constexpr int oAdg = oNw + kDModel * 2;                // adapter g [128] fp16
 constexpr int oRed = oAdg + 256;                       // GEMV cross-warp sums [2][4][32][4] f32
 constexpr int oBar = oRed + 2 * 4 * 32 * 4 * 4;        // full[kNst], empty[kNst]
 constexpr int oSBar = oBar + 2 * kNst * 8;             // staging mbarriers: layer inputs, norm weight, (unused), inputs free
@@ -1057,14 +1057,15 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     stage_wait(sbNw, (uint32_t)nw_phase);
     nw_phase ^= 1;
     uint16_t* res_out = cta == 0 ? P.res + ((l + 1) & 1) * kDModel : nullptr;
-    block_norm(P, P.h, l > 0 ? P.res + (l & 1) * kDModel : nullptr, res_out, Nw + (l & 1) * kDModel,
+    block_norm(P, P.h, l > 0 ? P.res + (l & 1) * kDModel : nullptr, res_out, Nw,
                l == 0 ? id : -1, hn, misc);
-    // next layer's norm weight (norm_f after the last layer) into the other half
+    // next layer's norm weight (norm_f after the last layer): block_norm's last CTA barrier
+    // has passed every read of this one
     if (tid == 0) {
       asm volatile("fence.proxy.async;" ::: "memory");
       mb_expect(sbNw, kDModel * 2);
       ++arms_nw;
-      bulk_g2s(Nw + ((l + 1) & 1) * kDModel, l + 1 < P.n_layer ? P.layers[l + 1].norm_w : P.norm_f, kDModel * 2, sbNw);
+      bulk_g2s(Nw, l + 1 < P.n_layer ? P.layers[l + 1].norm_w : P.norm_f, kDModel * 2, sbNw);
     }
     DTRACE(l, 1);
     DWARP(l, 0);
@@ -1131,7 +1132,7 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
   stage_wait(sbNw, (uint32_t)nw_phase);                          // norm_f
   nw_phase ^= 1;
   // final norm (norm_f) and the greedy head
-  block_norm(P, P.h, P.res + (P.n_layer & 1) * kDModel, nullptr, Nw + (P.n_layer & 1) * kDModel, -1, hn, misc);
+  block_norm(P, P.h, P.res + (P.n_layer & 1) * kDModel, nullptr, Nw, -1, hn, misc);
   if (step + 1 < P.steps && tid == 0) {                          // next token's layer-0 norm weight
     asm volatile("fence.proxy.async;" ::: "memory");
     mb_expect(sbNw, kDModel * 2);
