@@ -396,7 +396,11 @@ def main():
         d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
         def timed(run):
-            run(4)
+            # warm-up: two full-length launches, also letting the SM clocks recover from the
+            # power-capped GEMM loop just before (a 4-token warm-up left the first timed launch
+            # ~15% slow)
+            for _ in range(2):
+                run(args.decode_steps)
             torch.cuda.synchronize()
             d0.record(s)
             run(args.decode_steps)
