@@ -145,6 +145,13 @@ def cpu_sample(tokens=512, layers=2, vocab_slice=32768, seed=0):
     return per_token, dict(tokens=tokens, layers=layers, vocab_slice=vocab_slice, seconds=t2 - t0)
 
 
+def workload_config(world, B=WINDOWS_PER_GPU, T=SEQLEN):
+    """The workload description both arms report (the reference arm on the same config)."""
+    return dict(workload='config4: 56-layer 8B scoring, FP4-G16 weights, SQ3.25 state, Resurface soft',
+                windows_per_gpu=B, seq_len=T, global_batch=world * B, vocab=VOCAB,
+                parallelism=f'dp{world} (window-sharded, one NLL all-reduce)', l2='inputs larger than L2')
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -159,8 +166,7 @@ def run_reference(args, rank, world):
     line = dict(metric=METRIC, value=v, unit=UNIT, n_gpus=args.gpus, steps=len(vals), warmup=args.warmup_ref,
                 ms_per_step=None, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='f32',
                 data='synthetic', impl='reference',
-                config=dict(workload='config4: 56-layer 8B scoring, 16 x 2049-token Zipf windows per GPU',
-                            windows_per_gpu=WINDOWS_PER_GPU, seq_len=SEQLEN, vocab=VOCAB),
+                config=workload_config(max(world, args.gpus)),
                 cpu_baseline=dict(value=v, unit=UNIT, cores=os.cpu_count(), kind='port',
                                   sample=f"oracle port, 1 window x {info['tokens']} tokens through {info['layers']} "
                                          f"layers + lm_head/CE over a {info['vocab_slice']}-row vocab slice, "
@@ -431,9 +437,7 @@ def main():
             metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
             ms_per_step=elapsed / args.steps * 1e3, higher_is_better=True, scaling='weak', vs_baseline=None,
             dtype='fp16 (fp32 accumulate)', data='synthetic',
-            config=dict(workload='config4: 56-layer 8B scoring, FP4-G16 weights, SQ3.25 state, Resurface soft',
-                        windows_per_gpu=B, seq_len=T, global_batch=world * B, vocab=VOCAB,
-                        parallelism=f'dp{world} (window-sharded, one NLL all-reduce)', l2='inputs larger than L2'),
+            config=workload_config(world, B, T),
             e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h),
             roofline=dict(bound='tensor', kernel='tcgen05 in_proj GEMM (M=%d,N=18560,K=4096)' % (B * T),
                           achieved=achieved, peak=pk['tf'], unit='TFLOP/s', frac=achieved / pk['tf'], traffic=GEMM_TRAFFIC_BYTES,
