@@ -835,7 +835,7 @@ __device__ __forceinline__ float gate_partial(const uint16_t* Us, const uint16_t
 // Resurface adapter + gated RMSNorm for one token, warp w = norm group w: the
 // resurface_gatednorm_kernel arithmetic with one group per CTA (head mix on the tensor
 // cores, correction, x = y * silu(z), RMSNorm over 1024 channels).  The gate partials were
-// computed earlier (gpart[8]); V (staged after the scan) and y sit in shared memory.
+// computed earlier (gpart[8]); V (staged one layer ahead) and y sit in shared memory.
 __device__ void resurface_norm(const DecodeParams& P, const DecLayer& L, const float* gpart, const uint16_t* Ys,
                                const uint16_t* Vs, const uint16_t* Gs, const uint16_t* Ns, uint16_t* zout, int layer) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
