@@ -126,12 +126,11 @@ def cpu_sample(tokens=512, layers=2, vocab_slice=32768, seed=0):
     `vocab_slice`-row slice of the vocabulary, all host threads.  Returns seconds per
     scored token extrapolated to 56 layers and the full 256000-row head.  The oracle model
     is built once per process and reused by later samples."""
-    sys.path.insert(0, str(ROOT / 'tests'))
-    from _models import build_pair
+    from oracle.pair import build_pair
     torch.set_num_threads(os.cpu_count())
     key = (layers, vocab_slice, seed)
     if key not in _CPU_MODELS:
-        _CPU_MODELS[key] = build_pair(n_layer=layers, vocab=vocab_slice, seed=seed, adapter=True, device='cpu')[1]
+        _CPU_MODELS[key] = build_pair(n_layer=layers, vocab=vocab_slice, seed=seed, adapter=True, device=None)[1]
     ora = _CPU_MODELS[key]
     rng = np.random.default_rng(seed)
     ids = zipf_tokens(tokens + 1, rng, vocab=vocab_slice)[None]

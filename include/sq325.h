@@ -74,6 +74,26 @@ typedef struct sq_scan_args {
 } sq_scan_args;
 int64_t sq_scan_workspace(int batch, int length, int heads, int groups, int layout);
 int sq_scan(const sq_scan_args* args, void* stream);
+/* The causal depthwise conv of StateQuant._convolution (mamba2_recall/state_quant.py:283-317)
+ * fused in front of the scan, as PredictorState._forward runs them
+ * (fp4_zero_predictor_codec_v1.py:341-352).  x / B / C of `args` point at the RAW in_proj
+ * xBC columns (channel h*dim+p, 8192+g*128+n, 9216+g*128+n; heads*dim = 8192 and
+ * groups*128 = 1024), and the conv output feeds the scan without a round trip.
+ * position == 0: prefill of `length` tokens from a reset (zero) ring, conv1d numerics
+ * (fp32 accumulate + bias, one fp16 rounding, SiLU); the ring receives the last four raw
+ * columns.  position > 0 requires length == 1: the one-token step numerics (fp16
+ * products summed, fp16, + bias, SiLU) over the three previous raw columns in the ring
+ * plus this token's, which replaces slot position % 4.  A continuing multi-token prefill
+ * is not fused (SQ_EINVAL).  args->workspace selects the two-kernel path as in sq_scan
+ * (prefill only). */
+typedef struct sq_conv_args {
+  const uint16_t* weight;     /* [10240,4] fp16 = conv1d.weight[:,0,:] */
+  const uint16_t* bias;       /* [10240] fp16 */
+  uint16_t* ring;             /* [batch][4][10240] fp16, slot = absolute position % 4 */
+  int64_t ring_batch_stride;  /* elements, >= 4*10240 */
+  int32_t position;           /* tokens this request consumed before the call */
+} sq_conv_args;
+int sq_scan_conv(const sq_scan_args* args, const sq_conv_args* conv, void* stream);
 
 /* ---------------------------------------------------------------- standalone codec
  * decode: rows (b,h,p) of the six PackedState buffers (mamba2_recall/state_codec.py:29-48,
@@ -104,6 +124,8 @@ int sq_fp4_decode(const uint8_t* codes, const uint8_t* block_scales, const float
  * m <= 64 runs the packed skinny-GEMM kernel (no workspace); larger m decodes into
  * `workspace` (>= sq_fp4_linear_workspace(m,n,k) bytes) and runs the tcgen05 GEMM. */
 int64_t sq_fp4_linear_workspace(int m, int n, int k);
+/* Asynchronous on `stream`.  A bounded device wait that expires (the context stays usable)
+ * sets this device's sticky error word, which sq_device_check() reports and clears. */
 int sq_fp4_linear(const uint8_t* codes, const uint8_t* block_scales, const float* global_scale,
                   int n, int k, const uint16_t* x, int64_t ldx, int m, uint16_t* y, int64_t ldy,
                   void* workspace, int64_t workspace_bytes, void* stream);
@@ -113,7 +135,8 @@ int sq_fp4_linear(const uint8_t* codes, const uint8_t* block_scales, const float
  * the device and can fail mid-run).  Same result as sq_fp4_linear; for m > 64 the decoded
  * weight rows are staged, in chunks of whole 256-row tiles, in a static device array of
  * SQ_FP4_LINEAR_STATIC_STAGE_BYTES inside this library, so k <= 32768 there
- * (sq_fp4_linear_static_max_k()); larger k returns SQ_EINVAL.
+ * (sq_fp4_linear_static_max_k()); larger k returns SQ_EINVAL, and so do row strides
+ * ldx < k or ldy < n (checked before any work, leaving y untouched).
  * The first call on each device does set-up (resolves the array's address, which may load
  * the module, and sets kernel attributes): make it before any stream capture.  The call is
  * synchronous on `stream`.  The array is shared by all callers in the process: calls that
@@ -123,9 +146,16 @@ int64_t sq_fp4_linear_static_max_k(void);
 int sq_fp4_linear_static(const uint8_t* codes, const uint8_t* block_scales, const float* global_scale,
                          int n, int k, const uint16_t* x, int64_t ldx, int m, uint16_t* y, int64_t ldy,
                          void* stream);
-/* tcgen05 fp16 GEMM C[m,n] = A[m,k] . B[n,k]^T (fp32 accumulate), k % 64 == 0. */
+/* tcgen05 fp16 GEMM C[m,n] = A[m,k] . B[n,k]^T (fp32 accumulate), k % 64 == 0.
+ * Asynchronous; expired waits are reported by sq_device_check(). */
 int sq_gemm_f16(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb,
                 uint16_t* c, int64_t ldc, int m, int n, int k, void* stream);
+/* Synchronises `stream`, then reads and clears the current device's error word of the
+ * standalone entry points above (sq_fp4_linear, sq_gemm_f16): SQ_ETIMEOUT if a bounded
+ * device-side wait of one of their kernels expired since the last check.  The model
+ * runtime has its own word (sq_model_check).  The reference reports no such condition
+ * (its GEMMs are cuBLAS calls); this replaces nothing. */
+int sq_device_check(void* stream);
 
 /* ---------------------------------------------------------------- model runtime
  * A native replacement for PredictorState (fp4_zero_predictor_codec_v1.py:239-367) driving
@@ -201,6 +231,13 @@ int sq_model_check(sq_model* model, void* stream);
  * in the model's greedy workspace.  Same tokens and states as sq_model_forward +
  * sq_model_greedy per step. */
 int sq_model_decode(sq_model* model, int64_t* tokens, int pos, int steps, int64_t* out_tokens, void* stream);
+/* Inspection (the role of the reference's per-layer forward hooks, e.g. the Resurface
+ * capture hooks of mamba2_recall/resurface_native.py:168-169): when `out` is non-NULL every
+ * later sq_model_forward with batch*tokens <= rows also copies each layer's mixer output
+ * (the out_proj result the Block adds to the residual) to out + layer*rows*4096, fp16
+ * [rows, 4096] per layer.  NULL turns it off.  The persistent decode kernel does not
+ * capture. */
+int sq_model_set_capture(sq_model* model, uint16_t* out, int64_t rows);
 /* Numerics of the one-token decode-step projections and of the greedy head (at most 64
  * rows).  exact = 0 (default): the exact fp16 products E2M1*E4M3 enter the tensor-core
  * product and the fp32 global scale multiplies each fp32 output once (factored scale), the

@@ -49,17 +49,23 @@ def build(force=False, verbose=False, ptxas_info=False):
                     '--expt-relaxed-constexpr']
     if ptxas_info:
         flags += ['-Xptxas', '-v']
-    objs = []
-    for src in SOURCES:
+    def compile_one(src):
         obj = objdir / (src + '.o')
         cmd = [cc, '-c', str(CSRC / src), '-o', str(obj)] + flags
         if verbose:
             print(' '.join(cmd), flush=True)
-        r = subprocess.run(cmd, capture_output=True, text=True)
+        return src, obj, subprocess.run(cmd, capture_output=True, text=True)
+
+    # translation units compile independently: one nvcc process per source
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=max(1, min(len(SOURCES), os.cpu_count() or 1))) as pool:
+        results = list(pool.map(compile_one, SOURCES))
+    objs = []
+    for src, obj, r in results:
         if r.returncode != 0:
             raise RuntimeError(f'nvcc failed for {src}:\n{r.stdout}\n{r.stderr}')
         if ptxas_info and r.stderr:
-            print(r.stderr, file=sys.stderr)
+            print(f'== {src}\n{r.stderr}', file=sys.stderr)
         objs.append(str(obj))
     tmp = OUT.with_suffix('.so.tmp')
     cmd = [cc, '-shared', '-o', str(tmp)] + objs + ARCH + ['-lcudart']

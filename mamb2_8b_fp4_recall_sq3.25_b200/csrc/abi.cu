@@ -4,6 +4,7 @@
 #include <atomic>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -15,6 +16,10 @@
 #include "scan.cuh"
 
 namespace sq {
+cudaError_t& last_launch_error() {
+  static thread_local cudaError_t e = cudaSuccess;
+  return e;
+}
 int launch_decode_rows(int layout, int batch, int heads, int dim, int groups, const uint8_t* lo,
                        const uint8_t* hi, const uint8_t* q4, const uint8_t* latent, const uint16_t* s8,
                        const uint16_t* s4, const uint16_t* latent_scale, float* tiers, float* z, cudaStream_t st);
@@ -35,6 +40,8 @@ int fail(int code, const std::string& msg) {
 }
 int cuda_fail(const char* what) {
   cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = last_launch_error();     // a launcher already consumed it
+  last_launch_error() = cudaSuccess;
   return fail(SQ_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 int check(int st, const char* what) {
@@ -53,6 +60,29 @@ bool aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
 constexpr int kDModel = 4096, kDInner = 8192, kXbc = 10240, kZx = 18560, kHeads = 128, kHeadDim = 64,
               kGroups = 8;
 constexpr int kLmChunk = 32768;    // lm_head rows decoded per staging pass
+
+// Device error word of the standalone entry points (sq_fp4_linear, sq_gemm_f16), one per
+// device, allocated on the first call made with that device current.  Kernels whose
+// bounded waits expire OR a bit into it; it stays set until sq_device_check() reads and
+// clears it.
+constexpr int kMaxDevices = 64;
+std::mutex g_err_mutex;
+int* g_dev_err[kMaxDevices] = {};
+
+int device_error_word(int** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cuda_fail("cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(SQ_EINVAL, "device ordinal >= 64");
+  std::lock_guard<std::mutex> lock(g_err_mutex);
+  if (!g_dev_err[dev]) {
+    int* p = nullptr;
+    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return cuda_fail("cudaMalloc (error word)");
+    if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) { cudaFree(p); return cuda_fail("cudaMemset (error word)"); }
+    g_dev_err[dev] = p;
+  }
+  *out = g_dev_err[dev];
+  return SQ_OK;
+}
 
 }  // namespace
 
@@ -81,6 +111,8 @@ struct sq_model {
   int dec_grid = 0;
   int* d_err = 0;
   size_t stage_elems = 0;
+  uint16_t* capture = nullptr;                // per-layer mixer outputs [n_layer][capture_rows][4096]
+  long long capture_rows = 0;
   std::atomic<int> busy{0};
 };
 
@@ -142,7 +174,9 @@ int64_t sq_scan_workspace(int batch, int length, int heads, int groups, int layo
   return scan_prep_bytes(batch, length, heads, groups, layout);
 }
 
-int sq_scan(const sq_scan_args* a, void* stream) {
+namespace {
+// Checks the pointer contract of sq_scan_args and fills the kernel parameter block.
+int scan_params(const sq_scan_args* a, ScanParams& P) {
   if (!a) return fail(SQ_EINVAL, "null scan args");
   const void* req[] = {a->x, a->dt, a->A, a->B, a->C, a->D, a->dt_bias, a->permutation, a->basis,
                        a->latent_scale, a->predictor, a->lo, a->hi, a->q4, a->latent, a->s8, a->s4, a->y};
@@ -151,7 +185,7 @@ int sq_scan(const sq_scan_args* a, void* stream) {
   const void* st16[] = {a->lo, a->hi, a->q4, a->latent, a->s8, a->s4, a->permutation, a->basis, a->predictor};
   for (const void* p : st16)
     if (!aligned(p, 16)) return fail(SQ_EINVAL, "scan: state buffers and static tables must be 16-byte aligned");
-  ScanParams P{};
+  P = ScanParams{};
   P.batch = a->batch; P.length = a->length; P.heads = a->heads; P.dim = a->dim; P.groups = a->groups;
   P.layout = a->layout;
   P.x = a->x; P.x_sb = a->x_batch_stride; P.x_st = a->x_token_stride;
@@ -169,7 +203,31 @@ int sq_scan(const sq_scan_args* a, void* stream) {
       return fail(SQ_EINVAL, "scan: workspace smaller than sq_scan_workspace() or not 256-byte aligned");
     scan_prep_bind(P, a->workspace);
   }
+  return SQ_OK;
+}
+}  // namespace
+
+int sq_scan(const sq_scan_args* a, void* stream) {
+  ScanParams P;
+  if (int s = scan_params(a, P)) return s;
   return check(launch_scan(P, (cudaStream_t)stream), "sq_scan");
+}
+
+int sq_scan_conv(const sq_scan_args* a, const sq_conv_args* c, void* stream) {
+  if (!c || !c->weight || !c->bias || !c->ring) return fail(SQ_EINVAL, "scan_conv: null conv argument");
+  ScanParams P;
+  if (int s = scan_params(a, P)) return s;
+  if (P.heads * P.dim + 2 * P.groups * 128 != kXbc)
+    return fail(SQ_EINVAL, "scan_conv: heads*dim + 2*groups*128 must equal the 10240 conv channels");
+  if (!aligned(c->ring, 16) || c->ring_batch_stride % 8 || c->ring_batch_stride < 4LL * kXbc)
+    return fail(SQ_EINVAL, "scan_conv: ring must be 16-byte aligned with a batch stride >= 4*10240 (multiple of 8)");
+  if (c->position < 0 || (c->position > 0 && P.length != 1))
+    return fail(SQ_EINVAL, "scan_conv: position 0 (prefill from a reset ring) or a one-token step (position > 0)");
+  P.conv_mode = c->position == 0 ? 1 : 2;
+  if (P.conv_mode == 2) P.prep_bc = nullptr, P.prep_pv = nullptr, P.prep_ddt = nullptr;   // one-token step kernel
+  P.conv_w = c->weight; P.conv_b = c->bias; P.conv_cache = c->ring; P.conv_pos = c->position;
+  P.conv_cache_sb = c->ring_batch_stride;
+  return check(launch_scan(P, (cudaStream_t)stream), "sq_scan_conv");
 }
 
 int sq_state_decode(int layout, int batch, int heads, int dim, int groups, const uint8_t* lo, const uint8_t* hi,
@@ -206,13 +264,11 @@ int sq_fp4_linear(const uint8_t* codes, const uint8_t* block_scales, const float
   if (!codes || !block_scales || !global_scale || !x || !y) return fail(SQ_EINVAL, "fp4_linear: null pointer");
   if (m <= 0 || n <= 0 || k <= 0 || k % 128) return fail(SQ_EINVAL, "fp4_linear: k must be a positive multiple of 128");
   if (!aligned(codes, 16) || !aligned(x, 16)) return fail(SQ_EINVAL, "fp4_linear: misaligned buffers");
+  if (ldx < k || ldy < n) return fail(SQ_EINVAL, "fp4_linear: row strides must satisfy ldx >= k and ldy >= n");
   Fp4Weight w{codes, block_scales, global_scale, n, k};
   cudaStream_t st = (cudaStream_t)stream;
-  static int* d_err = nullptr;
-  if (!d_err) {
-    if (cudaMalloc(&d_err, sizeof(int)) != cudaSuccess) return cuda_fail("cudaMalloc");
-    cudaMemset(d_err, 0, sizeof(int));
-  }
+  int* d_err = nullptr;
+  if (int s = device_error_word(&d_err)) return s;
   if (m <= 64) {
     if (k % 256 == 0 && aligned(block_scales, 16) && aligned(x, 16) && ldx % 8 == 0)
       return check(launch_fp4_gemv_stream(w, nullptr, x, ldx, m, y, ldy, d_err, st), "fp4 gemv");
@@ -228,16 +284,23 @@ int sq_fp4_linear(const uint8_t* codes, const uint8_t* block_scales, const float
 int sq_gemm_f16(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, uint16_t* c, int64_t ldc, int m,
                 int n, int k, void* stream) {
   if (!a || !b || !c) return fail(SQ_EINVAL, "gemm: null pointer");
-  static int* d_err = nullptr;
-  if (!d_err) {
-    if (cudaMalloc(&d_err, sizeof(int)) != cudaSuccess) return cuda_fail("cudaMalloc");
-    cudaMemset(d_err, 0, sizeof(int));
-  }
-  SQ_TRY(launch_gemm_f16(a, lda, b, ldb, c, ldc, m, n, k, 0, nullptr, d_err, (cudaStream_t)stream), "tcgen05 gemm");
-  cudaStreamSynchronize((cudaStream_t)stream);
+  int* d_err = nullptr;
+  if (int s = device_error_word(&d_err)) return s;
+  return check(launch_gemm_f16(a, lda, b, ldb, c, ldc, m, n, k, 0, nullptr, d_err, (cudaStream_t)stream),
+               "tcgen05 gemm");
+}
+
+int sq_device_check(void* stream) {
+  if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return cuda_fail("stream synchronize");
+  int* d_err = nullptr;
+  if (int s = device_error_word(&d_err)) return s;
   int h = 0;
-  cudaMemcpy(&h, d_err, sizeof(int), cudaMemcpyDeviceToHost);
-  if (h) { cudaMemset(d_err, 0, sizeof(int)); return fail(SQ_ETIMEOUT, "tcgen05 gemm: device wait expired"); }
+  if (cudaMemcpy(&h, d_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return cuda_fail("read error word");
+  if (h) {
+    if (cudaMemset(d_err, 0, sizeof(int)) != cudaSuccess) return cuda_fail("clear error word");
+    return fail(SQ_ETIMEOUT, "device: a bounded wait of sq_fp4_linear / sq_gemm_f16 expired (code " +
+                                 std::to_string(h) + ")");
+  }
   return SQ_OK;
 }
 
@@ -418,6 +481,10 @@ int sq_model_forward(sq_model* m, const int64_t* ids, int batch, int tokens, int
                                       m->cfg.eps, m->yn, M, st), "resurface + gated norm");
     s = linear(m, L.out_proj, &m->out_maps[l], m->yn, kDInner, M, m->h, kDModel, !step || m->exact_skinny, st);
     if (s != SQ_OK) return s;
+    if (m->capture && M <= m->capture_rows &&
+        cudaMemcpyAsync(m->capture + (size_t)l * m->capture_rows * kDModel, m->h, (size_t)M * kDModel * 2,
+                        cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+      return cuda_fail("forward: layer capture copy");
   }
   SQ_TRY(launch_add_rmsnorm(m->h, m->res, 1, m->norm_f, m->cfg.eps, hidden_out, M, kDModel, st), "norm_f");
   return SQ_OK;
@@ -550,6 +617,14 @@ int sq_model_decode(sq_model* m, int64_t* tokens, int pos, int steps, int64_t* o
   P.pos = pos;
   P.steps = steps;
   SQ_TRY(launch_decode_step(P, m->dec_grid, (cudaStream_t)stream), "persistent decode");
+  return SQ_OK;
+}
+
+int sq_model_set_capture(sq_model* m, uint16_t* out, int64_t rows) {
+  if (!m || (out && rows <= 0)) return fail(SQ_EINVAL, "set_capture: bad arguments");
+  if (out && !aligned(out, 16)) return fail(SQ_EINVAL, "set_capture: buffer must be 16-byte aligned");
+  m->capture = out;
+  m->capture_rows = out ? rows : 0;
   return SQ_OK;
 }
 

@@ -106,7 +106,7 @@ int launch_decode_rows(int layout, int batch, int heads, int dim, int groups,
   decode_rows_kernel<<<(unsigned)((rows + th - 1) / th), th, 0, st>>>(
       kLayouts[layout].n8, kLayouts[layout].n4, rows, heads, dim, heads / groups,
       lo, hi, q4, latent, s8, s4, latent_scale, tiers, z);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 int launch_encode_rows(int layout, int batch, int heads, int dim, int groups, int mode,
@@ -121,7 +121,7 @@ int launch_encode_rows(int layout, int batch, int heads, int dim, int groups, in
   encode_rows_kernel<<<(unsigned)((rows + th - 1) / th), th, 0, st>>>(
       kLayouts[layout].n8, kLayouts[layout].n4, rows, heads, dim, heads / groups, mode,
       tiers, z, latent_scale, lo, hi, q4, latent, s8, s4);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 }  // namespace sq

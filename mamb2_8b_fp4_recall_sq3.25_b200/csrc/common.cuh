@@ -59,4 +59,15 @@ __device__ __forceinline__ void stage16(void* smem_dst, const void* gsrc, int by
 // Bounded mbarrier / flag waits: every spin has an iteration limit.
 constexpr uint32_t kSpinLimit = 1u << 26;
 
+// The CUDA error of the calling thread's last failed launch (abi.cu).  Launchers consume
+// the runtime's sticky-free launch error with cudaGetLastError(); recording it here lets
+// the C-ABI report the real cause instead of "no error".
+cudaError_t& last_launch_error();
+inline int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return kOk;
+  last_launch_error() = e;
+  return kECuda;
+}
+
 }  // namespace sq

@@ -1241,7 +1241,9 @@ int launch_decode_step(const DecodeParams& p, int grid, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, decode_step_kernel, p) == cudaSuccess ? kOk : kECuda;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_step_kernel, p);
+  if (e != cudaSuccess) { cudaGetLastError(); last_launch_error() = e; return kECuda; }
+  return kOk;
 }
 
 }  // namespace sq

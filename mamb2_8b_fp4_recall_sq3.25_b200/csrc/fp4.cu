@@ -390,7 +390,7 @@ int gemv_stream(const Fp4Weight& W, const Fp4Maps* maps, const uint16_t* X, long
   }
   fp4_gemv_stream_kernel<MT, EXACT><<<grid, 32 * (1 + kGvConsumers), smem, st>>>(
       maps->codes, maps->scales, W.global_scale, W.rows, W.cols, KC, X, ldx, M, Y, ldy, err);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 template <int MT>
@@ -403,7 +403,7 @@ int gemv_mt(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_
   } else {
     fp4_gemv_kernel<MT, 4><<<grid, 128, 0, st>>>(W.codes, W.scales, W.global_scale, W.rows, W.cols, X, ldx, M, Y, ldy);
   }
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 }  // namespace
@@ -414,13 +414,13 @@ int launch_fp4_decode(const Fp4Weight& W, uint16_t* out, long long ldo, cudaStre
   const int th = 256;
   fp4_decode_kernel<<<(unsigned)((n + th - 1) / th), th, 0, st>>>(W.codes, W.scales, W.global_scale, W.rows,
                                                                    W.cols, out, ldo);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 int launch_fp4_embed(const Fp4Weight& E, const long long* ids, int ntok, uint16_t* out, int* err, cudaStream_t st) {
   if (E.cols % 16 || ntok <= 0) return kEInval;
   fp4_embed_kernel<<<ntok, 256, 0, st>>>(E.codes, E.scales, E.global_scale, E.rows, E.cols, ids, ntok, out, err);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 bool make_fp4_maps(const Fp4Weight& W, Fp4Maps* maps) {

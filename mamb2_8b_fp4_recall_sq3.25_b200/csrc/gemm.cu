@@ -389,7 +389,7 @@ int launch_gemm_f16(const uint16_t* A, long long lda, const uint16_t* B, long lo
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < g_num_sms ? tiles : g_num_sms;
   tc_gemm_kernel<<<grid, 192, smem, st>>>(ma, mb, a);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 }  // namespace sq

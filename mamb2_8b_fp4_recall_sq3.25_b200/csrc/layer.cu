@@ -345,7 +345,7 @@ int launch_add_rmsnorm(const uint16_t* h, uint16_t* res, int has_res, const uint
                        uint16_t* out, int rows, int D, cudaStream_t st) {
   if (rows <= 0 || D % 8 || D > 8192) return kEInval;
   add_rmsnorm_kernel<<<rows, 256, 0, st>>>(h, res, has_res, w, eps, out, D);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 int launch_conv_prefill(const uint16_t* raw, long long raw_sb, long long raw_st, int B, int L, int C,
@@ -355,7 +355,7 @@ int launch_conv_prefill(const uint16_t* raw, long long raw_sb, long long raw_st,
   dim3 grid((C + 255) / 256, (L + kConvChunk - 1) / kConvChunk, B);
   conv_prefill_kernel<<<grid, 256, 0, st>>>(raw, raw_sb, raw_st, B, L, C, w, bias, cache, cache_sb, pos0, out,
                                             out_sb, out_st);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 template <int GPB>
@@ -373,7 +373,7 @@ int launch_rg(const uint16_t* y, const uint16_t* z, long long z_st, const uint16
   if (!y) return kOk;                                // prepare-only call
   dim3 grid(8 / GPB, ty);
   resurface_gatednorm_kernel<GPB><<<grid, 32 * GPB, smem, st>>>(y, z, z_st, u, u_st, a, has_ad, norm_w, eps, out, T);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 int prepare_layer_kernels() {
@@ -408,13 +408,13 @@ int launch_ce_finalize(const float2* partials, int ntiles, const float* tlogit, 
                        cudaStream_t st) {
   if (rows <= 0 || ntiles <= 0) return kEInval;
   ce_finalize_kernel<<<(rows + 7) / 8, 256, 0, st>>>(partials, ntiles, tlogit, rows, nll);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 int launch_window_sum(const float* nll, int windows, int per, const int* counts, double* out, cudaStream_t st) {
   if (windows <= 0 || per <= 0) return kEInval;
   window_sum_kernel<<<windows, 256, 0, st>>>(nll, per, counts, out);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 int argmax_workspace_bytes(int rows, int V) {
@@ -429,7 +429,7 @@ int launch_argmax(const uint16_t* logits, int rows, int V, long long ld, long lo
   int* pi = reinterpret_cast<int*>(pv + rows * ns);
   argmax_partial_kernel<<<dim3(ns, rows), 256, 0, st>>>(logits, V, ld, pv, pi, ns);
   argmax_final_kernel<<<rows, 32, 0, st>>>(pv, pi, ns, out);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 }  // namespace sq

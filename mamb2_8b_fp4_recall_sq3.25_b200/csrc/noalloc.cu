@@ -61,7 +61,10 @@ int scratch_for_current_device(unsigned char** out) {
 int launch_error(int st, const char* what) {
   if (st == kOk) return SQ_OK;
   if (st == kECuda) {
-    std::string msg = std::string(what) + ": " + cudaGetErrorString(cudaGetLastError());
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = last_launch_error();   // the launcher consumed it and recorded it
+    last_launch_error() = cudaSuccess;
+    std::string msg = std::string(what) + ": " + cudaGetErrorString(e);
     return set_last_error(SQ_ECUDA, msg.c_str());
   }
   return set_last_error(st, (std::string(what) + ": invalid arguments").c_str());
@@ -81,6 +84,10 @@ int sq_fp4_linear_static(const uint8_t* codes, const uint8_t* block_scales, cons
     return set_last_error(SQ_EINVAL, "fp4_linear_static: k must be a positive multiple of 128");
   if (((uintptr_t)codes % 16) || ((uintptr_t)x % 16))
     return set_last_error(SQ_EINVAL, "fp4_linear_static: misaligned buffers");
+  // Row strides are checked here, before any chunk runs: the chunked GEMM below sees only
+  // `rows` output columns per launch, so it cannot catch ldy < n itself.
+  if (ldx < k || ldy < n)
+    return set_last_error(SQ_EINVAL, "fp4_linear_static: row strides must satisfy ldx >= k and ldy >= n");
   if (m > 64 && k > sq_fp4_linear_static_max_k())
     return set_last_error(SQ_EINVAL,
                           "fp4_linear_static: k exceeds the static scratch (256 decoded rows of k fp16 must fit "

@@ -847,7 +847,7 @@ int launch_chunked(const ScanParams& P, bool prepare_only, cudaStream_t stream) 
   kp<<<gp, 256, prep_smem, stream>>>(P);
   dim3 gc(P.heads / (128 / P.dim), P.batch);
   kc<<<gc, 128, chunk_smem, stream>>>(P);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 template <int N8, int N4, int KJ, int MODE, int TC = (MODE == 2 ? 1 : kTC)>
@@ -864,7 +864,7 @@ int launch_kj(const ScanParams& P, int hpc, cudaStream_t stream) {
   if (hpc == 0) return kOk;                         // prepare-only call (attributes set, no launch)
   dim3 grid(P.heads / hpc, P.batch);
   kern<<<grid, hpc * P.dim, smem, stream>>>(P);
-  return cudaGetLastError() == cudaSuccess ? kOk : kECuda;
+  return launch_status();
 }
 
 template <int N8, int N4>

@@ -42,6 +42,10 @@ class ScanArgs(C.Structure):
                 ('workspace', p), ('workspace_bytes', i64)]
 
 
+class ConvArgs(C.Structure):
+    _fields_ = [('weight', p), ('bias', p), ('ring', p), ('ring_batch_stride', i64), ('position', i32)]
+
+
 class ModelConfig(C.Structure):
     _fields_ = [('n_layer', i32), ('vocab', i32), ('eps', C.c_float)]
 
@@ -64,17 +68,20 @@ _PROTOS = {
     'sq_layout_counts': (C.c_int, [C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     'sq_state_bytes': (i64, [C.c_int, C.c_int, C.c_int]),
     'sq_scan': (C.c_int, [C.POINTER(ScanArgs), p]),
+    'sq_scan_conv': (C.c_int, [C.POINTER(ScanArgs), C.POINTER(ConvArgs), p]),
     'sq_state_decode': (C.c_int, [C.c_int] * 5 + [p] * 9 + [p]),
     'sq_state_encode': (C.c_int, [C.c_int] * 6 + [p] * 9 + [p]),
     'sq_fp4_decode': (C.c_int, [p, p, p, C.c_int, C.c_int, p, i64, p]),
     'sq_scan_workspace': (i64, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
     'sq_model_set_exact_skinny': (C.c_int, [p, C.c_int]),
+    'sq_model_set_capture': (C.c_int, [p, p, i64]),
     'sq_model_decode': (C.c_int, [p, p, C.c_int, C.c_int, p, p]),
     'sq_fp4_linear_workspace': (i64, [C.c_int, C.c_int, C.c_int]),
     'sq_fp4_linear': (C.c_int, [p, p, p, C.c_int, C.c_int, p, i64, C.c_int, p, i64, p, i64, p]),
     'sq_fp4_linear_static_max_k': (i64, []),
     'sq_fp4_linear_static': (C.c_int, [p, p, p, C.c_int, C.c_int, p, i64, C.c_int, p, i64, p]),
     'sq_gemm_f16': (C.c_int, [p, i64, p, i64, p, i64, C.c_int, C.c_int, C.c_int, p]),
+    'sq_device_check': (C.c_int, [p]),
     'sq_model_create': (C.c_int, [C.POINTER(ModelConfig), C.POINTER(p)]),
     'sq_model_destroy': (C.c_int, [p]),
     'sq_model_set_layer': (C.c_int, [p, C.c_int, C.POINTER(LayerDesc)]),

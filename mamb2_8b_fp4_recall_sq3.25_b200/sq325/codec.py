@@ -180,6 +180,67 @@ def scan(x, dt, A, B, C_, D, dt_bias, state, permutation, basis, latent_scale, p
 
 
 @torch.no_grad()
+def scan_with_conv(xbc, dt, A, D, dt_bias, state, permutation, basis, latent_scale, predictor, conv_weight,
+                   conv_bias, conv_ring, position, *, layout, fused=False):
+    """Causal conv + codec scan in one pass (the conv of mamba2_recall/state_quant.py:283-317
+    followed by `scan`, as PredictorState._forward runs them, :341-352).
+
+    xbc fp16 [batch, L, 10240] holds the RAW in_proj xBC columns (x | B | C); dt fp16
+    [batch, L, 128].  conv_ring fp16 [batch, 4, 10240] is the conv cache in ring order (slot
+    = absolute position % 4).  position == 0 runs a prefill from a reset ring (conv1d
+    numerics); position > 0 with L == 1 runs the one-token step numerics.  Mutates `state`
+    and `conv_ring`; returns (y fp16 [batch, L, 128, 64], None)."""
+    spec = layout_descriptor(layout)
+    if xbc.ndim != 3 or xbc.dtype != torch.float16 or not xbc.is_cuda or xbc.shape[2] != 10240 or \
+            xbc.stride(2) != 1:
+        raise ValueError('xbc must be CUDA FP16 [batch,tokens,10240] with unit channel stride')
+    batch, length, _ = xbc.shape
+    heads, dim, groups = 128, 64, 8
+    if state.shape != (batch, heads, dim, 128):
+        raise ValueError('Positive sequence and matching latent state required')
+    validate_state(state, xbc.device, layout)
+    if tuple(conv_ring.shape) != (batch, 4, 10240) or conv_ring.dtype != torch.float16 or \
+            not conv_ring.is_contiguous() or conv_ring.device != xbc.device:
+        raise ValueError('conv_ring must be contiguous CUDA FP16 [batch,4,10240]')
+    if tuple(conv_weight.shape) != (10240, 4) or tuple(conv_bias.shape) != (10240,) or \
+            conv_weight.dtype != torch.float16 or conv_bias.dtype != torch.float16:
+        raise ValueError('conv weight [10240,4] and bias [10240] must be FP16')
+    if type(position) is not int or position < 0 or (position > 0 and length != 1):
+        raise ValueError('position 0 (prefill from a reset ring) or a one-token step required')
+    if tuple(dt.shape) != (batch, length, heads) or dt.dtype != torch.float16:
+        raise ValueError('dt must be FP16 [batch,tokens,128]')
+    dt, A, D, dt_bias, permutation, basis, latent_scale, predictor, conv_weight, conv_bias = (
+        v.contiguous() for v in (dt, A, D, dt_bias, permutation, basis, latent_scale, predictor, conv_weight,
+                                 conv_bias))
+    y = torch.empty((batch, length, heads, dim), device=xbc.device, dtype=torch.float16)
+    a = _lib.ScanArgs()
+    a.batch, a.length, a.heads, a.dim, a.groups, a.layout = batch, length, heads, dim, groups, layout_index(layout)
+    sb, st = xbc.stride(0), xbc.stride(1)
+    base = xbc.data_ptr()
+    a.x, a.x_batch_stride, a.x_token_stride = base, sb, st
+    a.B, a.b_batch_stride, a.b_token_stride = base + 8192 * 2, sb, st
+    a.C, a.c_batch_stride, a.c_token_stride = base + 9216 * 2, sb, st
+    a.dt, a.dt_batch_stride, a.dt_token_stride = dt.data_ptr(), length * heads, heads
+    a.A = A.data_ptr()
+    a.D, a.d_is_f32 = D.data_ptr(), int(D.dtype == torch.float32)
+    a.dt_bias, a.dt_bias_is_f32 = dt_bias.data_ptr(), int(dt_bias.dtype == torch.float32)
+    a.permutation, a.basis, a.latent_scale, a.predictor = (permutation.data_ptr(), basis.data_ptr(),
+                                                           latent_scale.data_ptr(), predictor.data_ptr())
+    t = state.tensors
+    a.lo, a.hi, a.q4, a.latent, a.s8, a.s4 = (t[k].data_ptr() for k in ('lo', 'hi', 'q4', 'latent', 's8', 's4'))
+    a.y, a.y_batch_stride, a.y_token_stride = y.data_ptr(), length * heads * dim, heads * dim
+    ws = None
+    if not fused and position == 0:
+        need = _lib.load().sq_scan_workspace(batch, length, heads, groups, layout_index(layout))
+        ws = torch.empty(need, device=xbc.device, dtype=torch.uint8)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), need
+    c = _lib.ConvArgs(conv_weight.data_ptr(), conv_bias.data_ptr(), conv_ring.data_ptr(), 4 * 10240, position)
+    with torch.cuda.device(xbc.device):
+        _lib.call('sq_scan_conv', C.byref(a), C.byref(c), _lib.stream_ptr())
+    return y, None
+
+
+@torch.no_grad()
 def decode_state(state, latent_scale, *, layout):
     """Packed rows -> (tiers fp32 [B,H,P,n8+n4] in tier order, z fp32 [B,H,P,2])."""
     spec = layout_descriptor(layout)

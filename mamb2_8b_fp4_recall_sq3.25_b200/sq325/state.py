@@ -302,6 +302,20 @@ class PredictorState:
             e.tokens += steps
         return out
 
+    def capture_layers(self, rows):
+        """Record every layer's mixer output during later backbone calls of at most `rows`
+        tokens (batch * tokens): returns the fp16 [n_layer, rows, 4096] buffer that each
+        forward fills.  capture_layers(0) turns it off."""
+        if not self._installed:
+            raise RuntimeError('Controller is not installed')
+        if rows <= 0:
+            _lib.call('sq_model_set_capture', self._handle, None, 0)
+            self._capture = None
+            return None
+        self._capture = torch.empty((self.model.n_layer, rows, D_MODEL), device=self.device, dtype=torch.float16)
+        _lib.call('sq_model_set_capture', self._handle, _lib.ptr(self._capture), rows)
+        return self._capture
+
     def check(self):
         """Synchronise and raise if a device-side check failed (bad token id, expired wait)."""
         _lib.call('sq_model_check', self._handle, _lib.stream_ptr())

@@ -255,20 +255,24 @@ def predictor_correction(C, permutation, predictor, layout):
 # ---------------------------------------------------------------- the scan
 
 def latent_scan(x, dt, A, B, C, D, dt_bias, state, permutation, basis, latent_scale,
-                predictor, layout, corr=None):
+                predictor, layout, corr=None, head_groups=None):
     """One call of the production codec over L tokens; mutates ``state``; returns y fp16.
 
     x fp16 [Bt,L,H,P]; dt fp16 [Bt,L,H]; A fp32 [H]; B, C fp16 [Bt,L,G,128];
     D, dt_bias fp16/fp32 [H]; permutation u8 [G,128]; basis f16 [G,nz,2];
     latent_scale f16 [G,2]; predictor f16 [G,n8+n4+2,nz].
+
+    Rows are independent given their group's B/C (the reference runs one program per
+    (batch, head, 16-row tile)), so a subset of heads can be checked on its own:
+    `head_groups` (int [H]) then gives the group of each head passed in x / dt / A / D /
+    dt_bias / state; by default head h belongs to group h // (H / G).
     """
     n8, n4, nz = layout_counts(layout)
     R8, R4, RZ = next_pow2(n8), next_pow2(n4), next_pow2(nz)
     x = np.asarray(x, np.float16)
     Bt, L, H, P = x.shape
     G = np.asarray(B).shape[2]
-    hg = H // G
-    gidx = np.arange(H) // hg
+    gidx = np.arange(H) // (H // G) if head_groups is None else np.asarray(head_groups, np.int64)
     if corr is None:
         corr = predictor_correction(C, permutation, predictor, layout)
     corr = np.asarray(corr, np.float32)

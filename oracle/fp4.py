@@ -46,16 +46,27 @@ def pack(codes):
     return (c[:, 0::2] | (c[:, 1::2] << 4)).astype(np.uint8)
 
 
+# value pair of every code byte: (low nibble = even column, high nibble = odd column)
+_PAIR_VALUES = np.stack((np.where(np.arange(256) & 8, -1, 1) * E2M1[np.arange(256) & 7],
+                         np.where((np.arange(256) >> 4) & 8, -1, 1) * E2M1[(np.arange(256) >> 4) & 7]),
+                        -1).astype(np.float32)
+
+
 def decode(codes_packed, block_scale_bytes, global_scale, cols=None):
-    """-> fp16 [rows, cols], bit-exact with the reference decode."""
-    p = np.asarray(codes_packed, np.uint8)
+    """-> fp16 [rows, cols], bit-exact with the reference decode.
+
+    Same three roundings as the reference (fp4.py:151-154): code * block is exact in
+    fp32, the product with the fp32 global rounds once to fp32, then once to fp16.  Runs
+    as torch CPU table lookups and elementwise products (multi-threaded)."""
+    import torch
+    p = torch.from_numpy(np.ascontiguousarray(codes_packed, np.uint8))
     rows = p.shape[0]
     cols = cols or p.shape[1] * 2
-    codes = unpack(p, cols)
-    blocks = E4M3_VALUES[np.asarray(block_scale_bytes, np.uint8)]          # [rows, cols/16]
-    vals = (e2m1_values(codes).reshape(rows, -1, 16) * blocks[:, :, None]).astype(np.float32)
-    vals = (vals * np.float32(global_scale)).astype(np.float32)
-    return vals.reshape(rows, cols).astype(np.float16)
+    pairs = torch.from_numpy(_PAIR_VALUES)[p.long()].reshape(rows, -1)[:, :cols]        # [rows, cols] fp32
+    blocks = torch.from_numpy(E4M3_VALUES)[torch.from_numpy(np.ascontiguousarray(block_scale_bytes, np.uint8)).long()]
+    vals = (pairs.reshape(rows, -1, 16) * blocks[:, :, None]).reshape(rows, cols)
+    vals = vals * torch.tensor(np.float32(global_scale), dtype=torch.float32)
+    return vals.half().numpy()
 
 
 def synthetic_matrix(rows, cols, rng, mu=-4.0, sigma=0.5, row_mu=None):
@@ -63,7 +74,9 @@ def synthetic_matrix(rows, cols, rng, mu=-4.0, sigma=0.5, row_mu=None):
     `row_mu` (optional, [rows]) overrides mu per output row."""
     codes = rng.integers(0, 256, size=(rows, cols // 2), dtype=np.uint8)
     mus = mu if row_mu is None else np.asarray(row_mu, np.float64)[:, None]
-    eff = np.exp(mus + sigma * rng.standard_normal(size=(rows, cols // 16))).astype(np.float32)
+    import torch
+    eff = torch.from_numpy(mus + sigma * rng.standard_normal(size=(rows, cols // 16))).exp().float().numpy()
     g = np.float32(eff.max() / 448.0)
-    blocks = f32_to_e4m3((eff / g).astype(np.float32))
+    # torch's RNE + saturating float8_e4m3fn cast (equal to f32_to_e4m3 on this range)
+    blocks = torch.from_numpy((eff / g).astype(np.float32)).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
     return codes, blocks, g

@@ -112,6 +112,8 @@ class LayerOracle:
         self.D, self.dt_bias, self.gnorm_w = D, dt_bias, gnorm_w
         self.layout, self.perm, self.basis, self.latent_scale, self.predictor = layout, perm, basis, latent_scale, predictor
         self.adapter = adapter           # None or (V, g, w, b, hard)
+        # the codec restatement: numpy (oracle.codec) or its bit-identical C form (oracle.cscan)
+        self.scan = oc.latent_scan
 
 
 def layer_forward(L, cache, u16, tokens_before):
@@ -128,9 +130,9 @@ def layer_forward(L, cache, u16, tokens_before):
     x = xbc[..., :D_INNER].reshape(B, T, HEADS, HEAD_DIM)
     Bm = xbc[..., D_INNER:D_INNER + 1024].reshape(B, T, GROUPS, 128)
     Cm = xbc[..., D_INNER + 1024:].reshape(B, T, GROUPS, 128)
-    y = oc.latent_scan(x.numpy(), dt.contiguous().numpy(), L.A.numpy(), Bm.numpy(), Cm.numpy(),
-                       L.D.numpy(), L.dt_bias.numpy(), cache['state'], L.perm.numpy(), L.basis.numpy(),
-                       L.latent_scale.numpy(), L.predictor.numpy(), L.layout)
+    y = L.scan(x.numpy(), dt.contiguous().numpy(), L.A.numpy(), Bm.numpy(), Cm.numpy(),
+               L.D.numpy(), L.dt_bias.numpy(), cache['state'], L.perm.numpy(), L.basis.numpy(),
+               L.latent_scale.numpy(), L.predictor.numpy(), L.layout)
     y = torch.from_numpy(y).reshape(B * T, D_INNER)
     if L.adapter is not None:
         V, g, w, b, hard = L.adapter
@@ -140,10 +142,15 @@ def layer_forward(L, cache, u16, tokens_before):
 
 
 class ModelOracle:
-    def __init__(self, embed16, head16, norm_f, layers, eps=1e-5):
+    def __init__(self, embed16, head16, norm_f, layers, eps=1e-5, fast_scan=True):
         self.embed16, self.head16, self.norm_f, self.layers, self.eps = embed16, head16, norm_f, layers, eps
+        if fast_scan:
+            from . import cscan
+            for L in layers:
+                L.scan = cscan.latent_scan
         self.caches = None
         self.tokens = 0
+        self.capture = None          # a list receives every layer's mixer output when set
 
     def reset(self, batch):
         self.caches = [dict(state=oc.allocate_state(batch, HEADS, HEAD_DIM, L.layout),
@@ -159,6 +166,8 @@ class ModelOracle:
             res = hcur if res is None else add16(hcur, res)
             u = rmsnorm(res, L.norm_w, self.eps)
             hcur = layer_forward(L, cache, u, self.tokens)
+            if self.capture is not None:
+                self.capture.append(hcur.clone())
         res = add16(hcur, res)
         self.tokens += T
         return rmsnorm(res, self.norm_f, self.eps)

@@ -2,7 +2,7 @@
 """Regenerate the golden vectors in this directory from the reference's own code.
 
 Runs ONLY in the build container, where the reference tree is mounted (path
-given by --reference, default /root/reference). The GPU box never runs it;
+given by the required --reference argument). The GPU box never runs it;
 tests read the committed .npz files.
 
 What is recorded
@@ -175,7 +175,8 @@ def adapter_case(reference, seed=11):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument('--reference', type=Path, default=Path('/root/reference'))
+    ap.add_argument('--reference', type=Path, required=True,
+                    help='root of a checkout of the reference repository (read only)')
     args = ap.parse_args()
     ref = install_shims(args.reference)
     layouts = ('32_32_64', '16_64_48', '8_80_40', '24_48_56', '36_24_68', '40_16_72', '44_8_76')

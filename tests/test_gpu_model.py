@@ -18,6 +18,11 @@ def pair():
     return build_pair(n_layer=2, vocab=512, seed=1, adapter=True)
 
 
+@pytest.fixture(scope='module')
+def hard_pair():
+    return build_pair(n_layer=2, vocab=512, seed=3, adapter=True, hard=True)
+
+
 def _ids(rng, B, T, vocab):
     return rng.integers(0, vocab, (B, T)).astype(np.int64)
 
@@ -206,4 +211,64 @@ def test_persistent_decode_split_calls_match_one_call(pair):
             outs.append((seq.cpu(), [e.state.tensors['lo'].clone() for e in ex._cache]))
     assert torch.equal(outs[0][0], outs[1][0])
     for a, b in zip(outs[0][1], outs[1][1]):
+        assert torch.equal(a, b)
+
+
+def test_hard_gate_prefill_and_decode(hard_pair):
+    """Resurface with the hard (threshold) gate (resurface_native.py:112-115): prefill hidden
+    state, window NLL and decode steps against the oracle's hard-gate adapter."""
+    from sq325 import PredictorState
+    gm, ora, statics = hard_pair
+    assert gm.adapter.gate_mode == 'hard'
+    rng = np.random.default_rng(17)
+    B, T = 2, 24
+    ids = _ids(rng, B, T + 1, gm.vocab)
+    with PredictorState(gm, *statics) as ex:
+        hid = ex.backbone(torch.from_numpy(ids[:, :-1]).cuda(), reset=True)
+        nll = ex.score(hid, torch.from_numpy(ids[:, 1:]).cuda())
+        torch.cuda.synchronize()
+        ex.check()
+        ora.reset(B)
+        href = ora.backbone(ids[:, :-1])
+        nref = ora.nll(href, ids[:, 1:])
+        assert rel_l2(hid.float(), href.float()) < 2e-2
+        got = nll.double().cpu().view(B, T).sum(1)
+        assert torch.allclose(got, nref.view(B, T).sum(1), rtol=NLL_RTOL, atol=0)
+        for _ in range(3):
+            nxt = rng.integers(0, gm.vocab, (B, 1)).astype(np.int64)
+            h = ex.backbone(torch.from_numpy(nxt).cuda())
+            assert rel_l2(h.float(), ora.backbone(nxt).float()) < 3e-2
+
+
+def test_persistent_decode_matches_graph_replay_full_size():
+    """The benchmarked size: 56 layers (released layouts), vocabulary 256,000, 16 greedy tokens
+    after a 64-token prompt.  The one-launch persistent kernel and the multi-kernel CUDA-graph
+    replay must give identical tokens, identical packed states and conv rings, and identical
+    logits of the last step."""
+    from sq325 import model as M, resurface as R
+    from sq325.state import PredictorState
+    model = M.synthetic_model(seed=4, n_layer=56, vocab=256000, device='cuda')
+    model.adapter = R.random_bank(56, seed=5, device='cuda')
+    statics = M.synthetic_statics(M.RELEASED_LAYOUTS, seed=4, device='cuda')
+    prompt = torch.from_numpy(np.random.default_rng(77).integers(0, 256000, (1, 64))).cuda()
+    runs = {}
+    for persistent in (False, True):
+        with PredictorState(model, *statics) as ex:
+            tok = ex.greedy(ex.backbone(prompt, reset=True)[:, -1]).clone()
+            if persistent:
+                seq = ex.decode_persistent(tok, 16)
+            else:
+                ex.capture_decode(tok)
+                seq = ex.replay_decode(16)
+            torch.cuda.synchronize()
+            ex.check()
+            states = [{k: v.view(torch.uint8).clone() for k, v in e.state.tensors.items()} for e in ex._cache]
+            rings = [ex.conv_chronological(l).clone() for l in range(56)]
+            runs[persistent] = (seq.cpu(), states, rings)
+            del ex
+    assert torch.equal(runs[True][0], runs[False][0]), (runs[True][0].ravel(), runs[False][0].ravel())
+    for layer, (a, b) in enumerate(zip(runs[True][1], runs[False][1])):
+        for k in a:
+            assert torch.equal(a[k], b[k]), (layer, k)
+    for a, b in zip(runs[True][2], runs[False][2]):
         assert torch.equal(a, b)

@@ -1,0 +1,222 @@
+"""GPU parity of the production scan kernels at the model's geometry (128 heads x 64 rows,
+8 groups, batch 16) against the CPU oracle (oracle.codec.latent_scan, pinned bit-exact to
+the reference kernel scripts/fp4_zero_predictor_codec_v1.py:76-181 run by the Triton
+interpreter).
+
+Covered paths, all through the C-ABI:
+  chunk   sq_scan with a workspace: scan_prep_kernel + ssu_chunk_kernel (the scoring path)
+  fused   sq_scan without a workspace: ssu_sq325_kernel
+  conv1   sq_scan_conv at position 0: the causal conv1d prefill fused in front of the scan
+          (chunk and fused variants; mamba2_recall/state_quant.py:305-317)
+  conv2   sq_scan_conv at position > 0: the one-token decode step with the conv step
+          numerics (state_quant.py:291-297)
+
+The oracle is the C restatement (oracle/csrc/latent_scan.c, bit-exact with the numpy
+restatement and the reference goldens).  Rows are independent given their group's B/C,
+so it checks every row of three batch entries (first, middle, last) of the full-geometry
+GPU run.
+
+Bar (the same as against the reference kernel's golden vectors): >= 99% of fp16 readouts
+bit-identical and all within rtol 2e-2 / atol 2e-2; >= 99% of requantised INT8 and INT4
+codes identical and none more than one code step apart.  Residual differences come from
+CUDA's expf/logf and FMA contraction against numpy's unfused fp32 (a code that straddles a
+half-integer moves by one step and feeds later tokens).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import codec as oc
+from oracle import cscan
+from oracle import model as om
+
+pytestmark = pytest.mark.gpu
+
+H, P, G = 128, 64, 8
+HEADS_CHECKED = np.arange(H)
+BATCH_CHECKED = np.array([0, 7, 15])
+Y_RTOL, Y_ATOL = 2e-2, 2e-2
+
+
+def _inputs(layout, B, L, seed, raw_xbc=False):
+    """Seeded host inputs (numpy) of one scan call at model geometry."""
+    rng = np.random.default_rng(seed)
+    n8, n4, nz = oc.layout_counts(layout)
+    d = dict(
+        dt=(rng.standard_normal((B, L, H)) * 0.5).astype(np.float16),
+        A=-(rng.random(H) * 3 + 0.1).astype(np.float32),
+        D=rng.standard_normal(H).astype(np.float16),
+        dt_bias=(rng.random(H) * 3 - 4).astype(np.float16),
+        permutation=np.stack([rng.permutation(128) for _ in range(G)]).astype(np.uint8),
+        basis=rng.standard_normal((G, nz, 2)).astype(np.float16),
+        latent_scale=(rng.random((G, 2)) + 0.1).astype(np.float16),
+        predictor=(rng.standard_normal((G, n8 + n4 + 2, nz)) / np.sqrt(n8 + n4 + 2)).astype(np.float16))
+    if raw_xbc:
+        d['xbc'] = rng.standard_normal((B, L, 10240)).astype(np.float16)
+        d['conv_w'] = (0.5 * rng.standard_normal((10240, 4))).astype(np.float16)
+        d['conv_b'] = (0.1 * rng.standard_normal(10240)).astype(np.float16)
+    else:
+        d['x'] = rng.standard_normal((B, L, H, P)).astype(np.float16)
+        d['B'] = rng.standard_normal((B, L, G, 128)).astype(np.float16)
+        d['C'] = rng.standard_normal((B, L, G, 128)).astype(np.float16)
+    st = oc.allocate_state(B, H, P, layout)
+    for k in ('lo', 'hi', 'q4'):
+        st[k][...] = rng.integers(0, 256, st[k].shape, dtype=np.uint8)
+    for k in ('s8', 's4'):
+        st[k][...] = (rng.random(st[k].shape) * 0.05).astype(np.float16)
+    st['latent'][...] = oc.f32_to_e4m3(rng.standard_normal(st['latent'].shape).astype(np.float32) * 8)
+    return d, st
+
+
+def _gpu_state(st, layout):
+    from sq325 import codec
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)).cuda() for k, v in st.items()}
+    t['latent'] = t['latent'].view(torch.float8_e4m3fn)
+    b, h, p = st['s8'].shape
+    return codec.PackedState('latent_fp8_' + layout, t, (b, h, p, 128))
+
+
+def _host_state(ps):
+    return {k: (v.view(torch.uint8) if v.dtype == torch.float8_e4m3fn else v).cpu().numpy()
+            for k, v in ps.tensors.items()}
+
+
+def _subset_state(st, bsel):
+    return {k: np.ascontiguousarray(v[bsel][:, HEADS_CHECKED]) for k, v in st.items()}
+
+
+def _oracle(d, st, layout, bsel, x=None, Bm=None, Cm=None):
+    """Oracle scan over the checked heads of batch entries `bsel`; returns (y, state)."""
+    x = d['x'] if x is None else x
+    Bm = d['B'] if Bm is None else Bm
+    Cm = d['C'] if Cm is None else Cm
+    sub = _subset_state(st, bsel)
+    y = cscan.latent_scan(x[bsel][:, :, HEADS_CHECKED], d['dt'][bsel][:, :, HEADS_CHECKED], d['A'][HEADS_CHECKED],
+                       Bm[bsel], Cm[bsel], d['D'][HEADS_CHECKED], d['dt_bias'][HEADS_CHECKED], sub,
+                       d['permutation'], d['basis'], d['latent_scale'], d['predictor'], layout,
+                       head_groups=HEADS_CHECKED // (H // G))
+    return y, sub
+
+
+def _assert_parity(y_gpu, st_gpu, y_ref, st_ref, layout, bsel, what):
+    y = np.ascontiguousarray(y_gpu[bsel][:, :, HEADS_CHECKED])
+    ident = float((y.view(np.uint16) == y_ref.view(np.uint16)).mean())
+    assert np.allclose(y.astype(np.float32), y_ref.astype(np.float32), rtol=Y_RTOL, atol=Y_ATOL), \
+        (what, float(np.abs(y.astype(np.float32) - y_ref.astype(np.float32)).max()))
+    assert ident >= 0.99, (what, ident)
+    sg = _subset_state(st_gpu, bsel)
+    q8, q4 = oc.decode_codes(sg, layout)
+    r8, r4 = oc.decode_codes(st_ref, layout)
+    a8, a4 = float((q8 == r8).mean()), float((q4 == r4).mean())
+    assert a8 >= 0.99 and a4 >= 0.99, (what, a8, a4)
+    assert np.abs(q8 - r8).max() <= 1 and np.abs(q4 - r4).max() <= 1, what
+    return ident, a8, a4
+
+
+def _T(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize('layout', oc.LAYOUTS)
+@pytest.mark.parametrize('length', [8, 37, 128])
+def test_scan_paths_match_oracle_at_model_geometry(layout, length):
+    from sq325 import codec
+    B = 16
+    d, st = _inputs(layout, B, length, seed=1000 + 7 * length + oc.LAYOUTS.index(layout))
+    bsel = BATCH_CHECKED
+    y_ref, st_ref = _oracle(d, st, layout, bsel)
+    args = [_T(d[k]) for k in ('x', 'dt', 'A', 'B', 'C', 'D', 'dt_bias')]
+    tables = [_T(d[k]) for k in ('permutation', 'basis', 'latent_scale', 'predictor')]
+    for fused in (False, True):
+        ps = _gpu_state(st, layout)
+        y, _ = codec.scan(*args, ps, *tables, layout=layout, fused=fused)
+        torch.cuda.synchronize()
+        _assert_parity(y.cpu().numpy(), _host_state(ps), y_ref, st_ref, layout, bsel,
+                       ('fused' if fused else 'chunk', layout, length))
+
+
+def _conv_prefill_oracle(d, B):
+    """conv1d prefill from a reset ring (state_quant.py:305-317) on the raw xBC columns."""
+    xbc, ring = om.conv_prefill(torch.from_numpy(d['xbc']), torch.zeros(B, 10240, 4, dtype=torch.float16), 0,
+                                torch.from_numpy(d['conv_w']), torch.from_numpy(d['conv_b']))
+    return xbc.numpy(), ring.numpy()
+
+
+def _split_xbc(xbc):
+    Bn, L = xbc.shape[:2]
+    return (xbc[..., :8192].reshape(Bn, L, H, P), xbc[..., 8192:9216].reshape(Bn, L, G, 128),
+            xbc[..., 9216:].reshape(Bn, L, G, 128))
+
+
+@pytest.mark.parametrize('layout', oc.LAYOUTS)
+@pytest.mark.parametrize('length', [3, 37])
+def test_conv_prefill_scan_matches_oracle(layout, length):
+    """Fused conv1d prefill (position 0) + scan: chunk and fused kernels against the oracle's
+    conv1d + scan, and the ring against the last four raw columns."""
+    from sq325 import codec
+    B = 16
+    d, st = _inputs(layout, B, length, seed=2000 + length + oc.LAYOUTS.index(layout), raw_xbc=True)
+    bsel = BATCH_CHECKED
+    xbc_c, ring_ref = _conv_prefill_oracle(d, B)
+    x, Bm, Cm = _split_xbc(xbc_c)
+    y_ref, st_ref = _oracle(d, st, layout, bsel, x, Bm, Cm)
+    for fused in (False, True):
+        ps = _gpu_state(st, layout)
+        ring = torch.zeros(B, 4, 10240, device='cuda', dtype=torch.float16)
+        y, _ = codec.scan_with_conv(_T(d['xbc']), _T(d['dt']), _T(d['A']), _T(d['D']), _T(d['dt_bias']), ps,
+                                    _T(d['permutation']), _T(d['basis']), _T(d['latent_scale']),
+                                    _T(d['predictor']), _T(d['conv_w']), _T(d['conv_b']), ring, 0, layout=layout,
+                                    fused=fused)
+        torch.cuda.synchronize()
+        _assert_parity(y.cpu().numpy(), _host_state(ps), y_ref, st_ref, layout, bsel,
+                       ('conv1-fused' if fused else 'conv1-chunk', layout, length))
+        # ring slot t % 4 holds raw column t for the last min(4, L) tokens; the rest stay zero
+        chron = ring.cpu()[:, [(length - 4 + k) % 4 for k in range(4)], :].transpose(1, 2).numpy()
+        assert np.array_equal(chron.view(np.uint16), ring_ref.view(np.uint16))
+
+
+@pytest.mark.parametrize('layout', oc.LAYOUTS)
+def test_conv_step_scan_matches_oracle(layout):
+    """One-token decode steps (position > 0, conv step numerics) for four consecutive
+    positions, so every ring slot is written once; state, y and ring against the oracle."""
+    from sq325 import codec
+    B, steps, pos0 = 16, 4, 9
+    rng = np.random.default_rng(3000 + oc.LAYOUTS.index(layout))
+    d, st = _inputs(layout, B, 1, seed=3100 + oc.LAYOUTS.index(layout), raw_xbc=True)
+    bsel = BATCH_CHECKED
+    ring_np = rng.standard_normal((B, 4, 10240)).astype(np.float16)        # ring slot = position % 4
+    ring = _T(ring_np)
+    ps = _gpu_state(st, layout)
+    st_o = _subset_state(st, bsel)
+    chron = np.ascontiguousarray(ring_np[:, [(pos0 - 4 + k) % 4 for k in range(4)], :].transpose(0, 2, 1))
+    cache = torch.from_numpy(chron)
+    tables = [_T(d[k]) for k in ('permutation', 'basis', 'latent_scale', 'predictor')]
+    for s in range(steps):
+        raw = rng.standard_normal((B, 1, 10240)).astype(np.float16)
+        dt = (rng.standard_normal((B, 1, H)) * 0.5).astype(np.float16)
+        y, _ = codec.scan_with_conv(_T(raw), _T(dt), _T(d['A']), _T(d['D']), _T(d['dt_bias']), ps, *tables,
+                                    _T(d['conv_w']), _T(d['conv_b']), ring, pos0 + s, layout=layout)
+        torch.cuda.synchronize()
+        out, cache = om.conv_step(torch.from_numpy(raw[:, 0]), cache, torch.from_numpy(d['conv_w']),
+                                  torch.from_numpy(d['conv_b']))
+        x, Bm, Cm = _split_xbc(out.numpy()[:, None])
+        y_ref = cscan.latent_scan(x[bsel][:, :, HEADS_CHECKED], dt[bsel][:, :, HEADS_CHECKED], d['A'][HEADS_CHECKED],
+                               Bm[bsel], Cm[bsel], d['D'][HEADS_CHECKED], d['dt_bias'][HEADS_CHECKED], st_o,
+                               d['permutation'], d['basis'], d['latent_scale'], d['predictor'], layout,
+                               head_groups=HEADS_CHECKED // (H // G))
+        _assert_parity(y.cpu().numpy(), _host_state(ps), y_ref, st_o, layout, bsel, ('conv2', layout, s))
+        got = ring.cpu()[:, [(pos0 + s - 3 + k) % 4 for k in range(4)], :].transpose(1, 2).numpy()
+        assert np.array_equal(got.view(np.uint16), cache.numpy().view(np.uint16)), s
+
+
+def test_scan_conv_rejects_continuing_prefill():
+    """A multi-token call at position > 0 is not fused (the model runs the conv separately)."""
+    from sq325 import codec
+    layout = '32_32_64'
+    d, st = _inputs(layout, 1, 2, seed=5, raw_xbc=True)
+    ps = _gpu_state(st, layout)
+    ring = torch.zeros(1, 4, 10240, device='cuda', dtype=torch.float16)
+    with pytest.raises(ValueError):
+        codec.scan_with_conv(_T(d['xbc']), _T(d['dt']), _T(d['A']), _T(d['D']), _T(d['dt_bias']), ps,
+                             *[_T(d[k]) for k in ('permutation', 'basis', 'latent_scale', 'predictor')],
+                             _T(d['conv_w']), _T(d['conv_b']), ring, 3, layout=layout)

@@ -144,3 +144,47 @@ def test_adapter_oracle_matches_reference(golden):
         om.HEADS, om.HEAD_DIM = old
     ref = torch.from_numpy(d['out']).reshape_as(out)
     assert torch.allclose(out.float(), ref.float(), rtol=2e-3, atol=2e-3)
+
+
+@pytest.mark.parametrize('layout', oc.LAYOUTS)
+def test_c_restatement_matches_reference_goldens(golden, layout):
+    """oracle/csrc/latent_scan.c (the fast checker) reproduces the reference kernel's golden
+    runs bit for bit: readouts and packed state bytes."""
+    from oracle import cscan
+    d = golden(f'codec_{layout}.npz')
+    for pre in ('scan_', 'ka_'):
+        st = {k: d[pre + 'in_' + k].copy() for k in ('lo', 'hi', 'q4', 'latent', 's8', 's4')}
+        y = cscan.latent_scan(*(d[pre + k] for k in ('x', 'dt', 'A', 'B', 'C', 'D', 'dt_bias')), st,
+                              *(d[pre + k] for k in ('permutation', 'basis', 'latent_scale', 'predictor')), layout)
+        assert np.array_equal(y.view(np.uint16), d[pre + 'y'].view(np.uint16)), pre
+        for k in ('lo', 'hi', 'q4', 's8', 's4'):
+            assert np.array_equal(st[k].view(np.uint8), d[pre + 'out_' + k].view(np.uint8)), (pre, k)
+
+
+@pytest.mark.parametrize('layout', oc.LAYOUTS)
+def test_c_restatement_matches_numpy_restatement(layout):
+    """Random multi-token calls at 32 heads x 64 rows (random packed rows and latents):
+    the C and numpy restatements give identical readouts and state bytes."""
+    from oracle import cscan
+    n8, n4, nz = oc.layout_counts(layout)
+    rng = np.random.default_rng(40 + oc.LAYOUTS.index(layout))
+    B, L, H, P, G = 2, 9, 32, 64, 8
+    args = (rng.standard_normal((B, L, H, P)).astype(np.float16), (rng.standard_normal((B, L, H)) * 0.5).astype(np.float16),
+            -(rng.random(H) * 3 + 0.1).astype(np.float32), rng.standard_normal((B, L, G, 128)).astype(np.float16),
+            rng.standard_normal((B, L, G, 128)).astype(np.float16), rng.standard_normal(H).astype(np.float16),
+            (rng.random(H) * 3 - 4).astype(np.float16))
+    tables = (np.stack([rng.permutation(128) for _ in range(G)]).astype(np.uint8),
+              rng.standard_normal((G, nz, 2)).astype(np.float16), (rng.random((G, 2)) + 0.1).astype(np.float16),
+              (rng.standard_normal((G, n8 + n4 + 2, nz)) / np.sqrt(n8 + n4 + 2)).astype(np.float16))
+    st = oc.allocate_state(B, H, P, layout)
+    for k in ('lo', 'hi', 'q4'):
+        st[k][...] = rng.integers(0, 256, st[k].shape, dtype=np.uint8)
+    for k in ('s8', 's4'):
+        st[k][...] = (rng.random(st[k].shape) * 0.05).astype(np.float16)
+    st['latent'][...] = oc.f32_to_e4m3(rng.standard_normal(st['latent'].shape).astype(np.float32) * 8)
+    st2 = {k: v.copy() for k, v in st.items()}
+    y1 = oc.latent_scan(*args, st, *tables, layout)
+    y2 = cscan.latent_scan(*args, st2, *tables, layout)
+    assert np.array_equal(y1.view(np.uint16), y2.view(np.uint16))
+    for k in st:
+        assert np.array_equal(st[k].view(np.uint8), st2[k].view(np.uint8)), k

@@ -68,3 +68,26 @@ def test_static_rejects_k_beyond_the_scratch():
     torch.cuda.synchronize()
     ref = fp4.linear(w, x[:8])
     assert bool((y[:8] == ref).all())
+
+
+@pytest.mark.parametrize('bad', ['ldy', 'ldx'])
+def test_static_rejects_short_row_strides(bad):
+    """ldy < n (or ldx < k) is refused before any chunk runs: with m > 64 the chunked GEMM sees
+    only one chunk's columns at a time, so it cannot catch a short output stride itself.  The
+    output buffer is sized for the (wrong) strides and must come back untouched."""
+    from sq325 import _lib, fp4
+    lib = _lib.load()
+    m, n, k = 128, 2048, 4096
+    rng = np.random.default_rng(11)
+    codes, blocks, g = of.synthetic_matrix(n, k, rng)
+    w = fp4.from_arrays(codes, blocks, g)
+    ldx = k if bad == 'ldy' else k - 128
+    ldy = n - 256 if bad == 'ldy' else n
+    x = torch.zeros((m, k), device='cuda', dtype=torch.float16)
+    y = torch.full((m * ldy,), 7.0, device='cuda', dtype=torch.float16)
+    rc = lib.sq_fp4_linear_static(_lib.ptr(w.codes), _lib.ptr(w.block_scale_bytes), _lib.ptr(w.global_scale),
+                                  n, k, _lib.ptr(x), ldx, m, _lib.ptr(y), ldy, C.c_void_p(0))
+    assert rc == _lib.SQ_EINVAL
+    assert b'row strides' in lib.sq_last_error()
+    torch.cuda.synchronize()
+    assert bool((y == 7.0).all())
