@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import platform
 import statistics
@@ -39,6 +40,10 @@ UNIT = 'tokens/s'
 WINDOWS_PER_GPU, SEQLEN, VOCAB, N_LAYER = 16, 2048, 256000, 56
 FLOP_PER_TOKEN = 2 * (56 * (18560 * 4096 + 4096 * 8192) + 256000 * 4096)   # 14,369,685,504
 DECODE_BYTES_B1 = 4_111_674_420
+# per decode step: FP4 layers + lm_head + fp16 small tensors + statics; per sequence: state
+# rows r+w + conv ring r+w + embedding row (the per-unit figures of the decode roofline)
+DECODE_FIXED_BYTES, DECODE_PER_SEQ_BYTES = 4_054_786_868, 56_887_552
+FLOP_PER_TOKEN_BACKBONE = 2 * 56 * (18560 * 4096 + 4096 * 8192)                 # prefill, no lm_head
 # dram__bytes_read.sum + dram__bytes_write.sum of one in_proj GEMM launch (M=32768), from
 # one ncu --set full capture of `python bench.py --case gemm --steps 2` on this build.
 GEMM_TRAFFIC_BYTES = 2_715_832_000 + 1_196_445_000
@@ -289,6 +294,156 @@ def run_case(args):
                           layers=args.layers if args.case == 'decode' else None)))
 
 
+L2_FLUSH_BYTES = 256 << 20      # > 126 MB of L2
+
+
+class L2Flush:
+    """Writes a buffer larger than L2 before each timed launch of a small-operand kernel."""
+
+    def __init__(self, device):
+        self.buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+
+    def __call__(self):
+        self.buf.zero_()
+
+
+def timed(call, reps, flush=None, stream=None):
+    """Median CUDA-event seconds of `call` on the current stream, L2 flushed before each."""
+    s = stream or torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ts = []
+    for _ in range(reps):
+        if flush:
+            flush()
+        torch.cuda.synchronize()
+        e0.record(s)
+        call()
+        e1.record(s)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) / 1e3)
+    return statistics.median(ts)
+
+
+@torch.no_grad()
+def measure_config2(device, pk, reps=7):
+    """FP4-G16 projections of one layer (in_proj 4096->18560, out_proj
+    8192->4096) at M = 1, 8, 64, 256 through sq_fp4_linear (the reference's decoded-weight
+    numerics), weights from seed 2; L2 flushed before every timed launch.  Algorithmic bytes
+    = packed weights (0.5625 B/weight + 4) + X + Y; FLOPs = 2 M N K."""
+    from sq325 import fp4 as F
+    gen = torch.Generator(device=device).manual_seed(2)
+    flush = L2Flush(device)
+    rows = []
+    for name, (N, K) in (('in_proj', (18560, 4096)), ('out_proj', (4096, 8192))):
+        w = F.synthetic(N, K, gen, device)
+        for M in (1, 8, 64, 256):
+            x = torch.randn(M, K, device=device, generator=gen).half()
+            call = lambda: F.linear(w, x)
+            for _ in range(3):
+                call()
+            t = timed(call, reps, flush)
+            byts = N * K * 9 // 16 + 4 + M * K * 2 + M * N * 2
+            flop = 2.0 * M * N * K
+            rows.append(dict(proj=name, M=M, us=t * 1e6, gbs=byts / t / 1e9, hbm_frac=byts / t / 1e9 / pk['hbm'],
+                             tflops=flop / t / 1e12, tensor_frac=flop / t / 1e12 / pk['tf'],
+                             path='skinny TMA GEMM (exact fp16 weights)' if M <= 64 else
+                             'fp4 decode + tcgen05 GEMM'))
+        del w
+    return rows
+
+
+@torch.no_grad()
+def measure_config3(device, pk, steps=512, batch=64):
+    """one Mamba-2 mixer layer (layout 32_32_64, no adapter, seed 3) decoding
+    512 one-token steps at batch 64 from a zero SQ3.25 carry, fp16 N(0,1) inputs, the carry
+    requantised every token.  The 512 steps are captured as one CUDA graph (each step: skinny
+    in_proj, fused conv-step + scan, gated norm, skinny out_proj) and replayed; CUDA events.
+    Bytes per step = both projections' packed weights + state rows read and written
+    (52 B x 2) + conv ring read and written + the step's input and output rows."""
+    from sq325 import model as M
+    from sq325.state import PredictorState
+    model = M.synthetic_model(seed=3, n_layer=1, vocab=256, device=device)
+    ex = PredictorState(model, *M.synthetic_statics(('32_32_64',), seed=3, device=device)).install()
+    try:
+        ex.reset(batch)
+        ex.reserve(batch)
+        gen = torch.Generator(device=device).manual_seed(3)
+        u = torch.randn(steps + 1, batch, 1, 4096, device=device, generator=gen).half()
+        out = torch.empty(batch, 1, 4096, device=device, dtype=torch.float16)
+        ex.mixer_forward(0, u[0], out)                      # position 0: prefill path, then one-token steps
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g, stream=side):
+                for i in range(steps):
+                    ex.mixer_forward(0, u[1 + i], out)
+        torch.cuda.current_stream(device).wait_stream(side)
+        g.replay()
+        torch.cuda.synchronize()
+        t = timed(g.replay, 3)
+        ex.check()
+        w = 18560 * 4096 * 9 // 16 + 4 + 4096 * 8192 * 9 // 16 + 4
+        byts = w + batch * 8192 * 52 * 2 + batch * 4 * 10240 * 2 * 2 + batch * 4096 * 2 * 2
+        finite = bool(torch.isfinite(out).all())
+        del g
+    finally:
+        ex.close()
+    return dict(steps=steps, batch=batch, us_per_step=t / steps * 1e6, tokens_per_s=steps * batch / t,
+                bytes_per_step=byts, gbs=byts * steps / t / 1e9, hbm_frac=byts * steps / t / 1e9 / pk['hbm'],
+                output_finite=finite, launches_per_step=4)
+
+
+@torch.no_grad()
+def measure_config5(ex, wins_rng_seed, device, pk, prompt_len=1024, new_tokens=256):
+    """greedy generation on the config-4 model (Resurface on): a 1024-token
+    Zipf prompt, then 256 new tokens, at batch 1 (persistent decode kernel, one launch for
+    all tokens; also the multi-kernel step as CUDA-graph replays, in both projection
+    numerics) and batch 32 (CUDA-graph replays).  Prefill rates count prompt tokens."""
+    rng = np.random.default_rng(wins_rng_seed)
+    prompts = torch.from_numpy(zipf_tokens(32 * prompt_len, rng).reshape(32, prompt_len)).to(device)
+    res = {}
+    roof1 = pk['hbm'] * 1e9 / DECODE_BYTES_B1
+    for batch in (1, 32):
+        p = prompts[:batch].contiguous()
+        ex.backbone(p, reset=True)                                  # warm-up
+        t_pre = timed(lambda: ex.backbone(p, reset=True), 2)
+        h = ex.backbone(p, reset=True)[:, -1]
+        tok = ex.greedy(h).clone()
+        n = new_tokens - 1
+        bytes_step = DECODE_FIXED_BYTES + batch * DECODE_PER_SEQ_BYTES
+        r = dict(prefill_tokens_per_s=batch * prompt_len / t_pre,
+                 prefill_tflops=FLOP_PER_TOKEN_BACKBONE * batch * prompt_len / t_pre / 1e12,
+                 bytes_per_step=bytes_step, roofline_tokens_per_s=batch * pk['hbm'] * 1e9 / bytes_step)
+        if batch == 1:
+            ex.decode_persistent(tok, n)                            # warm-up at full length
+            t = timed(lambda: ex.decode_persistent(tok, n), 1)
+            ex.check()
+            r.update(tokens_per_s=n / t, ms_per_token=t / n * 1e3, frac=(n / t) / roof1, kernel='persistent')
+            ex.capture_decode(tok)
+            ex.replay_decode(n)
+            tg = timed(lambda: ex.replay_decode(n), 1)
+            r['graph_replay_tokens_per_s'] = n / tg
+            ex.set_exact_projections(True)
+            try:
+                ex.capture_decode(tok)
+                ex.replay_decode(8)
+                te = timed(lambda: ex.replay_decode(n), 1)
+            finally:
+                ex.set_exact_projections(False)
+            r['exact_graph_replay_tokens_per_s'] = n / te
+        else:
+            ex.capture_decode(tok)
+            ex.replay_decode(8)
+            t = timed(lambda: ex.replay_decode(n), 1)
+            ex.check()
+            r.update(tokens_per_s=batch * n / t, ms_per_step=t / n * 1e3,
+                     frac=(batch * n / t) / r['roofline_tokens_per_s'], kernel='graph replay')
+        res[f'batch{batch}'] = r
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
@@ -297,7 +452,8 @@ def main():
     ap.add_argument('--impl', default='native', choices=['native', 'reference'])
     ap.add_argument('--ref-tokens', type=int, default=512)
     ap.add_argument('--no-cpu-baseline', action='store_true')
-    ap.add_argument('--decode-steps', type=int, default=32)
+    ap.add_argument('--no-extras', action='store_true',
+                    help='skip the config 2 / 3 / 5 measurements of the one-GPU line')
     ap.add_argument('--case', choices=['gemm', 'scan', 'decode'], default=None,
                     help='time one kernel on a small case (for ncu captures) instead of the bench')
     ap.add_argument('--layout', default='32_32_64', help='scan layout of --case scan')
@@ -322,21 +478,23 @@ def main():
     B, T = WINDOWS_PER_GPU, SEQLEN
     ex.reserve(B * T)
     ids_dev = torch.from_numpy(wins).to(device)
-    inp, tgt = ids_dev[:, :-1].contiguous(), ids_dev[:, 1:].contiguous()
-    hid = torch.empty((B, T, 4096), device=device, dtype=torch.float16)
-    nll = torch.empty(B * T, device=device, dtype=torch.float32)
-    red = torch.zeros(2, device=device, dtype=torch.float64)
+    # The global window list: rank r owns windows r, r + N, r + 2N, ... (the round-robin split
+    # of evaluate_ppl); each rank fills in its own 16 windows, on the device for `value` and
+    # in pinned host memory for `e2e`.  Other ranks' entries are never touched.
+    starts = [(i * world + rank) * (SEQLEN + 1) for i in range(B)]
+    dev_windows = [(0, None)] * (world * B)
+    host_windows = [(0, None)] * (world * B)
+    for i in range(B):
+        dev_windows[i * world + rank] = (starts[i], ids_dev[i])
+        host_windows[i * world + rank] = (starts[i], torch.from_numpy(wins[i]).pin_memory())
 
-    def step():
-        ex.backbone(inp, reset=True, out=hid)
-        ex.score(hid, tgt, out=nll)
-        red[0] = nll.double().sum()
-        red[1] = float(B * T)
-        if world > 1:
-            dist.all_reduce(red)
+    def step(windows):
+        # the public scoring API: local windows batched, one NLL all-reduce (+ the per-window
+        # records gathered on the host) across ranks
+        return scoring.evaluate_ppl(ex, windows, batch_windows=B, rank=rank, world=world)
 
     for _ in range(args.warmup):
-        step()
+        step(dev_windows)
     torch.cuda.synchronize()
     ex.check()
     if world > 1:
@@ -350,7 +508,7 @@ def main():
         dist.barrier()
     e0.record(s)
     for _ in range(args.steps):
-        step()
+        res = step(dev_windows)
     e1.record(s)
     torch.cuda.synchronize()
     if world > 1:
@@ -364,22 +522,20 @@ def main():
     elapsed = float(t)
     tokens_all = world * B * T * args.steps
     value = tokens_all / elapsed
+    assert res['target_tokens'] == world * B * T and len(res['windows']) == world * B and math.isfinite(res['ppl'])
 
-    # e2e through the public scoring API from pinned host windows
-    host_wins = [(i * (SEQLEN + 1), torch.from_numpy(wins[i]).pin_memory()) for i in range(B)]
+    # e2e: the same API from pinned host windows (H2D of the windows and D2H of the NLL sums
+    # inside the timed region, every step)
     h2d = B * (SEQLEN + 1) * 8
     d2h = B * 8
-    scoring.evaluate_ppl(ex, host_wins, batch_windows=B, rank=0, world=1)
+    step(host_windows)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
     e2e_steps = max(1, min(args.steps, 2))
     for _ in range(e2e_steps):
-        res = scoring.evaluate_ppl(ex, host_wins, batch_windows=B, rank=0, world=1)
-        if world > 1:
-            buf = torch.tensor([res['nll'], float(res['target_tokens'])], dtype=torch.float64, device=device)
-            dist.all_reduce(buf)
+        step(host_windows)
     torch.cuda.synchronize()
     e2e_el = time.perf_counter() - t0
     te = torch.tensor([e2e_el], device=device, dtype=torch.float64)
@@ -392,37 +548,21 @@ def main():
     gemm_s, gemm_flop = time_gemm_kernel(model, B * T, device)
     achieved = gemm_flop / gemm_s / 1e12
 
-    # batch-1 decode (greedy generation token step, CUDA-graph replay) on this GPU
+    extras = {}
+    if rank == 0 and world == 1 and not args.no_extras:
+        extras['config5_generation'] = measure_config5(ex, 5, device, pk)
+        extras['config2_fp4_linear'] = measure_config2(device, pk)
+        extras['config3_layer_step'] = measure_config3(device, pk)
     decode = None
-    if rank == 0 and args.decode_steps > 0:
-        prompt = torch.from_numpy(wins[0, :64][None]).to(device)
-        h = ex.backbone(prompt, reset=True)[:, -1]
-        tok = ex.greedy(h).clone()
-        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-
-        def timed(run):
-            # warm-up: two full-length launches, also letting the SM clocks recover from the
-            # power-capped GEMM loop just before (a 4-token warm-up left the first timed launch
-            # ~15% slow)
-            for _ in range(2):
-                run(args.decode_steps)
-            torch.cuda.synchronize()
-            d0.record(s)
-            run(args.decode_steps)
-            d1.record(s)
-            torch.cuda.synchronize()
-            ex.check()
-            return d0.elapsed_time(d1) / 1e3 / args.decode_steps
-
-        dt = timed(lambda n: ex.decode_persistent(tok, n))      # one cooperative launch for n tokens
-        ex.capture_decode(tok)
-        dt_graph = timed(ex.replay_decode)                      # multi-kernel step, CUDA-graph replay
-        roof = pk['hbm'] * 1e9 / DECODE_BYTES_B1
-        decode = dict(tokens_per_s=1.0 / dt, ms_per_token=dt * 1e3, roofline_tokens_per_s=roof,
-                      frac=(1.0 / dt) / roof, bytes_per_token=DECODE_BYTES_B1,
-                      graph_replay_tokens_per_s=1.0 / dt_graph,
-                      note='batch 1, 64-token prompt, persistent kernel (one cooperative launch runs all timed tokens); '
-                           'graph_replay = the multi-kernel step replayed as CUDA graphs')
+    if 'config5_generation' in extras:
+        b1 = extras['config5_generation']['batch1']
+        decode = dict(tokens_per_s=b1['tokens_per_s'], ms_per_token=b1['ms_per_token'],
+                      roofline_tokens_per_s=b1['roofline_tokens_per_s'], frac=b1['frac'],
+                      bytes_per_token=DECODE_BYTES_B1, graph_replay_tokens_per_s=b1['graph_replay_tokens_per_s'],
+                      exact_graph_replay_tokens_per_s=b1['exact_graph_replay_tokens_per_s'],
+                      note='config 5: 1024-token prompt, 255 greedy tokens in one persistent cooperative launch '
+                           '(factored-scale projections, the default for decode steps); graph replays = the '
+                           'multi-kernel step as CUDA graphs, also with the exact per-weight fp16 decode')
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -442,11 +582,11 @@ def main():
                           achieved=achieved, peak=pk['tf'], unit='TFLOP/s', frac=achieved / pk['tf'], traffic=GEMM_TRAFFIC_BYTES,
                           peak_source=pk['src'] + ' bf16_tflops (burst)'),
             step_roofline=dict(flop_per_token=FLOP_PER_TOKEN,
-                               achieved_tflops=FLOP_PER_TOKEN * B * T * world / elapsed * args.steps / 1e12 / world,
+                               achieved_tflops=FLOP_PER_TOKEN * value / world / 1e12,
                                frac=FLOP_PER_TOKEN * value / world / 1e12 / pk['tf_sus']),
             decode_b1=decode, cpu_baseline=cpu, clocks=clk,
-            gpu_launches=launches_per_step(B * T) * args.steps + (1 if world > 1 else 0) * 0,
-            setup_seconds=setup_s)
+            gpu_launches=launches_per_step(B * T) * args.steps,
+            setup_seconds=setup_s, **extras)
         print(json.dumps(line), flush=True)
     ex.close()
     if world > 1:

@@ -95,6 +95,28 @@ typedef struct sq_conv_args {
 } sq_conv_args;
 int sq_scan_conv(const sq_scan_args* args, const sq_conv_args* conv, void* stream);
 
+/* ---------------------------------------------------------------- S16 control scan
+ * Replaces scan(..., state) for the FP16-state mode 's16' of mamba2_recall/state_codec.py
+ * (_s16_scan :65-102, host wrapper :203-262), the reference's control / teacher arm: the
+ * carry fp16 [batch,heads,dim,128] is updated in place (fp32 arithmetic, rounded to fp16
+ * after every token) and y fp16 is written for every token.  Strides as in sq_scan_args.
+ * stats (optional, NULL = off): fp32 [batch,heads,ceil(dim/16),128], per 16-row block the
+ * sum over tokens and rows of |fp16 carry| (collect_stats=True). */
+typedef struct sq_s16_args {
+  int32_t batch, length, heads, dim, groups;
+  const uint16_t* x;  int64_t x_batch_stride, x_token_stride;
+  const uint16_t* dt; int64_t dt_batch_stride, dt_token_stride;
+  const float* A;
+  const uint16_t* B;  int64_t b_batch_stride, b_token_stride;
+  const uint16_t* C;  int64_t c_batch_stride, c_token_stride;
+  const void* D;       int32_t d_is_f32;
+  const void* dt_bias; int32_t dt_bias_is_f32;
+  uint16_t* state;
+  uint16_t* y; int64_t y_batch_stride, y_token_stride;
+  float* stats;
+} sq_s16_args;
+int sq_s16_scan(const sq_s16_args* args, void* stream);
+
 /* ---------------------------------------------------------------- standalone codec
  * decode: rows (b,h,p) of the six PackedState buffers (mamba2_recall/state_codec.py:29-48,
  * fp4_zero_predictor_codec_v1.py:39-49) -> tiers fp32 [rows, n8+n4] in tier order and
@@ -118,6 +140,12 @@ int sq_state_encode(int layout, int batch, int heads, int dim, int groups, int m
  * sq_fp4_decode replaces fp4.decode_packet (mamba2_recall/fp4.py:225-250), bit-exact. */
 int sq_fp4_decode(const uint8_t* codes, const uint8_t* block_scales, const float* global_scale,
                   int rows, int cols, uint16_t* out, int64_t ldo, void* stream);
+/* The content checks of fp4.decode_packet (mamba2_recall/fp4.py:235-249) on the device;
+ * synchronous.  SQ_EINVAL (the reference's ValueError) with its message: "Invalid stored
+ * scale" (a negative or NaN E4M3 block scale), "Nonzero code in a zero-scale group", or
+ * "Nonfinite decoded FP16 weights".  Calls on one device share a flag word: serialise them. */
+int sq_fp4_validate(const uint8_t* codes, const uint8_t* block_scales, const float* global_scale,
+                    int rows, int cols, void* stream);
 /* Y[m,n] = X[m,k] . W[n,k]^T with W decoded exactly on the fly; replaces the FP16
  * nn.Linear calls mx.in_proj / mx.out_proj / model.lm_head
  * (fp4_zero_predictor_codec_v1.py:338,357,360; run_fp4_ridge_resurface_v3.py:107).
@@ -156,6 +184,14 @@ int sq_gemm_f16(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb,
  * runtime has its own word (sq_model_check).  The reference reports no such condition
  * (its GEMMs are cuBLAS calls); this replaces nothing. */
 int sq_device_check(void* stream);
+/* Failure detection: the limit, in nanoseconds, of the skinny-GEMM kernel's pipeline waits
+ * (sq_fp4_linear with m <= 64, the model's decode-step projections and greedy head) on
+ * the current device; 0 restores the default of 2 s.  When a wait reaches the limit the
+ * kernel records an error bit, waits (with the default limit) for its own copies in
+ * flight and returns, leaving the context usable; the call's check (sq_device_check or
+ * sq_model_check) then returns SQ_ETIMEOUT.  Tests set a tiny limit to drive that path;
+ * no reference counterpart (its GEMMs are cuBLAS calls). */
+int sq_set_wait_limit_ns(uint64_t ns);
 
 /* ---------------------------------------------------------------- model runtime
  * A native replacement for PredictorState (fp4_zero_predictor_codec_v1.py:239-367) driving
@@ -212,6 +248,14 @@ int sq_model_reserve(sq_model* model, int max_tokens);
  * [batch*tokens, 4096] after norm_f. */
 int sq_model_forward(sq_model* model, const int64_t* ids, int batch, int tokens, int pos0,
                      uint16_t* hidden_out, void* stream);
+/* One mixer layer, PredictorState._forward (fp4_zero_predictor_codec_v1.py:314-367): u is
+ * the Block's normed input fp16 [batch*tokens, 4096] (what mamba_ssm's Block hands the
+ * mixer), out receives the mixer output fp16 [batch*tokens, 4096].  in_proj -> causal conv
+ * -> SQ3.25 scan (the layer's bound state, advanced in place) -> Resurface -> gated
+ * RMSNorm -> out_proj, with the same kernels and numerics as sq_model_forward.  pos0 is
+ * the number of tokens this layer's state has consumed. */
+int sq_model_mixer_forward(sq_model* model, int layer, const uint16_t* u, int batch, int tokens, int pos0,
+                           uint16_t* out, void* stream);
 /* Scoring head (run_fp4_ridge_resurface_v3.py:105-109): per-row next-token NLL of the
  * fp16 logits lm_head(hidden).float(), computed without materialising the logits. */
 int sq_model_score(sq_model* model, const uint16_t* hidden, int rows, const int64_t* targets,

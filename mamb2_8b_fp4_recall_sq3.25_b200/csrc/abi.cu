@@ -13,6 +13,7 @@
 #include "decode.cuh"
 #include "fp4.cuh"
 #include "layer.cuh"
+#include "s16.cuh"
 #include "scan.cuh"
 
 namespace sq {
@@ -76,8 +77,9 @@ int device_error_word(int** out) {
   std::lock_guard<std::mutex> lock(g_err_mutex);
   if (!g_dev_err[dev]) {
     int* p = nullptr;
-    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return cuda_fail("cudaMalloc (error word)");
-    if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) { cudaFree(p); return cuda_fail("cudaMemset (error word)"); }
+    // [0]: the sticky error word; [1]: per-call flags of sq_fp4_validate
+    if (cudaMalloc(&p, 2 * sizeof(int)) != cudaSuccess) return cuda_fail("cudaMalloc (error word)");
+    if (cudaMemset(p, 0, 2 * sizeof(int)) != cudaSuccess) { cudaFree(p); return cuda_fail("cudaMemset (error word)"); }
     g_dev_err[dev] = p;
   }
   *out = g_dev_err[dev];
@@ -230,6 +232,25 @@ int sq_scan_conv(const sq_scan_args* a, const sq_conv_args* c, void* stream) {
   return check(launch_scan(P, (cudaStream_t)stream), "sq_scan_conv");
 }
 
+int sq_s16_scan(const sq_s16_args* a, void* stream) {
+  if (!a || !a->x || !a->dt || !a->A || !a->B || !a->C || !a->D || !a->dt_bias || !a->state || !a->y)
+    return fail(SQ_EINVAL, "s16_scan: null pointer argument");
+  if (a->batch <= 0 || a->length <= 0 || a->heads <= 0 || a->dim <= 0 || a->groups <= 0 || a->heads % a->groups)
+    return fail(SQ_EINVAL, "heads must be divisible by B/C groups");
+  if (!aligned(a->state, 4)) return fail(SQ_EINVAL, "s16_scan: state must be 4-byte aligned");
+  S16Params P{};
+  P.batch = a->batch; P.length = a->length; P.heads = a->heads; P.dim = a->dim; P.groups = a->groups;
+  P.x = a->x; P.x_sb = a->x_batch_stride; P.x_st = a->x_token_stride;
+  P.dt = a->dt; P.dt_sb = a->dt_batch_stride; P.dt_st = a->dt_token_stride;
+  P.A = a->A;
+  P.B = a->B; P.b_sb = a->b_batch_stride; P.b_st = a->b_token_stride;
+  P.C = a->C; P.c_sb = a->c_batch_stride; P.c_st = a->c_token_stride;
+  P.D = a->D; P.d_is_f32 = a->d_is_f32; P.dt_bias = a->dt_bias; P.dt_bias_is_f32 = a->dt_bias_is_f32;
+  P.state = a->state; P.y = a->y; P.y_sb = a->y_batch_stride; P.y_st = a->y_token_stride;
+  P.stats = a->stats;
+  return check(launch_s16_scan(P, (cudaStream_t)stream), "sq_s16_scan");
+}
+
 int sq_state_decode(int layout, int batch, int heads, int dim, int groups, const uint8_t* lo, const uint8_t* hi,
                     const uint8_t* q4, const uint8_t* latent, const uint16_t* s8, const uint16_t* s4,
                     const uint16_t* latent_scale, float* tiers, float* z, void* stream) {
@@ -254,6 +275,28 @@ int sq_fp4_decode(const uint8_t* codes, const uint8_t* block_scales, const float
   if (!aligned(codes, 4) || !aligned(out, 16)) return fail(SQ_EINVAL, "fp4_decode: misaligned buffers");
   Fp4Weight w{codes, block_scales, global_scale, rows, cols};
   return check(launch_fp4_decode(w, out, ldo, (cudaStream_t)stream), "sq_fp4_decode");
+}
+
+int sq_fp4_validate(const uint8_t* codes, const uint8_t* block_scales, const float* global_scale, int rows, int cols,
+                    void* stream) {
+  if (!codes || !block_scales || !global_scale) return fail(SQ_EINVAL, "fp4_validate: null pointer");
+  if (rows <= 0 || cols <= 0 || cols % 16) return fail(SQ_EINVAL, "fp4_validate: Invalid packet shape");
+  if (!aligned(codes, 8)) return fail(SQ_EINVAL, "fp4_validate: codes must be 8-byte aligned");
+  int* d_err = nullptr;
+  if (int s = device_error_word(&d_err)) return s;
+  int* flags = d_err + 1;                            // per-call flags, cleared on the stream
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(flags, 0, sizeof(int), st) != cudaSuccess) return cuda_fail("fp4_validate: clear flags");
+  Fp4Weight w{codes, block_scales, global_scale, rows, cols};
+  SQ_TRY(launch_fp4_validate(w, flags, st), "fp4_validate");
+  int h = 0;
+  if (cudaMemcpyAsync(&h, flags, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return cuda_fail("fp4_validate: read flags");
+  if (h & 1) return fail(SQ_EINVAL, "Invalid stored scale");
+  if (h & 2) return fail(SQ_EINVAL, "Nonzero code in a zero-scale group");
+  if (h & 4) return fail(SQ_EINVAL, "Nonfinite decoded FP16 weights");   // ValueError, as the reference
+  return SQ_OK;
 }
 
 int64_t sq_fp4_linear_workspace(int m, int n, int k) { return m <= 64 ? 0 : (int64_t)n * k * 2; }
@@ -288,6 +331,10 @@ int sq_gemm_f16(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, 
   if (int s = device_error_word(&d_err)) return s;
   return check(launch_gemm_f16(a, lda, b, ldb, c, ldc, m, n, k, 0, nullptr, d_err, (cudaStream_t)stream),
                "tcgen05 gemm");
+}
+
+int sq_set_wait_limit_ns(uint64_t ns) {
+  return check(set_gemv_wait_limit_ns((unsigned long long)ns), "set_wait_limit");
 }
 
 int sq_device_check(void* stream) {
@@ -432,6 +479,64 @@ struct Busy {
 };
 }  // namespace
 
+namespace {
+// One mixer layer, PredictorState._forward (fp4_zero_predictor_codec_v1.py:314-367): u is the
+// Block's normed input [batch*tokens, 4096]; the result goes to `out` [batch*tokens, 4096].
+// in_proj -> causal conv -> SQ3.25 scan -> Resurface (router on u) -> gated RMSNorm -> out_proj.
+// Workspaces zx / xbc / y / yn / prep / stage are the model's.
+int mixer_forward(sq_model* m, int l, const uint16_t* u, int batch, int tokens, int pos0, uint16_t* out,
+                  cudaStream_t st) {
+  const sq_layer_desc& L = m->layers[l];
+  const sq_model::St& S = m->states[l];
+  const int M = batch * tokens;
+  const bool step = pos0 > 0 && tokens == 1;
+  int s = linear(m, L.in_proj, &m->in_maps[l], u, kDModel, M, m->zx, kZx, !step || m->exact_skinny, st);
+  if (s != SQ_OK) return s;
+  ScanParams P{};
+  P.batch = batch; P.length = tokens; P.heads = kHeads; P.dim = kHeadDim; P.groups = kGroups; P.layout = L.layout;
+  P.dt = m->zx + 2 * kDInner + 2 * 1024; P.dt_sb = (long long)tokens * kZx; P.dt_st = kZx;
+  P.A = L.A; P.D = L.D; P.d_is_f32 = 0; P.dt_bias = L.dt_bias; P.dt_bias_is_f32 = 0;
+  P.perm = L.permutation; P.basis = L.basis; P.latent_scale = L.latent_scale; P.predictor = L.predictor;
+  P.lo = S.lo; P.hi = S.hi; P.q4 = S.q4; P.latent = S.latent; P.s8 = S.s8; P.s4 = S.s4;
+  P.y = m->y; P.y_sb = (long long)tokens * kDInner; P.y_st = kDInner;
+  if (step || pos0 == 0) {
+    // conv fused into the scan: step numerics for a one-token step, conv1d numerics
+    // for a prefill from a reset state
+    const uint16_t* raw = m->zx + kDInner;
+    P.x = raw; P.B = raw + kDInner; P.C = raw + kDInner + 1024;
+    P.x_sb = P.b_sb = P.c_sb = (long long)tokens * kZx; P.x_st = P.b_st = P.c_st = kZx;
+    P.conv_mode = step ? 2 : 1;
+    P.conv_w = L.conv_weight; P.conv_b = L.conv_bias; P.conv_cache = S.ring; P.conv_pos = pos0;
+    P.conv_cache_sb = 4LL * kXbc;
+  } else {
+    SQ_TRY(launch_conv_prefill(m->zx + kDInner, (long long)tokens * kZx, kZx, batch, tokens, kXbc, L.conv_weight,
+                               L.conv_bias, S.ring, 4LL * kXbc, pos0, m->xbc, (long long)tokens * kXbc, kXbc, st),
+           "conv prefill");
+    P.x = m->xbc; P.B = m->xbc + kDInner; P.C = m->xbc + kDInner + 1024;
+    P.x_sb = P.b_sb = P.c_sb = (long long)tokens * kXbc; P.x_st = P.b_st = P.c_st = kXbc;
+  }
+  if (!step) scan_prep_bind(P, m->prep);
+  SQ_TRY(launch_scan(P, st), "ssu scan");
+  const AdapterPtrs& ad = m->adapters[l];
+  SQ_TRY(launch_resurface_gatednorm(m->y, m->zx, kZx, u, kDModel, ad.V ? &ad : nullptr, L.gated_norm_weight,
+                                    m->cfg.eps, m->yn, M, st), "resurface + gated norm");
+  return linear(m, L.out_proj, &m->out_maps[l], m->yn, kDInner, M, out, kDModel, !step || m->exact_skinny, st);
+}
+}  // namespace
+
+int sq_model_mixer_forward(sq_model* m, int layer, const uint16_t* u, int batch, int tokens, int pos0, uint16_t* out,
+                           void* stream) {
+  if (!m || !u || !out || batch <= 0 || tokens <= 0 || pos0 < 0 || layer < 0 || layer >= (m ? m->cfg.n_layer : 0))
+    return fail(SQ_EINVAL, "mixer_forward: bad args");
+  Busy busy(m);
+  if (!busy.ok) return fail(SQ_ESTATE, "mixer_forward: concurrent/reentrant use of one model context");
+  if (batch * tokens > m->max_tokens) return fail(SQ_EINVAL, "mixer_forward: batch*tokens exceeds reserved workspace");
+  if (!m->layers[layer].in_proj.codes) return fail(SQ_ESTATE, "mixer_forward: layer weights not set");
+  if (m->states[layer].batch != batch) return fail(SQ_ESTATE, "mixer_forward: state batch differs from the call");
+  if (!aligned(u, 16) || !aligned(out, 16)) return fail(SQ_EINVAL, "mixer_forward: u / out must be 16-byte aligned");
+  return mixer_forward(m, layer, u, batch, tokens, pos0, out, (cudaStream_t)stream);
+}
+
 int sq_model_forward(sq_model* m, const int64_t* ids, int batch, int tokens, int pos0, uint16_t* hidden_out,
                      void* stream) {
   if (!m || !ids || !hidden_out || batch <= 0 || tokens <= 0 || pos0 < 0) return fail(SQ_EINVAL, "forward: bad args");
@@ -442,45 +547,12 @@ int sq_model_forward(sq_model* m, const int64_t* ids, int batch, int tokens, int
   if (!m->embed.codes || !m->norm_f) return fail(SQ_ESTATE, "forward: globals not set");
   cudaStream_t st = (cudaStream_t)stream;
   SQ_TRY(launch_fp4_embed(fw(m->embed), (const long long*)ids, M, m->h, m->d_err, st), "embedding");
-  const bool step = pos0 > 0 && tokens == 1;
   for (int l = 0; l < m->cfg.n_layer; ++l) {
     const sq_layer_desc& L = m->layers[l];
-    const sq_model::St& S = m->states[l];
     if (!L.in_proj.codes) return fail(SQ_ESTATE, "forward: layer weights not set");
-    if (S.batch != batch) return fail(SQ_ESTATE, "forward: state batch differs from the call (reset required)");
+    if (m->states[l].batch != batch) return fail(SQ_ESTATE, "forward: state batch differs from the call (reset required)");
     SQ_TRY(launch_add_rmsnorm(m->h, m->res, l > 0, L.norm_weight, m->cfg.eps, m->hn, M, kDModel, st), "add_rmsnorm");
-    int s = linear(m, L.in_proj, &m->in_maps[l], m->hn, kDModel, M, m->zx, kZx, !step || m->exact_skinny, st);
-    if (s != SQ_OK) return s;
-    ScanParams P{};
-    P.batch = batch; P.length = tokens; P.heads = kHeads; P.dim = kHeadDim; P.groups = kGroups; P.layout = L.layout;
-    P.dt = m->zx + 2 * kDInner + 2 * 1024; P.dt_sb = (long long)tokens * kZx; P.dt_st = kZx;
-    P.A = L.A; P.D = L.D; P.d_is_f32 = 0; P.dt_bias = L.dt_bias; P.dt_bias_is_f32 = 0;
-    P.perm = L.permutation; P.basis = L.basis; P.latent_scale = L.latent_scale; P.predictor = L.predictor;
-    P.lo = S.lo; P.hi = S.hi; P.q4 = S.q4; P.latent = S.latent; P.s8 = S.s8; P.s4 = S.s4;
-    P.y = m->y; P.y_sb = (long long)tokens * kDInner; P.y_st = kDInner;
-    if (step || pos0 == 0) {
-      // conv fused into the scan: step numerics for a one-token step, conv1d numerics
-      // for a prefill from a reset state
-      const uint16_t* raw = m->zx + kDInner;
-      P.x = raw; P.B = raw + kDInner; P.C = raw + kDInner + 1024;
-      P.x_sb = P.b_sb = P.c_sb = (long long)tokens * kZx; P.x_st = P.b_st = P.c_st = kZx;
-      P.conv_mode = step ? 2 : 1;
-      P.conv_w = L.conv_weight; P.conv_b = L.conv_bias; P.conv_cache = S.ring; P.conv_pos = pos0;
-      P.conv_cache_sb = 4LL * kXbc;
-    } else {
-      SQ_TRY(launch_conv_prefill(m->zx + kDInner, (long long)tokens * kZx, kZx, batch, tokens, kXbc, L.conv_weight,
-                                 L.conv_bias, S.ring, 4LL * kXbc, pos0, m->xbc, (long long)tokens * kXbc, kXbc, st),
-             "conv prefill");
-      P.x = m->xbc; P.B = m->xbc + kDInner; P.C = m->xbc + kDInner + 1024;
-      P.x_sb = P.b_sb = P.c_sb = (long long)tokens * kXbc; P.x_st = P.b_st = P.c_st = kXbc;
-    }
-    if (!step) scan_prep_bind(P, m->prep);
-    SQ_TRY(launch_scan(P, st), "ssu scan");
-    const AdapterPtrs& ad = m->adapters[l];
-    SQ_TRY(launch_resurface_gatednorm(m->y, m->zx, kZx, m->hn, kDModel, ad.V ? &ad : nullptr, L.gated_norm_weight,
-                                      m->cfg.eps, m->yn, M, st), "resurface + gated norm");
-    s = linear(m, L.out_proj, &m->out_maps[l], m->yn, kDInner, M, m->h, kDModel, !step || m->exact_skinny, st);
-    if (s != SQ_OK) return s;
+    if (int s = mixer_forward(m, l, m->hn, batch, tokens, pos0, m->h, st)) return s;
     if (m->capture && M <= m->capture_rows &&
         cudaMemcpyAsync(m->capture + (size_t)l * m->capture_rows * kDModel, m->h, (size_t)M * kDModel * 2,
                         cudaMemcpyDeviceToDevice, st) != cudaSuccess)

@@ -36,6 +36,45 @@ __global__ void fp4_decode_kernel(const uint8_t* __restrict__ codes, const uint8
   *reinterpret_cast<uint4*>(out + r * ldo + c8 * 8) = o;
 }
 
+// decode_packet's checks (mamba2_recall/fp4.py:235-249) over a packed matrix, one thread per
+// 16-column group: bit 1 = a block scale that is negative or NaN ('Invalid stored scale'),
+// bit 2 = a nonzero code (other than +-0) in a zero-scale group, bit 4 = a decoded weight
+// that is not finite in fp16.
+__global__ void fp4_validate_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales,
+                                    const float* __restrict__ gptr, long long rows, int cols, int* __restrict__ flags) {
+  const long long groups = rows * (cols / 16);
+  const float g = *gptr;
+  const float2 g2 = make_float2(g, g);
+  int bad = 0;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < groups;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / (cols / 16);
+    const int gcol = (int)(i - r * (cols / 16));
+    const uint8_t sb = scales[i];
+    if ((sb & 0x7F) == 0x7F || ((sb & 0x80) && (sb & 0x7F))) bad |= 1;
+    const uint4 w = *reinterpret_cast<const uint4*>(codes + r * (cols / 2) + gcol * 8);
+    const uint32_t ws[2] = {w.x, w.y};
+    if ((sb & 0x7F) == 0) {
+      // every nibble must be 0 or 8 (+0 / -0)
+      if (((ws[0] | ws[1]) & 0x77777777u) != 0) bad |= 2;
+    } else {
+      const uint32_t bs = e4m3_splat_f16x2(sb);
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        uint32_t m[4];
+        e2m1x8_to_f16x2(ws[q], m);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t v = scale_pair(m[k], bs, g2);
+          // fp16 exponent all ones: inf or NaN
+          if ((v & 0x7C00u) == 0x7C00u || (v & 0x7C000000u) == 0x7C000000u) bad |= 4;
+        }
+      }
+    }
+  }
+  if (bad) atomicOr(flags, bad);
+}
+
 __global__ void fp4_embed_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales,
                                  const float* __restrict__ gptr, int vocab, int cols,
                                  const long long* __restrict__ ids, int ntok, uint16_t* __restrict__ out,
@@ -180,14 +219,21 @@ __device__ __forceinline__ bool gv_try(uint32_t a, uint32_t parity) {
                : "=r"(ok) : "r"(a), "r"(parity) : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ bool gv_wait(uint32_t a, uint32_t parity) {
+// Limit of the pipeline's waits (producer on a free stage, consumers on a loaded one),
+// settable per device for failure-detection tests (set_gemv_wait_limit_ns).  The drain
+// waits after an expiry keep the fixed kGvWaitNs, so copies already in flight always land
+// before the CTA exits.
+__device__ unsigned long long g_gv_wait_ns = kGvWaitNs;
+__device__ __forceinline__ bool gv_wait_for(uint32_t a, uint32_t parity, unsigned long long limit) {
   if (gv_try(a, parity)) return true;
   const uint64_t t0 = gv_time();
   for (;;) {
     for (int i = 0; i < 32; ++i) if (gv_try(a, parity)) return true;
-    if (gv_time() - t0 > kGvWaitNs) return false;
+    if (gv_time() - t0 > limit) return false;
   }
 }
+__device__ __forceinline__ bool gv_wait(uint32_t a, uint32_t parity) { return gv_wait_for(a, parity, g_gv_wait_ns); }
+__device__ __forceinline__ bool gv_drain_wait(uint32_t a, uint32_t parity) { return gv_wait_for(a, parity, kGvWaitNs); }
 
 __device__ __forceinline__ void gv_tma2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
   asm volatile(
@@ -246,7 +292,7 @@ fp4_gemv_stream_kernel(const __grid_constant__ CUtensorMap mcodes, const __grid_
         atomicOr(err, (int)kDevTimeoutProducer);
         for (int i = 0; i < kGvStages && issued > 0; ++i, --issued) {   // drain own copies
           if (--stage < 0) { stage = kGvStages - 1; phase ^= 1; }
-          gv_wait(fbar + 8 * stage, phase);
+          gv_drain_wait(fbar + 8 * stage, phase);
         }
       }
     }
@@ -417,6 +463,15 @@ int launch_fp4_decode(const Fp4Weight& W, uint16_t* out, long long ldo, cudaStre
   return launch_status();
 }
 
+int launch_fp4_validate(const Fp4Weight& W, int* flags, cudaStream_t st) {
+  if (W.rows <= 0 || W.cols <= 0 || W.cols % 16 || ((uintptr_t)W.codes % 8) || !flags) return kEInval;
+  const long long groups = (long long)W.rows * (W.cols / 16);
+  const long long blocks = (groups + 255) / 256;
+  fp4_validate_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, st>>>(
+      W.codes, W.scales, W.global_scale, W.rows, W.cols, flags);
+  return launch_status();
+}
+
 int launch_fp4_embed(const Fp4Weight& E, const long long* ids, int ntok, uint16_t* out, int* err, cudaStream_t st) {
   if (E.cols % 16 || ntok <= 0) return kEInval;
   fp4_embed_kernel<<<ntok, 256, 0, st>>>(E.codes, E.scales, E.global_scale, E.rows, E.cols, ids, ntok, out, err);
@@ -446,6 +501,11 @@ int prepare_fp4_kernels() {
            gemv_stream<4, false>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0) |
            gemv_stream<8, false>(none, nullptr, nullptr, 0, 1, nullptr, 0, nullptr, 0);
   return st ? kECuda : kOk;
+}
+
+int set_gemv_wait_limit_ns(unsigned long long ns) {
+  const unsigned long long v = ns ? ns : kGvWaitNs;
+  return cudaMemcpyToSymbol(g_gv_wait_ns, &v, sizeof(v)) == cudaSuccess ? kOk : kECuda;
 }
 
 int launch_fp4_gemv_stream(const Fp4Weight& W, const Fp4Maps* maps, const uint16_t* X, long long ldx, int M,

@@ -17,6 +17,9 @@ struct Fp4Weight {
 };
 
 int launch_fp4_decode(const Fp4Weight& W, uint16_t* out, long long ldo, cudaStream_t st);
+// decode_packet's checks; ORs 1 (invalid scale), 2 (nonzero code in a zero-scale group),
+// 4 (nonfinite decoded weight) into *flags (device int, caller-cleared).
+int launch_fp4_validate(const Fp4Weight& W, int* flags, cudaStream_t st);
 int launch_fp4_embed(const Fp4Weight& E, const long long* ids, int ntok, uint16_t* out, int* err, cudaStream_t st);
 int launch_fp4_gemv(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,
                     cudaStream_t st);
@@ -52,6 +55,10 @@ struct GemmCE {
 int launch_gemm_f16(const uint16_t* A, long long lda, const uint16_t* B, long long ldb,
                     uint16_t* C, long long ldc, int M, int N, int K, int mode, const GemmCE* ce,
                     int* dev_err, cudaStream_t st);
+// Limit (ns) of the skinny GEMM's pipeline waits on the current device; 0 restores the
+// default 2 s.  A short limit makes the waits expire: the kernel sets its error bit,
+// drains its copies and returns (failure-detection tests).
+int set_gemv_wait_limit_ns(unsigned long long ns);
 int gemm_num_ntiles(int N);
 int prepare_fp4_kernels();
 int prepare_gemm_kernel();

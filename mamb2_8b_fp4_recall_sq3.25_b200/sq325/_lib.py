@@ -42,6 +42,17 @@ class ScanArgs(C.Structure):
                 ('workspace', p), ('workspace_bytes', i64)]
 
 
+class S16Args(C.Structure):
+    _fields_ = [('batch', i32), ('length', i32), ('heads', i32), ('dim', i32), ('groups', i32),
+                ('x', p), ('x_batch_stride', i64), ('x_token_stride', i64),
+                ('dt', p), ('dt_batch_stride', i64), ('dt_token_stride', i64),
+                ('A', p),
+                ('B', p), ('b_batch_stride', i64), ('b_token_stride', i64),
+                ('C', p), ('c_batch_stride', i64), ('c_token_stride', i64),
+                ('D', p), ('d_is_f32', i32), ('dt_bias', p), ('dt_bias_is_f32', i32),
+                ('state', p), ('y', p), ('y_batch_stride', i64), ('y_token_stride', i64), ('stats', p)]
+
+
 class ConvArgs(C.Structure):
     _fields_ = [('weight', p), ('bias', p), ('ring', p), ('ring_batch_stride', i64), ('position', i32)]
 
@@ -69,9 +80,11 @@ _PROTOS = {
     'sq_state_bytes': (i64, [C.c_int, C.c_int, C.c_int]),
     'sq_scan': (C.c_int, [C.POINTER(ScanArgs), p]),
     'sq_scan_conv': (C.c_int, [C.POINTER(ScanArgs), C.POINTER(ConvArgs), p]),
+    'sq_s16_scan': (C.c_int, [C.POINTER(S16Args), p]),
     'sq_state_decode': (C.c_int, [C.c_int] * 5 + [p] * 9 + [p]),
     'sq_state_encode': (C.c_int, [C.c_int] * 6 + [p] * 9 + [p]),
     'sq_fp4_decode': (C.c_int, [p, p, p, C.c_int, C.c_int, p, i64, p]),
+    'sq_fp4_validate': (C.c_int, [p, p, p, C.c_int, C.c_int, p]),
     'sq_scan_workspace': (i64, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
     'sq_model_set_exact_skinny': (C.c_int, [p, C.c_int]),
     'sq_model_set_capture': (C.c_int, [p, p, i64]),
@@ -82,6 +95,7 @@ _PROTOS = {
     'sq_fp4_linear_static': (C.c_int, [p, p, p, C.c_int, C.c_int, p, i64, C.c_int, p, i64, p]),
     'sq_gemm_f16': (C.c_int, [p, i64, p, i64, p, i64, C.c_int, C.c_int, C.c_int, p]),
     'sq_device_check': (C.c_int, [p]),
+    'sq_set_wait_limit_ns': (C.c_int, [C.c_uint64]),
     'sq_model_create': (C.c_int, [C.POINTER(ModelConfig), C.POINTER(p)]),
     'sq_model_destroy': (C.c_int, [p]),
     'sq_model_set_layer': (C.c_int, [p, C.c_int, C.POINTER(LayerDesc)]),
@@ -90,6 +104,7 @@ _PROTOS = {
     'sq_model_bind_state': (C.c_int, [p, C.c_int, C.c_int, p, p, p, p, p, p, p]),
     'sq_model_reserve': (C.c_int, [p, C.c_int]),
     'sq_model_forward': (C.c_int, [p, p, C.c_int, C.c_int, C.c_int, p, p]),
+    'sq_model_mixer_forward': (C.c_int, [p, C.c_int, p, C.c_int, C.c_int, C.c_int, p, p]),
     'sq_model_score': (C.c_int, [p, p, C.c_int, p, p, p]),
     'sq_model_greedy': (C.c_int, [p, p, C.c_int, p, p, p]),
     'sq_model_check': (C.c_int, [p, p]),

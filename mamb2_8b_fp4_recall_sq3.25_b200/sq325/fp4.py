@@ -69,11 +69,23 @@ def from_packet(packet, device='cuda'):
     return Fp4Tensor(codes, scales, g, (rows, cols))
 
 
+def validate(w):
+    """decode_packet's content checks (mamba2_recall/fp4.py:235-249) on the device: ValueError
+    for a negative / NaN block scale, a nonzero code in a zero-scale group, or a weight that
+    decodes to a nonfinite fp16 value (the reference's messages)."""
+    with torch.cuda.device(w.codes.device):
+        _lib.call('sq_fp4_validate', _lib.ptr(w.codes), _lib.ptr(w.block_scale_bytes), _lib.ptr(w.global_scale),
+                  w.rows, w.cols, _lib.stream_ptr())
+    return w
+
+
 @torch.no_grad()
 def decode_packet(w):
-    """Bit-exact FP16 decode of a packed matrix (replaces fp4.decode_packet)."""
+    """Bit-exact FP16 decode of a packed matrix (replaces fp4.decode_packet), with the
+    reference's checks first."""
     if isinstance(w, dict):
         w = from_packet(w)
+    validate(w)
     out = torch.empty(w.shape, device=w.codes.device, dtype=torch.float16)
     with torch.cuda.device(w.codes.device):
         _lib.call('sq_fp4_decode', _lib.ptr(w.codes), _lib.ptr(w.block_scale_bytes), _lib.ptr(w.global_scale),

@@ -24,6 +24,7 @@ class AdapterBank:
     g: list                 # fp16 [128]
     w: list                 # fp16 [4096]
     b: list                 # fp16 [1]
+    base_hashes: dict = None  # the base-parameter ledger given to install_fp16, if any
 
     @property
     def nbytes(self):
@@ -67,13 +68,83 @@ def bank_from_payload(payload, n_layer, device):
                        [get(i, 'router_b').reshape(1) for i in range(n_layer)])
 
 
+def tensor_hash(value):
+    """sha256 of a tensor's bytes in row order (resurface_native.tensor_hash, :49-57)."""
+    import hashlib
+    t = value.detach()
+    return hashlib.sha256(t.cpu().contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()
+
+
+def base_parameter_names(model):
+    """The base model's parameter names as the reference's MambaLMHeadModel names them."""
+    from .checkpoint import tensor_inventory
+    return set(tensor_inventory(model.n_layer, model.vocab))
+
+
+@torch.no_grad()
+def base_tensor_hashes(model, chunk_rows=16384):
+    """sha256 ledger of the base parameters under the reference's names, as ResurfaceNative
+    hashes them (resurface_native.py:140-141, 285-297): the FP4 matrices as their decoded
+    FP16 weights (decoded on the device in row chunks, hashed in row order), the fp16
+    tensors as stored (conv1d.weight as its [10240, 1, 4] bytes, identical to [10240, 4])."""
+    import hashlib
+    from . import fp4 as F
+    out = {}
+
+    def packed(name, w):
+        d = hashlib.sha256()
+        for r0 in range(0, w.rows, chunk_rows):
+            rows = min(chunk_rows, w.rows - r0)
+            part = F.Fp4Tensor(w.codes[r0:r0 + rows], w.block_scale_bytes[r0:r0 + rows], w.global_scale,
+                               (rows, w.cols))
+            d.update(F.decode_packet(part).cpu().numpy().tobytes())
+        out[name] = d.hexdigest()
+
+    packed('backbone.embedding.weight', model.embedding)
+    packed('lm_head.weight', model.lm_head)
+    out['backbone.norm_f.weight'] = tensor_hash(model.norm_f)
+    for i, L in enumerate(model.layers):
+        p = f'backbone.layers.{i}.'
+        packed(p + 'mixer.in_proj.weight', L.in_proj)
+        packed(p + 'mixer.out_proj.weight', L.out_proj)
+        for name, t in (('norm.weight', L.norm_weight), ('mixer.A_log', L.A_log), ('mixer.D', L.D),
+                        ('mixer.dt_bias', L.dt_bias), ('mixer.conv1d.weight', L.conv_weight),
+                        ('mixer.conv1d.bias', L.conv_bias), ('mixer.norm.weight', L.gated_norm_weight)):
+            out[p + name] = tensor_hash(t)
+    return out
+
+
 def install_fp16(model, path, *, expected_binding=None, expected_base_hashes=None):
-    """Load an exported adapter onto `model` (replaces resurface_native.install_fp16)."""
+    """Load an exported adapter onto `model` (replaces resurface_native.install_fp16, :363-375).
+
+    expected_base_hashes, when given, is the independently supplied ledger of the base
+    parameters (name -> sha256): it must cover every base parameter exactly (ValueError as in
+    ResurfaceNative.__init__ :140-142) and is kept for `assert_base_frozen(check_values=True)`."""
     if getattr(model, 'adapter', None) is not None:
         raise RuntimeError('A Resurface adapter is already attached to this model')
+    if expected_base_hashes is not None and set(expected_base_hashes) != base_parameter_names(model):
+        raise ValueError('Expected base ledger must cover every original parameter')
     payload = read_fp16(path, expected_binding)
-    model.adapter = bank_from_payload(payload, model.n_layer, model.device)
+    bank = bank_from_payload(payload, model.n_layer, model.device)
+    bank.base_hashes = dict(expected_base_hashes) if expected_base_hashes is not None else None
+    model.adapter = bank
     return model.adapter
+
+
+def assert_base_frozen(model, check_values=False):
+    """ResurfaceNative.assert_base_frozen (:285-300): with check_values the base parameters'
+    content is re-hashed against the ledger given to install_fp16."""
+    bank = getattr(model, 'adapter', None)
+    if bank is None:
+        raise RuntimeError('No Resurface adapter is attached to this model')
+    if check_values:
+        if bank.base_hashes is None:
+            raise ValueError('Content audit requires an independently supplied base hash ledger')
+        now = base_tensor_hashes(model)
+        for name, digest in now.items():
+            if digest != bank.base_hashes[name]:
+                raise RuntimeError(f'Base content changed: {name}')
+    return {'tensors': len(base_parameter_names(model)), 'actual_content_checked': bool(check_values)}
 
 
 def remove(model):

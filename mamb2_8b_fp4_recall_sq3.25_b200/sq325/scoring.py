@@ -14,6 +14,7 @@
 from __future__ import annotations
 
 import hashlib
+import json
 import math
 
 import numpy as np
@@ -36,8 +37,9 @@ def ppl_windows(ids, seqlen, nwin=None):
 
 
 @torch.no_grad()
-def score_local(execution, windows, batch_windows=16):
-    """Score windows on this device; returns per-window records in input order."""
+def score_local(execution, windows, batch_windows=16, on_batch=None):
+    """Score windows on this device; returns per-window records in input order.
+    `on_batch(records)` is called after every batch (records of unscored windows are None)."""
     dev = execution.device
     records = [None] * len(windows)
     by_len = {}
@@ -48,25 +50,103 @@ def score_local(execution, windows, batch_windows=16):
             raise ValueError('A window needs at least one target token')
         for c in range(0, len(idxs), batch_windows):
             chunk = idxs[c:c + batch_windows]
-            toks = torch.stack([torch.as_tensor(windows[i][1], dtype=torch.long) for i in chunk]).to(dev)
+            toks = torch.stack([torch.as_tensor(windows[i][1], dtype=torch.long) for i in chunk])
+            host = toks if toks.device.type == 'cpu' else None
+            toks = toks.to(dev)
             hidden = execution.backbone(toks[:, :-1].contiguous(), reset=True)
             nll = execution.score(hidden, toks[:, 1:].contiguous())
             sums = nll.view(len(chunk), length - 1).double().sum(1).cpu().tolist()
-            for i, s in zip(chunk, sums):
+            if host is None:                          # windows resident on the device
+                host = toks.cpu()
+            for k, (i, s) in enumerate(zip(chunk, sums)):
                 if not math.isfinite(s):
                     raise FloatingPointError('Nonfinite PPL NLL')
-                start, w = windows[i]
-                records[i] = dict(start=int(start), target_tokens=length - 1,
-                                  token_sha256_int64le=token_digest(np.asarray(w)), nll=s,
+                records[i] = dict(start=int(windows[i][0]), target_tokens=length - 1,
+                                  token_sha256_int64le=token_digest(host[k].numpy()), nll=s,
                                   ppl=math.exp(s / (length - 1)))
+            if on_batch is not None:
+                on_batch(records)
     return records
 
 
+def cache_identity(execution):
+    """sha256 of every cache tensor, keyed '<layer>.<name>' (the six PackedState tensors and
+    'conv' in the reference's chronological [batch, 10240, 4] order), as the reference's
+    evaluation scripts record it (scripts/run_fp4_latent_state_quality_v1.py:49-61)."""
+    from .resurface import tensor_hash
+    out = {}
+    for index, entry in enumerate(execution._cache):
+        for key, value in entry.state.tensors.items():
+            out[f'{index}.{key}'] = tensor_hash(value)
+        out[f'{index}.conv'] = tensor_hash(execution.conv_chronological(index))
+    return out
+
+
+def _put(path, row):
+    """Write the report row atomically (the reference rewrites its JSON after every window)."""
+    from pathlib import Path
+    path = Path(path)
+    tmp = path.with_suffix(path.suffix + '.tmp')
+    tmp.write_text(json.dumps(row, indent=1, allow_nan=False) + '\n')
+    tmp.replace(path)
+
+
 @torch.no_grad()
-def evaluate_ppl(execution, windows, batch_windows=16, rank=0, world=1, group=None):
-    """Pooled perplexity over `windows`; sharded over `world` ranks when world > 1."""
+def repeated_reset_probe(execution, window, tokens=128):
+    """scripts/run_fp4_ridge_resurface_v3.py:90-98: the first `tokens` of a window scored twice
+    from a reset state must give identical hidden states and identical cache bytes."""
+    from .resurface import tensor_hash
+    probe = torch.as_tensor(window[:tokens], dtype=torch.long).to(execution.device)[None]
+    first = execution.backbone(probe, reset=True).clone()
+    identity = cache_identity(execution)
+    second = execution.backbone(probe, reset=True)
+    if not (torch.equal(first, second) and identity == cache_identity(execution) and
+            bool(torch.isfinite(first).all())):
+        raise RuntimeError('Repeated reset differs')
+    return dict(tokens=int(probe.shape[1]), hidden_sha256=tensor_hash(first), hidden_and_cache_exact=True,
+                cache_tensor_sha256=identity, token_sha256_int64le=token_digest(probe.cpu().numpy()),
+                cache=execution.cache_breakdown())
+
+
+@torch.no_grad()
+def evaluate_ppl(execution, windows, batch_windows=16, rank=0, world=1, group=None, *, path=None, common=None,
+                 frozen=None, probe_tokens=128):
+    """Pooled perplexity over `windows` (a list of (start, int64 tokens)); sharded over
+    `world` ranks when world > 1: rank r scores windows r, r + world, ... and ONE all-reduce of
+    [sum NLL, sum targets] (fp64) combines them; the per-window records are gathered so every
+    rank returns the full list in window order.
+
+    With `path`, rank 0 keeps the reference's report (run_fp4_ridge_resurface_v3.py:81-121):
+    a JSON row {**common, complete, ppl: {windows, nll, target_tokens, ppl}, static basis /
+    scale / predictor sha256, layer_layouts, repeated_reset_probe, cache, storage_descriptor}
+    rewritten after every batch of windows, and the repeated-reset probe on the first
+    `probe_tokens` of window 0 before scoring.  `frozen`, if given, is an object whose
+    check() result is recorded at the end (the reference's frozen-source check)."""
+    from .resurface import tensor_hash
     local = list(range(rank, len(windows), world))
-    recs = score_local(execution, [windows[i] for i in local], batch_windows) if local else []
+    report = path is not None and rank == 0
+    row = None
+    if report:
+        row = dict(common or {}, complete=False, ppl=dict(windows=[]),
+                   static_basis_sha256=[tensor_hash(x) for x in execution.bases],
+                   static_scale_sha256=[tensor_hash(x) for x in execution.latent_scales],
+                   static_predictor_sha256=[[tensor_hash(x) for x in p] for p in execution.predictors],
+                   layer_layouts=list(execution.layouts))
+        _put(path, row)
+        row['repeated_reset_probe'] = repeated_reset_probe(execution, windows[0][1], probe_tokens)
+        row['storage_descriptor_probe'] = execution.storage_descriptor()
+
+    def progress(recs):
+        if report:
+            row['ppl']['windows'] = [r for r in recs if r is not None]
+            done = row['ppl']['windows']
+            nll = sum(r['nll'] for r in done)
+            count = sum(r['target_tokens'] for r in done)
+            row['ppl'].update(nll=nll, target_tokens=count, ppl=math.exp(nll / count))
+            row['cache'], row['storage_descriptor'] = execution.cache_breakdown(), execution.storage_descriptor()
+            _put(path, row)
+
+    recs = score_local(execution, [windows[i] for i in local], batch_windows, on_batch=progress) if local else []
     total = sum(r['nll'] for r in recs)
     count = sum(r['target_tokens'] for r in recs)
     if world > 1:
@@ -80,7 +160,14 @@ def evaluate_ppl(execution, windows, batch_windows=16, rank=0, world=1, group=No
         dist.all_gather_object(gathered, [(i, r) for i, r in zip(local, recs)], group=group)
         merged = sorted((x for part in gathered for x in part), key=lambda t: t[0])
         recs = [r for _, r in merged]
-    return dict(ppl=math.exp(total / count), nll=total, target_tokens=count, windows=recs)
+    result = dict(ppl=math.exp(total / count), nll=total, target_tokens=count, windows=recs)
+    if report:
+        row['ppl'] = dict(windows=recs, nll=total, target_tokens=count, ppl=result['ppl'])
+        row.update(complete=True, ppl_complete=True)
+        if frozen is not None:
+            row['frozen_source'] = frozen.check()
+        _put(path, row)
+    return result
 
 
 @torch.no_grad()

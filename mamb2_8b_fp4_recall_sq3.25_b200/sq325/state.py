@@ -212,6 +212,34 @@ class PredictorState:
             self._inside_backbone = False
 
     @torch.no_grad()
+    def mixer_forward(self, layer, u, out=None):
+        """One mixer layer (the reference's patched `mixer.forward`, PredictorState._forward
+        fp4_zero_predictor_codec_v1.py:314-367): u fp16 [batch, tokens, 4096] is the Block's
+        normed input; returns the mixer output and advances this layer's cache position."""
+        if not self._installed:
+            raise RuntimeError('Controller is not installed')
+        if not self._cache:
+            raise RuntimeError('reset() the controller before running a layer')
+        if self._failed:
+            raise RuntimeError('Controller is inactive or failed; reset before reusing it')
+        if u.ndim != 3 or u.shape[0] != self._batch_size or u.shape[2] != D_MODEL or u.dtype != torch.float16 \
+                or u.device != self.device:
+            raise ValueError('u must be CUDA fp16 [batch, tokens, 4096] matching the reset batch')
+        B, T = u.shape[:2]
+        u = u.contiguous()
+        self.reserve(B * T)
+        out = out if out is not None else torch.empty_like(u)
+        e = self._cache[layer]
+        try:
+            _lib.call('sq_model_mixer_forward', self._handle, layer, _lib.ptr(u), B, T, e.tokens, _lib.ptr(out),
+                      _lib.stream_ptr())
+        except Exception:
+            self._failed = True
+            raise
+        e.tokens += T
+        return out
+
+    @torch.no_grad()
     def score(self, hidden, targets, out=None):
         """Per-row next-token NLL (fp32) of fp16 logits lm_head(hidden).float()."""
         h2 = hidden.reshape(-1, D_MODEL).contiguous()

@@ -373,3 +373,61 @@ def latent_scan(x, dt, A, B, C, D, dt_bias, state, permutation, basis, latent_sc
     state['s8'][...] = s8.astype(np.float16)
     state['s4'][...] = s4.astype(np.float16)
     return y
+
+
+# ---------------------------------------------------------------- S16 control scan
+
+def s16_scan(x, dt, A, B, C, D, dt_bias, state, collect_stats=False, tile=4, rp=16):
+    """The FP16-state control scan (mamba2_recall/state_codec.py:65-102) plus the statistics
+    reduction of its host wrapper (:256-262); mutates ``state`` (fp16 [Bt,H,P,128]); returns
+    (y fp16 [Bt,L,H,P], stats fp32 [Bt,H,ceil(P/rp),128] or None).
+
+    Per token, as the kernel: dt = softplus(dt + bias) (threshold 20), decay = exp(A dt),
+    state = state * decay + (B * dt) * x, y = sum_n state * C + x * D (fp32, stored fp16),
+    then the carry is rounded to fp16.  Statistics: per row the sum over tokens of
+    |fp16 carry|, summed over each 4-row kernel tile, then over the 4 tiles of a 16-row
+    block (the wrapper's reshape + sum)."""
+    x = np.asarray(x, np.float16)
+    Bt, L, H, P = x.shape
+    G = np.asarray(B).shape[2]
+    gidx = np.arange(H) // (H // G)
+    av = np.asarray(A, np.float32)[None, :]
+    dv = np.asarray(D).astype(np.float32)[None, :, None]
+    bias = np.asarray(dt_bias).astype(np.float32)[None, :]
+    Bf = np.asarray(B, np.float16).astype(np.float32)
+    Cf = np.asarray(C, np.float16).astype(np.float32)
+    st = np.asarray(state, np.float16).astype(np.float32)
+    acc = np.zeros_like(st) if collect_stats else None
+    y = np.zeros((Bt, L, H, P), np.float16)
+    for t in range(L):
+        xv = x[:, t].astype(np.float32)
+        dtv = np.asarray(dt, np.float16)[:, t].astype(np.float32) + bias
+        with np.errstate(over='ignore'):
+            dtv = np.where(dtv <= F32(20.0), np.log(np.exp(dtv) + F32(1.0)), dtv).astype(np.float32)
+        decay = np.exp(av * dtv).astype(np.float32)                          # [Bt,H]
+        bv, cv = Bf[:, t][:, gidx], Cf[:, t][:, gidx]                        # [Bt,H,128]
+        dB = (bv * dtv[..., None]).astype(np.float32)
+        st = (st * decay[..., None, None] + dB[:, :, None, :] * xv[..., None]).astype(np.float32)
+        out = np.sum(st * cv[:, :, None, :], -1)
+        out = (out + xv * dv).astype(np.float32)
+        y[:, t] = out.astype(np.float16)
+        st = st.astype(np.float16).astype(np.float32)
+        if collect_stats:
+            acc = (acc + np.abs(st)).astype(np.float32)
+    state[...] = st.astype(np.float16)
+    if not collect_stats:
+        return y, None
+    ntile = -(-P // tile)
+    pad = np.zeros((Bt, H, ntile * tile - P, 128), np.float32)
+    a = np.concatenate((acc, pad), 2).reshape(Bt, H, ntile, tile, 128)
+    tiles = a[:, :, :, 0]
+    for r in range(1, tile):
+        tiles = (tiles + a[:, :, :, r]).astype(np.float32)
+    target = -(-P // rp)
+    per = rp // tile
+    tiles = np.concatenate((tiles, np.zeros((Bt, H, target * per - ntile, 128), np.float32)), 2)
+    tiles = tiles.reshape(Bt, H, target, per, 128)
+    stats = tiles[:, :, :, 0]
+    for k in range(1, per):
+        stats = (stats + tiles[:, :, :, k]).astype(np.float32)
+    return y, stats

@@ -16,6 +16,9 @@ What is recorded
                        seeded matrix (codes, E4M3 block bytes, global, FP16).
   adapter.npz          mamba2_recall/resurface_native._Adapter.forward (soft
                        gate, FP16 parameters) on CPU.
+  s16.npz              the FP16-state control scan `_s16_scan`
+                       (mamba2_recall/state_codec.py:65-102) under the interpreter,
+                       without and with the calibration statistics (:256-262).
 
 Interpreter shims (the interpreter cannot run two device intrinsics as the
 GPU does):
@@ -132,6 +135,38 @@ def codec_case(ref, layout, seed, batch=2, length=4, heads=4, dim=32, groups=2, 
     return rec
 
 
+def s16_case(reference, seed, collect, batch=2, length=5, heads=4, dim=24, groups=2):
+    """mamba2_recall/state_codec.py _s16_scan (:65-102), launched as scan() does for the s16
+    mode (:245-253) — scan() itself refuses CPU tensors — with the statistics reduction of
+    :256-262 applied to the kernel's per-4-row tiles."""
+    sys.path.insert(0, str(reference))
+    from mamba2_recall import state_codec as sc
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(batch, length, heads, dim, generator=gen).half()
+    dt = (torch.randn(batch, length, heads, generator=gen) * 0.7).half()
+    A = -(torch.rand(heads, generator=gen) * 3 + 0.05).float()
+    Bm = torch.randn(batch, length, groups, 128, generator=gen).half()
+    Cm = torch.randn(batch, length, groups, 128, generator=gen).half()
+    D = torch.randn(heads, generator=gen).half()
+    dt_bias = (torch.rand(heads, generator=gen) * 3 - 4).half()
+    state = (torch.randn(batch, heads, dim, 128, generator=gen) * 0.3).half()
+    initial = state.clone()
+    out = torch.empty_like(x)
+    ntile = triton.cdiv(dim, sc.S16_TILE)
+    stats = torch.empty((batch, heads, ntile, 128), dtype=torch.float32) if collect else None
+    sc._s16_scan[(batch, heads, ntile)](x, dt, A, Bm, Cm, D, dt_bias, state, out,
+                                        stats if stats is not None else out, length, heads, dim, groups,
+                                        collect, sc.S16_TILE, num_warps=4)
+    rec = dict(x=x, dt=dt, A=A, B=Bm, C=Cm, D=D, dt_bias=dt_bias, state_in=initial, state_out=state, y=out)
+    if collect:
+        target = triton.cdiv(dim, sc.RP)
+        if stats.shape[2] != target * (sc.RP // sc.S16_TILE):
+            pad = torch.zeros((batch, heads, target * (sc.RP // sc.S16_TILE) - stats.shape[2], 128))
+            stats = torch.cat((stats, pad), 2)
+        rec['stats'] = stats.reshape(batch, heads, target, sc.RP // sc.S16_TILE, 128).sum(3)
+    return {k: v.numpy() for k, v in rec.items()}
+
+
 def fp4_case(reference, seed=7):
     sys.path.insert(0, str(reference))
     from mamba2_recall import fp4
@@ -177,7 +212,17 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', type=Path, required=True,
                     help='root of a checkout of the reference repository (read only)')
+    ap.add_argument('--cases', default='codec,s16', help='comma list: codec (+ fp4, adapter), s16')
     args = ap.parse_args()
+    ap_cases = args.cases.split(',')
+    if 's16' in ap_cases:
+        rec = {}
+        for tag, seed, collect in (('plain_', 300, False), ('stats_', 301, True)):
+            rec.update({tag + k: v for k, v in s16_case(args.reference, seed, collect).items()})
+        np.savez_compressed(HERE / 's16.npz', **rec)
+        print('wrote s16')
+    if 'codec' not in ap_cases:
+        return
     ref = install_shims(args.reference)
     layouts = ('32_32_64', '16_64_48', '8_80_40', '24_48_56', '36_24_68', '40_16_72', '44_8_76')
     for i, layout in enumerate(layouts):

@@ -66,3 +66,29 @@ def test_tcgen05_gemm(mnk):
     ref = a.float() @ b.float().T
     err = (c.float() - ref).abs()
     assert float(err.max()) <= 2e-3 * float(ref.abs().max()) + 1e-2, float(err.max())
+
+
+@pytest.mark.parametrize('case', ['zero_scale_code', 'negative_scale', 'nan_scale', 'overflow'])
+def test_decode_packet_rejects_what_the_reference_rejects(case):
+    """mamba2_recall/fp4.py:235-249: a nonzero code in a zero-scale group, a negative or NaN
+    block scale, and a weight that decodes past fp16's range are refused with the
+    reference's ValueError messages; a clean matrix with zero-scale groups holding only
+    +-0 codes decodes."""
+    from sq325 import fp4
+    rng = np.random.default_rng(12)
+    codes, blocks, g = of.synthetic_matrix(64, 256, rng)
+    blocks[3, 2] = 0                                  # a zero-scale group ...
+    codes[3, 16:24] = np.array([0x80, 0x08, 0x00, 0x88] * 2, np.uint8)   # ... holding only +-0 codes
+    fp4.decode_packet(fp4.from_arrays(codes, blocks, g))                  # accepted
+    msg = {'zero_scale_code': 'Nonzero code in a zero-scale group', 'negative_scale': 'Invalid stored scale',
+           'nan_scale': 'Invalid stored scale', 'overflow': 'Nonfinite decoded FP16 weights'}[case]
+    if case == 'zero_scale_code':
+        codes[3, 20] = 0x10
+    elif case == 'negative_scale':
+        blocks[5, 1] = 0x80 | 0x38
+    elif case == 'nan_scale':
+        blocks[7, 0] = 0x7F
+    else:
+        g = np.float32(1e6)                           # 6 * 448 * 1e6 overflows fp16
+    with pytest.raises(ValueError, match=msg):
+        fp4.decode_packet(fp4.from_arrays(codes, blocks, g))

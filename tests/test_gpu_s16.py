@@ -1,0 +1,74 @@
+"""GPU parity of the FP16-state control scan (sq_s16_scan, the reference's 's16' mode of
+mamba2_recall/state_codec.py) against the reference kernel's golden runs and the oracle.
+
+The readout is summed in the reference kernel's order and every product / sum is rounded
+once, so the only source of differences is CUDA's expf / logf against numpy's (dt softplus
+and decay, per head and token).  Bar: >= 99% of readouts and carry values fp16-identical,
+all readouts within rtol 2e-2 / atol 2e-2, statistics within 1e-3 relative."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import codec as oc
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(d, tag, collect):
+    from sq325 import state_codec as sc
+    T = lambda k: torch.from_numpy(np.ascontiguousarray(d[tag + k])).cuda()
+    x = T('x')
+    st = sc.allocate_state(x.shape[0], x.shape[2], x.shape[3], 128, 's16', 'cuda')
+    st.tensors['state'].copy_(T('state_in'))
+    y, stats = sc.scan(x, T('dt'), T('A'), T('B'), T('C'), T('D'), T('dt_bias'), st, collect_stats=collect)
+    torch.cuda.synchronize()
+    return y.cpu().numpy(), st.tensors['state'].cpu().numpy(), (stats.cpu().numpy() if stats is not None else None)
+
+
+def _check(y, st, stats, y_ref, st_ref, stats_ref):
+    assert np.allclose(y.astype(np.float32), y_ref.astype(np.float32), rtol=2e-2, atol=2e-2)
+    assert (y.view(np.uint16) == y_ref.view(np.uint16)).mean() >= 0.99
+    assert (st.view(np.uint16) == st_ref.view(np.uint16)).mean() >= 0.99
+    if stats_ref is not None:
+        assert np.allclose(stats, stats_ref, rtol=1e-3, atol=1e-6)
+
+
+@pytest.mark.parametrize('tag', ['plain_', 'stats_'])
+def test_s16_matches_reference_golden(golden, tag):
+    d = golden('s16.npz')
+    y, st, stats = _run(d, tag, tag == 'stats_')
+    _check(y, st, stats, d[tag + 'y'], d[tag + 'state_out'], d['stats_stats'] if tag == 'stats_' else None)
+
+
+@pytest.mark.parametrize('dim', [64, 40])
+def test_s16_matches_oracle_at_model_geometry(dim):
+    """128 heads, 8 groups, 37 tokens, batch 2, with statistics; dim 40 leaves a partial
+    16-row statistics block and a partial CTA."""
+    rng = np.random.default_rng(dim)
+    B, L, H, G = 2, 37, 128, 8
+    d = dict(x=rng.standard_normal((B, L, H, dim)).astype(np.float16),
+             dt=(rng.standard_normal((B, L, H)) * 0.5).astype(np.float16),
+             A=-(rng.random(H) * 3 + 0.1).astype(np.float32),
+             B=rng.standard_normal((B, L, G, 128)).astype(np.float16),
+             C=rng.standard_normal((B, L, G, 128)).astype(np.float16),
+             D=rng.standard_normal(H).astype(np.float16), dt_bias=(rng.random(H) * 3 - 4).astype(np.float16),
+             state_in=(rng.standard_normal((B, H, dim, 128)) * 0.3).astype(np.float16))
+    st_ref = d['state_in'].copy()
+    y_ref, stats_ref = oc.s16_scan(*(d[k] for k in ('x', 'dt', 'A', 'B', 'C', 'D', 'dt_bias')), st_ref,
+                                   collect_stats=True)
+    y, st, stats = _run(d, '', True)
+    _check(y, st, stats, y_ref, st_ref, stats_ref)
+
+
+def test_s16_rejects_what_the_reference_rejects():
+    from sq325 import state_codec as sc
+    with pytest.raises(ValueError):
+        sc.allocate_state(1, 4, 16, 64, 's16', 'cuda')
+    st = sc.allocate_state(1, 4, 16, 128, 's16', 'cuda')
+    x = torch.zeros(1, 2, 4, 16, device='cuda', dtype=torch.float16)
+    h = lambda *s: torch.zeros(*s, device='cuda', dtype=torch.float16)
+    with pytest.raises(ValueError, match='permutation'):
+        sc.scan(x, h(1, 2, 4), torch.zeros(4, device='cuda'), h(1, 2, 2, 128), h(1, 2, 2, 128), h(4), h(4), st,
+                permutation=torch.zeros(2, 128, dtype=torch.uint8, device='cuda'))
+    with pytest.raises(ValueError, match='divisible'):
+        sc.scan(x, h(1, 2, 4), torch.zeros(4, device='cuda'), h(1, 2, 3, 128), h(1, 2, 3, 128), h(4), h(4), st)

@@ -65,14 +65,39 @@ def test_adapter_export_round_trip(tmp_path):
 
 
 class _FakeExecution:
-    """Stands in for PredictorState on CPU: deterministic per-token NLL from the ids."""
+    """Stands in for PredictorState on CPU: deterministic per-token NLL from the ids, and the
+    controller attributes the report row reads (statics, caches, descriptors)."""
     device = torch.device('cpu')
+    layouts = ('32_32_64', '8_80_40')
+    bases = [torch.ones(8, 68, 2, dtype=torch.float16), torch.zeros(8, 44, 2, dtype=torch.float16)]
+    latent_scales = [torch.ones(8, 2, dtype=torch.float16)] * 2
+    predictors = [torch.zeros(8, 62, 68, dtype=torch.float16), torch.zeros(8, 86, 44, dtype=torch.float16)]
+
+    def __init__(self):
+        class _E:
+            pass
+        self._cache = []
+        for _ in range(2):
+            e = _E()
+            e.state = type('S', (), {'tensors': {'lo': torch.zeros(1, 2, 2, dtype=torch.uint8)}})()
+            self._cache.append(e)
+        self.seen = None
 
     def backbone(self, ids, reset=False, out=None):
+        self.seen = ids.clone()
         return ids.double()[..., None]
 
     def score(self, hidden, targets, out=None):
         return ((hidden[..., 0] * 7 + targets) % 13).reshape(-1).double() / 3.0
+
+    def conv_chronological(self, layer):
+        return self.seen.double().sum().reshape(1, 1, 1).half()
+
+    def cache_breakdown(self):
+        return {'total_bytes': 0}
+
+    def storage_descriptor(self):
+        return {'format': 'FP4_LATENT_STATE_STORAGE_V1'}
 
 
 def _worker(rank, world, port, windows, q):
@@ -88,7 +113,8 @@ def _worker(rank, world, port, windows, q):
         dist.destroy_process_group()
 
 
-def test_window_sharding_gloo_two_ranks():
+@pytest.mark.parametrize('world', [2, 4])
+def test_window_sharding_gloo(world):
     import socket
     import torch.multiprocessing as mp
     from sq325.scoring import evaluate_ppl, ppl_windows
@@ -98,7 +124,7 @@ def test_window_sharding_gloo_two_ranks():
     s = socket.socket(); s.bind(('127.0.0.1', 0)); port = s.getsockname()[1]; s.close()
     ctx = mp.get_context('spawn')
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, windows, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, windows, q)) for r in range(world)]
     for p in procs:
         p.start()
     nll, count, starts = q.get(timeout=120)
@@ -108,3 +134,39 @@ def test_window_sharding_gloo_two_ranks():
     assert math.isclose(nll, single['nll'], rel_tol=1e-12)
     assert count == single['target_tokens']
     assert starts == [w[0] for w in windows]
+
+
+def test_evaluate_ppl_report_row_and_probe(tmp_path):
+    """The reference's report contract (run_fp4_ridge_resurface_v3.py:81-121): the row is
+    written with the static hashes and the repeated-reset probe, rewritten per batch, and
+    marked complete with the pooled figures."""
+    import json
+    from sq325.scoring import evaluate_ppl, ppl_windows
+    ids = np.random.default_rng(1).integers(0, 1000, 3 * 16 + 5)
+    windows = [(s, torch.from_numpy(w)) for s, w in ppl_windows(ids, 16)]
+    path = tmp_path / 'ppl.json'
+    res = evaluate_ppl(_FakeExecution(), windows, batch_windows=2, path=path, common={'arm': 'test'}, probe_tokens=8)
+    row = json.loads(path.read_text())
+    assert row['arm'] == 'test' and row['complete'] is True and row['ppl_complete'] is True
+    assert row['layer_layouts'] == ['32_32_64', '8_80_40']
+    assert len(row['static_basis_sha256']) == 2 and len(row['static_predictor_sha256'][0]) == 8
+    probe = row['repeated_reset_probe']
+    assert probe['tokens'] == 8 and probe['hidden_and_cache_exact'] is True
+    assert set(probe['cache_tensor_sha256']) == {'0.lo', '0.conv', '1.lo', '1.conv'}
+    assert math.isclose(row['ppl']['nll'], res['nll']) and row['ppl']['target_tokens'] == res['target_tokens']
+    assert [w['start'] for w in row['ppl']['windows']] == [s for s, _ in windows]
+
+
+def test_install_fp16_requires_a_complete_base_ledger(tmp_path):
+    """ResurfaceNative's rule (resurface_native.py:140-142): an expected base ledger must name
+    every base parameter, no more and no less."""
+    from sq325 import model as M, resurface as R
+    model = M.synthetic_model(seed=1, n_layer=2, vocab=64, device='cpu')
+    path = tmp_path / 'adapter_fp16.pt'
+    R.export_fp16(R.random_bank(2, seed=1, device='cpu'), path)
+    names = R.base_parameter_names(model)
+    assert len(names) == 3 + 9 * 2
+    with pytest.raises(ValueError, match='cover every original parameter'):
+        R.install_fp16(model, path, expected_base_hashes={n: '0' for n in list(names)[1:]})
+    bank = R.install_fp16(model, path, expected_base_hashes={n: '0' for n in names})
+    assert bank.base_hashes is not None and model.adapter is bank

@@ -188,3 +188,17 @@ def test_c_restatement_matches_numpy_restatement(layout):
     assert np.array_equal(y1.view(np.uint16), y2.view(np.uint16))
     for k in st:
         assert np.array_equal(st[k].view(np.uint8), st2[k].view(np.uint8)), k
+
+
+@pytest.mark.parametrize('tag', ['plain_', 'stats_'])
+def test_s16_oracle_matches_reference_kernel(golden, tag):
+    """oracle.codec.s16_scan against the reference's _s16_scan run by the interpreter
+    (mamba2_recall/state_codec.py:65-102), statistics reduction included (:256-262)."""
+    d = golden('s16.npz')
+    st = d[tag + 'state_in'].copy()
+    y, stats = oc.s16_scan(*(d[tag + k] for k in ('x', 'dt', 'A', 'B', 'C', 'D', 'dt_bias')), st,
+                           collect_stats=(tag == 'stats_'))
+    assert np.array_equal(y.view(np.uint16), d[tag + 'y'].view(np.uint16))
+    assert np.array_equal(st.view(np.uint16), d[tag + 'state_out'].view(np.uint16))
+    if tag == 'stats_':
+        assert np.array_equal(stats.view(np.uint32), d['stats_stats'].view(np.uint32))
