@@ -151,6 +151,7 @@ class ModelOracle:
         self.caches = None
         self.tokens = 0
         self.capture = None          # a list receives every layer's mixer output when set
+        self.capture_inputs = None   # a list receives every layer's normed input u when set
 
     def reset(self, batch):
         self.caches = [dict(state=oc.allocate_state(batch, HEADS, HEAD_DIM, L.layout),
@@ -165,6 +166,8 @@ class ModelOracle:
         for L, cache in zip(self.layers, self.caches):
             res = hcur if res is None else add16(hcur, res)
             u = rmsnorm(res, L.norm_w, self.eps)
+            if self.capture_inputs is not None:
+                self.capture_inputs.append(u.clone())
             hcur = layer_forward(L, cache, u, self.tokens)
             if self.capture is not None:
                 self.capture.append(hcur.clone())

@@ -16,6 +16,8 @@ What is recorded
                        seeded matrix (codes, E4M3 block bytes, global, FP16).
   adapter.npz          mamba2_recall/resurface_native._Adapter.forward (soft
                        gate, FP16 parameters) on CPU.
+  mk_cases.json        sha256 of the reference's public MK recall prompts
+                       (mamba2_recall/evaluation.py:82-119, both splits).
   s16.npz              the FP16-state control scan `_s16_scan`
                        (mamba2_recall/state_codec.py:65-102) under the interpreter,
                        without and with the calibration statistics (:256-262).
@@ -167,6 +169,22 @@ def s16_case(reference, seed, collect, batch=2, length=5, heads=4, dim=24, group
     return {k: v.numpy() for k, v in rec.items()}
 
 
+def mk_case(reference):
+    """Digest of the reference's public MK prompts (mamba2_recall/evaluation.py:82-119) for
+    both splits: sha256 of the canonical JSON of the case list, plus the counts."""
+    import hashlib
+    import json
+    sys.path.insert(0, str(reference))
+    from mamba2_recall import evaluation as ev
+    out = {}
+    for split in ('validation', 'test'):
+        cases = ev.synthetic_mk_cases(split, 8)
+        raw = json.dumps(cases, sort_keys=True, separators=(',', ':')).encode()
+        out[split] = dict(count=len(cases), sha256=hashlib.sha256(raw).hexdigest(),
+                          first_id=cases[0]['id'], first_answer=cases[0]['answer'])
+    return out
+
+
 def fp4_case(reference, seed=7):
     sys.path.insert(0, str(reference))
     from mamba2_recall import fp4
@@ -212,7 +230,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', type=Path, required=True,
                     help='root of a checkout of the reference repository (read only)')
-    ap.add_argument('--cases', default='codec,s16', help='comma list: codec (+ fp4, adapter), s16')
+    ap.add_argument('--cases', default='codec,s16,mk', help='comma list: codec (+ fp4, adapter), s16, mk')
     args = ap.parse_args()
     ap_cases = args.cases.split(',')
     if 's16' in ap_cases:
@@ -221,6 +239,10 @@ def main():
             rec.update({tag + k: v for k, v in s16_case(args.reference, seed, collect).items()})
         np.savez_compressed(HERE / 's16.npz', **rec)
         print('wrote s16')
+    if 'mk' in ap_cases:
+        import json
+        (HERE / 'mk_cases.json').write_text(json.dumps(mk_case(args.reference), indent=1, sort_keys=True) + '\n')
+        print('wrote mk')
     if 'codec' not in ap_cases:
         return
     ref = install_shims(args.reference)

@@ -5,11 +5,13 @@
                 repacks the carry), seed 0.  Per step: INT8 / INT4 code agreement between the
                 GPU (sq_scan) and the oracle (oracle.cscan, bit-exact with the reference
                 kernel), max-abs / relative error of the decoded carry and of the readout
-                against the oracle and against the fp32 unquantised recurrence.
+                against the oracle and against the fp32 unquantised recurrence; teacher-forced
+                (every step starts from the oracle's carry) and free-running.
   model_run     a full-depth forward (56 layers, the released per-layer layouts) of a short
-                window plus decode steps, GPU (sq_model_forward) against oracle.model: per
-                layer the relative error of the mixer output, the code agreement of the final
-                state, then the final hidden state, logits and per-window NLL.
+                window plus decode steps, GPU against oracle.model: per layer, teacher-forced
+                (the GPU mixer, sq_model_mixer_forward, gets the oracle's input of that layer)
+                the mixer output error, state code agreement and conv ring; free-running
+                (sq_model_forward) the per-layer drift, final hidden state, logits and NLL.
 
 The -m gpu tests (test_gpu_parity_long.py) run these and assert the bars; running this file
 directly writes the full per-step / per-layer report:
@@ -44,8 +46,14 @@ def _rel(a, b):
 
 
 @torch.no_grad()
-def config1_run(layout, steps=2048, seed=0):
-    """Returns per-step arrays and a summary dict (see the module docstring)."""
+def config1_run(layout, steps=2048, seed=0, teacher_forced=False):
+    """Returns per-step arrays and a summary dict (see the module docstring).
+
+    Free-running (default): GPU and oracle each carry their own state for all steps, so a
+    code that flips at a rounding boundary (CUDA expf / logf and FMA contraction against
+    numpy's unfused fp32) persists through the decay (up to 0.99 per step here) and the two
+    carries drift apart.  teacher_forced=True copies the oracle's carry into the GPU state
+    before every step: each step then measures one call's own arithmetic."""
     from sq325 import codec
     n8, n4, nz = oc.layout_counts(layout)
     NS = n8 + n4
@@ -79,9 +87,13 @@ def config1_run(layout, steps=2048, seed=0):
     dtv, dec = cscan.per_token_scalars(dt_raw, A, dtb)
     dtv, dec = dtv[0, 0].astype(np.float64), dec[0, 0].astype(np.float64)
     gidx = np.arange(H) // (H // G)
-    rows = dict(agree8=[], agree4=[], maxcode=[], carry_abs_oracle=[], carry_rel_oracle=[], carry_rel_fp32=[],
+    rows = dict(agree8=[], agree4=[], maxcode=[], within1=[], carry_abs_oracle=[], carry_rel_oracle=[], carry_rel_fp32=[],
                 y_abs_oracle=[], y_rel_oracle=[], y_rel_fp32=[], y_bits_oracle=[])
     for step in range(steps):
+        if teacher_forced:
+            for k, v in st_o.items():
+                t = torch.from_numpy(v.copy()).cuda()
+                st_g.tensors[k].copy_(t.view(torch.float8_e4m3fn) if k == 'latent' else t)
         x = rng.standard_normal((1, 1, H, P)).astype(np.float16)
         Bm = rng.standard_normal((1, 1, G, 128)).astype(np.float16)
         Cm = rng.standard_normal((1, 1, G, 128)).astype(np.float16)
@@ -104,6 +116,7 @@ def config1_run(layout, steps=2048, seed=0):
         rows['agree8'].append(float((q8 == r8).mean()))
         rows['agree4'].append(float((q4 == r4).mean()))
         rows['maxcode'].append(int(max(np.abs(q8 - r8).max(), np.abs(q4 - r4).max())))
+        rows['within1'].append(float(np.concatenate([(np.abs(q8 - r8) <= 1).ravel(), (np.abs(q4 - r4) <= 1).ravel()]).mean()))
         rows['carry_abs_oracle'].append(float(np.abs(tg - to).max()))
         rows['carry_rel_oracle'].append(_rel(tg, to))
         rows['carry_rel_fp32'].append(_rel(tg, s_full[..., :NS]))
@@ -111,7 +124,8 @@ def config1_run(layout, steps=2048, seed=0):
         rows['y_rel_oracle'].append(_rel(yg, y_o))
         rows['y_rel_fp32'].append(_rel(yg[0, 0], y_f[0]))
         rows['y_bits_oracle'].append(float((yg.view(np.uint16) == y_o.view(np.uint16)).mean()))
-    summary = dict(layout=layout, steps=steps,
+    summary = dict(layout=layout, steps=steps, mode='teacher-forced' if teacher_forced else 'free-running',
+                   codes_within_one_step_min=min(rows['within1']),
                    code_agreement_min=min(min(rows['agree8']), min(rows['agree4'])),
                    code_agreement_mean=float(np.mean(rows['agree8'] + rows['agree4'])),
                    max_code_step=max(rows['maxcode']),
@@ -147,8 +161,11 @@ def model_run(n_layer=56, vocab=2048, tokens=16, decode_steps=4, seed=7):
         gcap = cap.float().cpu().numpy()
         ora.reset(1)
         ora.capture = []
+        ora.capture_inputs = []
         href = ora.backbone(prompt)
         nref = ora.nll(href, ids[:, 1:tokens + 1])
+        # scoring head on the oracle's own final hidden state (teacher-forced head)
+        nll_tf = float(ex.score(href.cuda(), torch.from_numpy(ids[:, 1:tokens + 1]).cuda()).double().sum())
         for l in range(n_layer):
             got, ref = gcap[l, :tokens], ora.capture[l].reshape(tokens, -1).float().numpy()
             layers.append(dict(layer=l, layout=layouts[l], mixer_rel_l2=_rel(got, ref),
@@ -165,6 +182,37 @@ def model_run(n_layer=56, vocab=2048, tokens=16, decode_steps=4, seed=7):
             r8, r4 = oc.decode_codes(ora.caches[l]['state'], layouts[l])
             layers[l]['prefill_code_agreement'] = float(np.concatenate([(q8 == r8).ravel(), (q4 == r4).ravel()]).mean())
         ex.capture_layers(0)
+        # teacher-forced per layer: every GPU layer gets the oracle's normed input for that
+        # layer (fresh states), so its error is its own, not the upstream layers'
+        ex.reset(1)
+        for l in range(n_layer):
+            u = ora.capture_inputs[l].cuda()
+            got = ex.mixer_forward(l, u).float().cpu().numpy().reshape(tokens, -1)
+            ref = ora.capture[l].reshape(tokens, -1).float().numpy()
+            sg = {k: (v.view(torch.uint8) if v.dtype == torch.float8_e4m3fn else v).cpu().numpy()
+                  for k, v in ex._cache[l].state.tensors.items()}
+            q8, q4 = oc.decode_codes(sg, layouts[l])
+            r8, r4 = oc.decode_codes(ora.caches[l]['state'], layouts[l])
+            diff = np.concatenate([np.abs(q8 - r8).ravel(), np.abs(q4 - r4).ravel()])
+            layers[l].update(tf_mixer_rel_l2=_rel(got, ref), tf_code_agreement=float((diff == 0).mean()),
+                             tf_max_code_step=int(diff.max()),
+                             tf_conv_ring_rel=_rel(ex.conv_chronological(l).float().cpu().numpy(),
+                                                   ora.caches[l]['conv'].float().numpy()))
+        tf_step = []
+        for s_ in range(decode_steps):
+            nxt = ids[:, tokens + s_:tokens + s_ + 1]
+            ora.capture, ora.capture_inputs = [], []
+            ora.backbone(nxt)
+            worst = 0.0
+            for l in range(n_layer):
+                got = ex.mixer_forward(l, ora.capture_inputs[l].cuda()).float().cpu().numpy()
+                worst = max(worst, _rel(got.reshape(-1), ora.capture[l].float().numpy().reshape(-1)))
+            tf_step.append(worst)
+        ora.capture = ora.capture_inputs = None
+        # free-running decode steps from the free-running prefill
+        ex.backbone(torch.from_numpy(prompt).cuda(), reset=True)
+        ora.reset(1)
+        ora.backbone(prompt)
         step_rel = []
         for s in range(decode_steps):
             nxt = ids[:, tokens + s:tokens + s + 1]
@@ -177,6 +225,12 @@ def model_run(n_layer=56, vocab=2048, tokens=16, decode_steps=4, seed=7):
         lref = ora.logits(h[:, -1].cpu())
         logits_rel = _rel(logits.float().cpu().numpy(), lref.float().numpy())
     summary = dict(n_layer=n_layer, vocab=vocab, tokens=tokens, decode_steps=decode_steps,
+                   tf_mixer_rel_l2_max=max(x['tf_mixer_rel_l2'] for x in layers),
+                   tf_code_agreement_min=min(x['tf_code_agreement'] for x in layers),
+                   tf_max_code_step=max(x['tf_max_code_step'] for x in layers),
+                   tf_conv_ring_rel_max=max(x['tf_conv_ring_rel'] for x in layers),
+                   tf_decode_mixer_rel_l2_max=max(tf_step),
+                   tf_head_nll_rel=abs(nll_tf - nll_o) / abs(nll_o),
                    hidden_rel_l2=hid_rel, window_nll_gpu=nll_g, window_nll_oracle=nll_o,
                    window_nll_rel=abs(nll_g - nll_o) / abs(nll_o), decode_hidden_rel_l2=step_rel,
                    decode_logits_rel_l2=logits_rel,
@@ -194,11 +248,13 @@ def main():
     args = ap.parse_args()
     args.out.mkdir(parents=True, exist_ok=True)
     report = dict(config1=[], model=None)
-    for layout in oc.LAYOUTS:
-        rows, summary = config1_run(layout, steps=args.steps)
-        report['config1'].append(summary)
-        np.savez_compressed(args.out / f'config1_{layout}.npz', **{k: np.asarray(v) for k, v in rows.items()})
-        print(json.dumps(summary), flush=True)
+    for tf in (True, False):
+        for layout in oc.LAYOUTS:
+            rows, summary = config1_run(layout, steps=args.steps, teacher_forced=tf)
+            report['config1'].append(summary)
+            np.savez_compressed(args.out / f"config1_{'tf' if tf else 'free'}_{layout}.npz",
+                                **{k: np.asarray(v) for k, v in rows.items()})
+            print(json.dumps(summary), flush=True)
     if not args.skip_model:
         layers, summary = model_run(n_layer=args.layers)
         report['model'] = dict(summary=summary, layers=layers)

@@ -170,3 +170,29 @@ def test_install_fp16_requires_a_complete_base_ledger(tmp_path):
         R.install_fp16(model, path, expected_base_hashes={n: '0' for n in list(names)[1:]})
     bank = R.install_fp16(model, path, expected_base_hashes={n: '0' for n in names})
     assert bank.base_hashes is not None and model.adapter is bank
+
+
+def test_mk_cases_match_reference_digest():
+    """sq325.recall.synthetic_mk_cases reproduces the reference's public MK prompts
+    (mamba2_recall/evaluation.py:82-119) exactly: same canonical-JSON digest for both splits."""
+    import hashlib
+    import json
+    from sq325.recall import synthetic_mk_cases
+    from conftest import GOLDEN
+    ref = json.loads((GOLDEN / 'mk_cases.json').read_text())
+    for split in ('validation', 'test'):
+        cases = [{k: v for k, v in c.items() if k != 'records'} for c in synthetic_mk_cases(split, 8)]
+        raw = json.dumps(cases, sort_keys=True, separators=(',', ':')).encode()
+        assert len(cases) == ref[split]['count'] == 96
+        assert hashlib.sha256(raw).hexdigest() == ref[split]['sha256']
+
+
+def test_mk_classification_and_matching():
+    from sq325.recall import SIX_DIGITS, classify_prediction
+    assert SIX_DIGITS.search(' 1234567 and 654321.').group() == '654321'
+    row = dict(answer='600001', condition='normal', records=[(100001, 600001), (100002, 600002)])
+    assert classify_prediction(dict(row, prediction='600001')) == 'correct_target'
+    assert classify_prediction(dict(row, prediction='600002')) == 'wrong_present_value'
+    assert classify_prediction(dict(row, prediction=None)) == 'unparseable'
+    assert classify_prediction(dict(row, prediction='999999')) == 'not_present_value'
+    assert classify_prediction(dict(row, condition='target_removed', prediction='600001')) == 'removed_target_match'
