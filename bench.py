@@ -11,7 +11,8 @@ already resident on the device; `e2e` = the same through the public scoring API 
 pinned host buffers (H2D of the windows, D2H of the per-window NLLs, every step).
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
-  python bench.py --case gemm|scan|decode [--layout L] [--layers N --vocab V] --steps K   (one kernel, for ncu)
+  python bench.py --case gemm|scan|decode|gemv|s16 [--layout L|all] [--layers N --vocab V] [--rows M]
+                  --steps K   (one kernel on a small case, for timing and ncu)
   torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU, NCCL)
 """
 from __future__ import annotations
@@ -125,7 +126,7 @@ def dist_init(n):
 _CPU_MODELS = {}
 
 
-def cpu_sample(tokens=512, layers=2, vocab_slice=32768, seed=0):
+def cpu_sample(tokens=2048, layers=3, vocab_slice=32768, seed=0):
     """The CPU oracle port (oracle/) on a bounded slice of the workload: one window of
     `tokens` tokens through `layers` full-geometry layers plus the lm_head + CE over a
     `vocab_slice`-row slice of the vocabulary, all host threads.  Returns seconds per
@@ -259,6 +260,25 @@ def run_case(args):
         call = lambda: _lib.call('sq_gemm_f16', _lib.ptr(a), K, _lib.ptr(b), K, _lib.ptr(c), N, M, N, K,
                                  _lib.stream_ptr())
         unit, work = 'TFLOP/s', 2.0 * M * N * K
+    elif args.case == 'gemv':                     # FP4 skinny GEMM, in_proj shape at M = args.rows (config 2)
+        from sq325 import fp4 as F
+        w = F.synthetic(18560, 4096, gen, 'cuda')
+        x = torch.randn(args.rows, 4096, device='cuda', generator=gen).half()
+        call = lambda: F.linear(w, x)
+        unit, work = 'GB/s', 18560 * 4096 * 9 / 16 + args.rows * (4096 + 18560) * 2
+    elif args.case == 's16':                      # FP16-state control scan, 16 x 128 x 64 rows, 512 tokens
+        from sq325 import state_codec as sc
+        B, L, H, P, G = 16, 512, 128, 64, 8
+        x = torch.randn(B, L, H, P, device='cuda', generator=gen).half()
+        dt = (torch.randn(B, L, H, device='cuda', generator=gen) * 0.5).half()
+        A = -(torch.rand(H, device='cuda', generator=gen) * 3 + 0.1)
+        Bm = torch.randn(B, L, G, 128, device='cuda', generator=gen).half()
+        Cm = torch.randn(B, L, G, 128, device='cuda', generator=gen).half()
+        D = torch.randn(H, device='cuda', generator=gen).half()
+        db = (torch.rand(H, device='cuda', generator=gen) * 3 - 4).half()
+        st = sc.allocate_state(B, H, P, 128, 's16', 'cuda')
+        call = lambda: sc.scan(x, dt, A, Bm, Cm, D, db, st)
+        unit, work = 'us/token', float(L)
     else:                                         # SQ3.25 scan: prep + chunk kernels, 16 x 128 x 64 rows
         B, L, H, P, G = 16, 512, 128, 64, 8
         spec = codec.layout_descriptor(args.layout)
@@ -288,10 +308,10 @@ def run_case(args):
         torch.cuda.synchronize()
         ts.append(ev[0].elapsed_time(ev[1]) / 1e3)
     t = statistics.median(ts)
-    val = work / t / 1e12 if unit == 'TFLOP/s' else t * 1e6 / work
+    val = work / t / 1e12 if unit == 'TFLOP/s' else (work / t / 1e9 if unit == 'GB/s' else t * 1e6 / work)
     print(json.dumps(dict(case=args.case, layout=args.layout if args.case == 'scan' else None, seconds=t,
-                          value=val, unit=unit, steps=args.steps,
-                          layers=args.layers if args.case == 'decode' else None)))
+                          value=val, unit=unit, steps=args.steps, rows=args.rows if args.case == 'gemv' else None,
+                          layers=args.layers if args.case == 'decode' else None)), flush=True)
 
 
 L2_FLUSH_BYTES = 256 << 20      # > 126 MB of L2
@@ -308,14 +328,19 @@ class L2Flush:
 
 
 def timed(call, reps, flush=None, stream=None):
-    """Median CUDA-event seconds of `call` on the current stream, L2 flushed before each."""
+    """Median CUDA-event seconds of `call` on the current stream, L2 flushed before each.
+
+    The flush (and a ~100 us device-side sleep behind it) is still running when the start
+    event and the launch are enqueued, so host launch overhead never falls inside the
+    measured interval."""
     s = stream or torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ts = []
     for _ in range(reps):
+        torch.cuda.synchronize()
         if flush:
             flush()
-        torch.cuda.synchronize()
+        torch.cuda._sleep(200000)
         e0.record(s)
         call()
         e1.record(s)
@@ -450,18 +475,25 @@ def main():
     ap.add_argument('--steps', type=int, default=4)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='native', choices=['native', 'reference'])
-    ap.add_argument('--ref-tokens', type=int, default=512)
+    ap.add_argument('--ref-tokens', type=int, default=2048)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-extras', action='store_true',
                     help='skip the config 2 / 3 / 5 measurements of the one-GPU line')
-    ap.add_argument('--case', choices=['gemm', 'scan', 'decode'], default=None,
+    ap.add_argument('--rows', type=int, default=1, help='M of --case gemv')
+    ap.add_argument('--case', choices=['gemm', 'scan', 'decode', 'gemv', 's16'], default=None,
                     help='time one kernel on a small case (for ncu captures) instead of the bench')
     ap.add_argument('--layout', default='32_32_64', help='scan layout of --case scan')
     ap.add_argument('--layers', type=int, default=4, help='layers of --case decode')
     ap.add_argument('--vocab', type=int, default=32768, help='vocabulary of --case decode')
     args = ap.parse_args()
     if args.case:
-        run_case(args)
+        if args.case == 'scan' and args.layout == 'all':
+            from sq325.codec import LAYOUTS
+            for layout in LAYOUTS:
+                args.layout = layout
+                run_case(args)
+        else:
+            run_case(args)
         return
     args.steps_ref = min(args.steps, 3)
     args.warmup_ref = 1 if args.warmup > 0 else 0

@@ -186,7 +186,9 @@ int sq_gemm_f16(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb,
 int sq_device_check(void* stream);
 /* Failure detection: the limit, in nanoseconds, of the skinny-GEMM kernel's pipeline waits
  * (sq_fp4_linear with m <= 64, the model's decode-step projections and greedy head) on
- * the current device; 0 restores the default of 2 s.  When a wait reaches the limit the
+ * the current device; 0 restores the default of 2 s, and a limit under 2 us (finer than the
+ * device timer resolves) makes each wait a single non-blocking test.  When a wait
+ * reaches the limit the
  * kernel records an error bit, waits (with the default limit) for its own copies in
  * flight and returns, leaving the context usable; the call's check (sq_device_check or
  * sq_model_check) then returns SQ_ETIMEOUT.  Tests set a tiny limit to drive that path;

@@ -223,8 +223,19 @@ __device__ __forceinline__ bool gv_try(uint32_t a, uint32_t parity) {
 // settable per device for failure-detection tests (set_gemv_wait_limit_ns).  The drain
 // waits after an expiry keep the fixed kGvWaitNs, so copies already in flight always land
 // before the CTA exits.
+// A limit below kGvTimerNs (shorter than %globaltimer can resolve) makes the wait a single
+// non-blocking test of the phase (mbarrier.try_wait itself may suspend the thread for a
+// while before it reports an incomplete phase).
 __device__ unsigned long long g_gv_wait_ns = kGvWaitNs;
+constexpr unsigned long long kGvTimerNs = 2000;
+__device__ __forceinline__ bool gv_test(uint32_t a, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n.reg .pred p;\nmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ bool gv_wait_for(uint32_t a, uint32_t parity, unsigned long long limit) {
+  if (limit < kGvTimerNs) return gv_test(a, parity);
   if (gv_try(a, parity)) return true;
   const uint64_t t0 = gv_time();
   for (;;) {

@@ -62,13 +62,17 @@ struct ScanSmem {
   static constexpr int kBytes = oW + 3 * 128 * 5 * 4;
 };
 
-// Resident CTAs per SM the register budget is sized for: 4 (<= 128 registers) while the
-// stored row fits, 3 for the widest layouts.
+// Resident CTAs per SM the register budget is sized for: 4 (<= 128 registers) for every
+// layout.  The folded multi-token readout (recur_row_fold) keeps one accumulation per pair,
+// which leaves room for the widest stored row (84 coordinates) in 128 registers.
 template <int N8, int N4>
-constexpr int scan_min_blocks() { return N8 + N4 >= 68 ? 3 : 4; }
+constexpr int scan_min_blocks() { return 4; }
+// The single fused kernel also holds the group dots' staging: 3 CTAs for the widest rows.
+template <int N8, int N4>
+constexpr int fused_min_blocks() { return N8 + N4 >= 68 ? 3 : 4; }
 
 template <int N8, int N4, int KJ, int MODE, int TC>
-__global__ void __launch_bounds__(128, MODE == 2 ? 1 : scan_min_blocks<N8, N4>())   // decode grids are small
+__global__ void __launch_bounds__(128, MODE == 2 ? 1 : fused_min_blocks<N8, N4>())   // decode grids are small
 ssu_sq325_kernel(const ScanParams P) {
   using L = ScanSmem<N8, N4, TC>;
   constexpr int NZ = L::NZ;
@@ -319,10 +323,20 @@ ssu_sq325_kernel(const ScanParams P) {
           acc1 = fmaf(tb[(j0 >> 1) * 4 + 3], pr[d + 1], acc1);
         }
         const float acc = acc0 + acc1;
-        if (f < N8 + N4) reinterpret_cast<float*>(sV2)[t * 128 + f] = acc;
+        // multi-token modes fold C into the correction vector (recur_row_fold)
+        if (f < N8 + N4) reinterpret_cast<float*>(sV2)[t * 128 + f] = MODE == 2 ? acc : tb[(f >> 1) * 4 + 2 + (f & 1)] + acc;
         else sDots[t * 8 + 5 + f - (N8 + N4)] = acc;
+      } else if (f == F && MODE != 2) {
+        // B.C over all 128 coordinates (the folded readout's current-token term)
+#pragma unroll 4
+        for (int j0 = 0; j0 < 128; j0 += 2) {
+          const float* q = tb + (j0 >> 1) * 4;
+          acc0 = fmaf(q[0], q[2], acc0);
+          acc1 = fmaf(q[1], q[3], acc1);
+        }
+        sDots[t * 8 + 0] = acc0 + acc1;
       } else {
-        const int k = f - F;   // 0: B.C, 1: basis0.C, 2: basis1.C, 3: basis0.B, 4: basis1.B
+        const int k = f - F;   // 0: B.C (zero tier), 1: basis0.C, 2: basis1.C, 3: basis0.B, 4: basis1.B
         const float* us = (k == 0) ? nullptr : sBasis + ((k - 1) & 1) * NZ;
         const int voff = (k >= 3 || k == 0) ? 0 : 2;   // 0 -> B, 2 -> C (within the float4)
 #pragma unroll 4
@@ -345,20 +359,20 @@ ssu_sq325_kernel(const ScanParams P) {
       const float dtv = sDD[(t * kMaxHpc + hl) * 2 + 0];
       const float dec = sDD[(t * kMaxHpc + hl) * 2 + 1];
       const float x = sX[t * 128 + tid];
-      float ysum, ycorr, m8, m4;
-      if (MODE == 2) {                                 // one-token step: four readout streams
-        recur_row4<N8, NP>(S, sP4 + t * 64, sV2 + t * 64, dec, dtv, x, ysum, ycorr, m8, m4);
-      } else {
-        float2 ya, yb, ca, cb;
-        recur_row<N8, NP>(S, sP4 + t * 64, sV2 + t * 64, dec, dtv, x, ya, yb, ca, cb, m8, m4);
-        ysum = (ya.x + ya.y) + (yb.x + yb.y);
-        ycorr = (ca.x + ca.y) + (cb.x + cb.y);
-      }
+      float m8, m4;
       float dots[7];
 #pragma unroll
       for (int i = 0; i < 7; ++i) dots[i] = sDots[t * 8 + i];
       TokenScales ts;
-      const float out = token_tail_sums(ysum, ycorr, m8, m4, x, dtv, dec, dv, dots, zz, ls2, nls2, ils2, ts);
+      float out;
+      if (MODE == 2) {                                 // one-token step: four readout streams
+        float ysum, ycorr;
+        recur_row4<N8, NP>(S, sP4 + t * 64, sV2 + t * 64, dec, dtv, x, ysum, ycorr, m8, m4);
+        out = token_tail_sums(ysum, ycorr, m8, m4, x, dtv, dec, dv, dots, zz, ls2, nls2, ils2, ts);
+      } else {                                         // multi-token: folded readout
+        const float yacc = recur_row_fold<N8, NP, false, true>(S, sP4 + t * 64, sV2 + t * 64, dec, dtv, x, m8, m4);
+        out = token_tail_fold(yacc, m8, m4, x, dtv, dec, dv, dots, zz, ls2, nls2, ils2, ts);
+      }
       P.y[(long long)b * P.y_sb + (long long)(c0 + t) * P.y_st + (long long)h * dim + p] = f2h(out);
       // INT8 / INT4 requant (:155-162, scripts/state_ppl_codec_v6.py:52-61)
       s8 = ts.s8; s4 = ts.s4;
@@ -427,7 +441,8 @@ ssu_sq325_kernel(const ScanParams P) {
 // the group: the B/C conv (mode 1), the predictor readout vector cvec, the pcz pair and the
 // five zero-tier dots, and dt/decay per head.  Its outputs go to a caller workspace:
 //   bc   [B][T][G][256] fp16   conv'd B (tier order) then conv'd C (tier order)
-//   pv   [B][T][G][FP]  fp32   cvec[0..NS) | pcz0 pcz1 | B.C, b0.C, b1.C, b0.B, b1.B | pad
+//   pv   [B][T][G][FP]  fp32   C + cvec [0..NS) | pcz0 pcz1 | B.C (all 128), b0.C, b1.C, b0.B,
+//                              b1.B | pad   (the folded readout, recur_row_fold)
 //   ddt  [B][T][H]      float2 (dt after softplus, exp(A dt))
 // ssu_chunk_kernel then streams x (raw in mode 1), bc, pv and ddt through a cp.async ring and
 // runs the recurrence with B*dt precomputed per head.  Same arithmetic, operation for
@@ -534,6 +549,16 @@ scan_prep_kernel(const ScanParams P) {
         acc1 = fmaf(tb[128 + NS + d + 1], pr[d + 1], acc1);
       }
       r = acc0 + acc1;
+      if (f < NS) r = tb[128 + f] + r;                  // C_j + cvec_j (the folded readout)
+    } else if (f == F) {
+      // B.C over all 128 coordinates, the same order as the fused kernel
+      float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 4
+      for (int j0 = 0; j0 < 128; j0 += 2) {
+        acc0 = fmaf(tb[j0], tb[128 + j0], acc0);
+        acc1 = fmaf(tb[j0 + 1], tb[128 + j0 + 1], acc1);
+      }
+      r = acc0 + acc1;
     } else if (f < F + 5) {
       const int k = f - F;   // 0: B.C, 1: basis0.C, 2: basis1.C, 3: basis0.B, 4: basis1.B
       const float* us = (k == 0) ? nullptr : sBasis + ((k - 1) & 1) * NZ;
@@ -615,7 +640,7 @@ ssu_chunk_kernel(const ScanParams P) {
   const uint16_t* xb = P.x + (long long)b * P.x_sb + (long long)h0 * dim;
   const bool vec = ((((uintptr_t)xb) & 15) == 0) && (P.x_st & 7) == 0;
   const long long btg = (long long)b * P.length;       // token row base of this batch entry
-  constexpr int kPcs = 16 + 32 + FP / 4;               // 16-byte pieces per token (x, bc, pv)
+  constexpr int kPcs = 16 + 16 + FP / 4;               // 16-byte pieces per token (x, B half of bc, pv)
 
   auto prefetch = [&](int c0) {
     const int nt = min(TC, P.length - c0);
@@ -631,10 +656,10 @@ ssu_chunk_kernel(const ScanParams P) {
 #pragma unroll
           for (int e = 0; e < 8; ++e) dst[e] = src[e];
         }
-      } else if (r < 48) {
+      } else if (r < 32) {
         cp_async16(slot + L::oBC + (r - 16) * 16, P.prep_bc + ((btg + tt) * P.groups + g) * 256 + (r - 16) * 8);
       } else if (r < kPcs) {
-        cp_async16(slot + L::oPV + (r - 48) * 16, P.prep_pv + ((btg + tt) * P.groups + g) * FP + (r - 48) * 4);
+        cp_async16(slot + L::oPV + (r - 32) * 16, P.prep_pv + ((btg + tt) * P.groups + g) * FP + (r - 32) * 4);
       } else {
         cp_async8(slot + L::oDD + (r - kPcs) * 8, P.prep_ddt + (btg + tt) * P.heads + h0 + (r - kPcs));
       }
@@ -719,7 +744,8 @@ ssu_chunk_kernel(const ScanParams P) {
           sX[t * 128 + tid] = xv;
           const uint16_t* bc = reinterpret_cast<const uint16_t*>(slot + L::oBC);
           const float2* dd = reinterpret_cast<const float2*>(slot + L::oDD);
-          const float bv = h2f(bc[j]), cv = h2f(bc[128 + j]);
+          const float bv = h2f(bc[j]);
+          const float cv = j < NS ? reinterpret_cast<const float*>(slot + L::oPV)[j] : 0.f;   // C_j + cvec_j
           for (int hh = 0; hh < hpc; ++hh) {
             float* q = sPf + ((t * hpc + hh) * 64 + (j >> 1)) * 4 + (j & 1);
             q[0] = bv * dd[hh].x;
@@ -738,25 +764,10 @@ ssu_chunk_kernel(const ScanParams P) {
       const float2 ddv = reinterpret_cast<const float2*>(slot + L::oDD)[hl];
       const float dtv = ddv.x, dec = ddv.y;
       const float x = sX[t * 128 + tid];
-      const float2 dd = make_float2(dec, dec), xx = make_float2(x, x);
       const float4* cp = sP4 + (t * hpc + hl) * 64;
       const float* pv = reinterpret_cast<const float*>(slot + L::oPV);
-      const float2* vp = reinterpret_cast<const float2*>(pv);
-      float2 ya = make_float2(0.f, 0.f), yb = ya, ca = ya, cb = ya;
-      float m8a = 0.f, m8b = 0.f, m4a = 0.f, m4b = 0.f;
-#pragma unroll
-      for (int jp = 0; jp < NP; ++jp) {
-        const float4 bc = cp[jp];
-        const float2 cv = vp[jp];
-        const float2 pr = make_float2(S[2 * jp], S[2 * jp + 1]);
-        const float2 upd = __fmul2_rn(make_float2(bc.x, bc.y), xx);                   // (B*dt)*x
-        const float2 sn = __ffma2_rn(pr, dd, upd);                                      // prior*decay + upd
-        S[2 * jp] = sn.x; S[2 * jp + 1] = sn.y;
-        if (jp & 1) { yb = __ffma2_rn(sn, make_float2(bc.z, bc.w), yb); cb = __ffma2_rn(pr, cv, cb); }
-        else        { ya = __ffma2_rn(sn, make_float2(bc.z, bc.w), ya); ca = __ffma2_rn(pr, cv, ca); }
-        if (2 * jp < N8) { m8a = fmaxf(m8a, fabsf(sn.x)); m8b = fmaxf(m8b, fabsf(sn.y)); }
-        else             { m4a = fmaxf(m4a, fabsf(sn.x)); m4b = fmaxf(m4b, fabsf(sn.y)); }
-      }
+      float m8, m4;
+      const float yacc = recur_row_fold<N8, NP, true, false>(S, cp, nullptr, dec, dtv, x, m8, m4);
       float dots[7];
       {
         const float2 d01 = *reinterpret_cast<const float2*>(pv + F), d23 = *reinterpret_cast<const float2*>(pv + F + 2);
@@ -765,8 +776,7 @@ ssu_chunk_kernel(const ScanParams P) {
         dots[5] = pz.x; dots[6] = pz.y;
       }
       TokenScales ts;
-      const float out = token_tail(ya, yb, ca, cb, fmaxf(m8a, m8b), fmaxf(m4a, m4b), x, dtv, dec, dv, dots, zz,
-                                   ls2, nls2, ils2, ts);
+      const float out = token_tail_fold(yacc, m8, m4, x, dtv, dec, dv, dots, zz, ls2, nls2, ils2, ts);
       P.y[(long long)b * P.y_sb + (long long)(c0 + t) * P.y_st + (long long)h * dim + p] = f2h(out);
       // INT8 / INT4 requant (:155-162, scripts/state_ppl_codec_v6.py:52-61)
       s8 = ts.s8; s4 = ts.s4;

@@ -88,6 +88,34 @@ __device__ __forceinline__ float token_tail(float2 ya, float2 yb, float2 ca, flo
                          z, ls, nls, ils, ts);
 }
 
+// Token tail of the folded multi-token readout (recur_row_fold): the stored tiers' readout
+// and the predictor correction arrive as one sum yacc = sum_j prior_j (C_j + cvec_j), and
+// the stored tiers' current-token term x dt sum_j B_j C_j joins the zero tier's under
+// dots[0] = B.C over all 128 coordinates:
+//   out = dec (yacc + z0 c0 + z1 c1 + z0 pcz0 + z1 pcz1) + (x dt) B.C + x D
+// (the same value as token_tail_sums with S_j = prior_j dec + (B_j dt) x substituted, summed
+// in another order).  dots = {B.C (all), b0.C, b1.C, b0.B, b1.B, pcz0, pcz1}.  The latent
+// update and the INT scales are token_tail_sums'.
+__device__ __forceinline__ float token_tail_fold(float yacc, float m8, float m4, float x, float dtv, float dec,
+                                                 float dv, const float (&dots)[7], float2& z, float2 ls, float2 nls,
+                                                 float2 ils, TokenScales& ts) {
+  const float xdt = x * dtv;
+  const float zc = fmaf(z.x, dots[1], z.y * dots[2]);
+  const float corr = fmaf(z.y, dots[6], fmaf(z.x, dots[5], yacc));
+  const float out = fmaf(dec, corr + zc, fmaf(xdt, dots[0], x * dv));
+  z = __ffma2_rn(z, make_float2(dec, dec), __fmul2_rn(make_float2(xdt, xdt), make_float2(dots[3], dots[4])));
+  float2 q = div_exact2(z, nls, ils);
+  q = make_float2(fminf(fmaxf(q.x, -448.f), 448.f), fminf(fmaxf(q.y, -448.f), 448.f));
+  const __half2_raw hz = __nv_cvt_fp8x2_to_halfraw2(__nv_cvt_float2_to_fp8x2(q, __NV_SATFINITE, __NV_E4M3), __NV_E4M3);
+  z = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&hz)), ls);
+  float2 sc = div_exact2(make_float2(m8, m4), make_float2(-127.f, -7.f), make_float2(1.0f / 127.0f, 1.0f / 7.0f));
+  sc = __half22float2(__float22half2_rn(make_float2(fmaxf(sc.x, 1e-8f), fmaxf(sc.y, 1e-8f))));
+  ts.s8 = sc.x; ts.s4 = sc.y;
+  ts.i8 = sc.x > 0.f ? __frcp_rn(sc.x) : 0.f;
+  ts.i4 = sc.y > 0.f ? __frcp_rn(sc.y) : 0.f;
+  return out;
+}
+
 // Requant of every stored pair with the row's new scales.
 template <int N8, int NP>
 __device__ __forceinline__ void requant_row(float (&S)[2 * NP], const TokenScales& ts) {
@@ -129,6 +157,37 @@ __device__ __forceinline__ void recur_row(float (&S)[2 * NP], const float4* __re
   }
   m8 = fmaxf(m8a, m8b);
   m4 = fmaxf(m4a, m4b);
+}
+
+// Folded multi-token form of recur_row (pairs with token_tail_fold): one accumulation of
+// prior_j (C_j + cvec_j) per pair instead of separate readout and correction sums.
+// cp[jp].xy = {B_j, B_j+1} (times dt when PREMUL, rounded once, as B * dt here) and the
+// pair {C_j + cvec_j, C_j+1 + cvec_j+1} is cp[jp].zw, or vp[jp] when SPLIT.  The new state is
+// prior * dec + (B dt) x as in recur_row; the readout accumulates in two chains (even / odd
+// pairs) added as (ya.x + ya.y) + (yb.x + yb.y).
+template <int N8, int NP, bool PREMUL, bool SPLIT>
+__device__ __forceinline__ float recur_row_fold(float (&S)[2 * NP], const float4* __restrict__ cp,
+                                                const float2* __restrict__ vp, float dec, float dtv, float x,
+                                                float& m8, float& m4) {
+  const float2 dd = make_float2(dec, dec), dt2 = make_float2(dtv, dtv), xx = make_float2(x, x);
+  float2 ya = make_float2(0.f, 0.f), yb = ya;
+  float m8a = 0.f, m8b = 0.f, m4a = 0.f, m4b = 0.f;
+#pragma unroll
+  for (int jp = 0; jp < NP; ++jp) {
+    const float4 bc = cp[jp];
+    const float2 cc = SPLIT ? vp[jp] : make_float2(bc.z, bc.w);
+    const float2 pr = make_float2(S[2 * jp], S[2 * jp + 1]);
+    const float2 bdt = PREMUL ? make_float2(bc.x, bc.y) : __fmul2_rn(make_float2(bc.x, bc.y), dt2);
+    const float2 sn = __ffma2_rn(pr, dd, __fmul2_rn(bdt, xx));                          // prior*decay + (B*dt)*x
+    S[2 * jp] = sn.x; S[2 * jp + 1] = sn.y;
+    if (jp & 1) yb = __ffma2_rn(pr, cc, yb);
+    else        ya = __ffma2_rn(pr, cc, ya);
+    if (2 * jp < N8) { m8a = fmaxf(m8a, fabsf(sn.x)); m8b = fmaxf(m8b, fabsf(sn.y)); }
+    else             { m4a = fmaxf(m4a, fabsf(sn.x)); m4b = fmaxf(m4b, fabsf(sn.y)); }
+  }
+  m8 = fmaxf(m8a, m8b);
+  m4 = fmaxf(m4a, m4b);
+  return (ya.x + ya.y) + (yb.x + yb.y);
 }
 
 // The one-token step's form of recur_row: the readout and correction sums run as four

@@ -83,12 +83,20 @@ def config1_run(layout, steps=2048, seed=0, teacher_forced=False):
     T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
     gperm, gbasis, gls, gpred, gA, gD, gdtb, gdt = (T(a) for a in (perm, basis, ls, pred, A, D, dtb, dt_raw))
     # fp32 unquantised recurrence in tier order (the zero tier carries state here too)
-    s_full = dense.astype(np.float64)
-    dtv, dec = cscan.per_token_scalars(dt_raw, A, dtb)
-    dtv, dec = dtv[0, 0].astype(np.float64), dec[0, 0].astype(np.float64)
     gidx = np.arange(H) // (H // G)
-    rows = dict(agree8=[], agree4=[], maxcode=[], within1=[], carry_abs_oracle=[], carry_rel_oracle=[], carry_rel_fp32=[],
-                y_abs_oracle=[], y_rel_oracle=[], y_rel_fp32=[], y_bits_oracle=[])
+    s_full = np.ascontiguousarray(dense[0])                                             # [H,P,128] fp32
+    dtv, dec = cscan.per_token_scalars(dt_raw, A, dtb)
+    dtv, dec = dtv[0, 0], dec[0, 0]                                                     # [H] fp32
+    Df = D.astype(np.float32)
+    rows = dict(agree8=[], agree4=[], maxcode=[], within1=[], carry_abs_oracle=[], carry_rel_oracle=[],
+                carry_rel_fp32=[], y_abs_oracle=[], y_rel_oracle=[], y_rel_fp32=[], y_bits_oracle=[])
+
+    def rel32(a, b):
+        a = np.asarray(a, np.float32).ravel()
+        b = np.asarray(b, np.float32).ravel()
+        d = a - b
+        return float(np.sqrt(np.dot(d, d)) / max(np.sqrt(np.dot(b, b)), 1e-30))
+
     for step in range(steps):
         if teacher_forced:
             for k, v in st_o.items():
@@ -99,13 +107,13 @@ def config1_run(layout, steps=2048, seed=0, teacher_forced=False):
         Cm = rng.standard_normal((1, 1, G, 128)).astype(np.float16)
         y_g, _ = codec.scan(T(x), gdt, gA, T(Bm), T(Cm), gD, gdtb, st_g, gperm, gbasis, gls, gpred, layout=layout)
         y_o = cscan.latent_scan(x, dt_raw, A, Bm, Cm, D, dtb, st_o, perm, basis, ls, pred, layout)
-        # unquantised: coordinates in tier order per group
-        b_tier = np.stack([Bm[0, 0, g].astype(np.float64)[perm[g]] for g in range(G)])        # [G,128]
-        c_tier = np.stack([Cm[0, 0, g].astype(np.float64)[perm[g]] for g in range(G)])
-        xv = x[0, 0].astype(np.float64)                                                          # [H,P]
-        s_full = s_full * dec[None, :, None, None] + \
-            (b_tier[gidx][None, :, None, :] * dtv[None, :, None, None]) * xv[None, :, :, None]
-        y_f = (s_full * c_tier[gidx][None, :, None, :]).sum(-1) + xv[None] * D.astype(np.float64)[None, :, None]
+        # unquantised fp32 recurrence, coordinates in tier order per group
+        b_tier = np.take_along_axis(Bm[0, 0].astype(np.float32), perm.astype(np.int64), 1)     # [G,128]
+        c_tier = np.take_along_axis(Cm[0, 0].astype(np.float32), perm.astype(np.int64), 1)
+        xv = x[0, 0].astype(np.float32)                                                         # [H,P]
+        s_full *= dec[:, None, None]
+        s_full += (b_tier[gidx] * dtv[:, None])[:, None, :] * xv[:, :, None]
+        y_f = np.einsum('hpn,hn->hp', s_full, c_tier[gidx]) + xv * Df[:, None]
         sg = {k: (v.view(torch.uint8) if v.dtype == torch.float8_e4m3fn else v).cpu().numpy()
               for k, v in st_g.tensors.items()}
         q8, q4 = oc.decode_codes(sg, layout)
@@ -113,16 +121,17 @@ def config1_run(layout, steps=2048, seed=0, teacher_forced=False):
         tg, _ = oc.decode_state(sg, layout, ls, H // G)
         to, _ = oc.decode_state(st_o, layout, ls, H // G)
         yg = y_g.cpu().numpy()
-        rows['agree8'].append(float((q8 == r8).mean()))
-        rows['agree4'].append(float((q4 == r4).mean()))
-        rows['maxcode'].append(int(max(np.abs(q8 - r8).max(), np.abs(q4 - r4).max())))
-        rows['within1'].append(float(np.concatenate([(np.abs(q8 - r8) <= 1).ravel(), (np.abs(q4 - r4) <= 1).ravel()]).mean()))
+        d8, d4 = np.abs(q8 - r8), np.abs(q4 - r4)
+        rows['agree8'].append(float((d8 == 0).mean()))
+        rows['agree4'].append(float((d4 == 0).mean()))
+        rows['maxcode'].append(int(max(d8.max(), d4.max())))
+        rows['within1'].append(float(((d8 <= 1).sum() + (d4 <= 1).sum()) / (d8.size + d4.size)))
         rows['carry_abs_oracle'].append(float(np.abs(tg - to).max()))
-        rows['carry_rel_oracle'].append(_rel(tg, to))
-        rows['carry_rel_fp32'].append(_rel(tg, s_full[..., :NS]))
+        rows['carry_rel_oracle'].append(rel32(tg, to))
+        rows['carry_rel_fp32'].append(rel32(tg[0], s_full[..., :NS]))
         rows['y_abs_oracle'].append(float(np.abs(yg.astype(np.float32) - y_o.astype(np.float32)).max()))
-        rows['y_rel_oracle'].append(_rel(yg, y_o))
-        rows['y_rel_fp32'].append(_rel(yg[0, 0], y_f[0]))
+        rows['y_rel_oracle'].append(rel32(yg, y_o))
+        rows['y_rel_fp32'].append(rel32(yg[0, 0], y_f))
         rows['y_bits_oracle'].append(float((yg.view(np.uint16) == y_o.view(np.uint16)).mean()))
     summary = dict(layout=layout, steps=steps, mode='teacher-forced' if teacher_forced else 'free-running',
                    codes_within_one_step_min=min(rows['within1']),

@@ -22,7 +22,8 @@ def test_decode_bit_exact_random(shape):
     from sq325 import fp4
     rng = np.random.default_rng(shape[0])
     codes, blocks, g = of.synthetic_matrix(*shape, rng)
-    blocks[0, :4] = 0                                         # zero block scale
+    blocks[0, :4] = 0                                         # zero block scale ...
+    codes[0, :32] = rng.choice(np.array([0x00, 0x08, 0x80, 0x88], np.uint8), 32)   # ... with +-0 codes only
     blocks[1, :4] = 1                                         # e4m3 subnormal block scale
     w = fp4.from_arrays(codes, blocks, g)
     out = fp4.decode_packet(w).cpu().numpy()
