@@ -132,11 +132,15 @@ void free_ws(sq_model* m) {
   m->max_tokens = 0;
 }
 
-// exact: per-weight fp16 decode in the skinny kernel; false only for one-token decode steps.
+// Routing by batch rows M: one row -> the packed skinny GEMM (exact = per-weight fp16 decode,
+// false only for one-token decode steps); 2..256 rows -> the tensor-core linear with the
+// exact decode fused in; more -> exact decode into the staging matrix + the tcgen05 GEMM.
+constexpr int kSkinnyMax = 1, kFusedMax = 256;
 int linear(sq_model* m, const sq_fp4_matrix& W, const Fp4Maps* maps, const uint16_t* X, long long ldx, int M,
            uint16_t* Y, long long ldy, bool exact, cudaStream_t st) {
   const Fp4Weight w = fw(W);
-  if (M <= 64) return check(launch_fp4_gemv_stream(w, maps, X, ldx, M, Y, ldy, m->d_err, st, exact), "fp4 gemv");
+  if (M <= kSkinnyMax) return check(launch_fp4_gemv_stream(w, maps, X, ldx, M, Y, ldy, m->d_err, st, exact), "fp4 gemv");
+  if (M <= kFusedMax) return check(launch_fp4_mma_linear(w, X, ldx, M, Y, ldy, m->d_err, st), "fp4 tensor-core linear");
   if ((size_t)W.rows * W.cols > m->stage_elems) return fail(SQ_EINVAL, "staging buffer too small");
   SQ_TRY(launch_fp4_decode(w, m->stage, W.cols, st), "fp4 decode");
   return check(launch_gemm_f16(X, ldx, m->stage, W.cols, Y, ldy, M, W.rows, W.cols, 0, nullptr, m->d_err, st),
@@ -299,7 +303,10 @@ int sq_fp4_validate(const uint8_t* codes, const uint8_t* block_scales, const flo
   return SQ_OK;
 }
 
-int64_t sq_fp4_linear_workspace(int m, int n, int k) { return m <= 64 ? 0 : (int64_t)n * k * 2; }
+int64_t sq_fp4_linear_workspace(int m, int n, int k) {
+  // rows up to 256 run a kernel that needs no staging (k % 256 == 0 there)
+  return (m <= 64 || (m <= kFusedMax && k % 256 == 0)) ? 0 : (int64_t)n * k * 2;
+}
 
 int sq_fp4_linear(const uint8_t* codes, const uint8_t* block_scales, const float* global_scale, int n, int k,
                   const uint16_t* x, int64_t ldx, int m, uint16_t* y, int64_t ldy, void* workspace,
@@ -312,11 +319,13 @@ int sq_fp4_linear(const uint8_t* codes, const uint8_t* block_scales, const float
   cudaStream_t st = (cudaStream_t)stream;
   int* d_err = nullptr;
   if (int s = device_error_word(&d_err)) return s;
-  if (m <= 64) {
-    if (k % 256 == 0 && aligned(block_scales, 16) && aligned(x, 16) && ldx % 8 == 0)
-      return check(launch_fp4_gemv_stream(w, nullptr, x, ldx, m, y, ldy, d_err, st), "fp4 gemv");
+  const bool tma_ok = k % 256 == 0 && aligned(block_scales, 16) && aligned(x, 16) && ldx % 8 == 0;
+  if (m <= kSkinnyMax || (m <= 64 && !tma_ok)) {
+    if (tma_ok) return check(launch_fp4_gemv_stream(w, nullptr, x, ldx, m, y, ldy, d_err, st), "fp4 gemv");
     return check(launch_fp4_gemv(w, x, ldx, m, y, ldy, st), "fp4 gemv");
   }
+  if (m <= kFusedMax && tma_ok)
+    return check(launch_fp4_mma_linear(w, x, ldx, m, y, ldy, d_err, st), "fp4 tensor-core linear");
   if (!workspace || workspace_bytes < sq_fp4_linear_workspace(m, n, k) || !aligned(workspace, 16))
     return fail(SQ_EINVAL, "fp4_linear: workspace too small");
   uint16_t* stg = (uint16_t*)workspace;
@@ -369,7 +378,7 @@ int sq_model_create(const sq_model_config* cfg, sq_model** out) {
   cudaMemset(m->d_err, 0, sizeof(int));
   // kernel attributes are set here, so later launches (and graph captures) never change them
   if (prepare_scan_kernels() != kOk || prepare_fp4_kernels() != kOk || prepare_gemm_kernel() != kOk ||
-      prepare_layer_kernels() != kOk) {
+      prepare_layer_kernels() != kOk || prepare_fp4_mma_kernel() != kOk) {
     cudaFree(m->d_err);
     delete m;
     return cuda_fail("kernel attribute setup");
@@ -592,9 +601,13 @@ int sq_model_greedy(sq_model* m, const uint16_t* hidden, int rows, uint16_t* log
   if (!m->logits) return fail(SQ_ESTATE, "greedy: reserve() first");
   cudaStream_t st = (cudaStream_t)stream;
   uint16_t* lg = logits_out ? logits_out : m->logits;
-  SQ_TRY(launch_fp4_gemv_stream(fw(m->head), &m->head_maps, hidden, kDModel, rows, lg, m->cfg.vocab, m->d_err, st,
-                                m->exact_skinny),
-         "lm_head gemv");
+  if (rows <= kSkinnyMax)
+    SQ_TRY(launch_fp4_gemv_stream(fw(m->head), &m->head_maps, hidden, kDModel, rows, lg, m->cfg.vocab, m->d_err, st,
+                                  m->exact_skinny),
+           "lm_head gemv");
+  else
+    SQ_TRY(launch_fp4_mma_linear(fw(m->head), hidden, kDModel, rows, lg, m->cfg.vocab, m->d_err, st),
+           "lm_head tensor-core linear");
   return check(launch_argmax(lg, rows, m->cfg.vocab, m->cfg.vocab, (long long*)tokens_out, m->partials, st),
                "argmax");
 }

@@ -93,3 +93,24 @@ def test_decode_packet_rejects_what_the_reference_rejects(case):
         g = np.float32(1e6)                           # 6 * 448 * 1e6 overflows fp16
     with pytest.raises(ValueError, match=msg):
         fp4.decode_packet(fp4.from_arrays(codes, blocks, g))
+
+
+@pytest.mark.parametrize('m', [2, 16, 17, 100, 256])
+@pytest.mark.parametrize('shape', [(5328, 4096), (4096, 8192)])
+def test_tensor_core_linear_with_fused_decode(m, shape):
+    """Batches of 2..256 rows run the tcgen05 linear that decodes the FP4 weights in shared
+    memory (one CTA per 128 weight rows; 5328 rows leave a partial last tile).  Same bar as
+    the other projections: fp32 reference product of the exactly decoded weights within
+    2e-3 relative + 1% of the mean magnitude."""
+    from sq325 import _lib, fp4
+    rng = np.random.default_rng(3 * m + shape[0])
+    codes, blocks, g = of.synthetic_matrix(*shape, rng)
+    w = fp4.from_arrays(codes, blocks, g)
+    x = torch.from_numpy(rng.standard_normal((m, shape[1])).astype(np.float16)).cuda()
+    y = fp4.linear(w, x)
+    torch.cuda.synchronize()
+    assert _lib.load().sq_device_check(_lib.stream_ptr()) == _lib.SQ_OK
+    ref = _ref_linear(x.cpu(), torch.from_numpy(of.decode(codes, blocks, g)))
+    err = (y.float().cpu() - ref).abs()
+    tol = 2e-3 * ref.abs() + 1e-2 * ref.abs().mean()
+    assert bool((err <= tol).all()), float(err.max())
