@@ -21,6 +21,14 @@ What is recorded
   s16.npz              the FP16-state control scan `_s16_scan`
                        (mamba2_recall/state_codec.py:65-102) under the interpreter,
                        without and with the calibration statistics (:256-262).
+  checkpoint_plan.json the packed-checkpoint container rules of
+                       mamba2_recall/fp4_checkpoint.py run on this model's tensor
+                       inventory: `make_plan` (:67-93) at two shard limits for the
+                       production 56-layer / 256,000-row model (sha256 of the
+                       canonical JSON) and for a 2-layer / 64-row model at 1 MiB
+                       (in full), `_file_specs` (:100-114) and every shard's
+                       `_header` bytes (:117-127; sha256 for production, hex in
+                       full for the small model).
 
 Interpreter shims (the interpreter cannot run two device intrinsics as the
 GPU does):
@@ -206,6 +214,41 @@ def fp4_case(reference, seed=7):
                 tie_codes=fp4.encode_e2m1(ties.float()).numpy())
 
 
+def checkpoint_case(reference):
+    """The reference's plan / file-spec / header builders (pure stdlib) on the tensor
+    inventory of the model (names and shapes of the mamba_ssm state dict, 507 tensors at 56
+    layers).  The inventory itself comes from sq325.checkpoint.tensor_inventory, which the
+    test also pins by count."""
+    import hashlib
+    import json
+    sys.path.insert(0, str(reference))
+    sys.path.insert(0, str(HERE.parents[1] / 'mamb2_8b_fp4_recall_sq3.25_b200'))
+    from mamba2_recall import fp4_checkpoint as rc
+    from sq325 import checkpoint as ck
+
+    def canon(x):
+        return hashlib.sha256(json.dumps(x, sort_keys=True, separators=(',', ':')).encode()).hexdigest()
+
+    out = {'production': {}, 'small': {}}
+    for n_layer, vocab, limits, key in ((56, 256000, (256 * 1024 * 1024, 1024 ** 3), 'production'),
+                                        (2, 64, (1024 * 1024,), 'small')):
+        inv = ck.tensor_inventory(n_layer, vocab)
+        ledger = {'tensors': {k: {'kind': v[0], 'shape': list(v[1])} for k, v in inv.items()}}
+        for limit in limits:
+            plan = rc.make_plan(ledger, limit)
+            specs = rc._file_specs(plan)
+            headers = {f: rc._header(spec) for f, spec in specs.items()}
+            rec = dict(n_layer=n_layer, vocab=vocab, shard_limit_bytes=limit, tensors=len(plan),
+                       files=len(specs), plan_sha256=canon(plan), specs_sha256=canon(specs),
+                       headers_sha256={f: hashlib.sha256(h[0]).hexdigest() for f, h in headers.items()},
+                       payload_bytes={f: h[2] for f, h in headers.items()})
+            if key == 'small':
+                rec['plan'] = plan
+                rec['headers_hex'] = {f: h[0].hex() for f, h in headers.items()}
+            out[key][str(limit)] = rec
+    return out
+
+
 def adapter_case(reference, seed=11):
     sys.path.insert(0, str(reference))
     from mamba2_recall import resurface_native as native
@@ -230,7 +273,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', type=Path, required=True,
                     help='root of a checkout of the reference repository (read only)')
-    ap.add_argument('--cases', default='codec,s16,mk', help='comma list: codec (+ fp4, adapter), s16, mk')
+    ap.add_argument('--cases', default='codec,s16,mk,checkpoint',
+                    help='comma list: codec (+ fp4, adapter), s16, mk, checkpoint')
     args = ap.parse_args()
     ap_cases = args.cases.split(',')
     if 's16' in ap_cases:
@@ -243,6 +287,11 @@ def main():
         import json
         (HERE / 'mk_cases.json').write_text(json.dumps(mk_case(args.reference), indent=1, sort_keys=True) + '\n')
         print('wrote mk')
+    if 'checkpoint' in ap_cases:
+        import json
+        (HERE / 'checkpoint_plan.json').write_text(
+            json.dumps(checkpoint_case(args.reference), indent=1, sort_keys=True) + '\n')
+        print('wrote checkpoint')
     if 'codec' not in ap_cases:
         return
     ref = install_shims(args.reference)

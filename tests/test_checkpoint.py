@@ -74,3 +74,50 @@ def test_state_config_round_trip(tmp_path):
     with pytest.raises(ValueError):
         ck.write_state_config(tmp_path / 's2.pt', bad, layouts, bases, scales, preds)
         ck.read_state_config(tmp_path / 's2.pt')
+
+
+def _canon(x):
+    import hashlib
+    return hashlib.sha256(json.dumps(x, sort_keys=True, separators=(',', ':')).encode()).hexdigest()
+
+
+@pytest.mark.parametrize('key', ['production', 'small'])
+def test_plan_specs_headers_match_reference_outputs(key):
+    """make_plan / file_specs / header_bytes against the reference's own make_plan, _file_specs
+    and _header (mamba2_recall/fp4_checkpoint.py:67-127) run on the same inventory
+    (tests/golden/checkpoint_plan.json, written by make_golden.py)."""
+    from conftest import GOLDEN
+    from sq325 import checkpoint as ck
+    gold = json.loads((GOLDEN / 'checkpoint_plan.json').read_text())[key]
+    for limit, rec in gold.items():
+        inv = ck.tensor_inventory(rec['n_layer'], rec['vocab'])
+        plan = ck.make_plan(inv, int(limit))
+        specs = ck.file_specs(plan)
+        assert len(plan) == rec['tensors'] and len(specs) == rec['files']
+        assert _canon(plan) == rec['plan_sha256'] and _canon(specs) == rec['specs_sha256']
+        import hashlib
+        for f, spec in specs.items():
+            raw, _, payload = ck.header_bytes(spec)
+            assert hashlib.sha256(raw).hexdigest() == rec['headers_sha256'][f], f
+            assert payload == rec['payload_bytes'][f], f
+
+
+def test_exported_shards_carry_the_reference_headers(tiny, tmp_path):
+    """Every shard export_packed writes starts with the exact header bytes the reference's
+    _header builds for that file (golden, 2 layers / 64 rows at a 1 MiB limit), and its size
+    is 8 + header + payload as the reference's inspect_shard requires (:147-164)."""
+    import struct
+    from conftest import GOLDEN
+    from sq325 import checkpoint as ck
+    rec = json.loads((GOLDEN / 'checkpoint_plan.json').read_text())['small'][str(1024 * 1024)]
+    d = tmp_path / 'weights'
+    ck.export_packed(tiny, d, shard_limit_bytes=1024 * 1024)
+    manifest = json.loads((d / 'weight_manifest.json').read_text())
+    assert manifest['layout'] == rec['plan']
+    assert set(rec['headers_hex']) <= {p.name for p in d.glob('*.safetensors')}
+    for f, hexraw in rec['headers_hex'].items():
+        raw = bytes.fromhex(hexraw)
+        blob = (d / f).read_bytes()
+        (n,) = struct.unpack('<Q', blob[:8])
+        assert blob[8:8 + n] == raw, f
+        assert len(blob) == 8 + n + rec['payload_bytes'][f], f
