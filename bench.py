@@ -371,8 +371,8 @@ def measure_config2(device, pk, reps=7):
             flop = 2.0 * M * N * K
             rows.append(dict(proj=name, M=M, us=t * 1e6, gbs=byts / t / 1e9, hbm_frac=byts / t / 1e9 / pk['hbm'],
                              tflops=flop / t / 1e12, tensor_frac=flop / t / 1e12 / pk['tf'],
-                             path='skinny TMA GEMM (exact fp16 weights)' if M <= 64 else
-                             'fp4 decode + tcgen05 GEMM'))
+                             path='skinny TMA GEMV (exact fp16 weights)' if M == 1 else
+                             'tcgen05 FP4 linear (exact decode fused, weights as the A operand)'))
         del w
     return rows
 

@@ -204,7 +204,7 @@ def model_run(n_layer=56, vocab=2048, tokens=16, decode_steps=4, seed=7):
             r8, r4 = oc.decode_codes(ora.caches[l]['state'], layouts[l])
             diff = np.concatenate([np.abs(q8 - r8).ravel(), np.abs(q4 - r4).ravel()])
             layers[l].update(tf_mixer_rel_l2=_rel(got, ref), tf_code_agreement=float((diff == 0).mean()),
-                             tf_max_code_step=int(diff.max()),
+                             tf_max_code_step=int(diff.max()), tf_codes_within_one=float((diff <= 1).mean()),
                              tf_conv_ring_rel=_rel(ex.conv_chronological(l).float().cpu().numpy(),
                                                    ora.caches[l]['conv'].float().numpy()))
         tf_step = []
@@ -237,6 +237,7 @@ def model_run(n_layer=56, vocab=2048, tokens=16, decode_steps=4, seed=7):
                    tf_mixer_rel_l2_max=max(x['tf_mixer_rel_l2'] for x in layers),
                    tf_code_agreement_min=min(x['tf_code_agreement'] for x in layers),
                    tf_max_code_step=max(x['tf_max_code_step'] for x in layers),
+                   tf_codes_within_one_min=min(x['tf_codes_within_one'] for x in layers),
                    tf_conv_ring_rel_max=max(x['tf_conv_ring_rel'] for x in layers),
                    tf_decode_mixer_rel_l2_max=max(tf_step),
                    tf_head_nll_rel=abs(nll_tf - nll_o) / abs(nll_o),

@@ -239,3 +239,29 @@ def test_scan_conv_rejects_continuing_prefill():
         codec.scan_with_conv(_T(d['xbc']), _T(d['dt']), _T(d['A']), _T(d['D']), _T(d['dt_bias']), ps,
                              *[_T(d[k]) for k in ('permutation', 'basis', 'latent_scale', 'predictor')],
                              _T(d['conv_w']), _T(d['conv_b']), ring, 3, layout=layout)
+
+
+@pytest.mark.parametrize('layout', oc.LAYOUTS)
+@pytest.mark.parametrize('length', [2, 9, 37])
+def test_conv_prefill_two_kernel_path_matches_fused_bytes(layout, length):
+    """Fused conv1d prefill at model geometry: the prep + chunk kernels and the
+    single fused kernel give the same y, packed state bytes and conv ring, bit for bit
+    (both run the same operations in the same order)."""
+    from sq325 import codec
+    B = 4
+    d, st = _inputs(layout, B, length, seed=2500 + length + oc.LAYOUTS.index(layout), raw_xbc=True)
+    outs = []
+    for fused in (False, True):
+        ps = _gpu_state(st, layout)
+        ring = torch.zeros(B, 4, 10240, device='cuda', dtype=torch.float16)
+        y, _ = codec.scan_with_conv(_T(d['xbc']), _T(d['dt']), _T(d['A']), _T(d['D']), _T(d['dt_bias']), ps,
+                                    _T(d['permutation']), _T(d['basis']), _T(d['latent_scale']),
+                                    _T(d['predictor']), _T(d['conv_w']), _T(d['conv_b']), ring, 0, layout=layout,
+                                    fused=fused)
+        torch.cuda.synchronize()
+        outs.append((y, ps, ring))
+    (y1, s1, r1), (y2, s2, r2) = outs
+    assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
+    for k in s1.tensors:
+        assert torch.equal(s1.tensors[k].view(torch.uint8), s2.tensors[k].view(torch.uint8)), k
+    assert torch.equal(r1.view(torch.int16), r2.view(torch.int16))
