@@ -132,15 +132,17 @@ void free_ws(sq_model* m) {
   m->max_tokens = 0;
 }
 
-// Routing by batch rows M: one row -> the packed skinny GEMM (exact = per-weight fp16 decode,
-// false only for one-token decode steps); 2..256 rows -> the tensor-core linear with the
-// exact decode fused in; more -> exact decode into the staging matrix + the tcgen05 GEMM.
+// Routing by batch rows M: one row -> the packed skinny GEMM; 2..256 rows -> the tensor-core
+// linear with the decode fused in; more -> exact decode into the staging matrix + the tcgen05
+// GEMM.  exact = per-weight fp16 decode (the reference's); false (one-token decode steps
+// unless set_exact_skinny) applies the fp32 global scale once per output.
 constexpr int kSkinnyMax = 1, kFusedMax = 256;
 int linear(sq_model* m, const sq_fp4_matrix& W, const Fp4Maps* maps, const uint16_t* X, long long ldx, int M,
            uint16_t* Y, long long ldy, bool exact, cudaStream_t st) {
   const Fp4Weight w = fw(W);
   if (M <= kSkinnyMax) return check(launch_fp4_gemv_stream(w, maps, X, ldx, M, Y, ldy, m->d_err, st, exact), "fp4 gemv");
-  if (M <= kFusedMax) return check(launch_fp4_mma_linear(w, X, ldx, M, Y, ldy, m->d_err, st), "fp4 tensor-core linear");
+  if (M <= kFusedMax)
+    return check(launch_fp4_mma_linear(w, X, ldx, M, Y, ldy, m->d_err, st, exact), "fp4 tensor-core linear");
   if ((size_t)W.rows * W.cols > m->stage_elems) return fail(SQ_EINVAL, "staging buffer too small");
   SQ_TRY(launch_fp4_decode(w, m->stage, W.cols, st), "fp4 decode");
   return check(launch_gemm_f16(X, ldx, m->stage, W.cols, Y, ldy, M, W.rows, W.cols, 0, nullptr, m->d_err, st),
@@ -606,7 +608,8 @@ int sq_model_greedy(sq_model* m, const uint16_t* hidden, int rows, uint16_t* log
                                   m->exact_skinny),
            "lm_head gemv");
   else
-    SQ_TRY(launch_fp4_mma_linear(fw(m->head), hidden, kDModel, rows, lg, m->cfg.vocab, m->d_err, st),
+    SQ_TRY(launch_fp4_mma_linear(fw(m->head), hidden, kDModel, rows, lg, m->cfg.vocab, m->d_err, st,
+                                 m->exact_skinny),
            "lm_head tensor-core linear");
   return check(launch_argmax(lg, rows, m->cfg.vocab, m->cfg.vocab, (long long*)tokens_out, m->partials, st),
                "argmax");

@@ -61,11 +61,12 @@ int launch_gemm_f16(const uint16_t* A, long long lda, const uint16_t* B, long lo
 int set_gemv_wait_limit_ns(unsigned long long ns);
 bool encode_2d_map(CUtensorMap* m, CUtensorMapDataType dtype, const void* base, long long rows, long long cols,
                    long long row_bytes, int box_cols, int box_rows, CUtensorMapSwizzle swizzle);
-// Y[M, N] = X[M, K] . W[N, K]^T on the tensor cores with the exact FP4 decode fused in
+// Y[M, N] = X[M, K] . W[N, K]^T on the tensor cores with the FP4 decode fused in
 // (fp4mma.cu), 1 <= M <= 256, K % 256 == 0, 16-byte aligned rows.  One CTA per 128 weight
-// rows; `err` receives an error bit if a bounded wait expires.
+// rows and K slice; `err` receives an error bit if a bounded wait expires.  exact = false
+// applies the fp32 global scale once per output instead of per weight.
 int launch_fp4_mma_linear(const Fp4Weight& W, const uint16_t* X, long long ldx, int M, uint16_t* Y, long long ldy,
-                          int* err, cudaStream_t st);
+                          int* err, cudaStream_t st, bool exact = true);
 int prepare_fp4_mma_kernel();
 int gemm_num_ntiles(int N);
 int prepare_fp4_kernels();

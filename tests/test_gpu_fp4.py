@@ -96,11 +96,13 @@ def test_decode_packet_rejects_what_the_reference_rejects(case):
 
 
 @pytest.mark.parametrize('m', [2, 16, 17, 100, 256])
-@pytest.mark.parametrize('shape', [(5328, 4096), (4096, 8192)])
+@pytest.mark.parametrize('shape', [(5328, 4096), (4096, 8192), (18560, 4096), (1000, 256)])
 def test_tensor_core_linear_with_fused_decode(m, shape):
     """Batches of 2..256 rows run the tcgen05 linear that decodes the FP4 weights in shared
-    memory (one CTA per 128 weight rows; 5328 rows leave a partial last tile).  Same bar as
-    the other projections: fp32 reference product of the exactly decoded weights within
+    memory (one CTA per 128 weight rows and K slice; 5328 and 1000 rows leave a partial last
+    tile; 5328 x 4096 and 4096 x 8192 split K over a cluster of 4 CTAs and reduce through
+    distributed shared memory, 18560 x 4096 runs unsplit, K = 256 cannot be split).  Same bar
+    as the other projections: fp32 reference product of the exactly decoded weights within
     2e-3 relative + 1% of the mean magnitude."""
     from sq325 import _lib, fp4
     rng = np.random.default_rng(3 * m + shape[0])
