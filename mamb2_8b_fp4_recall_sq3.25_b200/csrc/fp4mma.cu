@@ -10,7 +10,10 @@
 // so every packed weight byte is read from HBM once.  The K walk advances in stages of 128
 // columns (two 64-column SWIZZLE_128B atoms): per stage the MMA thread waits twice, issues
 // eight tcgen05.mma (M = 128 weight rows, N = the batch rounded up to 16, K = 16) and commits
-// twice, so the per-stage handshake cost is spread over 16K weights.  Roles, by warp:
+// twice, so the per-stage handshake cost is spread over 16K weights.  At small N an MMA's
+// pipeline latency, not its work, sets the rate when every MMA accumulates into the same
+// TMEM tile, so the eight MMAs of a stage rotate over four accumulators (K-step kk adds into
+// accumulator kk % 4) and the epilogue sums them, ((a0 + a1) + a2) + a3.  Roles, by warp:
 //   0        TMA lane: packed codes (SWIZZLE_128B) and E4M3 block scales, 256-column chunks,
 //            4-deep ring;
 //   1        TMEM owner and the elected MMA issuer;
@@ -51,6 +54,7 @@ constexpr int kAtom = 64;                   // K columns per SWIZZLE_128B atom (
 constexpr int kNP = 4;                      // packed-chunk ring depth
 constexpr int kNAMax = 3, kNXMax = 8;       // decoded-stage / activation-stage ring depths (max)
 constexpr int kMaxBatch = 128;              // rows per launch (larger batches: two launches)
+constexpr int kNAcc = 4;                    // independent TMEM accumulators (4 x 128 columns max)
 constexpr int kCodeBytes = kRowsW * kChunk / 2;          // 16 KB, SWIZZLE_128B rows of 128 B
 constexpr int kScaleBytes = kRowsW * kChunk / 16;        // 2 KB, rows of 16 B
 constexpr int kPBytes = kCodeBytes + kScaleBytes;        // 18 KB (a 1024-multiple)
@@ -118,7 +122,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 fp4_mma_linear_kernel(const __grid_constant__ CUtensorMap mcodes, const __grid_constant__ CUtensorMap mscales,
                       const __grid_constant__ CUtensorMap mx, const LinArgs args) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  // 1024-byte aligned base derived by pointer arithmetic on the shared array, so that the
+  // compiler keeps every converter access a shared-memory (not generic) load / store
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + oBar;
@@ -142,7 +148,8 @@ fp4_mma_linear_kernel(const __grid_constant__ CUtensorMap mcodes, const __grid_c
   const int nA = args.mbox <= 64 ? kNAMax : 2;
   const uint32_t oX = (uint32_t)(oA + nA * kABytes);
   const int nX = min(kNXMax, (int)((oEnd - oX) / xbytes));
-  const uint32_t tcols = args.mbox <= 32 ? 32 : (args.mbox <= 64 ? 64 : 128);
+  // TMEM: kNAcc accumulators of mbox fp32 columns each, accumulator a at column a * mbox
+  const uint32_t tcols = args.mbox <= 16 ? 64 : (args.mbox <= 32 ? 128 : (args.mbox <= 64 ? 256 : 512));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kNP; ++s) { mbar_init(PFULL(s), 1); mbar_init(PEMPTY(s), kConv); }
@@ -221,10 +228,10 @@ fp4_mma_linear_kernel(const __grid_constant__ CUtensorMap mcodes, const __grid_c
         const uint64_t da1 = da + (kAtomBytes >> 4), dx1 = dx + (xatom >> 4);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)            // descriptor address field: 16-byte units
-          umma_f16(tmem, da + 2 * kk, dx + 2 * kk, idesc, (t | kk) != 0);
+          umma_f16(tmem + (uint32_t)(kk * args.mbox), da + 2 * kk, dx + 2 * kk, idesc, t != 0);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          umma_f16(tmem, da1 + 2 * kk, dx1 + 2 * kk, idesc, 1);
+          umma_f16(tmem + (uint32_t)(kk * args.mbox), da1 + 2 * kk, dx1 + 2 * kk, idesc, 1);
         umma_commit(AEMPTY(as));
         umma_commit(XEMPTY(xs));
         if (++as == nA) { as = 0; aph ^= 1; }
@@ -301,18 +308,42 @@ fp4_mma_linear_kernel(const __grid_constant__ CUtensorMap mcodes, const __grid_c
       const int n = n0 + r;
       const float gsc = EXACT ? 1.0f : *args.g;
       float* part = reinterpret_cast<float*>(smem + oP);   // [mbox][128], split-K only
+      const uint32_t trow = tmem + ((uint32_t)(qd * 32) << 16);
+      // 32 batch columns at a time: s[i] = ((a0 + a1) + a2) + a3 of column c0 + i
       for (int c0 = 0; c0 < args.mbox; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)c0, v);
+        float sacc[32];
+        uint32_t u[32];
+        if (args.mbox == 16) {                  // the four 16-column accumulators in two loads
+          tmem_ld32(trow, u);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) sacc[i] = __uint_as_float(u[i]) + __uint_as_float(u[16 + i]);
+          tmem_ld32(trow + 32, u);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            sacc[i] = (sacc[i] + __uint_as_float(u[i])) + __uint_as_float(u[16 + i]);
+            sacc[16 + i] = 0.f;
+          }
+        } else {
+          tmem_ld32(trow + (uint32_t)c0, u);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sacc[i] = __uint_as_float(u[i]);
+#pragma unroll
+          for (int a = 1; a < kNAcc; ++a) {
+            tmem_ld32(trow + (uint32_t)(a * args.mbox + c0), u);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) sacc[i] += __uint_as_float(u[i]);
+          }
+        }
+        const int ncol = min(32, args.mbox - c0);
         if (args.ksplit > 1) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) part[(c0 + i) * kRowsW + r] = __uint_as_float(v[i]);
+          for (int i = 0; i < 32; ++i)
+            if (i < ncol) part[(c0 + i) * kRowsW + r] = sacc[i];
         } else if (n < args.N) {
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            if (c0 + i < args.M)
-              args.Y[(long long)(c0 + i) * args.ldy + n] =
-                  f2h(EXACT ? __uint_as_float(v[i]) : __uint_as_float(v[i]) * gsc);
+            if (i < ncol && c0 + i < args.M)
+              args.Y[(long long)(c0 + i) * args.ldy + n] = f2h(EXACT ? sacc[i] : sacc[i] * gsc);
         }
       }
     } else if (lane == 0) {
