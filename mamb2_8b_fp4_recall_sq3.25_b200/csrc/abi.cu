@@ -231,8 +231,7 @@ int sq_scan_conv(const sq_scan_args* a, const sq_conv_args* c, void* stream) {
     return fail(SQ_EINVAL, "scan_conv: ring must be 16-byte aligned with a batch stride >= 4*10240 (multiple of 8)");
   if (c->position < 0 || (c->position > 0 && P.length != 1))
     return fail(SQ_EINVAL, "scan_conv: position 0 (prefill from a reset ring) or a one-token step (position > 0)");
-  P.conv_mode = c->position == 0 ? 1 : 2;
-  if (P.conv_mode == 2) P.prep_bc = nullptr, P.prep_pv = nullptr, P.prep_ddt = nullptr;   // one-token step kernel
+  P.conv_mode = c->position == 0 ? 1 : 2;   // with a workspace, both run the two-kernel path
   P.conv_w = c->weight; P.conv_b = c->bias; P.conv_cache = c->ring; P.conv_pos = c->position;
   P.conv_cache_sb = c->ring_batch_stride;
   return check(launch_scan(P, (cudaStream_t)stream), "sq_scan_conv");
@@ -526,7 +525,7 @@ int mixer_forward(sq_model* m, int l, const uint16_t* u, int batch, int tokens, 
     P.x = m->xbc; P.B = m->xbc + kDInner; P.C = m->xbc + kDInner + 1024;
     P.x_sb = P.b_sb = P.c_sb = (long long)tokens * kXbc; P.x_st = P.b_st = P.c_st = kXbc;
   }
-  if (!step) scan_prep_bind(P, m->prep);
+  scan_prep_bind(P, m->prep);
   SQ_TRY(launch_scan(P, st), "ssu scan");
   const AdapterPtrs& ad = m->adapters[l];
   SQ_TRY(launch_resurface_gatednorm(m->y, m->zx, kZx, u, kDModel, ad.V ? &ad : nullptr, L.gated_norm_weight,

@@ -860,6 +860,289 @@ int launch_chunked(const ScanParams& P, bool prepare_only, cudaStream_t stream) 
   return launch_status();
 }
 
+// ============================================================================================
+// Two-kernel path of the one-token decode step (mode 2: conv step numerics, conv ring).
+//
+// The single fused kernel redoes, in each of the eight CTAs of a B/C group, the staging of the
+// group's predictor (F x NZ fp16), basis and conv taps and the F + 5 group dots; at batch 32-64
+// that fixed cost dominates the step.  step_prep_kernel does it once per (batch, group):
+//   bc   [B][G][256] fp16   conv'd B then conv'd C, tier order (conv step values are fp16)
+//   pv   [B][G][FP]  fp32   cvec [0..NS) | pcz0 pcz1 | B.C (zero tier), b0.C, b1.C, b0.B, b1.B
+//   ddt  [B][H]      float2 (dt after softplus, exp(A dt))
+// and writes the new raw B/C columns into the ring; ssu_step_kernel then runs the rows of two
+// heads (one thread per row) from those arrays, the conv'd x of its 128 channels, and writes
+// the x columns into the ring.  Every value is computed by the same functions in the same
+// order as the fused kernel's mode 2 (recur_row4 / token_tail_sums), so y, the state bytes and
+// the ring are bit-identical to it, and to the persistent decode kernel.
+// ============================================================================================
+
+template <int N8, int N4>
+__global__ void __launch_bounds__(256)
+step_prep_kernel(const ScanParams P) {
+  using PL = PrepLayout<N8, N4>;
+  constexpr int NS = PL::NS, NZ = PL::NZ, F = PL::F, FP = PL::FP;
+  constexpr int oPred = 256 * 4;                                     // sBC [256] fp32 first
+  constexpr int oBasis = oPred + (F * (NZ + 1) * 4 + 15) / 16 * 16;
+  constexpr int oPerm = oBasis + (2 * NZ * 4 + 15) / 16 * 16;
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* sBC = reinterpret_cast<float*>(smem);                       // [256] conv'd B | C (tier order)
+  float* sPred = reinterpret_cast<float*>(smem + oPred);             // [F][NZ+1]
+  float* sBasis = reinterpret_cast<float*>(smem + oBasis);           // [2][NZ]
+  int* sPerm = reinterpret_cast<int*>(smem + oPerm);                 // [128]
+  uint16_t* rawPred = reinterpret_cast<uint16_t*>(smem + oPerm + 512);
+  uint16_t* rawBasis = rawPred + (F * NZ * 2 + 15) / 16 * 8;
+  uint8_t* rawPerm = reinterpret_cast<uint8_t*>(rawBasis + (NZ * 4 + 15) / 16 * 8);
+
+  const int tid = threadIdx.x;
+  const int g = blockIdx.x, b = blockIdx.y;
+  stage16(rawPred, P.predictor + (long long)g * F * NZ, F * NZ * 2, tid, 256);
+  stage16(rawBasis, P.basis + (long long)g * NZ * 2, NZ * 4, tid, 256);
+  stage16(rawPerm, P.perm + g * 128, 128, tid, 256);
+  cp_async_wait_all();
+  __syncthreads();
+  for (int i = tid; i < F * NZ; i += 256) {
+    const int f = i / NZ, d = i - f * NZ;
+    sPred[f * (NZ + 1) + d] = h2f(rawPred[i]);
+  }
+  for (int i = tid; i < NZ; i += 256) {
+    sBasis[i] = h2f(rawBasis[2 * i + 0]);
+    sBasis[NZ + i] = h2f(rawBasis[2 * i + 1]);
+  }
+  if (tid < 128) sPerm[tid] = rawPerm[tid];
+  __syncthreads();
+
+  // ---- conv step of B (tid < 128) or C (tid >= 128) at tier coordinate j ----
+  {
+    const int j = tid & 127;
+    const bool isC = tid >= 128;
+    const int n = sPerm[j];
+    const int ch = (isC ? 9216 : 8192) + g * 128 + n;
+    float w[5];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = h2f(P.conv_w[ch * 4 + i]);
+    w[4] = h2f(P.conv_b[ch]);
+    uint16_t* ring = P.conv_cache + (long long)b * P.conv_cache_sb;
+    const float h1 = h2f(ring[((P.conv_pos - 3) & 3) * 10240 + ch]);
+    const float h2 = h2f(ring[((P.conv_pos - 2) & 3) * 10240 + ch]);
+    const float h3 = h2f(ring[((P.conv_pos - 1) & 3) * 10240 + ch]);
+    const uint16_t rawb = (isC ? P.C + (long long)b * P.c_sb : P.B + (long long)b * P.b_sb)[g * 128 + n];
+    const float v = conv_step_value(w, h1, h2, h3, h2f(rawb));
+    sBC[tid] = v;
+    P.prep_bc[((long long)b * P.groups + g) * 256 + tid] = f2h(v);   // v is an fp16 value: exact
+    ring[(P.conv_pos & 3) * 10240 + ch] = rawb;                      // the newest raw column
+  }
+  // ---- dt / decay for the group's heads ----
+  {
+    const int hpg = P.heads / P.groups;
+    for (int i = tid; i < hpg; i += 256) {
+      const int h = g * hpg + i;
+      const float bias = P.dt_bias_is_f32 ? reinterpret_cast<const float*>(P.dt_bias)[h]
+                                          : h2f(reinterpret_cast<const uint16_t*>(P.dt_bias)[h]);
+      const float dtv = softplus_ref(h2f(P.dt[(long long)b * P.dt_sb + h]) + bias);
+      P.prep_ddt[(long long)b * P.heads + h] = make_float2(dtv, expf(P.A[h] * dtv));
+    }
+  }
+  __syncthreads();
+  // ---- group dots, the fused kernel's pairing and order ----
+  float* pv = P.prep_pv + ((long long)b * P.groups + g) * FP;
+  for (int f = tid; f < FP; f += 256) {
+    float r = 0.f;
+    if (f < F) {
+      const float* pr = sPred + f * (NZ + 1);
+      float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 4
+      for (int d = 0; d < NZ; d += 2) {
+        acc0 = fmaf(sBC[128 + NS + d], pr[d], acc0);
+        acc1 = fmaf(sBC[128 + NS + d + 1], pr[d + 1], acc1);
+      }
+      r = acc0 + acc1;                                  // cvec (f < NS) or pcz (f = NS, NS + 1)
+    } else if (f < F + 5) {
+      const int k = f - F;   // 0: B.C (zero tier), 1: basis0.C, 2: basis1.C, 3: basis0.B, 4: basis1.B
+      const float* us = (k == 0) ? nullptr : sBasis + ((k - 1) & 1) * NZ;
+      const int voff = (k >= 3 || k == 0) ? 0 : 128;   // 0 -> B, 128 -> C
+      float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 4
+      for (int d = 0; d < NZ; d += 2) {
+        const float u0 = (k == 0) ? sBC[NS + d] : us[d], u1 = (k == 0) ? sBC[NS + d + 1] : us[d + 1];
+        const float v0 = (k == 0) ? sBC[128 + NS + d] : sBC[voff + NS + d];
+        const float v1 = (k == 0) ? sBC[128 + NS + d + 1] : sBC[voff + NS + d + 1];
+        acc0 = fmaf(u0, v0, acc0);
+        acc1 = fmaf(u1, v1, acc1);
+      }
+      r = acc0 + acc1;
+    }
+    pv[f] = r;
+  }
+}
+
+// Rows of the one-token step: one thread per state row, 128-thread CTAs of `hpc` heads.
+template <int N8, int N4>
+__global__ void __launch_bounds__(128, 4)
+ssu_step_kernel(const ScanParams P) {
+  using PL = PrepLayout<N8, N4>;
+  constexpr int NS = N8 + N4, F = NS + 2, FP = PL::FP;
+  constexpr int W8 = N8 / 2, W4 = N4 / 2, NP = NS / 2;
+  constexpr int rows = 128;
+  __shared__ __align__(16) unsigned char sPack[rows * 52];
+  __shared__ __align__(16) float4 sP4[64];          // {b_j, b_j+1, c_j, c_j+1} per pair
+  __shared__ __align__(16) float2 sV2[64];          // cvec pairs
+  __shared__ float sDots[8];
+  __shared__ float2 sDD[8];
+
+  const int tid = threadIdx.x;
+  const int dim = P.dim;
+  const int hpc = 128 / dim;
+  const int b = blockIdx.y;
+  const int h0 = blockIdx.x * hpc;
+  const int hl = tid / dim;
+  const int p = tid - hl * dim;
+  const int h = h0 + hl;
+  const int hpg = P.heads / P.groups;
+  const int g = h0 / hpg;
+  const long long row0 = ((long long)b * P.heads + h0) * dim;
+
+  unsigned char* pLo = sPack;
+  unsigned char* pHi = pLo + rows * W8;
+  unsigned char* pQ4 = pHi + rows * W8;
+  unsigned char* pLat = pQ4 + rows * W4;
+  uint16_t* pS8 = reinterpret_cast<uint16_t*>(pLat + rows * 2);
+  uint16_t* pS4 = pS8 + rows;
+  stage16(pLo, P.lo + row0 * W8, rows * W8, tid, 128);
+  stage16(pHi, P.hi + row0 * W8, rows * W8, tid, 128);
+  stage16(pQ4, P.q4 + row0 * W4, rows * W4, tid, 128);
+  stage16(pLat, P.latent + row0 * 2, rows * 2, tid, 128);
+  stage16(pS8, P.s8 + row0, rows * 2, tid, 128);
+  stage16(pS4, P.s4 + row0, rows * 2, tid, 128);
+  // the group's tables from the prep kernel
+  {
+    const uint16_t* bc = P.prep_bc + ((long long)b * P.groups + g) * 256;
+    const float* pvg = P.prep_pv + ((long long)b * P.groups + g) * FP;
+    if (tid < 64) {
+      const __half2 bb = reinterpret_cast<const __half2*>(bc)[tid];
+      const __half2 cc = reinterpret_cast<const __half2*>(bc + 128)[tid];
+      const float2 bf = __half22float2(bb), cf = __half22float2(cc);
+      sP4[tid] = make_float4(bf.x, bf.y, cf.x, cf.y);
+      if (2 * tid < NS) sV2[tid] = make_float2(pvg[2 * tid], pvg[2 * tid + 1]);
+    } else if (tid < 64 + 7) {
+      const int k = tid - 64;                          // dots {B.C, b0.C, b1.C, b0.B, b1.B, pcz0, pcz1}
+      sDots[k] = k < 5 ? pvg[F + k] : pvg[NS + k - 5];
+    } else if (tid < 64 + 7 + hpc) {
+      sDD[tid - 71] = P.prep_ddt[(long long)b * P.heads + h0 + tid - 71];
+    }
+  }
+  // conv step of this thread's x channel (channel h0 * dim + tid); the newest raw column
+  // goes into the ring
+  float xv;
+  {
+    const int ch = h0 * dim + tid;
+    float w[5];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = h2f(P.conv_w[ch * 4 + i]);
+    w[4] = h2f(P.conv_b[ch]);
+    uint16_t* ring = P.conv_cache + (long long)b * P.conv_cache_sb;
+    const float h1 = h2f(ring[((P.conv_pos - 3) & 3) * 10240 + ch]);
+    const float h2 = h2f(ring[((P.conv_pos - 2) & 3) * 10240 + ch]);
+    const float h3 = h2f(ring[((P.conv_pos - 1) & 3) * 10240 + ch]);
+    const uint16_t raw = P.x[(long long)b * P.x_sb + ch];
+    xv = conv_step_value(w, h1, h2, h3, h2f(raw));
+    ring[(P.conv_pos & 3) * 10240 + ch] = raw;
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  // ---- decode own row (:81-114) ----
+  float S[NS];
+  {
+    const float s8 = h2f(pS8[tid]), s4 = h2f(pS4[tid]);
+#pragma unroll
+    for (int j = 0; j < N8; ++j) {
+      int lo = (pLo[tid * W8 + j / 2] >> (4 * (j & 1))) & 15;
+      int hi = (pHi[tid * W8 + j / 2] >> (4 * (j & 1))) & 15;
+      int ub = (hi << 4) | lo;
+      S[j] = (float)(ub - 256 * (ub > 127)) * s8;
+    }
+#pragma unroll
+    for (int j = 0; j < N4; ++j) {
+      int nib = (pQ4[tid * W4 + j / 2] >> (4 * (j & 1))) & 15;
+      S[N8 + j] = (float)(nib - 16 * (nib > 7)) * s4;
+    }
+  }
+  const float ls0 = h2f(P.latent_scale[g * 2 + 0]), ls1 = h2f(P.latent_scale[g * 2 + 1]);
+  const float ils0 = __frcp_rn(ls0), ils1 = __frcp_rn(ls1);
+  const float2 ls2 = make_float2(ls0, ls1), nls2 = make_float2(-ls0, -ls1), ils2 = make_float2(ils0, ils1);
+  float2 zz = make_float2(e4m3_to_f32(pLat[tid * 2 + 0]) * ls0, e4m3_to_f32(pLat[tid * 2 + 1]) * ls1);
+  const float dv = P.d_is_f32 ? reinterpret_cast<const float*>(P.D)[h] : h2f(reinterpret_cast<const uint16_t*>(P.D)[h]);
+
+  // ---- one token: recurrence, four-stream readout, latent and INT requant (:115-162) ----
+  float s8, s4;
+  {
+    const float dtv = sDD[hl].x, dec = sDD[hl].y;
+    float dots[7];
+#pragma unroll
+    for (int i = 0; i < 7; ++i) dots[i] = sDots[i];
+    float ysum, ycorr, m8, m4;
+    recur_row4<N8, NP>(S, sP4, sV2, dec, dtv, xv, ysum, ycorr, m8, m4);
+    TokenScales ts;
+    const float out = token_tail_sums(ysum, ycorr, m8, m4, xv, dtv, dec, dv, dots, zz, ls2, nls2, ils2, ts);
+    P.y[(long long)b * P.y_sb + (long long)h * dim + p] = f2h(out);
+    s8 = ts.s8; s4 = ts.s4;
+    requant_row<N8, NP>(S, ts);
+  }
+
+  // ---- pack (:163-181) and store coalesced ----
+  __syncthreads();
+  {
+    const float i8 = s8 > 0.f ? __frcp_rn(s8) : 0.f;
+    const float i4 = s4 > 0.f ? __frcp_rn(s4) : 0.f;
+#pragma unroll
+    for (int j = 0; j < N8; j += 2) {
+      const int qa = __float2int_rn(div_exact(S[j], s8, i8));
+      const int qb = __float2int_rn(div_exact(S[j + 1], s8, i8));
+      pLo[tid * W8 + j / 2] = (unsigned char)((qa & 15) | ((qb & 15) << 4));
+      pHi[tid * W8 + j / 2] = (unsigned char)(((qa >> 4) & 15) | (((qb >> 4) & 15) << 4));
+    }
+#pragma unroll
+    for (int j = 0; j < N4; j += 2) {
+      const int qa = __float2int_rn(div_exact(S[N8 + j], s4, i4));
+      const int qb = __float2int_rn(div_exact(S[N8 + j + 1], s4, i4));
+      pQ4[tid * W4 + j / 2] = (unsigned char)((qa & 15) | ((qb & 15) << 4));
+    }
+    pLat[tid * 2 + 0] = f32_to_e4m3(fminf(fmaxf(div_exact(zz.x, ls0, ils0), -448.f), 448.f));
+    pLat[tid * 2 + 1] = f32_to_e4m3(fminf(fmaxf(div_exact(zz.y, ls1, ils1), -448.f), 448.f));
+    pS8[tid] = f2h(s8);
+    pS4[tid] = f2h(s4);
+  }
+  __syncthreads();
+  auto copy_out = [&](unsigned char* dst, const unsigned char* src, int bytes) {
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (int i = tid; i < bytes / 16; i += 128) d[i] = s[i];
+  };
+  copy_out(P.lo + row0 * W8, pLo, rows * W8);
+  copy_out(P.hi + row0 * W8, pHi, rows * W8);
+  copy_out(P.q4 + row0 * W4, pQ4, rows * W4);
+  copy_out(P.latent + row0 * 2, pLat, rows * 2);
+  copy_out(reinterpret_cast<unsigned char*>(P.s8 + row0), reinterpret_cast<unsigned char*>(pS8), rows * 2);
+  copy_out(reinterpret_cast<unsigned char*>(P.s4 + row0), reinterpret_cast<unsigned char*>(pS4), rows * 2);
+}
+
+template <int N8, int N4>
+int launch_step2(const ScanParams& P, bool prepare_only, cudaStream_t stream) {
+  using PL = PrepLayout<N8, N4>;
+  constexpr int smem = 256 * 4 + (PL::F * (PL::NZ + 1) * 4 + 15) / 16 * 16 + (2 * PL::NZ * 4 + 15) / 16 * 16 + 512 +
+                       (PL::F * PL::NZ * 2 + 15) / 16 * 16 + (PL::NZ * 4 + 15) / 16 * 16 + 128;
+  auto kp = step_prep_kernel<N8, N4>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kp, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return kECuda;
+    attr = true;
+  }
+  if (prepare_only) return kOk;
+  kp<<<dim3(P.groups, P.batch), 256, smem, stream>>>(P);
+  ssu_step_kernel<N8, N4><<<dim3(P.heads / (128 / P.dim), P.batch), 128, 0, stream>>>(P);
+  return launch_status();
+}
+
 template <int N8, int N4, int KJ, int MODE, int TC = (MODE == 2 ? 1 : kTC)>
 int launch_kj(const ScanParams& P, int hpc, cudaStream_t stream) {
   const size_t smem = ScanSmem<N8, N4, TC>::kBytes;
@@ -883,6 +1166,8 @@ int launch_t(const ScanParams& P, int hpc, cudaStream_t stream) {
   if (P.conv_mode != 2 && P.prep_bc && P.prep_pv && P.prep_ddt && bd == 128 && hpc <= 2)
     return P.conv_mode == 1 ? launch_chunked<N8, N4, 1>(P, false, stream) : launch_chunked<N8, N4, 0>(P, false, stream);
   if (P.conv_mode == 1) return bd == 128 ? launch_kj<N8, N4, 1, 1>(P, hpc, stream) : kEInval;
+  if (P.conv_mode == 2 && P.prep_bc && P.prep_pv && P.prep_ddt && bd == 128 && hpc <= 2)
+    return launch_step2<N8, N4>(P, false, stream);
   if (P.conv_mode == 2) return bd == 128 ? launch_kj<N8, N4, 1, 2>(P, hpc, stream) : kEInval;
   if (bd >= 128) return launch_kj<N8, N4, 1, 0>(P, hpc, stream);
   if (bd >= 64) return launch_kj<N8, N4, 2, 0>(P, hpc, stream);
@@ -902,6 +1187,7 @@ int prepare_t() {
   st |= launch_kj<N8, N4, 1, 2>(P, 0, 0);
   st |= launch_chunked<N8, N4, 0>(P, true, 0);
   st |= launch_chunked<N8, N4, 1>(P, true, 0);
+  st |= launch_step2<N8, N4>(P, true, 0);
   return st;
 }
 

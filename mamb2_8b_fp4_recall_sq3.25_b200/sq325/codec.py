@@ -230,7 +230,7 @@ def scan_with_conv(xbc, dt, A, D, dt_bias, state, permutation, basis, latent_sca
     a.lo, a.hi, a.q4, a.latent, a.s8, a.s4 = (t[k].data_ptr() for k in ('lo', 'hi', 'q4', 'latent', 's8', 's4'))
     a.y, a.y_batch_stride, a.y_token_stride = y.data_ptr(), length * heads * dim, heads * dim
     ws = None
-    if not fused and position == 0:
+    if not fused:          # the two-kernel path (prefill or one-token step); fused: one kernel
         need = _lib.load().sq_scan_workspace(batch, length, heads, groups, layout_index(layout))
         ws = torch.empty(need, device=xbc.device, dtype=torch.uint8)
         a.workspace, a.workspace_bytes = ws.data_ptr(), need

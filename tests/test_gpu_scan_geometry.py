@@ -265,3 +265,32 @@ def test_conv_prefill_two_kernel_path_matches_fused_bytes(layout, length):
     for k in s1.tensors:
         assert torch.equal(s1.tensors[k].view(torch.uint8), s2.tensors[k].view(torch.uint8)), k
     assert torch.equal(r1.view(torch.int16), r2.view(torch.int16))
+
+
+@pytest.mark.parametrize('layout', oc.LAYOUTS)
+@pytest.mark.parametrize('B', [1, 8])
+def test_conv_step_two_kernel_path_matches_fused_bytes(layout, B):
+    """One-token decode steps (position > 0): the prep + step kernels (group tables once per
+    batch row and group) and the single fused kernel give the same y, packed state bytes and
+    conv ring, bit for bit, over four consecutive positions (every ring slot written)."""
+    from sq325 import codec
+    rng = np.random.default_rng(4000 + oc.LAYOUTS.index(layout) + B)
+    d, st = _inputs(layout, B, 1, seed=4100 + oc.LAYOUTS.index(layout) + B, raw_xbc=True)
+    tables = [_T(d[k]) for k in ('permutation', 'basis', 'latent_scale', 'predictor')]
+    ring_np = rng.standard_normal((B, 4, 10240)).astype(np.float16)
+    paths = []
+    for fused in (False, True):
+        paths.append([_gpu_state(st, layout), _T(ring_np)])
+    for s in range(4):
+        raw = _T(rng.standard_normal((B, 1, 10240)).astype(np.float16))
+        dt = _T((rng.standard_normal((B, 1, H)) * 0.5).astype(np.float16))
+        ys = []
+        for fused, (ps, ring) in zip((False, True), paths):
+            y, _ = codec.scan_with_conv(raw, dt, _T(d['A']), _T(d['D']), _T(d['dt_bias']), ps, *tables,
+                                        _T(d['conv_w']), _T(d['conv_b']), ring, 7 + s, layout=layout, fused=fused)
+            ys.append(y)
+        torch.cuda.synchronize()
+        assert torch.equal(ys[0].view(torch.int16), ys[1].view(torch.int16)), s
+        for k in paths[0][0].tensors:
+            assert torch.equal(paths[0][0].tensors[k].view(torch.uint8), paths[1][0].tensors[k].view(torch.uint8)), (s, k)
+        assert torch.equal(paths[0][1].view(torch.int16), paths[1][1].view(torch.int16)), s
