@@ -861,6 +861,315 @@ int launch_chunked(const ScanParams& P, bool prepare_only, cudaStream_t stream) 
 }
 
 // ============================================================================================
+// Half-row chunk kernel (modes 0 and 1, dim 64, batch 1 or 2): the chunk kernel's arithmetic
+// with two threads per state row and one head per CTA.  A multi-token call at batch 1 gives
+// the one-thread-per-row kernel only 64 CTAs (43% of the SMs) for a long sequential walk over
+// the tokens; this kernel runs 128 CTAs whose threads carry half a row each (<= 42 stored
+// floats in 72 registers), so each token step is about half as long.  At larger batches the
+// row kernel is faster (the token tail runs in both halves: 23% more instructions).
+//
+// Pair split: with N8/2 and N4/2 even for every released layout, thread half h of a row takes
+// the global pairs jp = 2i + h (i = 0..NP/2-1).  Both halves then see the same tier boundary
+// (local pair i < N8/4 is INT8), so the instruction stream is identical and only the table
+// offset differs.  Half 0 accumulates exactly the chunk kernel's even-pair readout chain and
+// half 1 its odd-pair chain; one shuffle adds them (IEEE addition is commutative, so both
+// halves form the same sum) and the two halves run the token tail redundantly on identical
+// inputs.  Results are bit-identical to ssu_chunk_kernel and ssu_sq325_kernel.
+//
+// Lane mapping: row r = warp * 16 + (lane & 15), half = lane >> 4; the halves of a row are
+// lanes l and l ^ 16 of one warp.
+// ============================================================================================
+
+template <int N8, int N4>
+struct HalfSmem {
+  static constexpr int FP = PrepLayout<N8, N4>::FP;
+  static constexpr int TC = kChunkTC, R = 2 * kChunkTC;
+  // ring slot: raw (mode 1) or conv'd x[64] fp16 | B in tier order [128] fp16 | pv[FP] fp32 | ddt
+  static constexpr int oX = 0, oBC = 128, oPV = 384, oDD = 384 + FP * 4;
+  static constexpr int kSlot = (oDD + 8 + 15) / 16 * 16;
+  static constexpr int oT = R * kSlot;
+  // token tables of one chunk: sP4 [TC][64] float4 {B*dt pair, C + cvec pair}, sX [TC][64];
+  // before the first / after the last chunk the packed rows (64 x 52 B)
+  static constexpr int kTok = TC * 64 * 16 + TC * 64 * 4;
+  static constexpr int kT = kTok > 64 * 52 ? kTok : 64 * 52;
+  static constexpr int oW = oT + kT;                  // x conv taps + bias [64][5] fp32
+  static constexpr int kBytes = oW + 64 * 5 * 4;
+};
+
+template <int N8, int N4, int MODE>
+__global__ void __launch_bounds__(128, 7)
+ssu_half_kernel(const ScanParams P) {
+  using L = HalfSmem<N8, N4>;
+  constexpr int NS = N8 + N4, F = NS + 2, FP = L::FP;
+  constexpr int TC = L::TC, R = L::R, SB = L::kSlot;
+  constexpr int W8 = N8 / 2, W4 = N4 / 2;
+  constexpr int NP = NS / 2, NPH = NP / 2;          // pairs per row / per half
+  constexpr int P8H = N8 / 4;                       // INT8 pairs per half
+  static_assert(N8 % 4 == 0 && N4 % 4 == 0, "each half takes the same tier pattern");
+  constexpr int dim = 64, rows = 64;
+
+  extern __shared__ __align__(16) unsigned char smem[];
+  unsigned char* ring = smem;
+  float4* sP4 = reinterpret_cast<float4*>(smem + L::oT);                   // [TC][64]
+  float* sX = reinterpret_cast<float*>(smem + L::oT + TC * 64 * 16);       // [TC][64]
+  float* sW = reinterpret_cast<float*>(smem + L::oW);                      // [64][5]
+  unsigned char* sPack = smem + L::oT;
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int half = lane >> 4;
+  const int r = (tid >> 5) * 16 + (lane & 15);
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int hpg = P.heads / P.groups;
+  const int g = h / hpg;
+  const long long row0 = ((long long)b * P.heads + h) * dim;
+
+  auto slot_of = [&](int t) { return ring + (t & (R - 1)) * SB; };
+  const uint16_t* xb = P.x + (long long)b * P.x_sb + (long long)h * dim;
+  const bool vec = ((((uintptr_t)xb) & 15) == 0) && (P.x_st & 7) == 0;
+  const long long btg = (long long)b * P.length;
+  constexpr int kPcs = 8 + 16 + FP / 4;             // 16-byte pieces per token (x, B half of bc, pv)
+
+  auto prefetch = [&](int c0) {
+    const int nt = min(TC, P.length - c0);
+    for (int i = tid; i < nt * (kPcs + 1); i += 128) {
+      const int t = i / (kPcs + 1), q = i - t * (kPcs + 1);
+      const long long tt = c0 + t;
+      unsigned char* slot = slot_of(c0 + t);
+      if (q < 8) {
+        const uint16_t* src = xb + tt * P.x_st + q * 8;
+        uint16_t* dst = reinterpret_cast<uint16_t*>(slot + L::oX) + q * 8;
+        if (vec) cp_async16(dst, src);
+        else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) dst[e] = src[e];
+        }
+      } else if (q < 24) {
+        cp_async16(slot + L::oBC + (q - 8) * 16, P.prep_bc + ((btg + tt) * P.groups + g) * 256 + (q - 8) * 8);
+      } else if (q < kPcs) {
+        cp_async16(slot + L::oPV + (q - 24) * 16, P.prep_pv + ((btg + tt) * P.groups + g) * FP + (q - 24) * 4);
+      } else {
+        cp_async8(slot + L::oDD, P.prep_ddt + (btg + tt) * P.heads + h);
+      }
+    }
+  };
+
+  // ---- stage packed rows; x conv taps; zero history ----
+  unsigned char* pLo = sPack;
+  unsigned char* pHi = pLo + rows * W8;
+  unsigned char* pQ4 = pHi + rows * W8;
+  unsigned char* pLat = pQ4 + rows * W4;
+  uint16_t* pS8 = reinterpret_cast<uint16_t*>(pLat + rows * 2);
+  uint16_t* pS4 = pS8 + rows;
+  stage16(pLo, P.lo + row0 * W8, rows * W8, tid, 128);
+  stage16(pHi, P.hi + row0 * W8, rows * W8, tid, 128);
+  stage16(pQ4, P.q4 + row0 * W4, rows * W4, tid, 128);
+  stage16(pLat, P.latent + row0 * 2, rows * 2, tid, 128);
+  stage16(pS8, P.s8 + row0, rows * 2, tid, 128);
+  stage16(pS4, P.s4 + row0, rows * 2, tid, 128);
+  if (MODE == 1 && tid < dim) {
+    const int ch = h * dim + tid;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sW[tid * 5 + i] = h2f(P.conv_w[ch * 4 + i]);
+    sW[tid * 5 + 4] = h2f(P.conv_b[ch]);
+#pragma unroll
+    for (int k = -3; k < 0; ++k) reinterpret_cast<uint16_t*>(slot_of(k) + L::oX)[tid] = 0;
+  }
+  prefetch(0);
+  cp_async_wait_all();
+  __syncthreads();
+
+  // ---- decode this half of the row (:81-114): local pair i = global pair 2i + half ----
+  float S[2 * NPH];
+  {
+    const float s8 = h2f(pS8[r]), s4 = h2f(pS4[r]);
+#pragma unroll
+    for (int i = 0; i < P8H; ++i) {
+      const int jp = 2 * i + half;
+      const int lo = pLo[r * W8 + jp], hi = pHi[r * W8 + jp];
+      const int ua = ((hi & 15) << 4) | (lo & 15), ub = (hi & 0xF0) | (lo >> 4);
+      S[2 * i] = (float)(ua - 256 * (ua > 127)) * s8;
+      S[2 * i + 1] = (float)(ub - 256 * (ub > 127)) * s8;
+    }
+#pragma unroll
+    for (int i = P8H; i < NPH; ++i) {
+      const int q = pQ4[r * W4 + 2 * (i - P8H) + half];
+      const int na = q & 15, nb = q >> 4;
+      S[2 * i] = (float)(na - 16 * (na > 7)) * s4;
+      S[2 * i + 1] = (float)(nb - 16 * (nb > 7)) * s4;
+    }
+  }
+  const float ls0 = h2f(P.latent_scale[g * 2 + 0]), ls1 = h2f(P.latent_scale[g * 2 + 1]);
+  const float ils0 = __frcp_rn(ls0), ils1 = __frcp_rn(ls1);
+  const float2 ls2 = make_float2(ls0, ls1), nls2 = make_float2(-ls0, -ls1), ils2 = make_float2(ils0, ils1);
+  float2 zz = make_float2(e4m3_to_f32(pLat[r * 2 + 0]) * ls0, e4m3_to_f32(pLat[r * 2 + 1]) * ls1);
+  const float dv = P.d_is_f32 ? reinterpret_cast<const float*>(P.D)[h] : h2f(reinterpret_cast<const uint16_t*>(P.D)[h]);
+  float s8 = 0.f, s4 = 0.f;
+  uint16_t* yrow = P.y + (long long)b * P.y_sb + (long long)h * dim + r;
+
+  for (int c0 = 0; c0 < P.length; c0 += TC) {
+    const int nt = min(TC, P.length - c0);
+    cp_async_wait_all();
+    __syncthreads();                                   // chunk landed; previous tables (or the
+                                                       // packed rows read by the decode) free
+    // -- conv'd x: channel c = tid % 64, tokens of parity tid / 64 (each token's conv reads
+    //    only raw ring values, so the tokens are independent) --
+    {
+      const int c = tid & 63;
+      const uint16_t* rx = reinterpret_cast<const uint16_t*>(ring + L::oX) + c;
+      float w[5];
+      if (MODE == 1) {
+#pragma unroll
+        for (int i = 0; i < 5; ++i) w[i] = sW[c * 5 + i];
+      }
+      for (int t = tid >> 6; t < nt; t += 2) {
+        const int tt = c0 + t;
+        const float raw = h2f(rx[(tt & (R - 1)) * (SB / 2)]);
+        float xv = raw;
+        if (MODE == 1)
+          xv = conv_prefill_value(w, h2f(rx[((tt - 3) & (R - 1)) * (SB / 2)]), h2f(rx[((tt - 2) & (R - 1)) * (SB / 2)]),
+                                  h2f(rx[((tt - 1) & (R - 1)) * (SB / 2)]), raw);
+        sX[t * 64 + c] = xv;
+      }
+    }
+    // -- per token and pair: {B*dt pair, C + cvec pair} (one 16-byte store per pair) --
+    for (int e = tid; e < nt * 64; e += 128) {
+      const int t = e >> 6, jp = e & 63;
+      const unsigned char* slot = slot_of(c0 + t);
+      const float dtv = reinterpret_cast<const float2*>(slot + L::oDD)->x;
+      const __half2 bb = reinterpret_cast<const __half2*>(slot + L::oBC)[jp];
+      const float2 bf = __half22float2(bb);
+      float2 cc = make_float2(0.f, 0.f);
+      if (2 * jp < NS) cc = reinterpret_cast<const float2*>(slot + L::oPV)[jp];      // C_j + cvec_j
+      sP4[t * 64 + jp] = make_float4(bf.x * dtv, bf.y * dtv, cc.x, cc.y);
+    }
+    __syncthreads();                                   // tables visible; raw x of the chunk consumed
+    if (c0 + TC < P.length) prefetch(c0 + TC);
+
+    // -- per half-row recurrence, readout and requant (:115-162) for the chunk's tokens --
+#pragma unroll 1
+    for (int t = 0; t < nt; ++t) {
+      const unsigned char* slot = slot_of(c0 + t);
+      const float2 ddv = *reinterpret_cast<const float2*>(slot + L::oDD);
+      const float dtv = ddv.x, dec = ddv.y;
+      const float x = sX[t * 64 + r];
+      const float4* cp = sP4 + t * 64 + half;
+      const float* pv = reinterpret_cast<const float*>(slot + L::oPV);
+      float m8a = 0.f, m8b = 0.f, m4a = 0.f, m4b = 0.f;
+      float2 ya = make_float2(0.f, 0.f);
+      {
+        const float2 dd = make_float2(dec, dec), xx = make_float2(x, x);
+#pragma unroll
+        for (int i = 0; i < NPH; ++i) {
+          const float4 bc = cp[2 * i];
+          const float2 pr = make_float2(S[2 * i], S[2 * i + 1]);
+          const float2 sn = __ffma2_rn(pr, dd, __fmul2_rn(make_float2(bc.x, bc.y), xx));   // prior*decay + (B*dt)*x
+          S[2 * i] = sn.x; S[2 * i + 1] = sn.y;
+          ya = __ffma2_rn(pr, make_float2(bc.z, bc.w), ya);
+          if (i < P8H) { m8a = fmaxf(m8a, fabsf(sn.x)); m8b = fmaxf(m8b, fabsf(sn.y)); }
+          else         { m4a = fmaxf(m4a, fabsf(sn.x)); m4b = fmaxf(m4b, fabsf(sn.y)); }
+        }
+      }
+      const float part = ya.x + ya.y;
+      const float yacc = part + __shfl_xor_sync(0xffffffffu, part, 16);
+      float m8 = fmaxf(m8a, m8b), m4 = fmaxf(m4a, m4b);
+      m8 = fmaxf(m8, __shfl_xor_sync(0xffffffffu, m8, 16));
+      m4 = fmaxf(m4, __shfl_xor_sync(0xffffffffu, m4, 16));
+      float dots[7];
+      {
+        const float2 d01 = *reinterpret_cast<const float2*>(pv + F), d23 = *reinterpret_cast<const float2*>(pv + F + 2);
+        const float2 pz = *reinterpret_cast<const float2*>(pv + NS);
+        dots[0] = d01.x; dots[1] = d01.y; dots[2] = d23.x; dots[3] = d23.y; dots[4] = pv[F + 4];
+        dots[5] = pz.x; dots[6] = pz.y;
+      }
+      TokenScales ts;
+      const float out = token_tail_fold(yacc, m8, m4, x, dtv, dec, dv, dots, zz, ls2, nls2, ils2, ts);
+      if (half == 0) yrow[(long long)(c0 + t) * P.y_st] = f2h(out);
+      s8 = ts.s8; s4 = ts.s4;
+      requant_row<2 * P8H, NPH>(S, ts);
+    }
+  }
+
+  // ---- conv cache update (mode 1): raw columns of the newest positions ----
+  if (MODE == 1) {
+    uint16_t* cache = P.conv_cache + (long long)b * P.conv_cache_sb;
+    const int nwrite = min(4, P.length);
+    for (int i = 0; i < nwrite; ++i) {
+      const int t = P.length - 1 - i;
+      const int cs = (P.conv_pos + t) & 3;
+      if (tid < dim) cache[cs * 10240 + h * dim + tid] = reinterpret_cast<const uint16_t*>(slot_of(t) + L::oX)[tid];
+      if ((h % hpg) == 0) {
+        cache[cs * 10240 + 8192 + g * 128 + tid] = P.B[(long long)b * P.b_sb + (long long)t * P.b_st + g * 128 + tid];
+        cache[cs * 10240 + 9216 + g * 128 + tid] = P.C[(long long)b * P.c_sb + (long long)t * P.c_st + g * 128 + tid];
+      }
+    }
+  }
+
+  // ---- pack once (:163-181) and store coalesced ----
+  __syncthreads();
+  {
+    const float i8 = s8 > 0.f ? __frcp_rn(s8) : 0.f;
+    const float i4 = s4 > 0.f ? __frcp_rn(s4) : 0.f;
+#pragma unroll
+    for (int i = 0; i < P8H; ++i) {
+      const int jp = 2 * i + half;
+      const int qa = __float2int_rn(div_exact(S[2 * i], s8, i8));
+      const int qb = __float2int_rn(div_exact(S[2 * i + 1], s8, i8));
+      pLo[r * W8 + jp] = (unsigned char)((qa & 15) | ((qb & 15) << 4));
+      pHi[r * W8 + jp] = (unsigned char)(((qa >> 4) & 15) | (((qb >> 4) & 15) << 4));
+    }
+#pragma unroll
+    for (int i = P8H; i < NPH; ++i) {
+      const int qa = __float2int_rn(div_exact(S[2 * i], s4, i4));
+      const int qb = __float2int_rn(div_exact(S[2 * i + 1], s4, i4));
+      pQ4[r * W4 + 2 * (i - P8H) + half] = (unsigned char)((qa & 15) | ((qb & 15) << 4));
+    }
+    if (half == 0) {
+      pLat[r * 2 + 0] = f32_to_e4m3(fminf(fmaxf(div_exact(zz.x, ls0, ils0), -448.f), 448.f));
+      pLat[r * 2 + 1] = f32_to_e4m3(fminf(fmaxf(div_exact(zz.y, ls1, ils1), -448.f), 448.f));
+      pS8[r] = f2h(s8);
+      pS4[r] = f2h(s4);
+    }
+  }
+  __syncthreads();
+  auto copy_out = [&](unsigned char* dst, const unsigned char* src, int bytes) {
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (int i = tid; i < bytes / 16; i += 128) d[i] = s[i];
+  };
+  copy_out(P.lo + row0 * W8, pLo, rows * W8);
+  copy_out(P.hi + row0 * W8, pHi, rows * W8);
+  copy_out(P.q4 + row0 * W4, pQ4, rows * W4);
+  copy_out(P.latent + row0 * 2, pLat, rows * 2);
+  copy_out(reinterpret_cast<unsigned char*>(P.s8 + row0), reinterpret_cast<unsigned char*>(pS8), rows * 2);
+  copy_out(reinterpret_cast<unsigned char*>(P.s4 + row0), reinterpret_cast<unsigned char*>(pS4), rows * 2);
+}
+
+template <int N8, int N4, int MODE>
+int launch_half(const ScanParams& P, bool prepare_only, cudaStream_t stream) {
+  using PL = PrepLayout<N8, N4>;
+  constexpr int prep_smem = kPrepTokens * 256 * 4 + (PL::F * (PL::NZ + 1) * 4 + 15) / 16 * 16 +
+                            (2 * PL::NZ * 4 + 15) / 16 * 16 + 128 * 4;
+  constexpr int half_smem = HalfSmem<N8, N4>::kBytes;
+  auto kp = scan_prep_kernel<N8, N4, MODE>;
+  auto kc = ssu_half_kernel<N8, N4, MODE>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kp, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem) != cudaSuccess ||
+        cudaFuncSetAttribute(kc, cudaFuncAttributeMaxDynamicSharedMemorySize, half_smem) != cudaSuccess ||
+        cudaFuncSetAttribute(kc, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+      return kECuda;
+    attr = true;
+  }
+  if (prepare_only) return kOk;
+  dim3 gp((P.length + kPrepTokens - 1) / kPrepTokens, P.groups, P.batch);
+  kp<<<gp, 256, prep_smem, stream>>>(P);
+  dim3 gc(P.heads, P.batch);
+  kc<<<gc, 128, half_smem, stream>>>(P);
+  return launch_status();
+}
+
+// ============================================================================================
 // Two-kernel path of the one-token decode step (mode 2: conv step numerics, conv ring).
 //
 // The single fused kernel redoes, in each of the eight CTAs of a B/C group, the staging of the
@@ -1163,6 +1472,8 @@ int launch_kj(const ScanParams& P, int hpc, cudaStream_t stream) {
 template <int N8, int N4>
 int launch_t(const ScanParams& P, int hpc, cudaStream_t stream) {
   const int bd = hpc * P.dim;
+  if (P.conv_mode != 2 && P.prep_bc && P.prep_pv && P.prep_ddt && P.dim == 64 && P.batch <= 2)
+    return P.conv_mode == 1 ? launch_half<N8, N4, 1>(P, false, stream) : launch_half<N8, N4, 0>(P, false, stream);
   if (P.conv_mode != 2 && P.prep_bc && P.prep_pv && P.prep_ddt && bd == 128 && hpc <= 2)
     return P.conv_mode == 1 ? launch_chunked<N8, N4, 1>(P, false, stream) : launch_chunked<N8, N4, 0>(P, false, stream);
   if (P.conv_mode == 1) return bd == 128 ? launch_kj<N8, N4, 1, 1>(P, hpc, stream) : kEInval;
@@ -1188,6 +1499,8 @@ int prepare_t() {
   st |= launch_chunked<N8, N4, 0>(P, true, 0);
   st |= launch_chunked<N8, N4, 1>(P, true, 0);
   st |= launch_step2<N8, N4>(P, true, 0);
+  st |= launch_half<N8, N4, 0>(P, true, 0);
+  st |= launch_half<N8, N4, 1>(P, true, 0);
   return st;
 }
 

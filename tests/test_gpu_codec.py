@@ -164,11 +164,13 @@ def _random_scan_inputs(layout, B, L, H, P, G, seed):
 
 @pytest.mark.parametrize('layout', oc.LAYOUTS)
 @pytest.mark.parametrize('length', [1, 7, 8, 37])
-def test_two_kernel_path_matches_fused_kernel_bytes(layout, length):
-    """Model geometry (128-thread CTAs): the prep + chunk kernels and the single fused kernel
-    must produce the same y and the same packed state bytes, for ragged chunk counts."""
+@pytest.mark.parametrize('batch', [2, 3])
+def test_two_kernel_path_matches_fused_kernel_bytes(layout, length, batch):
+    """Model geometry (128-thread CTAs): the prep + chunk kernels (the half-row variant at
+    batch <= 2, one thread per row above) and the single fused kernel must produce the same y
+    and the same packed state bytes, for ragged chunk counts."""
     from sq325 import codec
-    args, st, tables = _random_scan_inputs(layout, 2, length, 128, 64, 8, seed=length)
+    args, st, tables = _random_scan_inputs(layout, batch, length, 128, 64, 8, seed=length)
     st2 = st.clone()
     y1, _ = codec.scan(*args, st, *tables, layout=layout, fused=True)
     y2, _ = codec.scan(*args, st2, *tables, layout=layout)

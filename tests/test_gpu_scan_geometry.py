@@ -4,7 +4,8 @@ the reference kernel scripts/fp4_zero_predictor_codec_v1.py:76-181 run by the Tr
 interpreter).
 
 Covered paths, all through the C-ABI:
-  chunk   sq_scan with a workspace: scan_prep_kernel + ssu_chunk_kernel (the scoring path)
+  chunk   sq_scan with a workspace: scan_prep_kernel + ssu_chunk_kernel (the scoring path;
+          ssu_half_kernel, two threads per row, at batch <= 2)
   fused   sq_scan without a workspace: ssu_sq325_kernel
   conv1   sq_scan_conv at position 0: the causal conv1d prefill fused in front of the scan
           (chunk and fused variants; mamba2_recall/state_quant.py:305-317)
@@ -243,12 +244,12 @@ def test_scan_conv_rejects_continuing_prefill():
 
 @pytest.mark.parametrize('layout', oc.LAYOUTS)
 @pytest.mark.parametrize('length', [2, 9, 37])
-def test_conv_prefill_two_kernel_path_matches_fused_bytes(layout, length):
-    """Fused conv1d prefill at model geometry: the prep + chunk kernels and the
-    single fused kernel give the same y, packed state bytes and conv ring, bit for bit
-    (both run the same operations in the same order)."""
+@pytest.mark.parametrize('B', [1, 4])
+def test_conv_prefill_two_kernel_path_matches_fused_bytes(layout, length, B):
+    """Fused conv1d prefill at model geometry: the prep + chunk kernels (half-row variant at
+    batch 1, one thread per row at batch 4) and the single fused kernel give the same y,
+    packed state bytes and conv ring, bit for bit (the same operations in the same order)."""
     from sq325 import codec
-    B = 4
     d, st = _inputs(layout, B, length, seed=2500 + length + oc.LAYOUTS.index(layout), raw_xbc=True)
     outs = []
     for fused in (False, True):
