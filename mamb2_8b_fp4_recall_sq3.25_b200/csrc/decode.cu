@@ -162,17 +162,14 @@ __device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned 
   asm volatile("red.release.gpu.global.add.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
 }
 // Split-phase form: grid_arrive adds this CTA's arrival (after a CTA barrier, so the release
-// covers every thread's earlier writes) and returns the count to wait for (0 after an abort);
-// work that does not depend on the other CTAs can run before grid_wait.  `nbar` counts the
-// barriers of the launch (the same in every thread).
+// covers every thread's earlier writes) and returns the count to wait for; work that does not
+// depend on the other CTAs can run before grid_wait.  The arrival never waits on a load (an
+// abort is seen by the wait's polling loop instead).  `nbar` counts the barriers of the launch
+// (the same in every thread).
 __device__ unsigned long long grid_arrive(const DecodeParams& P, unsigned& nbar) {
   bar_sync(1, kCompute);
   const unsigned long long target = (unsigned long long)(++nbar) * gridDim.x;
-  if (threadIdx.x == 0) {
-    DecodeSync* s = P.sync;
-    if (ld_abort(s)) return 0;
-    red_release_add(&s->count, 1ull);
-  }
+  if (threadIdx.x == 0) red_release_add(&P.sync->count, 1ull);
   return target;
 }
 __device__ bool grid_wait(const DecodeParams& P, unsigned long long target, int* flag) {
