@@ -202,8 +202,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__
           const float nm = fmaxf(mx, cm);
           float s = 0.f;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s += __expf(v[i] - nm);
-          sm = (mx == -INFINITY ? 0.f : sm * __expf(mx - nm)) + s;
+          for (int i = 0; i < 32; ++i) s += expf(v[i] - nm);       // CUDA's accurate expf
+          sm = (mx == -INFINITY ? 0.f : sm * expf(mx - nm)) + s;
           mx = nm;
         }
         if (row < args.M) {
