@@ -117,6 +117,36 @@ typedef struct sq_s16_args {
 } sq_s16_args;
 int sq_s16_scan(const sq_s16_args* args, void* stream);
 
+/* ---------------------------------------------------------------- legacy sq3p25 scan + STE
+ * sq_sq3p25_scan replaces scan(..., state) for the mode 'sq3p25' of
+ * mamba2_recall/state_codec.py (`_sq_scan` :105-176, host wrapper :204-262): a fixed split
+ * of each row into 16 INT8 + 64 INT4 stored coordinates and 48 pruned ones (the group's
+ * permutation orders them), 52 bytes per row: lo / hi u8 [batch,heads,dim,8], q4 u8
+ * [...,32], s8 / s4 fp16 [batch,heads,dim], updated in place; y fp16 for every token.
+ * sq_ste_backward is the straight-through backward of scan_training
+ * (mamba2_recall/state_training_scan.py :24-221) for a scan from a fresh zero state:
+ * inputs contiguous as in the forward call, dy fp16 [B,L,H,P]; writes dx fp32 [B,L,H,P],
+ * d(dt) fp32 [B,L,H], dB / dC fp32 [B,L,G,128] (zeroed by the call).  chunk = tokens between
+ * carry checkpoints (1..256); the workspace holds the checkpoints, one chunk of carries and
+ * the adjoint carry: sq_ste_workspace(batch, length, heads, dim, chunk) bytes. */
+typedef struct sq_sq3p25_args {
+  int32_t batch, length, heads, dim, groups;
+  const uint16_t* x;  int64_t x_batch_stride, x_token_stride;
+  const uint16_t* dt; int64_t dt_batch_stride, dt_token_stride;
+  const float* A;
+  const uint16_t* B;  int64_t b_batch_stride, b_token_stride;
+  const uint16_t* C;  int64_t c_batch_stride, c_token_stride;
+  const void* D;       int32_t d_is_f32;
+  const void* dt_bias; int32_t dt_bias_is_f32;
+  const uint8_t* permutation;
+  uint8_t* lo; uint8_t* hi; uint8_t* q4; uint16_t* s8; uint16_t* s4;
+  uint16_t* y; int64_t y_batch_stride, y_token_stride;
+} sq_sq3p25_args;
+int sq_sq3p25_scan(const sq_sq3p25_args* args, void* stream);
+int64_t sq_ste_workspace(int batch, int length, int heads, int dim, int chunk);
+int sq_ste_backward(const sq_sq3p25_args* args, int chunk, const uint16_t* dy, float* dx, float* ddt, float* db,
+                    float* dc, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------- standalone codec
  * decode: rows (b,h,p) of the six PackedState buffers (mamba2_recall/state_codec.py:29-48,
  * fp4_zero_predictor_codec_v1.py:39-49) -> tiers fp32 [rows, n8+n4] in tier order and

@@ -20,7 +20,8 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / 'csrc'
 INCLUDE = HERE.parent / 'include'
 OUT = HERE / 'sq325' / 'libsq325.so'
-SOURCES = ['scan.cu', 'codec.cu', 'fp4.cu', 'gemm.cu', 'layer.cu', 'decode.cu', 's16.cu', 'fp4mma.cu', 'abi.cu', 'noalloc.cu']
+SOURCES = ['scan.cu', 'codec.cu', 'fp4.cu', 'gemm.cu', 'layer.cu', 'decode.cu', 's16.cu', 'ste.cu', 'fp4mma.cu', 'abi.cu',
+           'noalloc.cu']
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 
 

@@ -14,6 +14,7 @@
 #include "fp4.cuh"
 #include "layer.cuh"
 #include "s16.cuh"
+#include "ste.cuh"
 #include "scan.cuh"
 
 namespace sq {
@@ -254,6 +255,60 @@ int sq_s16_scan(const sq_s16_args* a, void* stream) {
   P.state = a->state; P.y = a->y; P.y_sb = a->y_batch_stride; P.y_st = a->y_token_stride;
   P.stats = a->stats;
   return check(launch_s16_scan(P, (cudaStream_t)stream), "sq_s16_scan");
+}
+
+namespace {
+int ste_params(const sq_sq3p25_args* a, SteParams& P, bool forward) {
+  if (!a || !a->x || !a->dt || !a->A || !a->B || !a->C || !a->D || !a->dt_bias || !a->permutation)
+    return fail(SQ_EINVAL, "sq3p25: null pointer argument");
+  if (forward && (!a->lo || !a->hi || !a->q4 || !a->s8 || !a->s4 || !a->y))
+    return fail(SQ_EINVAL, "sq3p25: null state or output");
+  if (a->batch <= 0 || a->length <= 0 || a->heads <= 0 || a->dim <= 0 || a->groups <= 0 || a->heads % a->groups)
+    return fail(SQ_EINVAL, "heads must be divisible by B/C groups");
+  if (a->dim > 128) return fail(SQ_EINVAL, "sq3p25: dim must be at most 128");
+  if (forward && (!aligned(a->lo, 8) || !aligned(a->hi, 8) || !aligned(a->q4, 16)))
+    return fail(SQ_EINVAL, "sq3p25: state buffers must be 16-byte aligned");
+  P = SteParams{};
+  P.batch = a->batch; P.length = a->length; P.heads = a->heads; P.dim = a->dim; P.groups = a->groups;
+  P.x = a->x; P.x_sb = a->x_batch_stride; P.x_st = a->x_token_stride;
+  P.dt = a->dt; P.dt_sb = a->dt_batch_stride; P.dt_st = a->dt_token_stride;
+  P.A = a->A;
+  P.B = a->B; P.b_sb = a->b_batch_stride; P.b_st = a->b_token_stride;
+  P.C = a->C; P.c_sb = a->c_batch_stride; P.c_st = a->c_token_stride;
+  P.D = a->D; P.d_is_f32 = a->d_is_f32; P.dt_bias = a->dt_bias; P.dt_bias_is_f32 = a->dt_bias_is_f32;
+  P.perm = a->permutation;
+  P.lo = a->lo; P.hi = a->hi; P.q4 = a->q4; P.s8 = a->s8; P.s4 = a->s4;
+  P.y = a->y; P.y_sb = a->y_batch_stride; P.y_st = a->y_token_stride;
+  return SQ_OK;
+}
+}  // namespace
+
+int sq_sq3p25_scan(const sq_sq3p25_args* a, void* stream) {
+  SteParams P;
+  if (int s = ste_params(a, P, true)) return s;
+  return check(launch_sq3p25_scan(P, (cudaStream_t)stream), "sq_sq3p25_scan");
+}
+
+int64_t sq_ste_workspace(int batch, int length, int heads, int dim, int chunk) {
+  return ste_workspace_bytes(batch, length, heads, dim, chunk);
+}
+
+int sq_ste_backward(const sq_sq3p25_args* a, int chunk, const uint16_t* dy, float* dx, float* ddt, float* db,
+                    float* dc, void* workspace, int64_t workspace_bytes, void* stream) {
+  SteParams P;
+  if (int s = ste_params(a, P, false)) return s;
+  if (!dy || !dx || !ddt || !db || !dc || !workspace) return fail(SQ_EINVAL, "ste_backward: null pointer argument");
+  if (chunk < 1 || chunk > 256) return fail(SQ_EINVAL, "chunk_size must be an integer in [1,256]");
+  const long long L = a->length, H = a->heads, Pd = a->dim, G = a->groups;
+  if (a->x_token_stride != H * Pd || a->x_batch_stride != L * H * Pd || a->dt_token_stride != H ||
+      a->dt_batch_stride != L * H || a->b_token_stride != G * 128 || a->b_batch_stride != L * G * 128 ||
+      a->c_token_stride != G * 128 || a->c_batch_stride != L * G * 128)
+    return fail(SQ_EINVAL, "ste_backward: inputs must be contiguous");
+  const long long need = ste_workspace_bytes(a->batch, a->length, a->heads, a->dim, chunk);
+  if (need < 0 || workspace_bytes < need || !aligned(workspace, 16))
+    return fail(SQ_EINVAL, "ste_backward: workspace smaller than sq_ste_workspace() or not 16-byte aligned");
+  P.dy = dy; P.dx = dx; P.ddt = ddt; P.db = db; P.dc = dc; P.chunk = chunk;
+  return check(launch_ste_backward(P, workspace, (cudaStream_t)stream), "sq_ste_backward");
 }
 
 int sq_state_decode(int layout, int batch, int heads, int dim, int groups, const uint8_t* lo, const uint8_t* hi,

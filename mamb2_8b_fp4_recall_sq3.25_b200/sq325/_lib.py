@@ -53,6 +53,19 @@ class S16Args(C.Structure):
                 ('state', p), ('y', p), ('y_batch_stride', i64), ('y_token_stride', i64), ('stats', p)]
 
 
+class Sq3p25Args(C.Structure):
+    _fields_ = [('batch', i32), ('length', i32), ('heads', i32), ('dim', i32), ('groups', i32),
+                ('x', p), ('x_batch_stride', i64), ('x_token_stride', i64),
+                ('dt', p), ('dt_batch_stride', i64), ('dt_token_stride', i64),
+                ('A', p),
+                ('B', p), ('b_batch_stride', i64), ('b_token_stride', i64),
+                ('C', p), ('c_batch_stride', i64), ('c_token_stride', i64),
+                ('D', p), ('d_is_f32', i32), ('dt_bias', p), ('dt_bias_is_f32', i32),
+                ('permutation', p),
+                ('lo', p), ('hi', p), ('q4', p), ('s8', p), ('s4', p),
+                ('y', p), ('y_batch_stride', i64), ('y_token_stride', i64)]
+
+
 class ConvArgs(C.Structure):
     _fields_ = [('weight', p), ('bias', p), ('ring', p), ('ring_batch_stride', i64), ('position', i32)]
 
@@ -81,6 +94,9 @@ _PROTOS = {
     'sq_scan': (C.c_int, [C.POINTER(ScanArgs), p]),
     'sq_scan_conv': (C.c_int, [C.POINTER(ScanArgs), C.POINTER(ConvArgs), p]),
     'sq_s16_scan': (C.c_int, [C.POINTER(S16Args), p]),
+    'sq_sq3p25_scan': (C.c_int, [C.POINTER(Sq3p25Args), p]),
+    'sq_ste_workspace': (i64, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
+    'sq_ste_backward': (C.c_int, [C.POINTER(Sq3p25Args), C.c_int, p, p, p, p, p, p, i64, p]),
     'sq_state_decode': (C.c_int, [C.c_int] * 5 + [p] * 9 + [p]),
     'sq_state_encode': (C.c_int, [C.c_int] * 6 + [p] * 9 + [p]),
     'sq_fp4_decode': (C.c_int, [p, p, p, C.c_int, C.c_int, p, i64, p]),

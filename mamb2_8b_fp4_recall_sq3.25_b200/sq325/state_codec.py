@@ -1,12 +1,16 @@
-"""The FP16-state control arm of mamba2_recall/state_codec.py (mode 's16').
+"""The two state modes of mamba2_recall/state_codec.py: the FP16-state control arm 's16'
+and the fixed-split packed codec 'sq3p25'.
 
-Same names, checks and results as the reference module for the s16 mode: `allocate_state`
-(:50-62), `scan` (:203-262, with `collect_stats`), `decode_state` / `encode_state_`
-(s16 branches of :269-331) and `validate_permutation` (:179-184).  The scan runs in
-libsq325.so (sq_s16_scan): fp32 arithmetic, the carry rounded to fp16 after every token,
-the readout summed in the reference kernel's order.  The reference's other mode, the fixed
-16/64/48 'sq3p25' codec (:105-176), is superseded by the latent codec that the released
-model runs (sq325.codec, scripts/fp4_zero_predictor_codec_v1.py) and is not provided here.
+Same names, checks and results as the reference module: `allocate_state` (:50-62), `scan`
+(:203-262, with `collect_stats` for s16), `decode_state` / `encode_state_` (:265-331) and
+`validate_permutation` (:179-184).
+  s16     sq_s16_scan: fp32 arithmetic, the carry rounded to fp16 after every token, the
+          readout summed in the reference kernel's order.
+  sq3p25  sq_sq3p25_scan: per row 16 INT8 + 64 INT4 stored coordinates (the group's
+          permutation orders them) and 48 pruned ones that read out only the current token,
+          52 bytes (lo / hi u8[8], q4 u8[32], s8 / s4 fp16); the codec the training scan
+          (sq325.state_training, mamba2_recall/state_training_scan.py) runs.  The released
+          model runs the latent codec instead (sq325.codec).
 """
 from __future__ import annotations
 
@@ -26,10 +30,13 @@ N = 128
 def allocate_state(batch, heads, dim, dstate, mode, device):
     if mode not in MODES or dstate != N or min(batch, heads, dim) <= 0:
         raise ValueError('Require s16/sq3p25, dstate=128, and positive geometry')
-    if mode != 's16':
-        raise ValueError('sq3p25 (the fixed 16/64/48 codec) is superseded by the latent codec: use sq325.codec')
     shape = (batch, heads, dim, dstate)
-    return PackedState(mode, {'state': torch.zeros(shape, dtype=torch.float16, device=device)}, shape)
+    if mode == 's16':
+        return PackedState(mode, {'state': torch.zeros(shape, dtype=torch.float16, device=device)}, shape)
+    tensors = {key: torch.zeros((batch, heads, dim, size), dtype=torch.uint8, device=device)
+               for key, size in (('lo', 8), ('hi', 8), ('q4', 32))}
+    tensors.update({key: torch.zeros((batch, heads, dim), dtype=torch.float16, device=device) for key in ('s8', 's4')})
+    return PackedState(mode, tensors, shape)
 
 
 def validate_permutation(permutation, groups):
@@ -43,14 +50,17 @@ def validate_permutation(permutation, groups):
 def _validate_state(state, device):
     if not isinstance(state, PackedState) or state.mode not in MODES:
         raise ValueError('Invalid packed state')
-    if state.mode != 's16':
-        raise ValueError('Only the s16 control state is provided here')
     b, h, p, n = state.shape
-    t = state.tensors.get('state')
-    if n != N or set(state.tensors) != {'state'}:
+    spec = ({'state': (state.shape, torch.float16)} if state.mode == 's16' else {
+        'lo': ((b, h, p, 8), torch.uint8), 'hi': ((b, h, p, 8), torch.uint8),
+        'q4': ((b, h, p, 32), torch.uint8), 's8': ((b, h, p), torch.float16),
+        's4': ((b, h, p), torch.float16)})
+    if n != N or set(state.tensors) != set(spec):
         raise ValueError('State keys or geometry differ')
-    if tuple(t.shape) != (b, h, p, n) or t.dtype != torch.float16 or t.device != device or not t.is_contiguous():
-        raise ValueError('Invalid state buffer state')
+    for key, (shape, dtype) in spec.items():
+        t = state.tensors[key]
+        if tuple(t.shape) != tuple(shape) or t.dtype != dtype or t.device != device or not t.is_contiguous():
+            raise ValueError(f'Invalid state buffer {key}')
 
 
 @torch.no_grad()
@@ -80,6 +90,13 @@ def scan(x, dt, A, B, C_, D, dt_bias, state, permutation=None, collect_stats=Fal
         raise ValueError('A must be FP32; dt/B/C must be FP16')
     if any(t.dtype not in (torch.float16, torch.float32) for t in (D, dt_bias)):
         raise ValueError('D and dt_bias must be FP16 or FP32')
+    if collect_stats and state.mode != 's16':
+        raise ValueError('Calibration statistics require s16')
+    if state.mode == 'sq3p25':
+        if permutation is None or permutation.dtype != torch.uint8 or tuple(permutation.shape) != (g, N) or \
+                permutation.device != x.device:
+            raise ValueError('SQ requires CUDA uint8[groups,128] permutation')
+        return _sq3p25_scan(x, dt, A, B, C_, D, dt_bias, state, permutation.contiguous()), None
     if permutation is not None:
         raise ValueError('s16 does not accept a permutation')
     x, dt, A, B, C_, D, dt_bias = (v.contiguous() for v in (x, dt, A, B, C_, D, dt_bias))
@@ -103,20 +120,103 @@ def scan(x, dt, A, B, C_, D, dt_bias, state, permutation=None, collect_stats=Fal
     return out, stats
 
 
+def sq3p25_args(x, dt, A, B, C_, D, dt_bias, permutation, state=None, y=None):
+    """ctypes argument block of sq_sq3p25_scan / sq_ste_backward over contiguous inputs."""
+    b, length, h, p = x.shape
+    g = B.shape[2]
+    a = _lib.Sq3p25Args()
+    a.batch, a.length, a.heads, a.dim, a.groups = b, length, h, p, g
+    a.x, a.x_batch_stride, a.x_token_stride = x.data_ptr(), length * h * p, h * p
+    a.dt, a.dt_batch_stride, a.dt_token_stride = dt.data_ptr(), length * h, h
+    a.A = A.data_ptr()
+    a.B, a.b_batch_stride, a.b_token_stride = B.data_ptr(), length * g * N, g * N
+    a.C, a.c_batch_stride, a.c_token_stride = C_.data_ptr(), length * g * N, g * N
+    a.D, a.d_is_f32 = D.data_ptr(), int(D.dtype == torch.float32)
+    a.dt_bias, a.dt_bias_is_f32 = dt_bias.data_ptr(), int(dt_bias.dtype == torch.float32)
+    a.permutation = permutation.data_ptr()
+    if state is not None:
+        t = state.tensors
+        a.lo, a.hi, a.q4, a.s8, a.s4 = (t[k].data_ptr() for k in ('lo', 'hi', 'q4', 's8', 's4'))
+    if y is not None:
+        a.y, a.y_batch_stride, a.y_token_stride = y.data_ptr(), length * h * p, h * p
+    return a
+
+
+def _sq3p25_scan(x, dt, A, B, C_, D, dt_bias, state, permutation):
+    x, dt, A, B, C_, D, dt_bias = (v.contiguous() for v in (x, dt, A, B, C_, D, dt_bias))
+    if x.shape[3] > 128:
+        raise ValueError('sq3p25 supports head dims up to 128')
+    out = torch.empty_like(x)
+    a = sq3p25_args(x, dt, A, B, C_, D, dt_bias, permutation, state, out)
+    with torch.cuda.device(x.device):
+        _lib.call('sq_sq3p25_scan', C.byref(a), _lib.stream_ptr())
+    return out
+
+
+def _unpack_nibbles(value):
+    return torch.stack((value & 15, (value >> 4) & 15), -1).flatten(-2).to(torch.int32)
+
+
 @torch.no_grad()
 def decode_state(state, permutation=None):
-    """s16: the carry in original coordinates as fp32."""
-    if state.mode != 's16':
+    """Diagnostic full FP32 decode.  s16: the carry.  sq3p25: the permuted coordinates (16 INT8,
+    64 INT4, 48 zeros), or the original coordinates when a [G,128] permutation is given."""
+    if state.mode == 's16':
+        return state.tensors['state'].float()
+    if state.mode != 'sq3p25':
         raise ValueError('Unsupported mode')
-    return state.tensors['state'].float()
+    t = state.tensors
+    ub = (_unpack_nibbles(t['hi']) << 4) | _unpack_nibbles(t['lo'])
+    q8 = ub - (ub > 127).to(torch.int32) * 256
+    q4 = _unpack_nibbles(t['q4'])
+    q4 = q4 - (q4 > 7).to(torch.int32) * 16
+    values = torch.cat((q8.float() * t['s8'].float()[..., None], q4.float() * t['s4'].float()[..., None],
+                        torch.zeros((*state.shape[:-1], 48), device=q8.device)), -1)
+    if permutation is None:
+        return values
+    g = permutation.shape[0]
+    validate_permutation(permutation, g)
+    b, h, p, _ = state.shape
+    if h % g:
+        raise ValueError('Invalid grouping')
+    indices = permutation.long().repeat_interleave(h // g, 0)[None, :, None, :].expand(b, h, p, N)
+    return torch.zeros_like(values).scatter_(-1, indices, values)
 
 
 @torch.no_grad()
 def encode_state_(state, dense_permuted):
-    """s16: copy a finite dense carry of the state's shape into it (fp16)."""
+    """Diagnostic initializer.  s16: copy a finite dense carry (fp16).  sq3p25: coordinates
+    already in permuted order; INT8 / INT4 codes with fp32 denominators max(|v|max / limit,
+    1e-8), round half away, clip; scales stored as fp16 (not the runtime rule)."""
     if tuple(dense_permuted.shape) != state.shape or not bool(torch.isfinite(dense_permuted).all()):
         raise ValueError('Diagnostic input must be finite and match state shape')
-    if state.mode != 's16':
+    if state.mode == 's16':
+        state.tensors['state'].copy_(dense_permuted)
+        return state
+    if state.mode != 'sq3p25':
         raise ValueError('Unsupported mode')
-    state.tensors['state'].copy_(dense_permuted)
+
+    v = dense_permuted.float()
+    parts = []
+    for block, limit in ((v[..., :16], 127), (v[..., 16:80], 7)):
+        den = torch.clamp_min(block.abs().amax(-1) / limit, 1e-8)
+        parts.append((block, den, limit))
+    if not all(bool(torch.isfinite(den.half()).all()) for _, den, _ in parts):
+        raise ValueError('Scale exceeds FP16 range')
+    codes = []
+    for block, den, limit in parts:
+        z = block / den[..., None]
+        codes.append(torch.clamp(torch.sign(z) * torch.floor(z.abs() + 0.5), -limit, limit).to(torch.int32))
+
+    def nibbles(q):
+        q = (q & 15).to(torch.uint8)
+        return q[..., 0::2] | (q[..., 1::2] << 4)
+
+    (q8, q4), (s8, s4) = codes, (parts[0][1], parts[1][1])
+    t = state.tensors
+    t['lo'].copy_(nibbles(q8))
+    t['hi'].copy_(nibbles(q8 >> 4))
+    t['q4'].copy_(nibbles(q4))
+    t['s8'].copy_(s8)
+    t['s4'].copy_(s4)
     return state

@@ -21,6 +21,12 @@ What is recorded
   s16.npz              the FP16-state control scan `_s16_scan`
                        (mamba2_recall/state_codec.py:65-102) under the interpreter,
                        without and with the calibration statistics (:256-262).
+  ste.npz              the legacy sq3p25 scan `_sq_scan` (mamba2_recall/state_codec.py:105-176)
+                       from a random packed state and from the zero state, and the
+                       straight-through training backward of
+                       mamba2_recall/state_training_scan.py (_carry_checkpoints,
+                       _chunk_history, _chunk_backward, :24-179) over 3 chunks, all
+                       under the interpreter.
   checkpoint_plan.json the packed-checkpoint container rules of
                        mamba2_recall/fp4_checkpoint.py run on this model's tensor
                        inventory: `make_plan` (:67-93) at two shard limits for the
@@ -249,6 +255,61 @@ def checkpoint_case(reference):
     return out
 
 
+def ste_case(reference, seed=500, batch=2, length=10, heads=4, dim=16, groups=2, chunk=4):
+    """sq3p25 forward (random packed start and fresh zero start) and the STE backward, run by
+    the interpreter exactly as scan / _StateQuantSTE.backward launch them."""
+    sys.path.insert(0, str(reference))
+    from mamba2_recall import state_codec as sc
+    from mamba2_recall import state_training_scan as sts
+
+    class _Libdevice:
+        round = _round_half_away
+
+    sc.libdevice = _Libdevice
+    sts.libdevice = _Libdevice
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(batch, length, heads, dim, generator=gen).half()
+    dt = (torch.randn(batch, length, heads, generator=gen) * 0.7).half()
+    A = -(torch.rand(heads, generator=gen) * 3 + 0.05).float()
+    Bm = torch.randn(batch, length, groups, 128, generator=gen).half()
+    Cm = torch.randn(batch, length, groups, 128, generator=gen).half()
+    D = torch.randn(heads, generator=gen).half()
+    dt_bias = (torch.rand(heads, generator=gen) * 3 - 4).half()
+    perm = torch.stack([torch.randperm(128, generator=gen) for _ in range(groups)]).to(torch.uint8)
+    dy = torch.randn(batch, length, heads, dim, generator=gen).half()
+    rec = dict(x=x, dt=dt, A=A, B=Bm, C=Cm, D=D, dt_bias=dt_bias, permutation=perm, dy=dy)
+    grid = (batch, heads, triton.cdiv(dim, 16))
+    for tag, random_start in (('rand_', True), ('zero_', False)):
+        st = {k: torch.zeros((batch, heads, dim, w), dtype=torch.uint8) for k, w in (('lo', 8), ('hi', 8), ('q4', 32))}
+        st.update({k: torch.zeros((batch, heads, dim), dtype=torch.float16) for k in ('s8', 's4')})
+        if random_start:
+            for k in ('lo', 'hi', 'q4'):
+                st[k] = torch.randint(0, 256, st[k].shape, generator=gen, dtype=torch.uint8)
+            st['s8'] = (torch.rand(batch, heads, dim, generator=gen) * 1e-2 + 1e-5).half()
+            st['s4'] = (torch.rand(batch, heads, dim, generator=gen) * 1e-1 + 1e-5).half()
+        rec.update({tag + 'in_' + k: v.clone() for k, v in st.items()})
+        out = torch.empty_like(x)
+        sc._sq_scan[grid](x, dt, A, Bm, Cm, D, dt_bias, perm, st['lo'], st['hi'], st['q4'], st['s8'], st['s4'],
+                          out, length, heads, dim, groups, 16)
+        rec[tag + 'y'] = out
+        rec.update({tag + 'out_' + k: v for k, v in st.items()})
+    nc = triton.cdiv(length, chunk)
+    cp = torch.empty((batch, nc, heads, dim, 80), dtype=torch.float32)
+    hist = torch.empty((batch, chunk, heads, dim, 80), dtype=torch.float32)
+    adj = torch.zeros((batch, heads, dim, 80), dtype=torch.float32)
+    dx = torch.empty(x.shape, dtype=torch.float32)
+    ddt = torch.zeros(dt.shape, dtype=torch.float32)
+    db = torch.zeros(Bm.shape, dtype=torch.float32)
+    dc = torch.zeros(Cm.shape, dtype=torch.float32)
+    sts._carry_checkpoints[grid](x, dt, A, Bm, dt_bias, perm, cp, length, heads, dim, groups, chunk, nc, 16)
+    for c in reversed(range(nc)):
+        sts._chunk_history[grid](x, dt, A, Bm, dt_bias, perm, cp, hist, length, heads, dim, groups, chunk, nc, c, 16)
+        sts._chunk_backward[grid](x, dt, A, Bm, Cm, D, dt_bias, perm, hist, adj, dy, dx, ddt, db, dc, length, heads,
+                                  dim, groups, chunk, c, 16)
+    rec.update(checkpoints=cp, dx=dx, ddt=ddt, db=db, dc=dc, chunk=torch.tensor(chunk))
+    return {k: v.numpy() for k, v in rec.items()}
+
+
 def adapter_case(reference, seed=11):
     sys.path.insert(0, str(reference))
     from mamba2_recall import resurface_native as native
@@ -273,8 +334,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', type=Path, required=True,
                     help='root of a checkout of the reference repository (read only)')
-    ap.add_argument('--cases', default='codec,s16,mk,checkpoint',
-                    help='comma list: codec (+ fp4, adapter), s16, mk, checkpoint')
+    ap.add_argument('--cases', default='codec,s16,mk,checkpoint,ste',
+                    help='comma list: codec (+ fp4, adapter), s16, mk, checkpoint, ste')
     args = ap.parse_args()
     ap_cases = args.cases.split(',')
     if 's16' in ap_cases:
@@ -287,6 +348,9 @@ def main():
         import json
         (HERE / 'mk_cases.json').write_text(json.dumps(mk_case(args.reference), indent=1, sort_keys=True) + '\n')
         print('wrote mk')
+    if 'ste' in ap_cases:
+        np.savez_compressed(HERE / 'ste.npz', **ste_case(args.reference))
+        print('wrote ste')
     if 'checkpoint' in ap_cases:
         import json
         (HERE / 'checkpoint_plan.json').write_text(

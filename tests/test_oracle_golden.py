@@ -202,3 +202,29 @@ def test_s16_oracle_matches_reference_kernel(golden, tag):
     assert np.array_equal(st.view(np.uint16), d[tag + 'state_out'].view(np.uint16))
     if tag == 'stats_':
         assert np.array_equal(stats.view(np.uint32), d['stats_stats'].view(np.uint32))
+
+
+@pytest.mark.parametrize('tag', ['rand_', 'zero_'])
+def test_sq3p25_oracle_matches_reference_kernel(golden, tag):
+    """oracle.ste.sq3p25_scan against the reference's packed `_sq_scan` run by the interpreter
+    (mamba2_recall/state_codec.py:105-176): readout and every state byte, from a random and
+    from a zero state."""
+    from oracle import ste
+    d = golden('ste.npz')
+    st = {k: d[f'{tag}in_{k}'].copy() for k in ('lo', 'hi', 'q4', 's8', 's4')}
+    y = ste.sq3p25_scan(*(d[k] for k in ('x', 'dt', 'A', 'B', 'C', 'D', 'dt_bias')), st, d['permutation'])
+    assert np.array_equal(y.view(np.uint16), d[tag + 'y'].view(np.uint16))
+    for k, v in st.items():
+        assert np.array_equal(v.view(np.uint8), d[f'{tag}out_{k}'].view(np.uint8)), k
+
+
+def test_ste_backward_oracle_matches_reference_kernels(golden):
+    """oracle.ste.ste_backward against `_carry_checkpoints` / `_chunk_history` /
+    `_chunk_backward` run by the interpreter (mamba2_recall/state_training_scan.py:24-211):
+    checkpoints, dx, ddt, dB and dC bit for bit."""
+    from oracle import ste
+    d = golden('ste.npz')
+    dx, ddt, db, dc, cp = ste.ste_backward(*(d[k] for k in ('x', 'dt', 'A', 'B', 'C', 'D', 'dt_bias',
+                                                            'permutation', 'dy')), int(d['chunk']))
+    for name, got in (('checkpoints', cp), ('dx', dx), ('ddt', ddt), ('db', db), ('dc', dc)):
+        assert np.array_equal(got.view(np.uint32), d[name].view(np.uint32)), name
