@@ -126,9 +126,11 @@ int sq_s16_scan(const sq_s16_args* args, void* stream);
  * sq_ste_backward is the straight-through backward of scan_training
  * (mamba2_recall/state_training_scan.py :24-221) for a scan from a fresh zero state:
  * inputs contiguous as in the forward call, dy fp16 [B,L,H,P]; writes dx fp32 [B,L,H,P],
- * d(dt) fp32 [B,L,H], dB / dC fp32 [B,L,G,128] (zeroed by the call).  chunk = tokens between
- * carry checkpoints (1..256); the workspace holds the checkpoints, one chunk of carries and
- * the adjoint carry: sq_ste_workspace(batch, length, heads, dim, chunk) bytes. */
+ * d(dt) fp32 [B,L,H], dB / dC fp32 [B,L,G,128] (every element written; sums in the
+ * reference's order, no atomics, so the results are deterministic).  chunk = tokens between
+ * carry checkpoints (1..256); the workspace holds the checkpoints, one chunk of carries, the
+ * adjoint carry and one chunk of per-(head, row tile) dB / dC partials:
+ * sq_ste_workspace(batch, length, heads, dim, chunk) bytes. */
 typedef struct sq_sq3p25_args {
   int32_t batch, length, heads, dim, groups;
   const uint16_t* x;  int64_t x_batch_stride, x_token_stride;

@@ -19,10 +19,16 @@
 //                          [B][H][P][80] crosses chunks), the current-token readout through
 //                          all 128; dx is stored, d(dt) (times the softplus slope) and dB /
 //                          dC are summed over the CTA's rows and added atomically.
+//   ste_bc_reduce_kernel   adds the per-(head, row tile) dB / dC partials of the chunk in
+//                          (head, tile) order and scatters them to the original coordinates.
 // Mapping: one CTA per (head, batch), one thread per row of the head (dim <= 128); the
 // group's B / C of a token are staged in shared memory in tier order.  Arithmetic is
-// unfused (__fmul_rn / __fadd_rn) like the reference's; sums run in thread order, so results
-// match the reference within float rounding (the CPU oracle in oracle/ste.py is bit-exact).
+// unfused (__fmul_rn / __fadd_rn) like the reference's, and every reduction runs in the order
+// of the reference kernels' golden runs (Triton interpreter, i.e. numpy): sums over a row's
+// lanes and over a tile's 16 rows for d(dt) in numpy's eight-accumulator pairwise order,
+// sums over rows for dB / dC sequentially, tiles and heads in program order.  Given the same
+// softplus / exp values the results are bit-identical to the golden runs, and no atomics are
+// used, so gradients are deterministic run to run.
 #include "common.cuh"
 #include "ste.cuh"
 
@@ -96,6 +102,17 @@ __device__ __forceinline__ void requant(float (&S)[kLive], float& sc8, float& sc
   }
 }
 
+// numpy's float32 sum of n lanes (n % 8 == 0, 8 <= n <= 128): eight running sums over the
+// lanes j, j + 8, j + 16, ..., combined as ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)).
+// `q` is the lane's position within the sum (a compile-time constant in unrolled loops).
+__device__ __forceinline__ void pw_add(float (&r)[8], int q, float v) {
+  if (q < 8) r[q] = v;
+  else r[q & 7] = fadd(r[q & 7], v);
+}
+__device__ __forceinline__ float pw_total(const float (&r)[8]) {
+  return fadd(fadd(fadd(r[0], r[1]), fadd(r[2], r[3])), fadd(fadd(r[4], r[5]), fadd(r[6], r[7])));
+}
+
 __device__ void load_perm(const SteParams& P, int g, int* perm) {
   for (int j = threadIdx.x; j < 128; j += blockDim.x) perm[j] = P.perm[g * 128 + j];
 }
@@ -141,12 +158,20 @@ __global__ void __launch_bounds__(128) sq3p25_scan_kernel(const SteParams P) {
     stage_token(P, b, t, h, g, perm, s, true);
     const float x = live ? h2f(P.x[(long long)b * P.x_sb + (long long)t * P.x_st + (long long)h * P.dim + r]) : 0.f;
     step_live(S, s, x);
-    float o8 = 0.f, o4 = 0.f, od = 0.f;
+    float acc[8], o8, o4, od;
 #pragma unroll
-    for (int j = 0; j < kLive8; ++j) o8 = fadd(o8, fmul(S[j], s.c[j]));
+    for (int j = 0; j < kLive8; ++j) pw_add(acc, j, fmul(S[j], s.c[j]));
+    o8 = pw_total(acc);
 #pragma unroll
-    for (int j = kLive8; j < kLive; ++j) o4 = fadd(o4, fmul(S[j], s.c[j]));
-    for (int j = kLive; j < 128; ++j) od = fadd(od, fmul(fmul(fmul(s.b[j], s.dt), x), s.c[j]));
+    for (int j = kLive8; j < kLive; ++j) pw_add(acc, j - kLive8, fmul(S[j], s.c[j]));
+    o4 = pw_total(acc);
+    // pruned tier: the reference's 64-wide block, 48 coordinates and 16 masked zero lanes
+#pragma unroll
+    for (int q = 0; q < 64; ++q) {
+      const float bj = q < 48 ? s.b[kLive + q] : 0.0f, cj = q < 48 ? s.c[kLive + q] : 0.0f;
+      pw_add(acc, q, fmul(fmul(fmul(bj, s.dt), x), cj));
+    }
+    od = pw_total(acc);
     const float out = fadd(fadd(o8, o4), fadd(od, fmul(x, dv)));
     if (live) P.y[(long long)b * P.y_sb + (long long)t * P.y_st + (long long)h * P.dim + r] = f2h(out);
     if (t + 1 < P.length) {
@@ -236,20 +261,26 @@ __global__ void __launch_bounds__(128) ste_history_kernel(const SteParams P, int
   }
 }
 
-// Sum of v over the CTA's rows, added to *dst by one thread: warp shuffles, then one shared
-// atomic per warp into red[slot].
-__device__ __forceinline__ void warp_sum_to(float v, float* red, int slot) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  if ((threadIdx.x & 31) == 0) atomicAdd(&red[slot], v);
+// Sum over a 16-row tile (lanes of one half-warp) in numpy's pairwise order: rows j and
+// j + 8, then neighbours, pairs and halves; every lane of the tile receives the sum.
+__device__ __forceinline__ float tile_pairwise16(float v) {
+  v = fadd(v, __shfl_xor_sync(0xffffffffu, v, 8));
+  v = fadd(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  v = fadd(v, __shfl_xor_sync(0xffffffffu, v, 2));
+  v = fadd(v, __shfl_xor_sync(0xffffffffu, v, 4));
+  return v;
 }
+
+constexpr int kStageLanes = 32;   // lanes of dB / dC terms staged per block
 
 __global__ void __launch_bounds__(128) ste_backward_kernel(const SteParams P, int c) {
   __shared__ TokenShared s;
   __shared__ int perm[128];
-  __shared__ float red[2 * 128 + 1];                  // dB [128] | dC [128] | d(delta)
+  __shared__ float stage[2][kStageLanes][129];       // [dB | dC][lane][row], padded
+  __shared__ float tile_dl[8];
   const int h = blockIdx.x, b = blockIdx.y, r = threadIdx.x;
   const int g = h / (P.heads / P.groups);
+  const int ntile = (P.dim + 15) / 16;
   const bool live = r < P.dim;
   load_perm(P, g, perm);
   const float av = P.A[h], dv = ldf(P.D, P.d_is_f32, h);
@@ -262,56 +293,100 @@ __global__ void __launch_bounds__(128) ste_backward_kernel(const SteParams P, in
     const int t = c * P.chunk + k;
     if (t >= P.length) continue;
     stage_token(P, b, t, h, g, perm, s, true);
-    for (int i = threadIdx.x; i < 2 * 128 + 1; i += blockDim.x) red[i] = 0.f;
-    __syncthreads();
     const long long xo = (long long)b * P.x_sb + (long long)t * P.x_st + (long long)h * P.dim + r;
     const float x = live ? h2f(P.x[xo]) : 0.f;
     const float gy = live ? h2f(P.dy[xo]) : 0.f;
     const float factor = fmul(s.dt, x);                 // 0 on rows past dim (x = 0 there)
     const float ad = fmul(av, s.decay);
     const float* prev = carry_at(P.hist, (((long long)b * P.chunk + k) * P.heads + h) * P.dim + (live ? r : 0));
-    float dx8 = 0.f, dx4 = 0.f, dxd = 0.f, dl8 = 0.f, dl4 = 0.f, dld = 0.f;
-#pragma unroll 4
-    for (int j = 0; j < kLive; ++j) {
-      const float pj = live ? prev[j] : 0.f;
-      const float bj = s.b[j], cj = s.c[j];
-      const float bdt = fmul(bj, s.dt);
-      const float v = fadd(fmul(gy, cj), adj[j]);                       // STE: identity on live lanes
-      const float hj = fadd(fmul(pj, s.decay), fmul(bdt, x));
-      const float e = fadd(fmul(pj, ad), fmul(bj, x));
-      if (j < kLive8) { dx8 = fadd(dx8, fmul(v, bdt)); dl8 = fadd(dl8, fmul(v, e)); }
-      else            { dx4 = fadd(dx4, fmul(v, bdt)); dl4 = fadd(dl4, fmul(v, e)); }
-      warp_sum_to(fmul(v, factor), red, j);
-      warp_sum_to(fmul(hj, gy), red, 128 + j);
-      adj[j] = fmul(v, s.decay);
+    // dB / dC partials of this (token, head): [tile][dB | dC][128 tier lanes]
+    float* part = P.part + (((long long)b * P.chunk + k) * P.heads + h) * ntile * 256;
+    float ax[8], al[8];
+    float dx8 = 0.f, dl8 = 0.f, dx4 = 0.f, dl4 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 128; ++j) {
+      float pb, pc;                                     // this row's dB and dC terms of lane j
+      if (j < kLive) {                                  // STE: identity through the live lanes
+        const float pj = live ? prev[j] : 0.f;
+        const float bj = s.b[j], cj = s.c[j];
+        const float bdt = fmul(bj, s.dt);
+        const float v = fadd(fmul(gy, cj), adj[j]);
+        const float hj = fadd(fmul(pj, s.decay), fmul(bdt, x));
+        const float e = fadd(fmul(pj, ad), fmul(bj, x));
+        const int q = j < kLive8 ? j : j - kLive8;
+        pw_add(ax, q, fmul(v, bdt));
+        pw_add(al, q, fmul(v, e));
+        pb = fmul(v, factor);
+        pc = fmul(hj, gy);
+        adj[j] = fmul(v, s.decay);
+        if (j == kLive8 - 1) { dx8 = pw_total(ax); dl8 = pw_total(al); }
+        if (j == kLive - 1) { dx4 = pw_total(ax); dl4 = pw_total(al); }
+      } else {                                          // pruned lanes: readout only
+        const float bj = s.b[j], cj = s.c[j];
+        const float bdt = fmul(bj, s.dt);
+        const float v = fmul(gy, cj);
+        pw_add(ax, j - kLive, fmul(v, bdt));
+        pw_add(al, j - kLive, fmul(v, fmul(bj, x)));
+        pb = fmul(v, factor);
+        pc = fmul(fmul(bdt, x), gy);
+      }
+      stage[0][j % kStageLanes][r] = pb;
+      stage[1][j % kStageLanes][r] = pc;
+      if (j % kStageLanes == kStageLanes - 1) {
+        __syncthreads();
+        // each tile's 16 rows summed in row order (numpy's order for a sum over rows)
+        for (int i = threadIdx.x; i < 2 * kStageLanes * ntile; i += blockDim.x) {
+          const int which = i / (kStageLanes * ntile), rem = i % (kStageLanes * ntile);
+          const int tile = rem / kStageLanes, lane = rem % kStageLanes;
+          const float* col = &stage[which][lane][tile * 16];
+          float acc = col[0];
+#pragma unroll
+          for (int q = 1; q < 16; ++q) acc = fadd(acc, col[q]);
+          part[(tile * 2 + which) * 128 + (j + 1 - kStageLanes) + lane] = acc;
+        }
+        __syncthreads();
+      }
     }
-    for (int j = kLive; j < 128; ++j) {                                   // pruned lanes: readout only
-      const float bj = s.b[j], cj = s.c[j];
-      const float bdt = fmul(bj, s.dt);
-      const float v = fmul(gy, cj);
-      dxd = fadd(dxd, fmul(v, bdt));
-      dld = fadd(dld, fmul(v, fmul(bj, x)));
-      warp_sum_to(fmul(v, factor), red, j);
-      warp_sum_to(fmul(fmul(bdt, x), gy), red, 128 + j);
+    // the pruned block is 64 wide in the reference: 16 masked zero lanes close the sums
+#pragma unroll
+    for (int q = 48; q < 64; ++q) {
+      const float v = fmul(gy, 0.0f);
+      pw_add(ax, q, fmul(v, fmul(0.0f, s.dt)));
+      pw_add(al, q, fmul(v, fmul(0.0f, x)));
     }
+    const float dxd = pw_total(ax), dld = pw_total(al);
     if (live) P.dx[xo] = fadd(fadd(dx8, dx4), fadd(dxd, fmul(gy, dv)));
-    warp_sum_to(live ? fadd(fadd(dl8, dl4), dld) : 0.f, red, 256);
+    const float dl = tile_pairwise16(live ? fadd(fadd(dl8, dl4), dld) : 0.f);
+    if ((r & 15) == 0 && (r >> 4) < ntile) tile_dl[r >> 4] = dl;
     __syncthreads();
-    // d(dt raw) = (sum over rows) * softplus'(raw); dB / dC per coordinate of the group
+    // d(dt raw) = sum over tiles, in tile order, of (tile sum) * softplus'(raw)
     if (threadIdx.x == 0) {
       const float sig = s.raw <= 20.0f ? __fdiv_rn(1.0f, fadd(1.0f, expf(-s.raw))) : 1.0f;
-      atomicAdd(P.ddt + ((long long)b * P.length + t) * P.heads + h, fmul(red[256], sig));
-    }
-    for (int j = threadIdx.x; j < 128; j += blockDim.x) {
-      const long long o = (((long long)b * P.length + t) * P.groups + g) * 128 + perm[j];
-      atomicAdd(P.db + o, red[j]);
-      atomicAdd(P.dc + o, red[128 + j]);
+      float acc = 0.0f;
+      for (int i = 0; i < ntile; ++i) acc = fadd(acc, fmul(tile_dl[i], sig));
+      P.ddt[((long long)b * P.length + t) * P.heads + h] = acc;
     }
   }
   if (live) {
 #pragma unroll
     for (int j = 0; j < kLive; ++j) adj_row[j] = adj[j];
   }
+}
+
+// dB / dC of one chunk: for every (token, batch, group) and coordinate, the partials of the
+// group's heads and row tiles added in (head, tile) order, scattered through the permutation.
+__global__ void __launch_bounds__(256) ste_bc_reduce_kernel(const SteParams P, int c) {
+  const int k = blockIdx.x, b = blockIdx.y, g = blockIdx.z;
+  const int t = c * P.chunk + k;
+  if (t >= P.length) return;
+  const int which = threadIdx.x >> 7, lane = threadIdx.x & 127;
+  const int per = P.heads / P.groups, ntile = (P.dim + 15) / 16;
+  const float* part = P.part + ((long long)b * P.chunk + k) * P.heads * ntile * 256 + which * 128 + lane;
+  float acc = 0.0f;
+  for (int hh = g * per; hh < (g + 1) * per; ++hh)
+    for (int tile = 0; tile < ntile; ++tile) acc = fadd(acc, part[((long long)hh * ntile + tile) * 256]);
+  const long long o = (((long long)b * P.length + t) * P.groups + g) * 128 + P.perm[g * 128 + lane];
+  (which ? P.dc : P.db)[o] = acc;
 }
 
 int threads_for(int dim) { return (dim + 31) / 32 * 32; }
@@ -328,8 +403,9 @@ int launch_sq3p25_scan(const SteParams& P, cudaStream_t st) {
 
 long long ste_workspace_bytes(int batch, int length, int heads, int dim, int chunk) {
   if (batch <= 0 || length <= 0 || heads <= 0 || dim <= 0 || chunk <= 0) return -1;
-  const long long nc = (length + chunk - 1) / chunk;
-  return (long long)batch * (nc + chunk + 1) * heads * dim * kLive * 4;
+  const long long nc = (length + chunk - 1) / chunk, ntile = (dim + 15) / 16;
+  return (long long)batch * (nc + chunk + 1) * heads * dim * kLive * 4 +   // carries
+         (long long)batch * chunk * heads * ntile * 256 * 4;                // dB / dC partials
 }
 
 int launch_ste_backward(SteParams P, void* workspace, cudaStream_t st) {
@@ -342,17 +418,16 @@ int launch_ste_backward(SteParams P, void* workspace, cudaStream_t st) {
   P.cp = w;
   P.hist = P.cp + rows * P.nchunk * kLive;
   P.adj = P.hist + rows * P.chunk * kLive;
-  if (cudaMemsetAsync(P.adj, 0, rows * kLive * 4, st) != cudaSuccess ||
-      cudaMemsetAsync(P.ddt, 0, (size_t)P.batch * P.length * P.heads * 4, st) != cudaSuccess ||
-      cudaMemsetAsync(P.db, 0, (size_t)P.batch * P.length * P.groups * 128 * 4, st) != cudaSuccess ||
-      cudaMemsetAsync(P.dc, 0, (size_t)P.batch * P.length * P.groups * 128 * 4, st) != cudaSuccess)
-    return kECuda;
+  P.part = P.adj + rows * kLive;
+  // dx, d(dt), dB and dC are written in full by the kernels; only the adjoint carry starts at 0
+  if (cudaMemsetAsync(P.adj, 0, rows * kLive * 4, st) != cudaSuccess) return kECuda;
   const dim3 grid(P.heads, P.batch);
   const int th = threads_for(P.dim);
   ste_checkpoint_kernel<<<grid, th, 0, st>>>(P);
   for (int c = P.nchunk - 1; c >= 0; --c) {
     ste_history_kernel<<<grid, th, 0, st>>>(P, c);
     ste_backward_kernel<<<grid, th, 0, st>>>(P, c);
+    ste_bc_reduce_kernel<<<dim3(P.chunk, P.batch, P.groups), 256, 0, st>>>(P, c);
   }
   return launch_status();
 }

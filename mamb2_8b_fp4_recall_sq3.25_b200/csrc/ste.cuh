@@ -23,7 +23,7 @@ struct SteParams {
   const uint16_t* dy;
   float* dx; float* ddt; float* db; float* dc;
   int chunk, nchunk;
-  float* cp; float* hist; float* adj;
+  float* cp; float* hist; float* adj; float* part;
 };
 
 int launch_sq3p25_scan(const SteParams& P, cudaStream_t st);

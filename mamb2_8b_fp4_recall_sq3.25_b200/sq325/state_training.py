@@ -6,9 +6,9 @@ codec's readout) and, in backward, the straight-through derivative of the refere
 coordinates, scales and rounding detached, current-token readout through all 128.  The
 backward (sq_ste_backward) recomputes the dequantized carries, checkpoints the stored
 coordinates every `chunk_size` tokens, rebuilds one chunk of history at a time and walks
-the adjoint carry backwards; dx / ddt / dB / dC are accumulated in fp32 (atomics across
-heads and rows) and returned in the inputs' dtype.  A, D and dt_bias are frozen: they
-receive no gradient.
+the adjoint carry backwards; dx / ddt / dB / dC are summed in fp32 in the reference's order
+(no atomics: deterministic) and returned in the inputs' dtype.  A, D and dt_bias are
+frozen: they receive no gradient.
 """
 from __future__ import annotations
 

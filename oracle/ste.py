@@ -57,7 +57,22 @@ def _requant(s8, s4):
     return q8, q4, (q8 * sc8[:, None]).astype(np.float32), (q4 * sc4[:, None]).astype(np.float32), sc8, sc4
 
 
-def sq3p25_scan(x, dt, A, B, C, D, dt_bias, state, perm):
+def _transcendentals(device_math, b, t, h, raw, av):
+    """softplus(raw), exp(A * softplus) and sigmoid(raw) of one (batch, token, head): numpy's,
+    or the device's own values when `device_math` (float32 [B,L,H] arrays 'softplus', 'decay',
+    'sigmoid') is given.  exp / log are the only operations whose last bit differs between
+    libraries; substituting the device's results lets a device run be checked bit for bit."""
+    if device_math is not None:
+        return (F32(device_math['softplus'][b, t, h]), F32(device_math['decay'][b, t, h]),
+                F32(device_math['sigmoid'][b, t, h]) if 'sigmoid' in device_math else None)
+    d = _softplus(raw)
+    decay = np.exp((av * d).astype(np.float32)).astype(np.float32)
+    sig = np.where(raw <= F32(20.0), (F32(1.0) / (F32(1.0) + np.exp(-raw))).astype(np.float32),
+                   F32(1.0)).astype(np.float32)
+    return d, decay, sig
+
+
+def sq3p25_scan(x, dt, A, B, C, D, dt_bias, state, perm, device_math=None):
     """Mutates `state` (dict of numpy lo/hi/q4 u8, s8/s4 f16); returns y fp16 [B,L,H,P]."""
     Bn, L, H, P = x.shape
     G = B.shape[2]
@@ -86,8 +101,8 @@ def sq3p25_scan(x, dt, A, B, C, D, dt_bias, state, perm):
                 for t in range(L):
                     xv = np.zeros(TILE, np.float32)
                     xv[:nr] = x[b, t, h, rows].astype(np.float32)
-                    d = _softplus((np.float32(dt[b, t, h]) + bias).astype(np.float32))
-                    decay = np.exp((av * d).astype(np.float32)).astype(np.float32)
+                    d, decay, _ = _transcendentals(device_math, b, t, h,
+                                                   (np.float32(dt[b, t, h]) + bias).astype(np.float32), av)
                     bv, cv = B[b, t, g].astype(np.float32), C[b, t, g].astype(np.float32)
                     bv8, cv8, bv4, cv4 = bv[pos8], cv[pos8], bv[pos4], cv[pos4]
                     bvd = np.where(dmask, bv[posd], F32(0)).astype(np.float32)
@@ -120,7 +135,7 @@ def _tile_step(s8, s4, xv, d, decay, bv8, bv4):
     return s8, s4
 
 
-def ste_backward(x, dt, A, B, C, D, dt_bias, perm, dy, chunk):
+def ste_backward(x, dt, A, B, C, D, dt_bias, perm, dy, chunk, device_math=None):
     """Returns (dx, ddt, dB, dC, checkpoints) in float32, the reference's backward with a fresh
     zero state: carries replayed exactly, identity derivative through the 80 live lanes, zero
     through the 48 pruned ones, current-token readout through all 128."""
@@ -142,9 +157,8 @@ def ste_backward(x, dt, A, B, C, D, dt_bias, perm, dy, chunk):
         xv[:nr] = x[b, t, h, rows_idx].astype(np.float32)
         bias = F32(np.float32(dt_bias[h]))
         raw = (np.float32(dt[b, t, h]) + bias).astype(np.float32)
-        d = _softplus(raw)
-        decay = np.exp((F32(A[h]) * d).astype(np.float32)).astype(np.float32)
-        return pos8, pos4, posd, xv, raw, d, decay
+        d, decay, sig = _transcendentals(device_math, b, t, h, raw, F32(A[h]))
+        return pos8, pos4, posd, xv, sig, d, decay
 
     # carry checkpoints: the carry entering each chunk
     for b in range(Bn):
@@ -202,11 +216,9 @@ def ste_backward(x, dt, A, B, C, D, dt_bias, perm, dy, chunk):
                         t = c * K + j
                         if t >= L:
                             continue
-                        pos8, pos4, posd, xv, raw, d, decay = token(b, t, h, g, rows_idx, nr)
+                        pos8, pos4, posd, xv, sig, d, decay = token(b, t, h, g, rows_idx, nr)
                         gy = np.zeros(TILE, np.float32)
                         gy[:nr] = dy[b, t, h, rows_idx].astype(np.float32)
-                        sig = np.where(raw <= F32(20.0), (F32(1.0) / (F32(1.0) + np.exp(-raw))).astype(np.float32),
-                                       F32(1.0)).astype(np.float32)
                         prev8 = hist[b, j, h, r0:r0 + TILE, :16]
                         prev4 = hist[b, j, h, r0:r0 + TILE, 16:]
                         bv, cv = B[b, t, g].astype(np.float32), C[b, t, g].astype(np.float32)

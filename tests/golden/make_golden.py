@@ -350,6 +350,10 @@ def main():
         print('wrote mk')
     if 'ste' in ap_cases:
         np.savez_compressed(HERE / 'ste.npz', **ste_case(args.reference))
+        # three 16-row tiles (the last one half masked), a partial last chunk, batch 1
+        np.savez_compressed(HERE / 'ste_ragged.npz',
+                            **ste_case(args.reference, seed=501, batch=1, length=9, heads=4, dim=40, groups=2,
+                                       chunk=4))
         print('wrote ste')
     if 'checkpoint' in ap_cases:
         import json

@@ -1,15 +1,20 @@
 """GPU parity of the packed 'sq3p25' scan (sq_sq3p25_scan) and its straight-through training
 backward (sq_ste_backward, scan_training) against the reference kernels' golden runs
-(tests/golden/ste.npz: mamba2_recall/state_codec.py:105-176 and
+(tests/golden/ste.npz, ste_ragged.npz: mamba2_recall/state_codec.py:105-176 and
 mamba2_recall/state_training_scan.py:24-211 under the Triton interpreter) and the oracle.
 
-Every product and sum is rounded once in the reference's order and the requantisation
-divides exactly, so the forward differs from the golden runs only where CUDA's expf / logf
-(softplus, decay) differ from numpy's by an ulp.  Bars: >= 99% of readouts and state bytes
-identical, readouts within 2e-2.  The backward accumulates dB / dC over heads and ddt over
-rows with atomics, whose order differs from the reference's tile order; bars: relative L2
-error <= 1e-4 and every element within 1e-3 of the largest magnitude (float32 sums), and
-checkpoints (no atomics) >= 99% bit-identical."""
+The kernels round every product and sum once, in the golden runs' order (numpy's pairwise
+lane sums, sequential row sums, program-ordered tile and head sums; no atomics), and divide
+exactly in the requantisation.  The one remaining difference is CUDA's expf / logf against
+numpy's (softplus, decay, sigmoid): an ulp there can move a near-tie requant rounding by one
+code, which then propagates.  Bars:
+  * against the oracle given the device's own softplus / decay / sigmoid (torch's CUDA exp /
+    log, the same CUDA math functions): readouts, state bytes, checkpoints and all four
+    gradients bit for bit (gradients compared as floats, so -0 equals +0);
+  * against the golden runs directly (numpy's exp / log): >= 98% of readouts and >= 99% of
+    state bytes and checkpoint words identical;
+  * gradients identical for every chunk size (1 .. 256).
+The oracle reproduces the golden runs bit for bit on the CPU (test_oracle_golden.py)."""
 import ctypes as C
 
 import numpy as np
@@ -28,6 +33,26 @@ def _cuda(d, k):
     return torch.from_numpy(np.ascontiguousarray(d[k])).cuda()
 
 
+def _device_math(d):
+    """softplus(dt + dt_bias), exp(A * softplus) and sigmoid(dt + dt_bias) with CUDA's expf /
+    logf, in the kernels' order of operations (each step rounded to float32)."""
+    raw = _cuda(d, 'dt').float() + _cuda(d, 'dt_bias').float()[None, None, :]
+    soft = torch.where(raw <= 20.0, torch.log(torch.exp(raw) + 1.0), raw)
+    decay = torch.exp(_cuda(d, 'A')[None, None, :] * soft)
+    sig = torch.where(raw <= 20.0, 1.0 / (1.0 + torch.exp(-raw)), torch.ones_like(raw))
+    return {'softplus': soft.cpu().numpy(), 'decay': decay.cpu().numpy(), 'sigmoid': sig.cpu().numpy()}
+
+
+def _oracle_forward(d, state_in):
+    st = {k: v.copy() for k, v in state_in.items()}
+    y = ost.sq3p25_scan(*(d[k] for k in KEYS), st, d['permutation'], device_math=_device_math(d))
+    return y, st
+
+
+def _oracle_backward(d, chunk):
+    return ost.ste_backward(*(d[k] for k in (*KEYS, 'permutation', 'dy')), chunk, device_math=_device_math(d))
+
+
 def _forward(d, state_in=None):
     from sq325 import state_codec as sc
     x = _cuda(d, 'x')
@@ -41,19 +66,25 @@ def _forward(d, state_in=None):
     return y.cpu().numpy(), {k: st.tensors[k].cpu().numpy() for k in STATE}
 
 
-def _check_forward(y, st, y_ref, st_ref):
-    assert np.allclose(y.astype(np.float32), y_ref.astype(np.float32), rtol=2e-2, atol=2e-2)
-    assert (y.view(np.uint16) == y_ref.view(np.uint16)).mean() >= 0.99
+def _exact(y, st, y_ref, st_ref):
+    assert np.array_equal(y.view(np.uint16), y_ref.view(np.uint16)), \
+        f'readouts: {(y.view(np.uint16) != y_ref.view(np.uint16)).sum()} of {y.size} differ'
     for k in STATE:
-        assert (st[k].view(np.uint8) == st_ref[k].view(np.uint8)).mean() >= 0.99, k
+        assert np.array_equal(st[k].view(np.uint8), st_ref[k].view(np.uint8)), k
 
 
-def _close(got, ref, name):
-    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
-    scale = max(np.abs(ref).max(), 1e-30)
-    rel_l2 = np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30)
-    worst = np.abs(got - ref).max() / scale
-    assert rel_l2 <= 1e-4 and worst <= 1e-3, f'{name}: rel_l2 {rel_l2:.3e}, max/scale {worst:.3e}'
+def _mostly(y, st, y_ref, st_ref):
+    same = (y.view(np.uint16) == y_ref.view(np.uint16)).mean()
+    assert same >= 0.98, f'readouts identical {same:.4f}'
+    for k in STATE:
+        same = (st[k].view(np.uint8) == st_ref[k].view(np.uint8)).mean()
+        assert same >= 0.99, f'{k} identical {same:.4f}'
+
+
+def _same(got, ref, name):
+    bad = got != ref
+    assert not bad.any(), (f'{name}: {bad.sum()} of {bad.size} differ, max |diff| '
+                           f'{np.abs(got.astype(np.float64) - ref).max():.3e} of max |ref| {np.abs(ref).max():.3e}')
 
 
 def _backward_abi(d, chunk):
@@ -76,11 +107,14 @@ def _backward_abi(d, chunk):
     return {k: v.cpu().numpy() for k, v in out.items()}, cp.cpu().numpy()
 
 
+@pytest.mark.parametrize('case', ['ste.npz', 'ste_ragged.npz'])
 @pytest.mark.parametrize('tag', ['rand_', 'zero_'])
-def test_sq3p25_scan_matches_reference_golden(golden, tag):
-    d = golden('ste.npz')
-    y, st = _forward(d, {k: d[f'{tag}in_{k}'] for k in STATE})
-    _check_forward(y, st, d[tag + 'y'], {k: d[f'{tag}out_{k}'] for k in STATE})
+def test_sq3p25_scan_matches_reference_golden(golden, tag, case):
+    d = golden(case)
+    state_in = {k: d[f'{tag}in_{k}'] for k in STATE}
+    y, st = _forward(d, state_in)
+    _exact(y, st, *_oracle_forward(d, state_in))
+    _mostly(y, st, d[tag + 'y'], {k: d[f'{tag}out_{k}'] for k in STATE})
 
 
 @pytest.mark.parametrize('dim', [64, 40])
@@ -94,25 +128,26 @@ def test_sq3p25_scan_matches_oracle_at_model_geometry(dim):
     st0 = sc.allocate_state(2, 32, dim, 128, 'sq3p25', 'cpu')
     sc.encode_state_(st0, dense)
     state_in = {k: v.numpy() for k, v in st0.tensors.items()}
-    st_ref = {k: v.copy() for k, v in state_in.items()}
-    y_ref = ost.sq3p25_scan(*(d[k] for k in KEYS), st_ref, d['permutation'])
     y, st = _forward(d, state_in)
-    _check_forward(y, st, y_ref, st_ref)
+    _exact(y, st, *_oracle_forward(d, state_in))
 
 
-def test_ste_backward_matches_reference_golden(golden):
-    d = golden('ste.npz')
+@pytest.mark.parametrize('case', ['ste.npz', 'ste_ragged.npz'])
+def test_ste_backward_matches_reference_golden(golden, case):
+    d = golden(case)
     grads, cp = _backward_abi(d, int(d['chunk']))
+    ref = _oracle_backward(d, int(d['chunk']))
     assert cp.shape == d['checkpoints'].shape
+    assert np.array_equal(cp.view(np.uint32), ref[4].view(np.uint32))
     assert (cp.view(np.uint32) == d['checkpoints'].view(np.uint32)).mean() >= 0.99
-    assert np.allclose(cp, d['checkpoints'], rtol=1e-3, atol=1e-3)
-    for k in ('dx', 'ddt', 'db', 'dc'):
-        _close(grads[k], d[k], k)
+    for k, r in zip(('dx', 'ddt', 'db', 'dc'), ref[:4]):
+        _same(grads[k], r, k)
 
 
 def test_scan_training_autograd_matches_reference_golden(golden):
-    """The autograd path: zero-state forward equal to the golden zero-start readout, and the
-    fp16 gradients of x, dt, B, C equal to the golden fp32 gradients rounded to fp16."""
+    """The autograd path: the zero-state forward and the fp16 gradients of x, dt, B, C equal
+    to the oracle's (device transcendentals; gradients rounded to fp16); A, D, dt_bias get
+    none."""
     from sq325.state_training import scan_training
     d = golden('ste.npz')
     t = {k: _cuda(d, k) for k in (*KEYS, 'permutation', 'dy')}
@@ -122,12 +157,14 @@ def test_scan_training_autograd_matches_reference_golden(golden):
     y.backward(t['dy'])
     torch.cuda.synchronize()
     ynp = y.detach().cpu().numpy()
-    assert (ynp.view(np.uint16) == d['zero_y'].view(np.uint16)).mean() >= 0.99
-    for k, g in (('x', 'dx'), ('dt', 'ddt'), ('B', 'db'), ('C', 'dc')):
+    zero = {k: np.zeros_like(d[f'zero_in_{k}']) for k in STATE}
+    assert np.array_equal(ynp.view(np.uint16), _oracle_forward(d, zero)[0].view(np.uint16))
+    assert (ynp.view(np.uint16) == d['zero_y'].view(np.uint16)).mean() >= 0.98
+    ref = _oracle_backward(d, int(d['chunk']))
+    for (k, g), r in zip((('x', 'dx'), ('dt', 'ddt'), ('B', 'db'), ('C', 'dc')), ref[:4]):
         grad = t[k].grad
         assert grad.dtype == torch.float16 and tuple(grad.shape) == d[g].shape
-        ref = d[g].astype(np.float16).astype(np.float32)
-        assert np.allclose(grad.float().cpu().numpy(), ref, rtol=2e-3, atol=1e-3 * np.abs(ref).max()), k
+        _same(grad.cpu().numpy(), r.astype(np.float16), k)
     assert t['A'].grad is None and t['D'].grad is None
 
 
@@ -148,15 +185,15 @@ def test_ste_backward_matches_oracle_and_is_chunk_invariant():
     gradients at chunks 1, 5, 24 and 256 (a chunk longer than the sequence)."""
     rng = np.random.default_rng(7)
     d = _inputs(rng, 2, 24, 8, 64, 2)
-    ref = ost.ste_backward(*(d[k] for k in (*KEYS, 'permutation', 'dy')), 8)
+    ref = _oracle_backward(d, 8)
     grads, cp = _backward_abi(d, 8)
-    assert np.allclose(cp, ref[4], rtol=1e-3, atol=1e-3)
+    assert np.array_equal(cp.view(np.uint32), ref[4].view(np.uint32))
     for k, r in zip(('dx', 'ddt', 'db', 'dc'), ref[:4]):
-        _close(grads[k], r, k)
+        _same(grads[k], r, k)
     for chunk in (1, 5, 24, 256):
         other, _ = _backward_abi(d, chunk)
         for k in ('dx', 'ddt', 'db', 'dc'):
-            _close(other[k], grads[k], f'{k} chunk {chunk}')
+            _same(other[k], grads[k], f'{k} chunk {chunk}')
 
 
 def test_ste_backward_rejects_bad_arguments():

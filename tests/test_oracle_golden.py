@@ -204,13 +204,14 @@ def test_s16_oracle_matches_reference_kernel(golden, tag):
         assert np.array_equal(stats.view(np.uint32), d['stats_stats'].view(np.uint32))
 
 
+@pytest.mark.parametrize('case', ['ste.npz', 'ste_ragged.npz'])
 @pytest.mark.parametrize('tag', ['rand_', 'zero_'])
-def test_sq3p25_oracle_matches_reference_kernel(golden, tag):
+def test_sq3p25_oracle_matches_reference_kernel(golden, tag, case):
     """oracle.ste.sq3p25_scan against the reference's packed `_sq_scan` run by the interpreter
     (mamba2_recall/state_codec.py:105-176): readout and every state byte, from a random and
-    from a zero state."""
+    from a zero state; ste_ragged has a half-masked 16-row tile (dim 40)."""
     from oracle import ste
-    d = golden('ste.npz')
+    d = golden(case)
     st = {k: d[f'{tag}in_{k}'].copy() for k in ('lo', 'hi', 'q4', 's8', 's4')}
     y = ste.sq3p25_scan(*(d[k] for k in ('x', 'dt', 'A', 'B', 'C', 'D', 'dt_bias')), st, d['permutation'])
     assert np.array_equal(y.view(np.uint16), d[tag + 'y'].view(np.uint16))
@@ -218,13 +219,35 @@ def test_sq3p25_oracle_matches_reference_kernel(golden, tag):
         assert np.array_equal(v.view(np.uint8), d[f'{tag}out_{k}'].view(np.uint8)), k
 
 
-def test_ste_backward_oracle_matches_reference_kernels(golden):
+@pytest.mark.parametrize('case', ['ste.npz', 'ste_ragged.npz'])
+def test_ste_backward_oracle_matches_reference_kernels(golden, case):
     """oracle.ste.ste_backward against `_carry_checkpoints` / `_chunk_history` /
     `_chunk_backward` run by the interpreter (mamba2_recall/state_training_scan.py:24-211):
-    checkpoints, dx, ddt, dB and dC bit for bit."""
+    checkpoints, dx, ddt, dB and dC bit for bit; ste_ragged has three row tiles (the last
+    half masked) and a partial last chunk."""
     from oracle import ste
-    d = golden('ste.npz')
+    d = golden(case)
     dx, ddt, db, dc, cp = ste.ste_backward(*(d[k] for k in ('x', 'dt', 'A', 'B', 'C', 'D', 'dt_bias',
                                                             'permutation', 'dy')), int(d['chunk']))
     for name, got in (('checkpoints', cp), ('dx', dx), ('ddt', ddt), ('db', db), ('dc', dc)):
         assert np.array_equal(got.view(np.uint32), d[name].view(np.uint32)), name
+
+
+def test_ste_oracle_device_math_hook_is_neutral(golden):
+    """Supplying numpy's own softplus / decay / sigmoid through `device_math` reproduces the
+    golden runs: the hook only swaps the transcendental values, nothing else."""
+    from oracle import ste
+    d = golden('ste.npz')
+    raw = (d['dt'].astype(np.float32) + d['dt_bias'].astype(np.float32)[None, None, :]).astype(np.float32)
+    soft = np.where(raw <= np.float32(20), np.log(np.exp(raw) + np.float32(1)), raw).astype(np.float32)
+    math = {'softplus': soft, 'decay': np.exp((d['A'][None, None, :] * soft).astype(np.float32)).astype(np.float32),
+            'sigmoid': np.where(raw <= np.float32(20), (np.float32(1) / (np.float32(1) + np.exp(-raw))).astype(np.float32),
+                                np.float32(1)).astype(np.float32)}
+    st = {k: d[f'zero_in_{k}'].copy() for k in ('lo', 'hi', 'q4', 's8', 's4')}
+    y = ste.sq3p25_scan(*(d[k] for k in ('x', 'dt', 'A', 'B', 'C', 'D', 'dt_bias')), st, d['permutation'],
+                        device_math=math)
+    assert np.array_equal(y.view(np.uint16), d['zero_y'].view(np.uint16))
+    got = ste.ste_backward(*(d[k] for k in ('x', 'dt', 'A', 'B', 'C', 'D', 'dt_bias', 'permutation', 'dy')),
+                           int(d['chunk']), device_math=math)
+    for name, g in zip(('dx', 'ddt', 'db', 'dc', 'checkpoints'), got):
+        assert np.array_equal(g.view(np.uint32), d[name].view(np.uint32)), name

@@ -85,8 +85,9 @@ def test_training_workspace_bytes_and_library_count():
     carries = 2 * (nc + 32 + 1) * 8 * 64 * 80 * 4
     assert got == {'carry_scratch_bytes': carries, 'gradient_scratch_bytes': 2 * 100 * (8 * 64 + 8 + 2 * 2 * 128) * 4,
                    'total_scratch_bytes': carries + 2 * 100 * (8 * 64 + 8 + 2 * 2 * 128) * 4}
-    # the library's scratch holds exactly the carries (gradients are the caller's outputs)
-    assert _lib.load().sq_ste_workspace(2, 100, 8, 64, 32) == carries
+    # the library's scratch: the same carries plus one chunk of dB / dC partials per
+    # (head, 16-row tile); the gradients themselves are the caller's outputs
+    assert _lib.load().sq_ste_workspace(2, 100, 8, 64, 32) == carries + 2 * 32 * 8 * 4 * 256 * 4
 
 
 def test_scan_training_checks_match_reference():
