@@ -279,6 +279,30 @@ def run_case(args):
         st = sc.allocate_state(B, H, P, 128, 's16', 'cuda')
         call = lambda: sc.scan(x, dt, A, Bm, Cm, D, db, st)
         unit, work = 'us/token', float(L)
+    elif args.case in ('sq3p25', 'ste'):          # packed sq3p25 scan / its STE backward, training geometry
+        import ctypes
+        from sq325 import state_codec as sc
+        B, L, H, P, G, K = STE_GEOMETRY
+        x = torch.randn(B, L, H, P, device='cuda', generator=gen).half()
+        dt = (torch.randn(B, L, H, device='cuda', generator=gen) * 0.5).half()
+        A = -(torch.rand(H, device='cuda', generator=gen) * 3 + 0.1)
+        Bm = torch.randn(B, L, G, 128, device='cuda', generator=gen).half()
+        Cm = torch.randn(B, L, G, 128, device='cuda', generator=gen).half()
+        D = torch.randn(H, device='cuda', generator=gen).half()
+        db = (torch.rand(H, device='cuda', generator=gen) * 3 - 4).half()
+        perm = torch.stack([torch.randperm(128, device='cuda', generator=gen) for _ in range(G)]).to(torch.uint8)
+        if args.case == 'sq3p25':
+            st = sc.allocate_state(B, H, P, 128, 'sq3p25', 'cuda')
+            call = lambda: sc.scan(x, dt, A, Bm, Cm, D, db, st, permutation=perm)
+        else:
+            dy = torch.randn(B, L, H, P, device='cuda', generator=gen).half()
+            grads = [torch.empty(t.shape, device='cuda', dtype=torch.float32) for t in (x, dt, Bm, Cm)]
+            nbytes = int(_lib.load().sq_ste_workspace(B, L, H, P, K))
+            ws = torch.empty(nbytes, device='cuda', dtype=torch.uint8)
+            sargs = sc.sq3p25_args(x, dt, A, Bm, Cm, D, db, perm)
+            call = lambda: _lib.call('sq_ste_backward', ctypes.byref(sargs), K, dy.data_ptr(),
+                                     *(g.data_ptr() for g in grads), ws.data_ptr(), nbytes, _lib.stream_ptr())
+        unit, work = 'us/token', float(L)
     else:                                         # SQ3.25 scan: prep + chunk kernels, 16 x 128 x 64 rows
         B, L, H, P, G = 16, 512, 128, 64, 8
         spec = codec.layout_descriptor(args.layout)
@@ -309,9 +333,44 @@ def run_case(args):
         ts.append(ev[0].elapsed_time(ev[1]) / 1e3)
     t = statistics.median(ts)
     val = work / t / 1e12 if unit == 'TFLOP/s' else (work / t / 1e9 if unit == 'GB/s' else t * 1e6 / work)
+    extra = {}
+    if args.case in ('sq3p25', 'ste'):
+        B, L, H, P, G, K = STE_GEOMETRY
+        extra = dict(geometry=dict(batch=B, tokens=L, heads=H, dim=P, groups=G, chunk=K),
+                     cpu_baseline=ste_cpu_sample(args.case, B * H * P))
     print(json.dumps(dict(case=args.case, layout=args.layout if args.case == 'scan' else None, seconds=t,
                           value=val, unit=unit, steps=args.steps, rows=args.rows if args.case == 'gemv' else None,
-                          layers=args.layers if args.case == 'decode' else None)), flush=True)
+                          layers=args.layers if args.case == 'decode' else None, **extra)), flush=True)
+
+
+STE_GEOMETRY = (4, 512, 128, 64, 8, 32)   # batch, tokens, heads, dim, groups, chunk (training defaults)
+
+
+def ste_cpu_sample(case, rows_full, tokens=64, heads=16, dim=64, chunk=32):
+    """The CPU oracle (oracle/ste.py, one thread) on a bounded sample of the --case sq3p25 /
+    ste workload: one sequence of `tokens` tokens over `heads` heads of one group; returns
+    microseconds per token extrapolated to `rows_full` state rows."""
+    from oracle import ste as ost
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((1, tokens, heads, dim)).astype(np.float16)
+    dt = (rng.standard_normal((1, tokens, heads)) * 0.5).astype(np.float16)
+    A = -(rng.random(heads) * 3 + 0.1).astype(np.float32)
+    Bm = rng.standard_normal((1, tokens, 1, 128)).astype(np.float16)
+    Cm = rng.standard_normal((1, tokens, 1, 128)).astype(np.float16)
+    D = rng.standard_normal(heads).astype(np.float16)
+    db = (rng.random(heads) * 3 - 4).astype(np.float16)
+    perm = rng.permutation(128).astype(np.uint8)[None]
+    t0 = time.perf_counter()
+    if case == 'sq3p25':
+        st = {k: np.zeros((1, heads, dim, n), np.uint8) for k, n in (('lo', 8), ('hi', 8), ('q4', 32))}
+        st.update({k: np.zeros((1, heads, dim), np.float16) for k in ('s8', 's4')})
+        ost.sq3p25_scan(x, dt, A, Bm, Cm, D, db, st, perm)
+    else:
+        ost.ste_backward(x, dt, A, Bm, Cm, D, db, perm, rng.standard_normal(x.shape).astype(np.float16), chunk)
+    sec = time.perf_counter() - t0
+    rows = heads * dim
+    return dict(value=sec / tokens * rows_full / rows * 1e6, unit='us/token', cores=1, kind='port',
+                sample=f'{tokens} tokens x {heads} heads x {dim} rows, extrapolated by rows', seconds=sec)
 
 
 L2_FLUSH_BYTES = 256 << 20      # > 126 MB of L2
@@ -480,7 +539,7 @@ def main():
     ap.add_argument('--no-extras', action='store_true',
                     help='skip the config 2 / 3 / 5 measurements of the one-GPU line')
     ap.add_argument('--rows', type=int, default=1, help='M of --case gemv')
-    ap.add_argument('--case', choices=['gemm', 'scan', 'decode', 'gemv', 's16'], default=None,
+    ap.add_argument('--case', choices=['gemm', 'scan', 'decode', 'gemv', 's16', 'sq3p25', 'ste'], default=None,
                     help='time one kernel on a small case (for ncu captures) instead of the bench')
     ap.add_argument('--layout', default='32_32_64', help='scan layout of --case scan')
     ap.add_argument('--layers', type=int, default=4, help='layers of --case decode')
@@ -535,6 +594,7 @@ def main():
     clocks.start()
     s = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ex.time_projection_gemm(True)        # CUDA events around each in_proj GEMM launch of the timed steps
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -543,6 +603,8 @@ def main():
         res = step(dev_windows)
     e1.record(s)
     torch.cuda.synchronize()
+    gemm_in_step_s, gemm_in_step_n = ex.projection_gemm_time()
+    ex.time_projection_gemm(False)
     if world > 1:
         dist.barrier()
     elapsed = e0.elapsed_time(e1) / 1e3
@@ -575,10 +637,16 @@ def main():
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = world * B * T * e2e_steps / float(te)
 
-    # dominant kernel roofline (in_proj GEMM at the workload's M)
+    # dominant kernel roofline: the in_proj GEMM launches of the timed steps (CUDA events on
+    # the launching stream inside the timed region), against the sustained peak since they run
+    # inside a seconds-long power-capped step; the same GEMM timed alone (burst) for context
     pk = peaks()
-    gemm_s, gemm_flop = time_gemm_kernel(model, B * T, device)
+    gemm_flop = 2.0 * B * T * 18560 * 4096
+    gemm_alone_s, _ = time_gemm_kernel(model, B * T, device)
+    in_step = gemm_in_step_n == N_LAYER * args.steps   # one M = B*T launch per layer and step
+    gemm_s = gemm_in_step_s / gemm_in_step_n if in_step else gemm_alone_s
     achieved = gemm_flop / gemm_s / 1e12
+    gemm_peak = pk['tf_sus'] if in_step else pk['tf']
 
     extras = {}
     if rank == 0 and world == 1 and not args.no_extras:
@@ -611,8 +679,14 @@ def main():
             config=workload_config(world, B, T),
             e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h),
             roofline=dict(bound='tensor', kernel='tcgen05 in_proj GEMM (M=%d,N=18560,K=4096)' % (B * T),
-                          achieved=achieved, peak=pk['tf'], unit='TFLOP/s', frac=achieved / pk['tf'], traffic=GEMM_TRAFFIC_BYTES,
-                          peak_source=pk['src'] + ' bf16_tflops (burst)'),
+                          achieved=achieved, peak=gemm_peak, unit='TFLOP/s', frac=achieved / gemm_peak,
+                          traffic=GEMM_TRAFFIC_BYTES,
+                          peak_source=pk['src'] + (' bf16_tflops_sustained (launches timed inside the step)' if in_step
+                                                   else ' bf16_tflops (burst; launch count differed, timed alone)'),
+                          launches_timed=gemm_in_step_n, ms_per_launch=gemm_s * 1e3,
+                          alone=dict(ms=gemm_alone_s * 1e3, achieved=gemm_flop / gemm_alone_s / 1e12, peak=pk['tf'],
+                                     frac=gemm_flop / gemm_alone_s / 1e12 / pk['tf'],
+                                     note='same GEMM timed alone after the step, burst peak')),
             step_roofline=dict(flop_per_token=FLOP_PER_TOKEN,
                                achieved_tflops=FLOP_PER_TOKEN * value / world / 1e12,
                                frac=FLOP_PER_TOKEN * value / world / 1e12 / pk['tf_sus']),

@@ -323,6 +323,13 @@ int sq_model_set_capture(sq_model* model, uint16_t* out, int64_t rows);
  * decoded FP16 weights (fp4.py:100-103), about three ALU instructions per weight.  Prompts,
  * scoring windows and the scoring head always use the exactly decoded weights. */
 int sq_model_set_exact_skinny(sq_model* model, int exact);
+/* Measurement: with enable = 1, every later large-M in_proj GEMM launch of sq_model_forward
+ * (the tcgen05 GEMM of prompts and scoring windows, more than 256 rows) is bracketed by a pair
+ * of CUDA events on its stream (not while the stream is being captured); enable = 0 stops.
+ * Either call discards earlier records.  sq_model_gemm_time waits for the recorded launches
+ * and returns their summed device time and count, then discards them. */
+int sq_model_time_gemm(sq_model* model, int enable);
+int sq_model_gemm_time(sq_model* model, double* seconds, int64_t* launches);
 
 #ifdef __cplusplus
 }

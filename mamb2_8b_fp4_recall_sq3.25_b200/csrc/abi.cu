@@ -116,6 +116,11 @@ struct sq_model {
   size_t stage_elems = 0;
   uint16_t* capture = nullptr;                // per-layer mixer outputs [n_layer][capture_rows][4096]
   long long capture_rows = 0;
+  // opt-in timing of the large-M in_proj tcgen05 GEMM launches (sq_model_time_gemm): an
+  // event pair per launch on the launching stream, read by sq_model_gemm_time
+  bool gemm_timing = false;
+  std::vector<cudaEvent_t> gemm_events;
+  size_t gemm_events_used = 0;
   std::atomic<int> busy{0};
 };
 
@@ -138,16 +143,36 @@ void free_ws(sq_model* m) {
 // GEMM.  exact = per-weight fp16 decode (the reference's); false (one-token decode steps
 // unless set_exact_skinny) applies the fp32 global scale once per output.
 constexpr int kSkinnyMax = 1, kFusedMax = 256;
+// Event pair around one timed GEMM launch; nullptr when timing is off or the stream is being
+// captured into a graph.
+cudaEvent_t* gemm_event_pair(sq_model* m, cudaStream_t st) {
+  if (!m->gemm_timing) return nullptr;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
+  while (m->gemm_events.size() < m->gemm_events_used + 2) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    m->gemm_events.push_back(e);
+  }
+  cudaEvent_t* pair = &m->gemm_events[m->gemm_events_used];
+  m->gemm_events_used += 2;
+  return pair;
+}
+
 int linear(sq_model* m, const sq_fp4_matrix& W, const Fp4Maps* maps, const uint16_t* X, long long ldx, int M,
-           uint16_t* Y, long long ldy, bool exact, cudaStream_t st) {
+           uint16_t* Y, long long ldy, bool exact, cudaStream_t st, bool timed = false) {
   const Fp4Weight w = fw(W);
   if (M <= kSkinnyMax) return check(launch_fp4_gemv_stream(w, maps, X, ldx, M, Y, ldy, m->d_err, st, exact), "fp4 gemv");
   if (M <= kFusedMax)
     return check(launch_fp4_mma_linear(w, X, ldx, M, Y, ldy, m->d_err, st, exact), "fp4 tensor-core linear");
   if ((size_t)W.rows * W.cols > m->stage_elems) return fail(SQ_EINVAL, "staging buffer too small");
   SQ_TRY(launch_fp4_decode(w, m->stage, W.cols, st), "fp4 decode");
-  return check(launch_gemm_f16(X, ldx, m->stage, W.cols, Y, ldy, M, W.rows, W.cols, 0, nullptr, m->d_err, st),
-               "tcgen05 gemm");
+  cudaEvent_t* ev = timed ? gemm_event_pair(m, st) : nullptr;
+  if (ev) cudaEventRecord(ev[0], st);
+  const int s = check(launch_gemm_f16(X, ldx, m->stage, W.cols, Y, ldy, M, W.rows, W.cols, 0, nullptr, m->d_err, st),
+                      "tcgen05 gemm");
+  if (ev) cudaEventRecord(ev[1], st);
+  return s;
 }
 
 }  // namespace
@@ -450,6 +475,7 @@ int sq_model_destroy(sq_model* m) {
   for (void* p : dec)
     if (p) cudaFree(p);
   if (m->d_err) cudaFree(m->d_err);
+  for (cudaEvent_t e : m->gemm_events) cudaEventDestroy(e);
   delete m;
   return SQ_OK;
 }
@@ -555,7 +581,7 @@ int mixer_forward(sq_model* m, int l, const uint16_t* u, int batch, int tokens, 
   const sq_model::St& S = m->states[l];
   const int M = batch * tokens;
   const bool step = pos0 > 0 && tokens == 1;
-  int s = linear(m, L.in_proj, &m->in_maps[l], u, kDModel, M, m->zx, kZx, !step || m->exact_skinny, st);
+  int s = linear(m, L.in_proj, &m->in_maps[l], u, kDModel, M, m->zx, kZx, !step || m->exact_skinny, st, true);
   if (s != SQ_OK) return s;
   ScanParams P{};
   P.batch = batch; P.length = tokens; P.heads = kHeads; P.dim = kHeadDim; P.groups = kGroups; P.layout = L.layout;
@@ -767,6 +793,29 @@ int sq_model_set_capture(sq_model* m, uint16_t* out, int64_t rows) {
   if (out && !aligned(out, 16)) return fail(SQ_EINVAL, "set_capture: buffer must be 16-byte aligned");
   m->capture = out;
   m->capture_rows = out ? rows : 0;
+  return SQ_OK;
+}
+
+int sq_model_time_gemm(sq_model* m, int enable) {
+  if (!m) return fail(SQ_EINVAL, "time_gemm: null model");
+  m->gemm_timing = enable != 0;
+  m->gemm_events_used = 0;
+  return SQ_OK;
+}
+
+int sq_model_gemm_time(sq_model* m, double* seconds, int64_t* launches) {
+  if (!m || !seconds || !launches) return fail(SQ_EINVAL, "gemm_time: null argument");
+  double total = 0.0;
+  for (size_t i = 0; i + 1 < m->gemm_events_used; i += 2) {
+    if (cudaEventSynchronize(m->gemm_events[i + 1]) != cudaSuccess) return cuda_fail("gemm_time: event synchronize");
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, m->gemm_events[i], m->gemm_events[i + 1]) != cudaSuccess)
+      return cuda_fail("gemm_time: elapsed time");
+    total += ms * 1e-3;
+  }
+  *seconds = total;
+  *launches = (int64_t)(m->gemm_events_used / 2);
+  m->gemm_events_used = 0;
   return SQ_OK;
 }
 

@@ -103,6 +103,8 @@ _PROTOS = {
     'sq_fp4_validate': (C.c_int, [p, p, p, C.c_int, C.c_int, p]),
     'sq_scan_workspace': (i64, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
     'sq_model_set_exact_skinny': (C.c_int, [p, C.c_int]),
+    'sq_model_time_gemm': (C.c_int, [p, C.c_int]),
+    'sq_model_gemm_time': (C.c_int, [p, C.POINTER(C.c_double), C.POINTER(i64)]),
     'sq_model_set_capture': (C.c_int, [p, p, i64]),
     'sq_model_decode': (C.c_int, [p, p, C.c_int, C.c_int, p, p]),
     'sq_fp4_linear_workspace': (i64, [C.c_int, C.c_int, C.c_int]),

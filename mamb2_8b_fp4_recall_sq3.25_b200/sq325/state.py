@@ -103,6 +103,20 @@ class PredictorState:
             raise
         return self
 
+    def time_projection_gemm(self, enable=True):
+        """Measurement hook: bracket every later large-M in_proj tcgen05 GEMM launch (prompts,
+        scoring windows) with a pair of CUDA events on its stream (sq_model_time_gemm)."""
+        if self._handle is None:
+            raise RuntimeError('install() the model first')
+        _lib.call('sq_model_time_gemm', self._handle, int(bool(enable)))
+
+    def projection_gemm_time(self):
+        """(device seconds, launches) of the GEMM launches recorded since
+        time_projection_gemm; the records are then discarded."""
+        sec, n = C.c_double(), C.c_int64()
+        _lib.call('sq_model_gemm_time', self._handle, C.byref(sec), C.byref(n))
+        return sec.value, n.value
+
     def set_exact_projections(self, exact=True):
         """One-token decode steps and the greedy head use the factored global scale by
         default (fp16 products E2M1*E4M3 on the tensor cores, fp32 global scale once per

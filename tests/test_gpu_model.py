@@ -272,3 +272,27 @@ def test_persistent_decode_matches_graph_replay_full_size():
             assert torch.equal(a[k], b[k]), (layer, k)
     for a, b in zip(runs[True][2], runs[False][2]):
         assert torch.equal(a, b)
+
+
+def test_projection_gemm_timer_counts_large_m_launches(pair):
+    """sq_model_time_gemm brackets every large-M in_proj GEMM launch (one per layer when
+    batch x tokens > 256) and nothing else; records are discarded once read, and nothing is
+    recorded after the timer is switched off."""
+    from sq325 import PredictorState
+    gm, _, statics = pair
+    rng = np.random.default_rng(9)
+    big = lambda: torch.from_numpy(_ids(rng, 2, 200, gm.vocab)).cuda()     # 400 rows: tcgen05 GEMM
+    small = lambda: torch.from_numpy(_ids(rng, 2, 8, gm.vocab)).cuda()     # 16 rows: fused FP4 linear
+    with PredictorState(gm, *statics) as ex:
+        ex.reserve(400)
+        ex.backbone(big(), reset=True)
+        ex.time_projection_gemm(True)
+        ex.backbone(big(), reset=True)
+        ex.backbone(small(), reset=True)
+        sec, n = ex.projection_gemm_time()
+        assert n == gm.n_layer and sec > 0
+        assert ex.projection_gemm_time() == (0.0, 0)
+        ex.time_projection_gemm(False)
+        ex.backbone(big(), reset=True)
+        assert ex.projection_gemm_time() == (0.0, 0)
+        ex.check()
