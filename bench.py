@@ -47,7 +47,7 @@ DECODE_FIXED_BYTES, DECODE_PER_SEQ_BYTES = 4_054_786_868, 56_887_552
 FLOP_PER_TOKEN_BACKBONE = 2 * 56 * (18560 * 4096 + 4096 * 8192)                 # prefill, no lm_head
 # dram__bytes_read.sum + dram__bytes_write.sum of one in_proj GEMM launch (M=32768), from
 # one ncu --set full capture of `python bench.py --case gemm --steps 2` on this build.
-GEMM_TRAFFIC_BYTES = 2_715_832_000 + 1_196_445_000
+GEMM_TRAFFIC_BYTES = 1_620_000_000 + 1_200_000_000   # ncu dram__bytes_read + write, one in_proj launch
 
 
 def peaks():

@@ -26,7 +26,7 @@ constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;           // 16 KB
 constexpr int B_BYTES = BN * BK * 2;           // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int GROUP_M = 16;                    // raster: 16 M-tiles share each pass over N
+constexpr int GROUP_M = 32;                    // raster: 32 M-tiles (32 MB of A) share each pass over N
 constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(BN >> 3) << 17) |
                             ((uint32_t)(BM >> 4) << 24);
 

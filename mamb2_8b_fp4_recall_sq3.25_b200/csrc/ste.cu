@@ -17,25 +17,31 @@
 //                          through the requantisation as identity on the 80 live lanes and as
 //                          zero through the 48 pruned ones (the adjoint carry adj
 //                          [B][H][P][80] crosses chunks), the current-token readout through
-//                          all 128; dx is stored, d(dt) (times the softplus slope) and dB /
-//                          dC are summed over the CTA's rows and added atomically.
-//   ste_bc_reduce_kernel   adds the per-(head, row tile) dB / dC partials of the chunk in
-//                          (head, tile) order and scatters them to the original coordinates.
-// Mapping: one CTA per (head, batch), one thread per row of the head (dim <= 128); the
-// group's B / C of a token are staged in shared memory in tier order.  Arithmetic is
-// unfused (__fmul_rn / __fadd_rn) like the reference's, and every reduction runs in the order
-// of the reference kernels' golden runs (Triton interpreter, i.e. numpy): sums over a row's
-// lanes and over a tile's 16 rows for d(dt) in numpy's eight-accumulator pairwise order,
-// sums over rows for dB / dC sequentially, tiles and heads in program order.  Given the same
-// softplus / exp values the results are bit-identical to the golden runs, and no atomics are
-// used, so gradients are deterministic run to run.
+//                          all 128; stores dx and d(dt) (times the softplus slope) and the
+//                          per-(head, 16-row tile) partial sums of dB / dC;
+//   ste_bc_reduce_kernel   adds the dB / dC partials of the chunk in (head, tile) order and
+//                          scatters them to the original coordinates.
+// Mapping: one CTA per (head, batch); four threads per row of the head (dim <= 128).  Thread
+// `sub` of a row owns, in every tier block of n lanes, the lanes q with q % 8 in {2 sub,
+// 2 sub + 1}: 4 INT8 + 16 INT4 stored coordinates (and 16 of the 64-wide pruned block), kept
+// in registers.  The group's B / C of a token are staged in shared memory in tier order.
+// Arithmetic is unfused (__fmul_rn / __fadd_rn) like the reference's, quotients are
+// correctly rounded, and every reduction runs in the order of the reference kernels' golden
+// runs (Triton interpreter, i.e. numpy): a sum over a row's lanes in numpy's eight-running-
+// sum pairwise order (the owner of lanes q % 8 = 2 sub, 2 sub + 1 holds running sums 2 sub
+// and 2 sub + 1 whole; two shuffles combine them as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7))),
+// a tile's 16 rows for d(dt) in the same pairwise order, a tile's rows for dB / dC
+// sequentially, tiles and heads in program order.  Given the same softplus / exp values the
+// results are bit-identical to the golden runs; no atomics, so gradients are deterministic.
 #include "common.cuh"
 #include "ste.cuh"
 
 namespace sq {
 namespace {
 
-constexpr int kLive8 = 16, kLive4 = 64, kLive = 80;   // stored lanes; lanes 80..127 are pruned
+constexpr int kLive8 = 16, kLive = 80;   // stored lanes (16 INT8, then 64 INT4); lanes 80..127 are pruned
+constexpr int kTPR = 4;                                // threads per state row
+constexpr int kOwn8 = 4, kOwn4 = 16, kOwn = kOwn8 + kOwn4, kOwnD = 16;   // lanes per thread
 
 __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
@@ -49,7 +55,37 @@ __device__ __forceinline__ float round_away(float q) {
   r = (a - r >= 0.5f) ? r + 1.0f : r;
   return q < 0.f ? 0.0f - r : r;
 }
+// RN(a / d) for a normal divisor d given inv = RN(1 / d): the remainder a - q0 d is exact in
+// one FMA and one corrected step gives the correctly rounded quotient (Markstein).  Quotients
+// below 0.5 in magnitude, the only ones that can be subnormal here, round to code 0 either way.
+__device__ __forceinline__ float div_rn_inv(float a, float d, float inv) {
+  const float q0 = fmul(a, inv);
+  const float r = fmaf(-q0, d, a);
+  return fmaf(r, inv, q0);
+}
 __device__ __forceinline__ float softplus20(float v) { return v <= 20.0f ? logf(fadd(expf(v), 1.0f)) : v; }
+
+// Lane ownership: the thread's k-th lane of a tier block (k = 2 i + e) is q = 8 i + 2 sub + e.
+__device__ __forceinline__ int own_lane(int k, int sub) { return 8 * (k >> 1) + 2 * sub + (k & 1); }
+// tier-order index j of the thread's m-th stored lane (m < 4: INT8 tier, else INT4 tier)
+__device__ __forceinline__ int stored_j(int m, int sub) {
+  return m < kOwn8 ? own_lane(m, sub) : kLive8 + own_lane(m - kOwn8, sub);
+}
+// running sum e = k & 1 of the thread's lanes in order; the first term is assigned
+__device__ __forceinline__ void run_add(float (&acc)[2], int k, float v) {
+  if (k < 2) acc[k & 1] = v;
+  else acc[k & 1] = fadd(acc[k & 1], v);
+}
+// reductions over the row's four threads (adjacent lanes of one warp)
+__device__ __forceinline__ float row_max(float v) {
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+}
+__device__ __forceinline__ float row_pairwise(const float (&acc)[2]) {
+  float v = fadd(acc[0], acc[1]);
+  v = fadd(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  return fadd(v, __shfl_xor_sync(0xffffffffu, v, 2));
+}
 
 // Per-token staging shared by every kernel: B / C of the row's group in tier order and the
 // head's dt / decay.  All threads of the CTA call it; returns after a CTA barrier.
@@ -77,173 +113,152 @@ __device__ void stage_token(const SteParams& P, int b, int t, int h, int g, cons
   __syncthreads();
 }
 
-// S = S decay + (B dt) x on the live lanes, then the requant of both tiers; returns the codes
-// of the last requant through q8 / q4 when asked.
-__device__ __forceinline__ void step_live(float (&S)[kLive], const TokenShared& s, float x) {
+// S = S decay + (B dt) x on the thread's stored lanes
+__device__ __forceinline__ void step_own(float (&S)[kOwn], const TokenShared& s, float x, int sub) {
 #pragma unroll
-  for (int j = 0; j < kLive; ++j) S[j] = fadd(fmul(S[j], s.decay), fmul(fmul(s.b[j], s.dt), x));
+  for (int m = 0; m < kOwn; ++m) S[m] = fadd(fmul(S[m], s.decay), fmul(fmul(s.b[stored_j(m, sub)], s.dt), x));
 }
-__device__ __forceinline__ void requant(float (&S)[kLive], float& sc8, float& sc4, float* q = nullptr) {
+// requant of the thread's stored lanes with the row's scales; the codes through q when asked
+__device__ __forceinline__ void requant(float (&S)[kOwn], float& sc8, float& sc4, float* q = nullptr) {
   float m8 = 0.f, m4 = 0.f;
 #pragma unroll
-  for (int j = 0; j < kLive8; ++j) m8 = fmaxf(m8, fabsf(S[j]));
+  for (int m = 0; m < kOwn8; ++m) m8 = fmaxf(m8, fabsf(S[m]));
 #pragma unroll
-  for (int j = kLive8; j < kLive; ++j) m4 = fmaxf(m4, fabsf(S[j]));
+  for (int m = kOwn8; m < kOwn; ++m) m4 = fmaxf(m4, fabsf(S[m]));
+  m8 = row_max(m8);
+  m4 = row_max(m4);
   const float den8 = fmaxf(__fdiv_rn(m8, 127.0f), 1e-8f), den4 = fmaxf(__fdiv_rn(m4, 7.0f), 1e-8f);
+  const float inv8 = __frcp_rn(den8), inv4 = __frcp_rn(den4);
   sc8 = h2f(f2h(den8));
   sc4 = h2f(f2h(den4));
 #pragma unroll
-  for (int j = 0; j < kLive; ++j) {
-    const bool t8 = j < kLive8;
+  for (int m = 0; m < kOwn; ++m) {
+    const bool t8 = m < kOwn8;
     const float lim = t8 ? 127.f : 7.f;
-    const float qq = fminf(fmaxf(round_away(__fdiv_rn(S[j], t8 ? den8 : den4)), -lim), lim);
-    if (q) q[j] = qq;
-    S[j] = fmul(qq, t8 ? sc8 : sc4);
+    const float qq = fminf(fmaxf(round_away(div_rn_inv(S[m], t8 ? den8 : den4, t8 ? inv8 : inv4)), -lim), lim);
+    if (q) q[m] = qq;
+    S[m] = fmul(qq, t8 ? sc8 : sc4);
   }
-}
-
-// numpy's float32 sum of n lanes (n % 8 == 0, 8 <= n <= 128): eight running sums over the
-// lanes j, j + 8, j + 16, ..., combined as ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)).
-// `q` is the lane's position within the sum (a compile-time constant in unrolled loops).
-__device__ __forceinline__ void pw_add(float (&r)[8], int q, float v) {
-  if (q < 8) r[q] = v;
-  else r[q & 7] = fadd(r[q & 7], v);
-}
-__device__ __forceinline__ float pw_total(const float (&r)[8]) {
-  return fadd(fadd(fadd(r[0], r[1]), fadd(r[2], r[3])), fadd(fadd(r[4], r[5]), fadd(r[6], r[7])));
 }
 
 __device__ void load_perm(const SteParams& P, int g, int* perm) {
   for (int j = threadIdx.x; j < 128; j += blockDim.x) perm[j] = P.perm[g * 128 + j];
 }
 
+__device__ __forceinline__ float* carry_at(float* base, long long idx) { return base + idx * kLive; }
+
 // ------------------------------------------------------------------------ forward scan
-__global__ void __launch_bounds__(128) sq3p25_scan_kernel(const SteParams P) {
+__global__ void __launch_bounds__(512) sq3p25_scan_kernel(const SteParams P) {
   __shared__ TokenShared s;
   __shared__ int perm[128];
-  const int h = blockIdx.x, b = blockIdx.y, r = threadIdx.x;
+  const int h = blockIdx.x, b = blockIdx.y, r = threadIdx.x / kTPR, sub = threadIdx.x % kTPR;
   const int g = h / (P.heads / P.groups);
   const bool live = r < P.dim;
-  const long long row = ((long long)b * P.heads + h) * P.dim + r;
+  const long long row = ((long long)b * P.heads + h) * P.dim + (live ? r : 0);
   load_perm(P, g, perm);
-  float S[kLive];
+  float S[kOwn];
   {
-    float s8 = 0.f, s4 = 0.f;
-    if (live) { s8 = h2f(P.s8[row]); s4 = h2f(P.s4[row]); }
+    const float s8 = live ? h2f(P.s8[row]) : 0.f, s4 = live ? h2f(P.s4[row]) : 0.f;
 #pragma unroll
-    for (int j = 0; j < kLive8; ++j) {
-      int v = 0;
-      if (live) {
-        const int lo = (P.lo[row * 8 + j / 2] >> (4 * (j & 1))) & 15;
-        const int hi = (P.hi[row * 8 + j / 2] >> (4 * (j & 1))) & 15;
-        const int ub = (hi << 4) | lo;
-        v = ub - 256 * (ub > 127);
-      }
-      S[j] = fmul((float)v, s8);
+    for (int m = 0; m < kOwn8; ++m) {
+      const int q = own_lane(m, sub), sh = 4 * (q & 1);
+      const int ub = (((P.hi[row * 8 + q / 2] >> sh) & 15) << 4) | ((P.lo[row * 8 + q / 2] >> sh) & 15);
+      S[m] = fmul(live ? (float)(ub - 256 * (ub > 127)) : 0.f, s8);
     }
 #pragma unroll
-    for (int j = 0; j < kLive4; ++j) {
-      int v = 0;
-      if (live) {
-        const int nib = (P.q4[row * 32 + j / 2] >> (4 * (j & 1))) & 15;
-        v = nib - 16 * (nib > 7);
-      }
-      S[kLive8 + j] = fmul((float)v, s4);
+    for (int m = 0; m < kOwn4; ++m) {
+      const int q = own_lane(m, sub);
+      const int nib = (P.q4[row * 32 + q / 2] >> (4 * (q & 1))) & 15;
+      S[kOwn8 + m] = fmul(live ? (float)(nib - 16 * (nib > 7)) : 0.f, s4);
     }
   }
   const float dv = ldf(P.D, P.d_is_f32, h);
-  float sc8 = 0.f, sc4 = 0.f;
-  uint32_t plo[2] = {0, 0}, phi[2] = {0, 0}, pq4[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  float sc8 = 0.f, sc4 = 0.f, qlast[kOwn];
   for (int t = 0; t < P.length; ++t) {
     stage_token(P, b, t, h, g, perm, s, true);
     const float x = live ? h2f(P.x[(long long)b * P.x_sb + (long long)t * P.x_st + (long long)h * P.dim + r]) : 0.f;
-    step_live(S, s, x);
-    float acc[8], o8, o4, od;
+    step_own(S, s, x, sub);
+    float a8[2], a4[2], ad[2];
 #pragma unroll
-    for (int j = 0; j < kLive8; ++j) pw_add(acc, j, fmul(S[j], s.c[j]));
-    o8 = pw_total(acc);
+    for (int m = 0; m < kOwn8; ++m) run_add(a8, m, fmul(S[m], s.c[own_lane(m, sub)]));
 #pragma unroll
-    for (int j = kLive8; j < kLive; ++j) pw_add(acc, j - kLive8, fmul(S[j], s.c[j]));
-    o4 = pw_total(acc);
-    // pruned tier: the reference's 64-wide block, 48 coordinates and 16 masked zero lanes
+    for (int m = 0; m < kOwn4; ++m) run_add(a4, m, fmul(S[kOwn8 + m], s.c[kLive8 + own_lane(m, sub)]));
+    // pruned tier: the reference's 64-wide block, 48 coordinates then 16 masked zero lanes
 #pragma unroll
-    for (int q = 0; q < 64; ++q) {
-      const float bj = q < 48 ? s.b[kLive + q] : 0.0f, cj = q < 48 ? s.c[kLive + q] : 0.0f;
-      pw_add(acc, q, fmul(fmul(fmul(bj, s.dt), x), cj));
+    for (int k = 0; k < kOwnD; ++k) {
+      const int q = own_lane(k, sub);
+      const bool real = k < 12;                       // q < 48
+      const float bj = real ? s.b[kLive + q] : 0.0f, cj = real ? s.c[kLive + q] : 0.0f;
+      run_add(ad, k, fmul(fmul(fmul(bj, s.dt), x), cj));
     }
-    od = pw_total(acc);
+    const float o8 = row_pairwise(a8), o4 = row_pairwise(a4), od = row_pairwise(ad);
     const float out = fadd(fadd(o8, o4), fadd(od, fmul(x, dv)));
-    if (live) P.y[(long long)b * P.y_sb + (long long)t * P.y_st + (long long)h * P.dim + r] = f2h(out);
-    if (t + 1 < P.length) {
-      requant(S, sc8, sc4);
-    } else {
-      float q[kLive];
-      requant(S, sc8, sc4, q);
-#pragma unroll
-      for (int j = 0; j < kLive8; ++j) {
-        const int c = (int)q[j];
-        plo[j / 8] |= (uint32_t)(c & 15) << (4 * (j % 8));
-        phi[j / 8] |= (uint32_t)((c >> 4) & 15) << (4 * (j % 8));
-      }
-#pragma unroll
-      for (int j = 0; j < kLive4; ++j) pq4[j / 8] |= (uint32_t)((int)q[kLive8 + j] & 15) << (4 * (j % 8));
-    }
+    if (live && sub == 0) P.y[(long long)b * P.y_sb + (long long)t * P.y_st + (long long)h * P.dim + r] = f2h(out);
+    if (t + 1 < P.length) requant(S, sc8, sc4);
+    else requant(S, sc8, sc4, qlast);
   }
   if (live) {
-    uint32_t* lo = reinterpret_cast<uint32_t*>(P.lo + row * 8);
-    uint32_t* hi = reinterpret_cast<uint32_t*>(P.hi + row * 8);
-    uint32_t* q4 = reinterpret_cast<uint32_t*>(P.q4 + row * 32);
-    lo[0] = plo[0]; lo[1] = plo[1]; hi[0] = phi[0]; hi[1] = phi[1];
+    // this thread's INT8 lanes are 2 sub, 2 sub + 1 (byte sub) and 2 sub + 8, 2 sub + 9 (byte
+    // 4 + sub); its INT4 lanes 8 i + 2 sub + {0, 1} form byte 4 i + sub
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q4[i] = pq4[i];
-    P.s8[row] = f2h(sc8);
-    P.s4[row] = f2h(sc4);
+    for (int p = 0; p < 2; ++p) {
+      const int c0 = (int)qlast[2 * p], c1 = (int)qlast[2 * p + 1];
+      P.lo[row * 8 + 4 * p + sub] = (uint8_t)((c0 & 15) | ((c1 & 15) << 4));
+      P.hi[row * 8 + 4 * p + sub] = (uint8_t)(((c0 >> 4) & 15) | (((c1 >> 4) & 15) << 4));
+    }
+#pragma unroll
+    for (int i = 0; i < kOwn4 / 2; ++i) {
+      const int c0 = (int)qlast[kOwn8 + 2 * i], c1 = (int)qlast[kOwn8 + 2 * i + 1];
+      P.q4[row * 32 + 4 * i + sub] = (uint8_t)((c0 & 15) | ((c1 & 15) << 4));
+    }
+    if (sub == 0) {
+      P.s8[row] = f2h(sc8);
+      P.s4[row] = f2h(sc4);
+    }
   }
 }
 
 // ------------------------------------------------------------------------ STE backward
-__device__ __forceinline__ float* carry_at(float* base, long long idx) { return base + idx * kLive; }
-
-__global__ void __launch_bounds__(128) ste_checkpoint_kernel(const SteParams P) {
+__global__ void __launch_bounds__(512) ste_checkpoint_kernel(const SteParams P) {
   __shared__ TokenShared s;
   __shared__ int perm[128];
-  const int h = blockIdx.x, b = blockIdx.y, r = threadIdx.x;
+  const int h = blockIdx.x, b = blockIdx.y, r = threadIdx.x / kTPR, sub = threadIdx.x % kTPR;
   const int g = h / (P.heads / P.groups);
   const bool live = r < P.dim;
   load_perm(P, g, perm);
-  float S[kLive];
+  float S[kOwn];
 #pragma unroll
-  for (int j = 0; j < kLive; ++j) S[j] = 0.f;
+  for (int m = 0; m < kOwn; ++m) S[m] = 0.f;
   float sc8, sc4;
   for (int c = 0; c < P.nchunk; ++c) {
     if (live) {
       float* dst = carry_at(P.cp, (((long long)b * P.nchunk + c) * P.heads + h) * P.dim + r);
 #pragma unroll
-      for (int j = 0; j < kLive; ++j) dst[j] = S[j];
+      for (int m = 0; m < kOwn; ++m) dst[stored_j(m, sub)] = S[m];
     }
     for (int k = 0; k < P.chunk; ++k) {
       const int t = c * P.chunk + k;
       if (t >= P.length) break;
       stage_token(P, b, t, h, g, perm, s, false);
       const float x = live ? h2f(P.x[(long long)b * P.x_sb + (long long)t * P.x_st + (long long)h * P.dim + r]) : 0.f;
-      step_live(S, s, x);
+      step_own(S, s, x, sub);
       requant(S, sc8, sc4);
     }
   }
 }
 
-__global__ void __launch_bounds__(128) ste_history_kernel(const SteParams P, int c) {
+__global__ void __launch_bounds__(512) ste_history_kernel(const SteParams P, int c) {
   __shared__ TokenShared s;
   __shared__ int perm[128];
-  const int h = blockIdx.x, b = blockIdx.y, r = threadIdx.x;
+  const int h = blockIdx.x, b = blockIdx.y, r = threadIdx.x / kTPR, sub = threadIdx.x % kTPR;
   const int g = h / (P.heads / P.groups);
   const bool live = r < P.dim;
   load_perm(P, g, perm);
-  float S[kLive];
+  float S[kOwn];
   {
     const float* src = carry_at(P.cp, (((long long)b * P.nchunk + c) * P.heads + h) * P.dim + (live ? r : 0));
 #pragma unroll
-    for (int j = 0; j < kLive; ++j) S[j] = live ? src[j] : 0.f;
+    for (int m = 0; m < kOwn; ++m) S[m] = live ? src[stored_j(m, sub)] : 0.f;
   }
   float sc8, sc4;
   for (int k = 0; k < P.chunk; ++k) {
@@ -252,124 +267,155 @@ __global__ void __launch_bounds__(128) ste_history_kernel(const SteParams P, int
     if (live) {
       float* dst = carry_at(P.hist, (((long long)b * P.chunk + k) * P.heads + h) * P.dim + r);
 #pragma unroll
-      for (int j = 0; j < kLive; ++j) dst[j] = S[j];
+      for (int m = 0; m < kOwn; ++m) dst[stored_j(m, sub)] = S[m];
     }
     stage_token(P, b, t, h, g, perm, s, false);
     const float x = live ? h2f(P.x[(long long)b * P.x_sb + (long long)t * P.x_st + (long long)h * P.dim + r]) : 0.f;
-    step_live(S, s, x);
+    step_own(S, s, x, sub);
     requant(S, sc8, sc4);
   }
 }
 
-// Sum over a 16-row tile (lanes of one half-warp) in numpy's pairwise order: rows j and
-// j + 8, then neighbours, pairs and halves; every lane of the tile receives the sum.
-__device__ __forceinline__ float tile_pairwise16(float v) {
-  v = fadd(v, __shfl_xor_sync(0xffffffffu, v, 8));
-  v = fadd(v, __shfl_xor_sync(0xffffffffu, v, 1));
-  v = fadd(v, __shfl_xor_sync(0xffffffffu, v, 2));
-  v = fadd(v, __shfl_xor_sync(0xffffffffu, v, 4));
-  return v;
+constexpr int kStageLanes = 32;   // tier lanes of dB / dC terms staged per block
+
+struct BackShared {
+  TokenShared s;
+  int perm[128];
+  float stage[2][kStageLanes][129];   // [dB | dC][lane in block][row], padded
+  float row_dl[128];
+};
+
+// Per-token quantities of one row in the reverse walk.
+struct RowCtx {
+  float x, gy, factor, ad;
+  const float* prev;
+  bool live;
+  int r;
+};
+
+// A stored lane (adjoint index m, tier index j, position k in its tier's running sums).
+__device__ __forceinline__ void back_live_lane(BackShared& sh, const RowCtx& rc, float (&adj)[kOwn], int m, int j,
+                                               int k, float (&ax)[2], float (&al)[2]) {
+  const TokenShared& s = sh.s;
+  const float pj = rc.live ? rc.prev[j] : 0.f;
+  const float bj = s.b[j], cj = s.c[j];
+  const float bdt = fmul(bj, s.dt);
+  const float v = fadd(fmul(rc.gy, cj), adj[m]);                 // STE: identity on live lanes
+  const float hj = fadd(fmul(pj, s.decay), fmul(bdt, rc.x));
+  const float e = fadd(fmul(pj, rc.ad), fmul(bj, rc.x));
+  run_add(ax, k, fmul(v, bdt));
+  run_add(al, k, fmul(v, e));
+  sh.stage[0][j % kStageLanes][rc.r] = fmul(v, rc.factor);
+  sh.stage[1][j % kStageLanes][rc.r] = fmul(hj, rc.gy);
+  adj[m] = fmul(v, s.decay);
+}
+// A lane of the pruned block (position k of the thread's 16; k >= 12 are the masked zeros).
+__device__ __forceinline__ void back_pruned_lane(BackShared& sh, const RowCtx& rc, int k, int sub, float (&ax)[2],
+                                                 float (&al)[2]) {
+  const TokenShared& s = sh.s;
+  if (k < 12) {
+    const int j = kLive + own_lane(k, sub);
+    const float bj = s.b[j], cj = s.c[j];
+    const float bdt = fmul(bj, s.dt);
+    const float v = fmul(rc.gy, cj);
+    run_add(ax, k, fmul(v, bdt));
+    run_add(al, k, fmul(v, fmul(bj, rc.x)));
+    sh.stage[0][j % kStageLanes][rc.r] = fmul(v, rc.factor);
+    sh.stage[1][j % kStageLanes][rc.r] = fmul(fmul(bdt, rc.x), rc.gy);
+  } else {
+    const float v = fmul(rc.gy, 0.0f);
+    run_add(ax, k, fmul(v, fmul(0.0f, s.dt)));
+    run_add(al, k, fmul(v, fmul(0.0f, rc.x)));
+  }
+}
+// Sum each row tile's 16 staged terms of lane block `blk` in row order into the partials.
+__device__ __forceinline__ void flush_block(BackShared& sh, float* part, int blk, int ntile) {
+  __syncthreads();
+  for (int i = threadIdx.x; i < 2 * kStageLanes * ntile; i += blockDim.x) {
+    const int which = i / (kStageLanes * ntile), rem = i % (kStageLanes * ntile);
+    const int tile = rem / kStageLanes, lane = rem % kStageLanes;
+    const float* col = &sh.stage[which][lane][tile * 16];
+    float acc = col[0];
+#pragma unroll
+    for (int q = 1; q < 16; ++q) acc = fadd(acc, col[q]);
+    part[(tile * 2 + which) * 128 + blk * kStageLanes + lane] = acc;
+  }
+  __syncthreads();
 }
 
-constexpr int kStageLanes = 32;   // lanes of dB / dC terms staged per block
-
-__global__ void __launch_bounds__(128) ste_backward_kernel(const SteParams P, int c) {
-  __shared__ TokenShared s;
-  __shared__ int perm[128];
-  __shared__ float stage[2][kStageLanes][129];       // [dB | dC][lane][row], padded
-  __shared__ float tile_dl[8];
-  const int h = blockIdx.x, b = blockIdx.y, r = threadIdx.x;
+__global__ void __launch_bounds__(512) ste_backward_kernel(const SteParams P, int c) {
+  __shared__ BackShared sh;
+  const int h = blockIdx.x, b = blockIdx.y, r = threadIdx.x / kTPR, sub = threadIdx.x % kTPR;
   const int g = h / (P.heads / P.groups);
   const int ntile = (P.dim + 15) / 16;
   const bool live = r < P.dim;
-  load_perm(P, g, perm);
+  load_perm(P, g, sh.perm);
   const float av = P.A[h], dv = ldf(P.D, P.d_is_f32, h);
-  float adj[kLive];
+  float adj[kOwn];
   float* adj_row = carry_at(P.adj, ((long long)b * P.heads + h) * P.dim + (live ? r : 0));
 #pragma unroll
-  for (int j = 0; j < kLive; ++j) adj[j] = live ? adj_row[j] : 0.f;
+  for (int m = 0; m < kOwn; ++m) adj[m] = live ? adj_row[stored_j(m, sub)] : 0.f;
   for (int rev = 0; rev < P.chunk; ++rev) {
     const int k = P.chunk - 1 - rev;
     const int t = c * P.chunk + k;
     if (t >= P.length) continue;
-    stage_token(P, b, t, h, g, perm, s, true);
+    stage_token(P, b, t, h, g, sh.perm, sh.s, true);
     const long long xo = (long long)b * P.x_sb + (long long)t * P.x_st + (long long)h * P.dim + r;
-    const float x = live ? h2f(P.x[xo]) : 0.f;
-    const float gy = live ? h2f(P.dy[xo]) : 0.f;
-    const float factor = fmul(s.dt, x);                 // 0 on rows past dim (x = 0 there)
-    const float ad = fmul(av, s.decay);
-    const float* prev = carry_at(P.hist, (((long long)b * P.chunk + k) * P.heads + h) * P.dim + (live ? r : 0));
+    RowCtx rc;
+    rc.live = live;
+    rc.r = r;
+    rc.x = live ? h2f(P.x[xo]) : 0.f;
+    rc.gy = live ? h2f(P.dy[xo]) : 0.f;
+    rc.factor = fmul(sh.s.dt, rc.x);                   // 0 on rows past dim (x = 0 there)
+    rc.ad = fmul(av, sh.s.decay);
+    rc.prev = carry_at(P.hist, (((long long)b * P.chunk + k) * P.heads + h) * P.dim + (live ? r : 0));
     // dB / dC partials of this (token, head): [tile][dB | dC][128 tier lanes]
     float* part = P.part + (((long long)b * P.chunk + k) * P.heads + h) * ntile * 256;
-    float ax[8], al[8];
-    float dx8 = 0.f, dl8 = 0.f, dx4 = 0.f, dl4 = 0.f;
+    float ax8[2], al8[2], ax4[2], al4[2], axd[2], ald[2];
+    // lane block 0: INT8 lanes (tier 0..15) and INT4 lanes of tier 16..31
 #pragma unroll
-    for (int j = 0; j < 128; ++j) {
-      float pb, pc;                                     // this row's dB and dC terms of lane j
-      if (j < kLive) {                                  // STE: identity through the live lanes
-        const float pj = live ? prev[j] : 0.f;
-        const float bj = s.b[j], cj = s.c[j];
-        const float bdt = fmul(bj, s.dt);
-        const float v = fadd(fmul(gy, cj), adj[j]);
-        const float hj = fadd(fmul(pj, s.decay), fmul(bdt, x));
-        const float e = fadd(fmul(pj, ad), fmul(bj, x));
-        const int q = j < kLive8 ? j : j - kLive8;
-        pw_add(ax, q, fmul(v, bdt));
-        pw_add(al, q, fmul(v, e));
-        pb = fmul(v, factor);
-        pc = fmul(hj, gy);
-        adj[j] = fmul(v, s.decay);
-        if (j == kLive8 - 1) { dx8 = pw_total(ax); dl8 = pw_total(al); }
-        if (j == kLive - 1) { dx4 = pw_total(ax); dl4 = pw_total(al); }
-      } else {                                          // pruned lanes: readout only
-        const float bj = s.b[j], cj = s.c[j];
-        const float bdt = fmul(bj, s.dt);
-        const float v = fmul(gy, cj);
-        pw_add(ax, j - kLive, fmul(v, bdt));
-        pw_add(al, j - kLive, fmul(v, fmul(bj, x)));
-        pb = fmul(v, factor);
-        pc = fmul(fmul(bdt, x), gy);
-      }
-      stage[0][j % kStageLanes][r] = pb;
-      stage[1][j % kStageLanes][r] = pc;
-      if (j % kStageLanes == kStageLanes - 1) {
-        __syncthreads();
-        // each tile's 16 rows summed in row order (numpy's order for a sum over rows)
-        for (int i = threadIdx.x; i < 2 * kStageLanes * ntile; i += blockDim.x) {
-          const int which = i / (kStageLanes * ntile), rem = i % (kStageLanes * ntile);
-          const int tile = rem / kStageLanes, lane = rem % kStageLanes;
-          const float* col = &stage[which][lane][tile * 16];
-          float acc = col[0];
+    for (int m = 0; m < kOwn8; ++m) back_live_lane(sh, rc, adj, m, own_lane(m, sub), m, ax8, al8);
 #pragma unroll
-          for (int q = 1; q < 16; ++q) acc = fadd(acc, col[q]);
-          part[(tile * 2 + which) * 128 + (j + 1 - kStageLanes) + lane] = acc;
-        }
-        __syncthreads();
-      }
-    }
-    // the pruned block is 64 wide in the reference: 16 masked zero lanes close the sums
+    for (int m = 0; m < 4; ++m) back_live_lane(sh, rc, adj, kOwn8 + m, kLive8 + own_lane(m, sub), m, ax4, al4);
+    flush_block(sh, part, 0, ntile);
+    // block 1: INT4 lanes of tier 32..63
 #pragma unroll
-    for (int q = 48; q < 64; ++q) {
-      const float v = fmul(gy, 0.0f);
-      pw_add(ax, q, fmul(v, fmul(0.0f, s.dt)));
-      pw_add(al, q, fmul(v, fmul(0.0f, x)));
-    }
-    const float dxd = pw_total(ax), dld = pw_total(al);
-    if (live) P.dx[xo] = fadd(fadd(dx8, dx4), fadd(dxd, fmul(gy, dv)));
-    const float dl = tile_pairwise16(live ? fadd(fadd(dl8, dl4), dld) : 0.f);
-    if ((r & 15) == 0 && (r >> 4) < ntile) tile_dl[r >> 4] = dl;
+    for (int m = 4; m < 12; ++m) back_live_lane(sh, rc, adj, kOwn8 + m, kLive8 + own_lane(m, sub), m, ax4, al4);
+    flush_block(sh, part, 1, ntile);
+    // block 2: INT4 lanes of tier 64..79, pruned lanes of tier 80..95
+#pragma unroll
+    for (int m = 12; m < 16; ++m) back_live_lane(sh, rc, adj, kOwn8 + m, kLive8 + own_lane(m, sub), m, ax4, al4);
+#pragma unroll
+    for (int kd = 0; kd < 4; ++kd) back_pruned_lane(sh, rc, kd, sub, axd, ald);
+    flush_block(sh, part, 2, ntile);
+    // block 3: pruned lanes of tier 96..127, then the masked zero lanes of the 64-wide block
+#pragma unroll
+    for (int kd = 4; kd < kOwnD; ++kd) back_pruned_lane(sh, rc, kd, sub, axd, ald);
+    flush_block(sh, part, 3, ntile);
+    const float dx8 = row_pairwise(ax8), dx4 = row_pairwise(ax4), dxd = row_pairwise(axd);
+    const float dl8 = row_pairwise(al8), dl4 = row_pairwise(al4), dld = row_pairwise(ald);
+    if (live && sub == 0) P.dx[xo] = fadd(fadd(dx8, dx4), fadd(dxd, fmul(rc.gy, dv)));
+    if (sub == 0) sh.row_dl[r] = live ? fadd(fadd(dl8, dl4), dld) : 0.f;
     __syncthreads();
-    // d(dt raw) = sum over tiles, in tile order, of (tile sum) * softplus'(raw)
+    // d(dt raw): each tile's 16 rows in numpy's pairwise order, times softplus'(raw), added
+    // over the tiles in order
     if (threadIdx.x == 0) {
-      const float sig = s.raw <= 20.0f ? __fdiv_rn(1.0f, fadd(1.0f, expf(-s.raw))) : 1.0f;
+      const float sig = sh.s.raw <= 20.0f ? __fdiv_rn(1.0f, fadd(1.0f, expf(-sh.s.raw))) : 1.0f;
       float acc = 0.0f;
-      for (int i = 0; i < ntile; ++i) acc = fadd(acc, fmul(tile_dl[i], sig));
+      for (int i = 0; i < ntile; ++i) {
+        const float* d = &sh.row_dl[i * 16];
+        float q[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[j] = fadd(d[j], d[j + 8]);
+        const float tsum = fadd(fadd(fadd(q[0], q[1]), fadd(q[2], q[3])), fadd(fadd(q[4], q[5]), fadd(q[6], q[7])));
+        acc = fadd(acc, fmul(tsum, sig));
+      }
       P.ddt[((long long)b * P.length + t) * P.heads + h] = acc;
     }
   }
   if (live) {
 #pragma unroll
-    for (int j = 0; j < kLive; ++j) adj_row[j] = adj[j];
+    for (int m = 0; m < kOwn; ++m) adj_row[stored_j(m, sub)] = adj[m];
   }
 }
 
@@ -389,7 +435,9 @@ __global__ void __launch_bounds__(256) ste_bc_reduce_kernel(const SteParams P, i
   (which ? P.dc : P.db)[o] = acc;
 }
 
-int threads_for(int dim) { return (dim + 31) / 32 * 32; }
+// four threads per row over whole 16-row tiles, so every tile's rows exist (rows past dim
+// carry zeros, as the reference's masked rows)
+int threads_for(int dim) { return kTPR * ((dim + 15) / 16 * 16); }
 
 }  // namespace
 
