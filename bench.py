@@ -514,9 +514,13 @@ def measure_config5(ex, wins_rng_seed, device, pk, prompt_len=1024, new_tokens=2
                 ex.capture_decode(tok)
                 ex.replay_decode(8)
                 te = timed(lambda: ex.replay_decode(n), 1)
+                ex.decode_persistent(tok, n)
+                tpe = timed(lambda: ex.decode_persistent(tok, n), 1)
+                ex.check()
             finally:
                 ex.set_exact_projections(False)
             r['exact_graph_replay_tokens_per_s'] = n / te
+            r['exact_tokens_per_s'] = n / tpe
         else:
             ex.capture_decode(tok)
             ex.replay_decode(8)
@@ -660,9 +664,12 @@ def main():
                       roofline_tokens_per_s=b1['roofline_tokens_per_s'], frac=b1['frac'],
                       bytes_per_token=DECODE_BYTES_B1, graph_replay_tokens_per_s=b1['graph_replay_tokens_per_s'],
                       exact_graph_replay_tokens_per_s=b1['exact_graph_replay_tokens_per_s'],
+                      exact_tokens_per_s=b1['exact_tokens_per_s'],
+                      exact_frac=b1['exact_tokens_per_s'] / b1['roofline_tokens_per_s'],
                       note='config 5: 1024-token prompt, 255 greedy tokens in one persistent cooperative launch '
-                           '(factored-scale projections, the default for decode steps); graph replays = the '
-                           'multi-kernel step as CUDA graphs, also with the exact per-weight fp16 decode')
+                           '(factored-scale projections, the default for decode steps; exact_* = the same '
+                           'launch with the exact per-weight fp16 decode, the reference numerics); graph '
+                           'replays = the multi-kernel step as CUDA graphs, in both numerics')
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

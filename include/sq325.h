@@ -304,10 +304,11 @@ int sq_model_check(sq_model* model, void* stream);
  * (the loop of infer_fp4_ridge_resurface_v1.py:100-110 after the prompt): step s feeds tokens[0] at
  * position pos + s, runs all layers, the final norm, lm_head and argmax, overwrites
  * tokens[0] with the pick and stores it in out_tokens[s] (device, may be NULL).  Requires
- * batch-1 states (pos > 0: prompt already consumed), reserve(), and the factored-scale
- * projections (sq_model_set_exact_skinny(model, 0)); the logits of the last step are left
- * in the model's greedy workspace.  Same tokens and states as sq_model_forward +
- * sq_model_greedy per step. */
+ * batch-1 states (pos > 0: prompt already consumed) and reserve(); the projections and the
+ * head follow sq_model_set_exact_skinny (factored global scale by default, the exactly
+ * decoded fp16 weights when set); the logits of the last step are left in the model's greedy
+ * workspace.  Same tokens and states as sq_model_forward + sq_model_greedy per step, in
+ * either mode. */
 int sq_model_decode(sq_model* model, int64_t* tokens, int pos, int steps, int64_t* out_tokens, void* stream);
 /* Inspection (the role of the reference's per-layer forward hooks, e.g. the Resurface
  * capture hooks of mamba2_recall/resurface_native.py:168-169): when `out` is non-NULL every

@@ -759,8 +759,6 @@ int sq_model_decode(sq_model* m, int64_t* tokens, int pos, int steps, int64_t* o
   if (!m || !tokens || steps <= 0 || pos <= 0) return fail(SQ_EINVAL, "decode: bad arguments (pos > 0: prefill first)");
   Busy busy(m);
   if (!busy.ok) return fail(SQ_ESTATE, "decode: concurrent/reentrant use of one model context");
-  if (m->exact_skinny)
-    return fail(SQ_EINVAL, "decode: the persistent kernel runs the factored-scale projections (exact mode is off)");
   if (!m->logits || !m->norm_f) return fail(SQ_ESTATE, "decode: reserve() and set_globals() first");
   if (m->dec_dirty) {
     const int s = decode_setup(m);
@@ -779,6 +777,7 @@ int sq_model_decode(sq_model* m, int64_t* tokens, int pos, int steps, int64_t* o
   P.sync = reinterpret_cast<DecodeSync*>(m->d_dbuf + kDecSync);
   P.err = m->d_err; P.tok = (long long*)tokens; P.out_tokens = (long long*)out_tokens;
   P.n_layer = m->cfg.n_layer; P.vocab = m->cfg.vocab; P.eps = m->cfg.eps;
+  P.exact = m->exact_skinny ? 1 : 0;
   // fresh barrier words (an aborted launch leaves its count and abort flag behind)
   if (cudaMemsetAsync(P.sync, 0, sizeof(DecodeSync), (cudaStream_t)stream) != cudaSuccess)
     return cuda_fail("decode: barrier reset");

@@ -282,11 +282,14 @@ __device__ __forceinline__ bool wait_chunk(const Ring& R, int c, const DecodeSyn
 }
 
 // One chunk (16 rows x 1024 columns in ring stage `cs`) of a tile: warp cw of the group takes
-// 128-column sub-chunks cw and cw + 4, decodes them into mma.sync A fragments (factored
-// global scale) and accumulates even / odd k-steps in acc / acc2.  xoff[s2][qq]: offset of the
-// 8 input values k = sub * 128 + tq * 32 + 8 qq of the chunk (x_offsets).
+// 128-column sub-chunks cw and cw + 4, decodes them into mma.sync A fragments and accumulates
+// even / odd k-steps in acc / acc2.  EXACT: every weight FP16(FP32(m b) g), the reference's
+// decoded weight (g2 = the global scale twice); otherwise the exact fp16 products m b, the
+// global scale applied per output by the caller.  xoff[s2][qq]: offset of the 8 input values
+// k = sub * 128 + tq * 32 + 8 qq of the chunk (x_offsets).
+template <bool EXACT>
 __device__ __forceinline__ void chunk_mma(const unsigned char* cs, const uint16_t* Xs, int kc, int cw, int lane,
-                                          const int (&xoff)[2][4], float (&acc)[4], float (&acc2)[4]) {
+                                          const int (&xoff)[2][4], float2 g2, float (&acc)[4], float (&acc2)[4]) {
   const int gq = lane >> 2, tq = lane & 3;
   constexpr int code_row = kKc / 2, scale_row = kKc / 16;
   const unsigned char* ss = cs + kCodeBytes;
@@ -315,10 +318,17 @@ __device__ __forceinline__ void chunk_mma(const unsigned char* cs, const uint16_
       for (int jj = 0; jj < 2; ++jj) {
         const int j = w4 * 2 + jj;
         uint32_t a[4];
-        a[0] = hmul2_u32(ma[2 * jj], bsA);
-        a[1] = hmul2_u32(mb[2 * jj], bsB);
-        a[2] = hmul2_u32(ma[2 * jj + 1], bsA);
-        a[3] = hmul2_u32(mb[2 * jj + 1], bsB);
+        if (EXACT) {
+          a[0] = scale_pair(ma[2 * jj], bsA, g2);
+          a[1] = scale_pair(mb[2 * jj], bsB, g2);
+          a[2] = scale_pair(ma[2 * jj + 1], bsA, g2);
+          a[3] = scale_pair(mb[2 * jj + 1], bsB, g2);
+        } else {
+          a[0] = hmul2_u32(ma[2 * jj], bsA);
+          a[1] = hmul2_u32(mb[2 * jj], bsB);
+          a[2] = hmul2_u32(ma[2 * jj + 1], bsA);
+          a[3] = hmul2_u32(mb[2 * jj + 1], bsB);
+        }
         const uint4 xq = xr[j >> 1];
         const uint32_t b0 = (j & 1) ? xq.z : xq.x, b1 = (j & 1) ? xq.w : xq.y;
         mma16816((j & 1) ? acc2 : acc, a, b0, b1);
@@ -346,9 +356,10 @@ __device__ __forceinline__ void x_offsets(int cw, int tq, int (&xoff)[2][4]) {
 // columns from ring counter ctr on (cpt per tile, cpt even); tiles alternate between the two
 // 4-warp consumer groups, and the producer issues each pair of tiles chunk-interleaved (tile
 // 2m chunk kc at ctr + 2m cpt + 2 kc, tile 2m + 1 one after it) so that both groups see the
-// whole ring ahead of them; per tile the fp4_gemv_stream_kernel arithmetic (factored
-// global scale), chunks taken two per wait, the four warps' sums added in order.
-template <bool XSWZ>
+// whole ring ahead of them; per tile the fp4_gemv_stream_kernel arithmetic (EXACT: weights
+// decoded exactly; else the factored global scale), chunks taken two per wait, the four
+// warps' sums added in order.
+template <bool XSWZ, bool EXACT>
 __device__ void gemv_phase(const DecodeParams& P, const Ring& R, const unsigned char* sm, int ctr, int t0, int t1,
                            int cpt, const uint16_t* Xs, const float* gptr, uint16_t* Y, float* red, bool argmax,
                            float& best, int& bidx, bool& ok) {
@@ -356,6 +367,7 @@ __device__ void gemv_phase(const DecodeParams& P, const Ring& R, const unsigned 
   const int q = warp >> 2, cw = warp & 3;
   const int gq = lane >> 2, tq = lane & 3;
   const float gsc = *gptr;
+  const float2 g2 = make_float2(gsc, gsc);
   int xoff[2][4];
   x_offsets<XSWZ>(cw, tq, xoff);
   for (int i = q; i < t1 - t0; i += 2) {
@@ -372,8 +384,8 @@ __device__ void gemv_phase(const DecodeParams& P, const Ring& R, const unsigned 
         set_abort(P, (int)kDevTimeoutMma);
       }
       if (ok) {
-        chunk_mma(sm + oRing + st0 * kStageBytes, Xs, kc, cw, lane, xoff, acc, acc2);
-        chunk_mma(sm + oRing + st1 * kStageBytes, Xs, kc + 1, cw, lane, xoff, acc, acc2);
+        chunk_mma<EXACT>(sm + oRing + st0 * kStageBytes, Xs, kc, cw, lane, xoff, g2, acc, acc2);
+        chunk_mma<EXACT>(sm + oRing + st1 * kStageBytes, Xs, kc + 1, cw, lane, xoff, g2, acc, acc2);
       }
       __syncwarp();
       if (lane == 0) {
@@ -390,8 +402,9 @@ __device__ void gemv_phase(const DecodeParams& P, const Ring& R, const unsigned 
       for (int w = 0; w < 4; ++w)
 #pragma unroll
         for (int e = 0; e < 4; ++e) sacc[e] += rq[(w * 32 + lane) * 4 + e];
+      if (!EXACT)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) sacc[e] *= gsc;
+        for (int e = 0; e < 4; ++e) sacc[e] *= gsc;
       if (tq == 0) {
         const int na = tile * kRows + gq, nb = na + 8;
         const uint16_t ya = f2h(sacc[0]), yb = f2h(sacc[2]);
@@ -971,6 +984,7 @@ drain:
   if (armed) mb_drain(full, (uint32_t)(armed - 1) & 1u);
 }
 
+template <bool EXACT>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_step_kernel(const __grid_constant__ DecodeParams P) {
   extern __shared__ __align__(1024) unsigned char sm[];
@@ -1066,7 +1080,8 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     }
     DTRACE(l, 1);
     DWARP(l, 0);
-    gemv_phase<false>(P, R, sm, ctr, rin.t0, rin.t1, kDModel / kKc, hn, L.in_g, P.zx, red, false, best, bidx, ok);
+    gemv_phase<false, EXACT>(P, R, sm, ctr, rin.t0, rin.t1, kDModel / kKc, hn, L.in_g, P.zx, red, false, best, bidx,
+                             ok);
     DWARP(l, 1);
     ctr += (rin.t1 - rin.t0) * (kDModel / kKc);
     DTRACE(l, 2);
@@ -1117,7 +1132,8 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     }
     DTRACE(l, 6);
     DWARP(l, 2);
-    gemv_phase<true>(P, R, sm, ctr, rout.t0, rout.t1, kDInner / kKc, yn, L.out_g, P.h, red, false, best, bidx, ok);
+    gemv_phase<true, EXACT>(P, R, sm, ctr, rout.t0, rout.t1, kDInner / kKc, yn, L.out_g, P.h, red, false, best, bidx,
+                            ok);
     DWARP(l, 3);
     ctr += (rout.t1 - rout.t0) * (kDInner / kKc);
     DTRACE(l, 7);
@@ -1136,7 +1152,8 @@ decode_step_kernel(const __grid_constant__ DecodeParams P) {
     ++arms_nw;
     bulk_g2s(Nw, P.layers[0].norm_w, kDModel * 2, sbNw);
   }
-  gemv_phase<false>(P, R, sm, ctr, rhead.t0, rhead.t1, kDModel / kKc, hn, P.head_g, P.logits, red, true, best, bidx, ok);
+  gemv_phase<false, EXACT>(P, R, sm, ctr, rhead.t0, rhead.t1, kDModel / kKc, hn, P.head_g, P.logits, red, true, best,
+                           bidx, ok);
   ctr += (rhead.t1 - rhead.t0) * (kDModel / kKc);
   // CTA candidate: warps 0 and 4 hold the per-lane picks of their group
   if ((warp & 3) == 0) {
@@ -1207,7 +1224,9 @@ extern "C" int sq_decode_arrive_read(unsigned long long* host) {
 int prepare_decode_kernel() {
   static bool done = false;
   if (done) return kOk;
-  if (cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+  if (cudaFuncSetAttribute(decode_step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(decode_step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
     return kECuda;
   done = true;
   return kOk;
@@ -1220,8 +1239,12 @@ int decode_grid() {
   cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
   if (!coop || sms <= 0) return -1;
   if (prepare_decode_kernel() != kOk) return -1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_step_kernel, kThreads, kSmem) != cudaSuccess ||
-      per_sm < 1)
+  int per_sm_exact = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_step_kernel<false>, kThreads, kSmem) !=
+          cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_exact, decode_step_kernel<true>, kThreads, kSmem) !=
+          cudaSuccess ||
+      per_sm < 1 || per_sm_exact < 1)
     return -1;
   return sms;
 }
@@ -1238,7 +1261,8 @@ int launch_decode_step(const DecodeParams& p, int grid, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_step_kernel, p);
+  const cudaError_t e = p.exact ? cudaLaunchKernelEx(&cfg, decode_step_kernel<true>, p)
+                                : cudaLaunchKernelEx(&cfg, decode_step_kernel<false>, p);
   if (e != cudaSuccess) { cudaGetLastError(); last_launch_error() = e; return kECuda; }
   return kOk;
 }

@@ -57,6 +57,7 @@ struct DecodeParams {
   long long* out_tokens;         // [steps] picks (may be null)
   int n_layer, vocab, pos, steps; // pos: position of the first step's token
   float eps;
+  int exact;                     // 1: projections and head with the exactly decoded fp16 weights
 };
 
 // Dynamic shared memory of the kernel; decode_grid() = CTAs of one cooperative launch (one

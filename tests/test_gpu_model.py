@@ -169,15 +169,18 @@ def test_factored_scale_projections_track_exact(pair):
     assert rel_l2(outs[False][1], outs[True][1]) < 5e-3
 
 
-def test_persistent_decode_matches_graph_replay(pair):
+@pytest.mark.parametrize('exact', [False, True])
+def test_persistent_decode_matches_graph_replay(pair, exact):
     """The one-launch-per-token decode kernel reproduces the multi-kernel graph replay:
-    identical greedy tokens, identical packed states and conv rings, identical last logits."""
+    identical greedy tokens, identical packed states and conv rings; with the factored global
+    scale and with the exactly decoded fp16 weights (the reference's)."""
     from sq325 import PredictorState, generate
     gm, _, statics = pair
     prompt = np.random.default_rng(31).integers(0, gm.vocab, (1, 9))
     runs = {}
     for persistent in (False, True):
         with PredictorState(gm, *statics) as ex:
+            ex.set_exact_projections(exact)
             seq = generate(ex, prompt, 13, graphs=True, persistent=persistent)
             torch.cuda.synchronize()
             ex.check()
@@ -243,35 +246,37 @@ def test_hard_gate_prefill_and_decode(hard_pair):
 def test_persistent_decode_matches_graph_replay_full_size():
     """The benchmarked size: 56 layers (released layouts), vocabulary 256,000, 16 greedy tokens
     after a 64-token prompt.  The one-launch persistent kernel and the multi-kernel CUDA-graph
-    replay must give identical tokens, identical packed states and conv rings, and identical
-    logits of the last step."""
+    replay must give identical tokens, identical packed states and conv rings, with the
+    factored global scale and with the exactly decoded fp16 weights (the reference's)."""
     from sq325 import model as M, resurface as R
     from sq325.state import PredictorState
     model = M.synthetic_model(seed=4, n_layer=56, vocab=256000, device='cuda')
     model.adapter = R.random_bank(56, seed=5, device='cuda')
     statics = M.synthetic_statics(M.RELEASED_LAYOUTS, seed=4, device='cuda')
     prompt = torch.from_numpy(np.random.default_rng(77).integers(0, 256000, (1, 64))).cuda()
-    runs = {}
-    for persistent in (False, True):
-        with PredictorState(model, *statics) as ex:
-            tok = ex.greedy(ex.backbone(prompt, reset=True)[:, -1]).clone()
-            if persistent:
-                seq = ex.decode_persistent(tok, 16)
-            else:
-                ex.capture_decode(tok)
-                seq = ex.replay_decode(16)
-            torch.cuda.synchronize()
-            ex.check()
-            states = [{k: v.view(torch.uint8).clone() for k, v in e.state.tensors.items()} for e in ex._cache]
-            rings = [ex.conv_chronological(l).clone() for l in range(56)]
-            runs[persistent] = (seq.cpu(), states, rings)
-            del ex
-    assert torch.equal(runs[True][0], runs[False][0]), (runs[True][0].ravel(), runs[False][0].ravel())
-    for layer, (a, b) in enumerate(zip(runs[True][1], runs[False][1])):
-        for k in a:
-            assert torch.equal(a[k], b[k]), (layer, k)
-    for a, b in zip(runs[True][2], runs[False][2]):
-        assert torch.equal(a, b)
+    for exact in (False, True):
+        runs = {}
+        for persistent in (False, True):
+            with PredictorState(model, *statics) as ex:
+                ex.set_exact_projections(exact)
+                tok = ex.greedy(ex.backbone(prompt, reset=True)[:, -1]).clone()
+                if persistent:
+                    seq = ex.decode_persistent(tok, 16)
+                else:
+                    ex.capture_decode(tok)
+                    seq = ex.replay_decode(16)
+                torch.cuda.synchronize()
+                ex.check()
+                states = [{k: v.view(torch.uint8).clone() for k, v in e.state.tensors.items()} for e in ex._cache]
+                rings = [ex.conv_chronological(l).clone() for l in range(56)]
+                runs[persistent] = (seq.cpu(), states, rings)
+                del ex
+        assert torch.equal(runs[True][0], runs[False][0]), (exact, runs[True][0].ravel(), runs[False][0].ravel())
+        for layer, (a, b) in enumerate(zip(runs[True][1], runs[False][1])):
+            for k in a:
+                assert torch.equal(a[k], b[k]), (exact, layer, k)
+        for a, b in zip(runs[True][2], runs[False][2]):
+            assert torch.equal(a, b), exact
 
 
 def test_projection_gemm_timer_counts_large_m_launches(pair):
