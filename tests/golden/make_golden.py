@@ -307,6 +307,22 @@ def ste_case(reference, seed=500, batch=2, length=10, heads=4, dim=16, groups=2,
         sts._chunk_backward[grid](x, dt, A, Bm, Cm, D, dt_bias, perm, hist, adj, dy, dx, ddt, db, dc, length, heads,
                                   dim, groups, chunk, c, 16)
     rec.update(checkpoints=cp, dx=dx, ddt=ddt, db=db, dc=dc, chunk=torch.tensor(chunk))
+    # the diagnostic encode / decode (state_codec.py:265-331) through the reference's own
+    # functions: a dense carry in permuted order with an all-zero row (scale floor 1e-8) and
+    # exact half-step values (ties away from zero), then decode in both coordinate orders
+    dense = torch.randn(batch, heads, dim, 128, generator=gen) * 3
+    dense[0, 0, 0] = 0
+    dense[0, 0, 1, :16] = torch.linspace(-127, 127, 16)
+    dense[0, 0, 1, 3] = -2.5
+    dense[0, 0, 1, 16:80] = torch.linspace(-7, 7, 64)
+    dense[0, 0, 1, 20] = 3.5
+    dense[0, 0, 1, 21] = -0.5
+    state = sc.allocate_state(batch, heads, dim, 128, 'sq3p25', 'cpu')
+    sc.encode_state_(state, dense)
+    rec['enc_dense'] = dense
+    rec.update({'enc_' + k: v.clone() for k, v in state.tensors.items()})
+    rec['dec_plain'] = sc.decode_state(state)
+    rec['dec_perm'] = sc.decode_state(state, perm)
     return {k: v.numpy() for k, v in rec.items()}
 
 

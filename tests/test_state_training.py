@@ -107,3 +107,19 @@ def test_ste_abi_validation_needs_no_gpu():
     assert lib.sq_sq3p25_scan(C.byref(a), None) == _lib.SQ_EINVAL
     assert b'null pointer' in lib.sq_last_error()
     assert lib.sq_ste_backward(C.byref(a), 4, None, None, None, None, None, None, 0, None) == _lib.SQ_EINVAL
+
+
+@pytest.mark.parametrize('case', ['ste.npz', 'ste_ragged.npz'])
+def test_sq3p25_encode_decode_match_reference(golden, case):
+    """encode_state_ and decode_state (both coordinate orders) against the reference's own
+    functions run on the same dense carry (state_codec.py:265-331): packed bytes and scales
+    bit for bit, including an all-zero row and exact half-step ties."""
+    d = golden(case)
+    b, h, p, _ = d['enc_dense'].shape
+    st = sc.allocate_state(b, h, p, 128, 'sq3p25', 'cpu')
+    sc.encode_state_(st, torch.from_numpy(d['enc_dense']))
+    for k in ('lo', 'hi', 'q4', 's8', 's4'):
+        assert np.array_equal(st.tensors[k].numpy().view(np.uint8), d['enc_' + k].view(np.uint8)), k
+    assert np.array_equal(sc.decode_state(st).numpy().view(np.uint32), d['dec_plain'].view(np.uint32))
+    perm = torch.from_numpy(d['permutation'])
+    assert np.array_equal(sc.decode_state(st, perm).numpy().view(np.uint32), d['dec_perm'].view(np.uint32))
