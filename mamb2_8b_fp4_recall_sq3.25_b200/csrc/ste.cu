@@ -113,10 +113,37 @@ __device__ void stage_token(const SteParams& P, int b, int t, int h, int g, cons
   __syncthreads();
 }
 
-// S = S decay + (B dt) x on the thread's stored lanes
-__device__ __forceinline__ void step_own(float (&S)[kOwn], const TokenShared& s, float x, int sub) {
+// The forward scan and the backward's carry replays stage kTS tokens per pair of CTA
+// barriers: B / C of the group in tier order, and dt / decay computed by kTS threads at once.
+constexpr int kTS = 8;
+struct ChunkShared {
+  float b[kTS][128], c[kTS][128];
+  float dt[kTS], decay[kTS];
+};
+// Stage tokens t0 .. t0 + n - 1 (n <= kTS); threads 0 .. n - 1 compute dt and decay.
+__device__ void stage_tokens(const SteParams& P, int b, int t0, int n, int h, int g, const int* perm,
+                             ChunkShared& s, bool need_c) {
+  __syncthreads();
+  for (int i = threadIdx.x; i < n * 128; i += blockDim.x) {
+    const int tk = i >> 7, j = i & 127;
+    s.b[tk][j] = h2f(P.B[(long long)b * P.b_sb + (long long)(t0 + tk) * P.b_st + g * 128 + perm[j]]);
+    if (need_c) s.c[tk][j] = h2f(P.C[(long long)b * P.c_sb + (long long)(t0 + tk) * P.c_st + g * 128 + perm[j]]);
+  }
+  if (threadIdx.x < n) {
+    const int t = t0 + threadIdx.x;
+    const float raw = fadd(h2f(P.dt[(long long)b * P.dt_sb + (long long)t * P.dt_st + h]),
+                           ldf(P.dt_bias, P.dt_bias_is_f32, h));
+    const float d = softplus20(raw);
+    s.dt[threadIdx.x] = d;
+    s.decay[threadIdx.x] = expf(fmul(P.A[h], d));
+  }
+  __syncthreads();
+}
+
+// S = S decay + (B dt) x on the thread's stored lanes (bt: the token's staged B)
+__device__ __forceinline__ void step_own(float (&S)[kOwn], const float* bt, float dt, float decay, float x, int sub) {
 #pragma unroll
-  for (int m = 0; m < kOwn; ++m) S[m] = fadd(fmul(S[m], s.decay), fmul(fmul(s.b[stored_j(m, sub)], s.dt), x));
+  for (int m = 0; m < kOwn; ++m) S[m] = fadd(fmul(S[m], decay), fmul(fmul(bt[stored_j(m, sub)], dt), x));
 }
 // requant of the thread's stored lanes with the row's scales; the codes through q when asked
 __device__ __forceinline__ void requant(float (&S)[kOwn], float& sc8, float& sc4, float* q = nullptr) {
@@ -149,7 +176,7 @@ __device__ __forceinline__ float* carry_at(float* base, long long idx) { return 
 
 // ------------------------------------------------------------------------ forward scan
 __global__ void __launch_bounds__(512) sq3p25_scan_kernel(const SteParams P) {
-  __shared__ TokenShared s;
+  __shared__ ChunkShared s;
   __shared__ int perm[128];
   const int h = blockIdx.x, b = blockIdx.y, r = threadIdx.x / kTPR, sub = threadIdx.x % kTPR;
   const int g = h / (P.heads / P.groups);
@@ -174,28 +201,35 @@ __global__ void __launch_bounds__(512) sq3p25_scan_kernel(const SteParams P) {
   }
   const float dv = ldf(P.D, P.d_is_f32, h);
   float sc8 = 0.f, sc4 = 0.f, qlast[kOwn];
-  for (int t = 0; t < P.length; ++t) {
-    stage_token(P, b, t, h, g, perm, s, true);
-    const float x = live ? h2f(P.x[(long long)b * P.x_sb + (long long)t * P.x_st + (long long)h * P.dim + r]) : 0.f;
-    step_own(S, s, x, sub);
-    float a8[2], a4[2], ad[2];
+  for (int t0 = 0; t0 < P.length; t0 += kTS) {
+    const int n = min(kTS, P.length - t0);
+    stage_tokens(P, b, t0, n, h, g, perm, s, true);
+    for (int tk = 0; tk < n; ++tk) {
+      const int t = t0 + tk;
+      const float* bt = s.b[tk];
+      const float* ct = s.c[tk];
+      const float dtv = s.dt[tk];
+      const float x = live ? h2f(P.x[(long long)b * P.x_sb + (long long)t * P.x_st + (long long)h * P.dim + r]) : 0.f;
+      step_own(S, bt, dtv, s.decay[tk], x, sub);
+      float a8[2], a4[2], ad[2];
 #pragma unroll
-    for (int m = 0; m < kOwn8; ++m) run_add(a8, m, fmul(S[m], s.c[own_lane(m, sub)]));
+      for (int m = 0; m < kOwn8; ++m) run_add(a8, m, fmul(S[m], ct[own_lane(m, sub)]));
 #pragma unroll
-    for (int m = 0; m < kOwn4; ++m) run_add(a4, m, fmul(S[kOwn8 + m], s.c[kLive8 + own_lane(m, sub)]));
-    // pruned tier: the reference's 64-wide block, 48 coordinates then 16 masked zero lanes
+      for (int m = 0; m < kOwn4; ++m) run_add(a4, m, fmul(S[kOwn8 + m], ct[kLive8 + own_lane(m, sub)]));
+      // pruned tier: the reference's 64-wide block, 48 coordinates then 16 masked zero lanes
 #pragma unroll
-    for (int k = 0; k < kOwnD; ++k) {
-      const int q = own_lane(k, sub);
-      const bool real = k < 12;                       // q < 48
-      const float bj = real ? s.b[kLive + q] : 0.0f, cj = real ? s.c[kLive + q] : 0.0f;
-      run_add(ad, k, fmul(fmul(fmul(bj, s.dt), x), cj));
+      for (int k = 0; k < kOwnD; ++k) {
+        const int q = own_lane(k, sub);
+        const bool real = k < 12;                     // q < 48
+        const float bj = real ? bt[kLive + q] : 0.0f, cj = real ? ct[kLive + q] : 0.0f;
+        run_add(ad, k, fmul(fmul(fmul(bj, dtv), x), cj));
+      }
+      const float o8 = row_pairwise(a8), o4 = row_pairwise(a4), od = row_pairwise(ad);
+      const float out = fadd(fadd(o8, o4), fadd(od, fmul(x, dv)));
+      if (live && sub == 0) P.y[(long long)b * P.y_sb + (long long)t * P.y_st + (long long)h * P.dim + r] = f2h(out);
+      if (t + 1 < P.length) requant(S, sc8, sc4);
+      else requant(S, sc8, sc4, qlast);
     }
-    const float o8 = row_pairwise(a8), o4 = row_pairwise(a4), od = row_pairwise(ad);
-    const float out = fadd(fadd(o8, o4), fadd(od, fmul(x, dv)));
-    if (live && sub == 0) P.y[(long long)b * P.y_sb + (long long)t * P.y_st + (long long)h * P.dim + r] = f2h(out);
-    if (t + 1 < P.length) requant(S, sc8, sc4);
-    else requant(S, sc8, sc4, qlast);
   }
   if (live) {
     // this thread's INT8 lanes are 2 sub, 2 sub + 1 (byte sub) and 2 sub + 8, 2 sub + 9 (byte
@@ -220,7 +254,7 @@ __global__ void __launch_bounds__(512) sq3p25_scan_kernel(const SteParams P) {
 
 // ------------------------------------------------------------------------ STE backward
 __global__ void __launch_bounds__(512) ste_checkpoint_kernel(const SteParams P) {
-  __shared__ TokenShared s;
+  __shared__ ChunkShared s;
   __shared__ int perm[128];
   const int h = blockIdx.x, b = blockIdx.y, r = threadIdx.x / kTPR, sub = threadIdx.x % kTPR;
   const int g = h / (P.heads / P.groups);
@@ -236,19 +270,22 @@ __global__ void __launch_bounds__(512) ste_checkpoint_kernel(const SteParams P) 
 #pragma unroll
       for (int m = 0; m < kOwn; ++m) dst[stored_j(m, sub)] = S[m];
     }
-    for (int k = 0; k < P.chunk; ++k) {
-      const int t = c * P.chunk + k;
-      if (t >= P.length) break;
-      stage_token(P, b, t, h, g, perm, s, false);
-      const float x = live ? h2f(P.x[(long long)b * P.x_sb + (long long)t * P.x_st + (long long)h * P.dim + r]) : 0.f;
-      step_own(S, s, x, sub);
-      requant(S, sc8, sc4);
+    const int cend = min(P.length, (c + 1) * P.chunk);
+    for (int t0 = c * P.chunk; t0 < cend; t0 += kTS) {
+      const int n = min(kTS, cend - t0);
+      stage_tokens(P, b, t0, n, h, g, perm, s, false);
+      for (int tk = 0; tk < n; ++tk) {
+        const int t = t0 + tk;
+        const float x = live ? h2f(P.x[(long long)b * P.x_sb + (long long)t * P.x_st + (long long)h * P.dim + r]) : 0.f;
+        step_own(S, s.b[tk], s.dt[tk], s.decay[tk], x, sub);
+        requant(S, sc8, sc4);
+      }
     }
   }
 }
 
 __global__ void __launch_bounds__(512) ste_history_kernel(const SteParams P, int c) {
-  __shared__ TokenShared s;
+  __shared__ ChunkShared s;
   __shared__ int perm[128];
   const int h = blockIdx.x, b = blockIdx.y, r = threadIdx.x / kTPR, sub = threadIdx.x % kTPR;
   const int g = h / (P.heads / P.groups);
@@ -261,18 +298,21 @@ __global__ void __launch_bounds__(512) ste_history_kernel(const SteParams P, int
     for (int m = 0; m < kOwn; ++m) S[m] = live ? src[stored_j(m, sub)] : 0.f;
   }
   float sc8, sc4;
-  for (int k = 0; k < P.chunk; ++k) {
-    const int t = c * P.chunk + k;
-    if (t >= P.length) break;
-    if (live) {
-      float* dst = carry_at(P.hist, (((long long)b * P.chunk + k) * P.heads + h) * P.dim + r);
+  const int cend = min(P.length, (c + 1) * P.chunk);
+  for (int t0 = c * P.chunk; t0 < cend; t0 += kTS) {
+    const int n = min(kTS, cend - t0);
+    stage_tokens(P, b, t0, n, h, g, perm, s, false);
+    for (int tk = 0; tk < n; ++tk) {
+      const int t = t0 + tk, k = t - c * P.chunk;
+      if (live) {
+        float* dst = carry_at(P.hist, (((long long)b * P.chunk + k) * P.heads + h) * P.dim + r);
 #pragma unroll
-      for (int m = 0; m < kOwn; ++m) dst[stored_j(m, sub)] = S[m];
+        for (int m = 0; m < kOwn; ++m) dst[stored_j(m, sub)] = S[m];
+      }
+      const float x = live ? h2f(P.x[(long long)b * P.x_sb + (long long)t * P.x_st + (long long)h * P.dim + r]) : 0.f;
+      step_own(S, s.b[tk], s.dt[tk], s.decay[tk], x, sub);
+      requant(S, sc8, sc4);
     }
-    stage_token(P, b, t, h, g, perm, s, false);
-    const float x = live ? h2f(P.x[(long long)b * P.x_sb + (long long)t * P.x_st + (long long)h * P.dim + r]) : 0.f;
-    step_own(S, s, x, sub);
-    requant(S, sc8, sc4);
   }
 }
 
