@@ -325,8 +325,8 @@ class PredictorState:
         """Greedy decode at batch 1 with one persistent cooperative kernel launch for all
         `steps` tokens (every layer, the final norm, lm_head and argmax per token).  `tokens` is an int64 [1]
         device tensor holding the token to feed first; it is overwritten with every pick.
-        Returns int64 [steps, 1] picks.  Same tokens and states as `replay_decode`; uses the
-        factored-scale projections."""
+        Returns int64 [steps, 1] picks.  Same tokens and states as `replay_decode`, with the
+        projection numerics that set_exact_projections selects (factored scale by default)."""
         if not self._cache or self._cache[0].tokens == 0:
             raise RuntimeError('Prefill the request before decoding')
         if self._batch_size != 1:
