@@ -61,3 +61,11 @@ def test_argument_validation_needs_no_gpu(lib):
     cfg = _lib.ModelConfig(0, 256000, 1e-5)
     h = C.c_void_p()
     assert lib.sq_model_create(C.byref(cfg), C.byref(h)) == _lib.SQ_EINVAL
+
+
+def test_gemm_timer_validation_needs_no_gpu(lib):
+    from sq325 import _lib
+    assert lib.sq_model_time_gemm(None, 1) == _lib.SQ_EINVAL
+    sec, n = C.c_double(), C.c_int64()
+    assert lib.sq_model_gemm_time(None, C.byref(sec), C.byref(n)) == _lib.SQ_EINVAL
+    assert b'null' in lib.sq_last_error()
